@@ -1,0 +1,316 @@
+// Public API: argument validation, the C++ overloads and the C ABI.
+//
+// Mirrors the reference's src/api/flash_attention_api.cu:
+//   * error strings byte-identical to :21-42 (pinned by the reference's
+//     tests/unit/test_error_handling.cu:236-254);
+//   * validation order of validate_common_params (:45-66): null pointer,
+//     non-positive dimension, unsupported head_dim, non-finite or negative
+//     scale (scale == 0 is accepted);
+//   * backward checks dO/dQ/dK/dV for null before the common checks (:69-79);
+//   * no CUDA call happens before validation succeeds, so invalid arguments
+//     are reported on a machine without a GPU.
+// Dispatch differs: fp16/bf16 go to the tcgen05 kernels, fp32 to the fp32
+// kernels; there is no CPU path.
+
+#include <cmath>
+
+#include "common.cuh"
+
+namespace cuflash {
+
+namespace {
+
+using detail::launch_bwd_f32;
+using detail::launch_bwd_sm100;
+using detail::launch_fwd_f32;
+using detail::launch_fwd_sm100;
+
+inline bool supported_head_dim(int d) { return d == 32 || d == 64 || d == 128; }
+
+FlashAttentionError validate_common(const void* Q, const void* K, const void* V, const void* O,
+                                    const void* L, int batch_size, int num_heads, int seq_len,
+                                    int head_dim, float scale) {
+    if (!Q || !K || !V || !O || !L) return FlashAttentionError::NULL_POINTER;
+    if (batch_size <= 0 || num_heads <= 0 || seq_len <= 0 || head_dim <= 0)
+        return FlashAttentionError::INVALID_DIMENSION;
+    if (!supported_head_dim(head_dim)) return FlashAttentionError::UNSUPPORTED_HEAD_DIM;
+    if (!std::isfinite(scale) || scale < 0.0f) return FlashAttentionError::INVALID_DIMENSION;
+    return FlashAttentionError::SUCCESS;
+}
+
+FlashAttentionError validate_backward(const void* Q, const void* K, const void* V, const void* O,
+                                      const void* L, const void* dO, const void* dQ,
+                                      const void* dK, const void* dV, int batch_size,
+                                      int num_heads, int seq_len, int head_dim, float scale) {
+    if (!dO || !dQ || !dK || !dV) return FlashAttentionError::NULL_POINTER;
+    return validate_common(Q, K, V, O, L, batch_size, num_heads, seq_len, head_dim, scale);
+}
+
+// The launchers index with 32-bit grid coordinates over batch*heads.
+bool fits_grid(int batch_size, int num_heads) {
+    return static_cast<long long>(batch_size) * num_heads <= 0x7fffffffLL;
+}
+
+template <typename T>
+FlashAttentionError forward_lowp(const T* Q, const T* K, const T* V, T* O, float* L, int B, int H,
+                                 int N, int D, float scale, bool causal, cudaStream_t stream) {
+    FlashAttentionError e = validate_common(Q, K, V, O, L, B, H, N, D, scale);
+    if (e != FlashAttentionError::SUCCESS) return e;
+    if (!fits_grid(B, H)) return FlashAttentionError::INVALID_DIMENSION;
+    return launch_fwd_sm100<T>(Q, K, V, O, L, B, H, N, N, D, scale, causal, 0, 0, false, stream);
+}
+
+template <typename T>
+FlashAttentionError backward_lowp(const T* Q, const T* K, const T* V, const T* O, const float* L,
+                                  const T* dO, T* dQ, T* dK, T* dV, int B, int H, int N, int D,
+                                  float scale, bool causal, cudaStream_t stream) {
+    FlashAttentionError e = validate_backward(Q, K, V, O, L, dO, dQ, dK, dV, B, H, N, D, scale);
+    if (e != FlashAttentionError::SUCCESS) return e;
+    if (!fits_grid(B, H)) return FlashAttentionError::INVALID_DIMENSION;
+    return launch_bwd_sm100<T>(Q, K, V, O, L, dO, dQ, dK, dV, B, H, N, D, scale, causal, stream);
+}
+
+}  // namespace
+
+const char* get_error_string(FlashAttentionError error) {
+    switch (error) {
+        case FlashAttentionError::SUCCESS:
+            return "Success";
+        case FlashAttentionError::INVALID_DIMENSION:
+            return "Invalid dimension: dimensions must be positive";
+        case FlashAttentionError::DIMENSION_MISMATCH:
+            return "Dimension mismatch: Q, K, V tensors have incompatible shapes";
+        case FlashAttentionError::NULL_POINTER:
+            return "Null pointer: input or output pointer is null";
+        case FlashAttentionError::CUDA_ERROR:
+            return "CUDA error occurred";
+        case FlashAttentionError::OUT_OF_MEMORY:
+            return "Out of memory: insufficient GPU memory";
+        case FlashAttentionError::UNSUPPORTED_HEAD_DIM:
+            return "Unsupported head_dim: must be 32, 64, or 128";
+        case FlashAttentionError::UNSUPPORTED_DTYPE:
+            return "Unsupported data type";
+        default:
+            return "Unknown error";
+    }
+}
+
+FlashAttentionError flash_attention_forward(const float* Q, const float* K, const float* V,
+                                            float* O, float* L, int batch_size, int num_heads,
+                                            int seq_len, int head_dim, float scale, bool causal,
+                                            cudaStream_t stream) {
+    FlashAttentionError e =
+        validate_common(Q, K, V, O, L, batch_size, num_heads, seq_len, head_dim, scale);
+    if (e != FlashAttentionError::SUCCESS) return e;
+    if (!fits_grid(batch_size, num_heads)) return FlashAttentionError::INVALID_DIMENSION;
+    return launch_fwd_f32(Q, K, V, O, L, batch_size, num_heads, seq_len, head_dim, scale, causal,
+                          stream);
+}
+
+FlashAttentionError flash_attention_forward(const half* Q, const half* K, const half* V, half* O,
+                                            float* L, int batch_size, int num_heads, int seq_len,
+                                            int head_dim, float scale, bool causal,
+                                            cudaStream_t stream) {
+    return forward_lowp<half>(Q, K, V, O, L, batch_size, num_heads, seq_len, head_dim, scale,
+                              causal, stream);
+}
+
+FlashAttentionError flash_attention_forward(const __nv_bfloat16* Q, const __nv_bfloat16* K,
+                                            const __nv_bfloat16* V, __nv_bfloat16* O, float* L,
+                                            int batch_size, int num_heads, int seq_len,
+                                            int head_dim, float scale, bool causal,
+                                            cudaStream_t stream) {
+    return forward_lowp<__nv_bfloat16>(Q, K, V, O, L, batch_size, num_heads, seq_len, head_dim,
+                                       scale, causal, stream);
+}
+
+FlashAttentionError flash_attention_backward(const float* Q, const float* K, const float* V,
+                                             const float* O, const float* L, const float* dO,
+                                             float* dQ, float* dK, float* dV, int batch_size,
+                                             int num_heads, int seq_len, int head_dim, float scale,
+                                             bool causal, cudaStream_t stream) {
+    FlashAttentionError e = validate_backward(Q, K, V, O, L, dO, dQ, dK, dV, batch_size,
+                                              num_heads, seq_len, head_dim, scale);
+    if (e != FlashAttentionError::SUCCESS) return e;
+    if (!fits_grid(batch_size, num_heads)) return FlashAttentionError::INVALID_DIMENSION;
+    return launch_bwd_f32(Q, K, V, O, L, dO, dQ, dK, dV, batch_size, num_heads, seq_len,
+                          head_dim, scale, causal, stream);
+}
+
+FlashAttentionError flash_attention_backward(const half* Q, const half* K, const half* V,
+                                             const half* O, const float* L, const half* dO,
+                                             half* dQ, half* dK, half* dV, int batch_size,
+                                             int num_heads, int seq_len, int head_dim, float scale,
+                                             bool causal, cudaStream_t stream) {
+    return backward_lowp<half>(Q, K, V, O, L, dO, dQ, dK, dV, batch_size, num_heads, seq_len,
+                               head_dim, scale, causal, stream);
+}
+
+FlashAttentionError flash_attention_backward(const __nv_bfloat16* Q, const __nv_bfloat16* K,
+                                             const __nv_bfloat16* V, const __nv_bfloat16* O,
+                                             const float* L, const __nv_bfloat16* dO,
+                                             __nv_bfloat16* dQ, __nv_bfloat16* dK,
+                                             __nv_bfloat16* dV, int batch_size, int num_heads,
+                                             int seq_len, int head_dim, float scale, bool causal,
+                                             cudaStream_t stream) {
+    return backward_lowp<__nv_bfloat16>(Q, K, V, O, L, dO, dQ, dK, dV, batch_size, num_heads,
+                                        seq_len, head_dim, scale, causal, stream);
+}
+
+}  // namespace cuflash
+
+namespace {
+
+using cuflash::FlashAttentionError;
+
+template <typename T>
+FlashAttentionError decode_impl(const T* Q, const T* K, const T* V, T* O, float* L, int B, int H,
+                                int kv_len, int D, float scale, int num_splits,
+                                cudaStream_t stream) {
+    if (!Q || !K || !V || !O || !L) return FlashAttentionError::NULL_POINTER;
+    if (B <= 0 || H <= 0 || kv_len <= 0 || D <= 0) return FlashAttentionError::INVALID_DIMENSION;
+    if (!(D == 32 || D == 64 || D == 128)) return FlashAttentionError::UNSUPPORTED_HEAD_DIM;
+    if (!std::isfinite(scale) || scale < 0.0f) return FlashAttentionError::INVALID_DIMENSION;
+    if (num_splits < 0 || num_splits > 64) return FlashAttentionError::INVALID_DIMENSION;
+    if (static_cast<long long>(B) * H > 0x7fffffffLL) return FlashAttentionError::INVALID_DIMENSION;
+    return cuflash::detail::launch_decode<T>(Q, K, V, O, L, B, H, kv_len, D, scale, num_splits,
+                                             stream);
+}
+
+template <typename T>
+FlashAttentionError partial_impl(const T* Q, const T* K, const T* V, float* O, float* L, int B,
+                                 int H, int seq_q, int seq_k, int D, float scale,
+                                 long long q_offset, long long k_offset, bool causal,
+                                 cudaStream_t stream) {
+    if (!Q || !K || !V || !O || !L) return FlashAttentionError::NULL_POINTER;
+    if (B <= 0 || H <= 0 || seq_q <= 0 || seq_k <= 0 || D <= 0)
+        return FlashAttentionError::INVALID_DIMENSION;
+    if (!(D == 32 || D == 64 || D == 128)) return FlashAttentionError::UNSUPPORTED_HEAD_DIM;
+    if (!std::isfinite(scale) || scale < 0.0f) return FlashAttentionError::INVALID_DIMENSION;
+    if (q_offset < 0 || k_offset < 0) return FlashAttentionError::INVALID_DIMENSION;
+    if (static_cast<long long>(B) * H > 0x7fffffffLL) return FlashAttentionError::INVALID_DIMENSION;
+    return cuflash::detail::launch_fwd_sm100<T>(Q, K, V, O, L, B, H, seq_q, seq_k, D, scale,
+                                                causal, q_offset, k_offset, true, stream);
+}
+
+}  // namespace
+
+extern "C" {
+
+int cuflash_attention_forward_f32(const float* Q, const float* K, const float* V, float* O,
+                                  float* L, int batch_size, int num_heads, int seq_len,
+                                  int head_dim, float scale, bool causal, cudaStream_t stream) {
+    return static_cast<int>(cuflash::flash_attention_forward(
+        Q, K, V, O, L, batch_size, num_heads, seq_len, head_dim, scale, causal, stream));
+}
+
+int cuflash_attention_backward_f32(const float* Q, const float* K, const float* V, const float* O,
+                                   const float* L, const float* dO, float* dQ, float* dK, float* dV,
+                                   int batch_size, int num_heads, int seq_len, int head_dim,
+                                   float scale, bool causal, cudaStream_t stream) {
+    return static_cast<int>(cuflash::flash_attention_backward(Q, K, V, O, L, dO, dQ, dK, dV,
+                                                              batch_size, num_heads, seq_len,
+                                                              head_dim, scale, causal, stream));
+}
+
+int cuflash_attention_forward_f16(const half* Q, const half* K, const half* V, half* O, float* L,
+                                  int batch_size, int num_heads, int seq_len, int head_dim,
+                                  float scale, bool causal, cudaStream_t stream) {
+    return static_cast<int>(cuflash::flash_attention_forward(
+        Q, K, V, O, L, batch_size, num_heads, seq_len, head_dim, scale, causal, stream));
+}
+
+int cuflash_attention_backward_f16(const half* Q, const half* K, const half* V, const half* O,
+                                   const float* L, const half* dO, half* dQ, half* dK, half* dV,
+                                   int batch_size, int num_heads, int seq_len, int head_dim,
+                                   float scale, bool causal, cudaStream_t stream) {
+    return static_cast<int>(cuflash::flash_attention_backward(Q, K, V, O, L, dO, dQ, dK, dV,
+                                                              batch_size, num_heads, seq_len,
+                                                              head_dim, scale, causal, stream));
+}
+
+int cuflash_attention_forward_bf16(const __nv_bfloat16* Q, const __nv_bfloat16* K,
+                                   const __nv_bfloat16* V, __nv_bfloat16* O, float* L,
+                                   int batch_size, int num_heads, int seq_len, int head_dim,
+                                   float scale, bool causal, cudaStream_t stream) {
+    return static_cast<int>(cuflash::flash_attention_forward(
+        Q, K, V, O, L, batch_size, num_heads, seq_len, head_dim, scale, causal, stream));
+}
+
+int cuflash_attention_backward_bf16(const __nv_bfloat16* Q, const __nv_bfloat16* K,
+                                    const __nv_bfloat16* V, const __nv_bfloat16* O, const float* L,
+                                    const __nv_bfloat16* dO, __nv_bfloat16* dQ, __nv_bfloat16* dK,
+                                    __nv_bfloat16* dV, int batch_size, int num_heads, int seq_len,
+                                    int head_dim, float scale, bool causal, cudaStream_t stream) {
+    return static_cast<int>(cuflash::flash_attention_backward(Q, K, V, O, L, dO, dQ, dK, dV,
+                                                              batch_size, num_heads, seq_len,
+                                                              head_dim, scale, causal, stream));
+}
+
+const char* cuflash_error_string(int error_code) {
+    return cuflash::get_error_string(static_cast<cuflash::FlashAttentionError>(error_code));
+}
+
+int cuflash_attention_decode_f16(const half* Q, const half* K, const half* V, half* O, float* L,
+                                 int batch_size, int num_heads, int kv_len, int head_dim,
+                                 float scale, int num_splits, cudaStream_t stream) {
+    return static_cast<int>(decode_impl<half>(Q, K, V, O, L, batch_size, num_heads, kv_len,
+                                              head_dim, scale, num_splits, stream));
+}
+
+int cuflash_attention_decode_bf16(const __nv_bfloat16* Q, const __nv_bfloat16* K,
+                                  const __nv_bfloat16* V, __nv_bfloat16* O, float* L,
+                                  int batch_size, int num_heads, int kv_len, int head_dim,
+                                  float scale, int num_splits, cudaStream_t stream) {
+    return static_cast<int>(decode_impl<__nv_bfloat16>(Q, K, V, O, L, batch_size, num_heads,
+                                                       kv_len, head_dim, scale, num_splits,
+                                                       stream));
+}
+
+int cuflash_attention_forward_partial_bf16(const __nv_bfloat16* Q, const __nv_bfloat16* K,
+                                           const __nv_bfloat16* V, float* O_part, float* L_part,
+                                           int batch_size, int num_heads, int seq_q, int seq_k,
+                                           int head_dim, float scale, long long q_offset,
+                                           long long k_offset, bool causal, cudaStream_t stream) {
+    return static_cast<int>(partial_impl<__nv_bfloat16>(Q, K, V, O_part, L_part, batch_size,
+                                                        num_heads, seq_q, seq_k, head_dim, scale,
+                                                        q_offset, k_offset, causal, stream));
+}
+
+int cuflash_attention_forward_partial_f16(const half* Q, const half* K, const half* V,
+                                          float* O_part, float* L_part, int batch_size,
+                                          int num_heads, int seq_q, int seq_k, int head_dim,
+                                          float scale, long long q_offset, long long k_offset,
+                                          bool causal, cudaStream_t stream) {
+    return static_cast<int>(partial_impl<half>(Q, K, V, O_part, L_part, batch_size, num_heads,
+                                               seq_q, seq_k, head_dim, scale, q_offset, k_offset,
+                                               causal, stream));
+}
+
+int cuflash_lse_merge_f32(float* O_acc, float* L_acc, const float* O_part, const float* L_part,
+                          long long rows, int head_dim, cudaStream_t stream) {
+    if (!O_acc || !L_acc || !O_part || !L_part)
+        return static_cast<int>(FlashAttentionError::NULL_POINTER);
+    if (rows <= 0 || head_dim <= 0) return static_cast<int>(FlashAttentionError::INVALID_DIMENSION);
+    return static_cast<int>(
+        cuflash::detail::launch_lse_merge(O_acc, L_acc, O_part, L_part, rows, head_dim, stream));
+}
+
+int cuflash_convert_f32_to_bf16(const float* src, __nv_bfloat16* dst, long long count,
+                                cudaStream_t stream) {
+    if (!src || !dst) return static_cast<int>(FlashAttentionError::NULL_POINTER);
+    if (count <= 0) return static_cast<int>(FlashAttentionError::INVALID_DIMENSION);
+    return static_cast<int>(
+        cuflash::detail::launch_convert_f32<__nv_bfloat16>(src, dst, count, stream));
+}
+
+int cuflash_convert_f32_to_f16(const float* src, half* dst, long long count,
+                               cudaStream_t stream) {
+    if (!src || !dst) return static_cast<int>(FlashAttentionError::NULL_POINTER);
+    if (count <= 0) return static_cast<int>(FlashAttentionError::INVALID_DIMENSION);
+    return static_cast<int>(cuflash::detail::launch_convert_f32<half>(src, dst, count, stream));
+}
+
+int cuflash_device_status(void) { return cuflash::detail::read_and_clear_device_status(); }
+
+}  // extern "C"

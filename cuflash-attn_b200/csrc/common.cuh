@@ -1,0 +1,125 @@
+#pragma once
+
+// Shared host/device helpers: dtype traits, tensor-map encoding, per-device
+// launch attributes and the internal launcher declarations used by api.cu.
+
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+#include "cuflash/flash_attention.h"
+#include "sm100.cuh"
+
+namespace cuflash {
+namespace detail {
+
+template <typename T>
+struct DType;
+
+template <>
+struct DType<__nv_bfloat16> {
+    static constexpr uint32_t kMmaFmt = sm100::kFmtBF16;
+    static constexpr CUtensorMapDataType kTmaType = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+    __device__ static __forceinline__ uint32_t pack2(float lo, float hi) {
+        __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+        return *reinterpret_cast<uint32_t*>(&v);
+    }
+    __device__ static __forceinline__ float2 unpack2(uint32_t u) {
+        __nv_bfloat162 v = *reinterpret_cast<__nv_bfloat162*>(&u);
+        return __bfloat1622float2(v);
+    }
+    __device__ static __forceinline__ float to_float(__nv_bfloat16 x) { return __bfloat162float(x); }
+    __device__ static __forceinline__ __nv_bfloat16 from_float(float x) {
+        return __float2bfloat16_rn(x);
+    }
+};
+
+template <>
+struct DType<half> {
+    static constexpr uint32_t kMmaFmt = sm100::kFmtF16;
+    static constexpr CUtensorMapDataType kTmaType = CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+    __device__ static __forceinline__ uint32_t pack2(float lo, float hi) {
+        __half2 v = __floats2half2_rn(lo, hi);
+        return *reinterpret_cast<uint32_t*>(&v);
+    }
+    __device__ static __forceinline__ float2 unpack2(uint32_t u) {
+        __half2 v = *reinterpret_cast<__half2*>(&u);
+        return __half22float2(v);
+    }
+    __device__ static __forceinline__ float to_float(half x) { return __half2float(x); }
+    __device__ static __forceinline__ half from_float(float x) { return __float2half_rn(x); }
+};
+
+// Encodes a 3-D tiled tensor map over a [outer, rows, inner] row-major
+// tensor: dim0 = inner (contiguous, `inner` elements), dim1 = rows,
+// dim2 = outer.  Box = {box_inner, box_rows, 1}.  Out-of-bounds reads return
+// zeros.  Returns false if the driver rejects the map (for example a base
+// address that is not 16-byte aligned).
+bool encode_tmap_3d(CUtensorMap* map, const void* base, CUtensorMapDataType dtype, int elem_bytes,
+                    uint64_t inner, uint64_t rows, uint64_t outer, uint32_t box_inner,
+                    uint32_t box_rows, CUtensorMapSwizzle swizzle);
+
+// Raises the dynamic shared memory limit of `kernel` to `bytes` on the
+// current device once (thread-safe, per device and kernel).  Returns false
+// if the device cannot provide that much.
+bool ensure_smem_attr(const void* kernel, int bytes);
+
+int current_sm_count();
+
+// Launchers (defined in the kernel .cu files).  All pointers are device
+// pointers; validation has already happened.
+template <typename T>
+FlashAttentionError launch_fwd_sm100(const T* Q, const T* K, const T* V, void* O, float* L, int B,
+                                     int H, int seq_q, int seq_k, int D, float scale, bool causal,
+                                     long long q_offset, long long k_offset, bool out_f32_partial,
+                                     cudaStream_t stream);
+
+template <typename T>
+FlashAttentionError launch_bwd_sm100(const T* Q, const T* K, const T* V, const T* O,
+                                     const float* L, const T* dO, T* dQ, T* dK, T* dV, int B,
+                                     int H, int N, int D, float scale, bool causal,
+                                     cudaStream_t stream);
+
+template <typename T>
+FlashAttentionError launch_fwd_simt(const T* Q, const T* K, const T* V, T* O, float* L, int B,
+                                    int H, int N, int D, float scale, bool causal,
+                                    cudaStream_t stream);
+
+template <typename T>
+FlashAttentionError launch_bwd_simt(const T* Q, const T* K, const T* V, const T* O,
+                                    const float* L, const T* dO, T* dQ, T* dK, T* dV, int B,
+                                    int H, int N, int D, float scale, bool causal,
+                                    cudaStream_t stream);
+
+FlashAttentionError launch_fwd_f32(const float* Q, const float* K, const float* V, float* O,
+                                   float* L, int B, int H, int N, int D, float scale, bool causal,
+                                   cudaStream_t stream);
+
+FlashAttentionError launch_bwd_f32(const float* Q, const float* K, const float* V,
+                                   const float* O, const float* L, const float* dO, float* dQ,
+                                   float* dK, float* dV, int B, int H, int N, int D, float scale,
+                                   bool causal, cudaStream_t stream);
+
+template <typename T>
+FlashAttentionError launch_decode(const T* Q, const T* K, const T* V, T* O, float* L, int B, int H,
+                                  int kv_len, int D, float scale, int num_splits,
+                                  cudaStream_t stream);
+
+FlashAttentionError launch_lse_merge(float* O_acc, float* L_acc, const float* O_part,
+                                     const float* L_part, long long rows, int D,
+                                     cudaStream_t stream);
+
+template <typename T>
+FlashAttentionError launch_convert_f32(const float* src, T* dst, long long count,
+                                       cudaStream_t stream);
+
+// Reads and clears the device status words of every kernel family.
+int read_and_clear_device_status();
+int fwd_sm100_status();
+int bwd_sm100_status();
+
+}  // namespace detail
+}  // namespace cuflash

@@ -1,0 +1,345 @@
+// Split-KV decode, log-sum-exp merge and fp32 -> fp16/bf16 conversion.
+//
+// Decode has no reference counterpart (the reference lists "FlashDecoding /
+// Split-KV" as future work, ROADMAP.md:22-26).  It computes, for one query
+// token per (batch, head), o = softmax(scale * q K^T) V over a KV cache of
+// kv_len rows.  M = 1, so this is a bandwidth problem, not a tensor-core one:
+// every K and V byte is read exactly once with 128-bit non-allocating loads.
+//
+// Thread layout: each lane owns 8 consecutive head_dim elements (16 bytes),
+// D/8 lanes cover one K/V row, a warp covers 32/(D/8) rows per load
+// instruction.  q.k is reduced across the row's lanes with xor shuffles, the
+// PV product needs no cross-lane traffic (a lane accumulates its own 8
+// output elements).  Each row group keeps its own online-softmax state
+// (m, l, acc); the groups are merged through shared memory at the end of
+// the split, and the splits are merged by the log-sum-exp combine kernel.
+//
+// The merge algebra is the reference's OnlineSoftmaxState merge
+// (src/kernels/impl/online_softmax.cuh:16-59) in the log2 domain.
+
+#include <cmath>
+
+#include "common.cuh"
+
+namespace cuflash {
+namespace detail {
+
+namespace {
+
+constexpr float kLn2f = 0.6931471805599453f;
+constexpr float kLog2ef = 1.4426950408889634f;
+constexpr int kDecodeThreads = 256;
+constexpr int kDecodeWarps = kDecodeThreads / 32;
+constexpr int kDecodeUnroll = 8;
+
+__device__ __forceinline__ uint4 ld_stream(const void* p) {
+    uint4 v;
+    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                 : "l"(p));
+    return v;
+}
+
+template <typename T>
+__device__ __forceinline__ void unpack8(const uint4& v, float (&f)[8]) {
+    float2 a = DType<T>::unpack2(v.x), b = DType<T>::unpack2(v.y), c = DType<T>::unpack2(v.z),
+           d = DType<T>::unpack2(v.w);
+    f[0] = a.x; f[1] = a.y; f[2] = b.x; f[3] = b.y;
+    f[4] = c.x; f[5] = c.y; f[6] = d.x; f[7] = d.y;
+}
+
+// grid (num_splits, B*H); one CTA streams rows [split*chunk, min(kv_len, (split+1)*chunk)).
+// kDirect: num_splits == 1, write the final O (dtype) and L; else write the
+// normalised split partial (fp32) and its log-sum-exp.
+template <typename T, int D, bool kDirect>
+__global__ void __launch_bounds__(kDecodeThreads)
+    decode_split_kernel(const T* __restrict__ Q, const T* __restrict__ K, const T* __restrict__ V,
+                        T* __restrict__ O, float* __restrict__ L, float* __restrict__ O_part,
+                        float* __restrict__ L_part, int kv_len, int chunk, float scale_log2) {
+    constexpr int LPR = D / 8;     // lanes per row
+    constexpr int RPW = 32 / LPR;  // rows per warp per load
+    constexpr int G = kDecodeWarps * RPW;  // row groups per CTA
+    constexpr int STEP = kDecodeWarps * RPW;
+
+    __shared__ float s_m[G];
+    __shared__ float s_l[G];
+    __shared__ float s_acc[G][D];
+
+    const int split = blockIdx.x;
+    const int num_splits = gridDim.x;
+    const long long bh = blockIdx.y;
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const int sub = lane / LPR;
+    const int li = lane % LPR;
+    const int grp = warp * RPW + sub;
+
+    float q[8];
+    {
+        const uint4 qv = *reinterpret_cast<const uint4*>(Q + bh * D + li * 8);
+        unpack8<T>(qv, q);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) q[e] *= scale_log2;
+    }
+
+    const int r_begin = split * chunk;
+    const int r_end = min(kv_len, r_begin + chunk);
+    const T* Kb = K + bh * static_cast<long long>(kv_len) * D + li * 8;
+    const T* Vb = V + bh * static_cast<long long>(kv_len) * D + li * 8;
+
+    float m = -INFINITY, l = 0.f;
+    float acc[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) acc[e] = 0.f;
+
+    // The loop bound is warp-uniform so that every lane reaches the shuffles.
+    for (int rb = r_begin + warp * RPW; rb < r_end; rb += STEP * kDecodeUnroll) {
+        uint4 kv[kDecodeUnroll], vv[kDecodeUnroll];
+#pragma unroll
+        for (int u = 0; u < kDecodeUnroll; ++u) {
+            const int row = rb + sub + u * STEP;
+            if (row < r_end) {
+                kv[u] = ld_stream(Kb + static_cast<long long>(row) * D);
+                vv[u] = ld_stream(Vb + static_cast<long long>(row) * D);
+            } else {
+                kv[u] = make_uint4(0, 0, 0, 0);
+                vv[u] = make_uint4(0, 0, 0, 0);
+            }
+        }
+        float s[kDecodeUnroll];
+#pragma unroll
+        for (int u = 0; u < kDecodeUnroll; ++u) {
+            float kf[8];
+            unpack8<T>(kv[u], kf);
+            float dot = 0.f;
+#pragma unroll
+            for (int e = 0; e < 8; ++e) dot = fmaf(q[e], kf[e], dot);
+#pragma unroll
+            for (int off = LPR / 2; off > 0; off >>= 1)
+                dot += __shfl_xor_sync(0xffffffffu, dot, off);
+            s[u] = (rb + sub + u * STEP < r_end) ? dot : -INFINITY;
+        }
+        float mx = s[0];
+#pragma unroll
+        for (int u = 1; u < kDecodeUnroll; ++u) mx = fmaxf(mx, s[u]);
+        const float m_new = fmaxf(m, mx);
+        if (m_new != -INFINITY) {
+            const float alpha = sm100::ex2_approx(m - m_new);
+            l *= alpha;
+#pragma unroll
+            for (int e = 0; e < 8; ++e) acc[e] *= alpha;
+#pragma unroll
+            for (int u = 0; u < kDecodeUnroll; ++u) {
+                const float pr = sm100::ex2_approx(s[u] - m_new);
+                l += pr;
+                float vf[8];
+                unpack8<T>(vv[u], vf);
+#pragma unroll
+                for (int e = 0; e < 8; ++e) acc[e] = fmaf(pr, vf[e], acc[e]);
+            }
+            m = m_new;
+        }
+    }
+
+    if (li == 0) {
+        s_m[grp] = m;
+        s_l[grp] = l;
+    }
+#pragma unroll
+    for (int e = 0; e < 8; ++e) s_acc[grp][li * 8 + e] = acc[e];
+    __syncthreads();
+
+    if (threadIdx.x < D) {
+        const int d = threadIdx.x;
+        float M = -INFINITY;
+        for (int g = 0; g < G; ++g) M = fmaxf(M, s_m[g]);
+        float lt = 0.f, o = 0.f;
+        if (M != -INFINITY) {
+            for (int g = 0; g < G; ++g) {
+                const float w = sm100::ex2_approx(s_m[g] - M);
+                lt = fmaf(w, s_l[g], lt);
+                o = fmaf(w, s_acc[g][d], o);
+            }
+        }
+        const float outv = lt > 0.f ? o / lt : 0.f;
+        const float lse = lt > 0.f ? (M + log2f(lt)) * kLn2f : -INFINITY;
+        if constexpr (kDirect) {
+            O[bh * D + d] = DType<T>::from_float(outv);
+            if (d == 0) L[bh] = lse;
+        } else {
+            O_part[(bh * num_splits + split) * D + d] = outv;
+            if (d == 0) L_part[bh * num_splits + split] = lse;
+        }
+    }
+}
+
+// grid (B*H); merges num_splits normalised partials by their log-sum-exp.
+template <typename T, int D>
+__global__ void __launch_bounds__(128)
+    decode_combine_kernel(const float* __restrict__ O_part, const float* __restrict__ L_part,
+                          T* __restrict__ O, float* __restrict__ L, int num_splits) {
+    const long long bh = blockIdx.x;
+    const float* lp = L_part + bh * num_splits;
+    float M = -INFINITY;
+    for (int s = 0; s < num_splits; ++s) M = fmaxf(M, lp[s]);
+    float tot = 0.f;
+    if (M != -INFINITY)
+        for (int s = 0; s < num_splits; ++s) tot += __expf(lp[s] - M);
+    const float lse = tot > 0.f ? M + logf(tot) : -INFINITY;
+    for (int d = threadIdx.x; d < D; d += blockDim.x) {
+        float o = 0.f;
+        if (tot > 0.f)
+            for (int s = 0; s < num_splits; ++s)
+                o = fmaf(__expf(lp[s] - lse), O_part[(bh * num_splits + s) * D + d], o);
+        O[bh * D + d] = DType<T>::from_float(o);
+    }
+    if (threadIdx.x == 0) L[bh] = lse;
+}
+
+// One warp per row: O_acc/L_acc <- merge(O_acc/L_acc, O_part/L_part).
+__global__ void __launch_bounds__(256)
+    lse_merge_kernel(float* __restrict__ O_acc, float* __restrict__ L_acc,
+                     const float* __restrict__ O_part, const float* __restrict__ L_part,
+                     long long rows, int D) {
+    const int lane = threadIdx.x & 31;
+    const long long warp_global = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+    const long long nwarps = (static_cast<long long>(gridDim.x) * blockDim.x) >> 5;
+    for (long long r = warp_global; r < rows; r += nwarps) {
+        const float la = L_acc[r];
+        const float lb = L_part[r];
+        const float M = fmaxf(la, lb);
+        float wa = 0.f, wb = 0.f, lse = -INFINITY;
+        if (M != -INFINITY) {
+            const float ea = __expf(la - M), eb = __expf(lb - M);
+            const float tot = ea + eb;
+            wa = ea / tot;
+            wb = eb / tot;
+            lse = M + logf(tot);
+        }
+        float* oa = O_acc + r * D;
+        const float* ob = O_part + r * D;
+        for (int d = lane; d < D; d += 32) {
+            const float a = (wa != 0.f) ? oa[d] : 0.f;
+            const float b = (wb != 0.f) ? ob[d] : 0.f;
+            oa[d] = wa * a + wb * b;
+        }
+        __syncwarp();
+        if (lane == 0) L_acc[r] = lse;
+    }
+}
+
+template <typename T>
+__global__ void convert_kernel(const float* __restrict__ src, T* __restrict__ dst, long long n) {
+    const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;
+    for (long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+         i += stride)
+        dst[i] = DType<T>::from_float(src[i]);
+}
+
+int auto_splits(long long bh, int kv_len) {
+    const long long target = 4LL * current_sm_count();  // a few CTAs per SM
+    long long s = (target + bh - 1) / bh;
+    const long long max_by_len = (kv_len + 511) / 512;  // keep >= 512 rows per split
+    if (s > max_by_len) s = max_by_len;
+    if (s < 1) s = 1;
+    if (s > 64) s = 64;
+    return static_cast<int>(s);
+}
+
+template <typename T, int D>
+FlashAttentionError decode_typed(const T* Q, const T* K, const T* V, T* O, float* L, int BH,
+                                 int kv_len, float scale, int num_splits, cudaStream_t stream) {
+    for (const void* p : {static_cast<const void*>(Q), static_cast<const void*>(K),
+                          static_cast<const void*>(V), static_cast<const void*>(O)})
+        if ((reinterpret_cast<uintptr_t>(p) & 15u) != 0) return FlashAttentionError::CUDA_ERROR;
+    int S = num_splits == 0 ? auto_splits(BH, kv_len) : num_splits;
+    if (S > kv_len) S = kv_len;
+    const int chunk = (kv_len + S - 1) / S;
+    S = (kv_len + chunk - 1) / chunk;  // no empty splits
+    const float sl2 = scale * kLog2ef;
+    if (S == 1) {
+        decode_split_kernel<T, D, true><<<dim3(1, BH), kDecodeThreads, 0, stream>>>(
+            Q, K, V, O, L, nullptr, nullptr, kv_len, chunk, sl2);
+        return cudaGetLastError() == cudaSuccess ? FlashAttentionError::SUCCESS
+                                                 : FlashAttentionError::CUDA_ERROR;
+    }
+    float* ws = nullptr;
+    const size_t part_elems = static_cast<size_t>(BH) * S * D;
+    const size_t bytes = (part_elems + static_cast<size_t>(BH) * S) * sizeof(float);
+    cudaError_t err = cudaMallocAsync(reinterpret_cast<void**>(&ws), bytes, stream);
+    if (err != cudaSuccess) {
+        cudaGetLastError();
+        return err == cudaErrorMemoryAllocation ? FlashAttentionError::OUT_OF_MEMORY
+                                                : FlashAttentionError::CUDA_ERROR;
+    }
+    float* o_part = ws;
+    float* l_part = ws + part_elems;
+    decode_split_kernel<T, D, false><<<dim3(S, BH), kDecodeThreads, 0, stream>>>(
+        Q, K, V, nullptr, nullptr, o_part, l_part, kv_len, chunk, sl2);
+    cudaError_t e1 = cudaGetLastError();
+    decode_combine_kernel<T, D><<<BH, 128, 0, stream>>>(o_part, l_part, O, L, S);
+    cudaError_t e2 = cudaGetLastError();
+    cudaFreeAsync(ws, stream);
+    return (e1 == cudaSuccess && e2 == cudaSuccess) ? FlashAttentionError::SUCCESS
+                                                    : FlashAttentionError::CUDA_ERROR;
+}
+
+}  // namespace
+
+template <typename T>
+FlashAttentionError launch_decode(const T* Q, const T* K, const T* V, T* O, float* L, int B, int H,
+                                  int kv_len, int D, float scale, int num_splits,
+                                  cudaStream_t stream) {
+    const int BH = B * H;
+    switch (D) {
+        case 32:
+            return decode_typed<T, 32>(Q, K, V, O, L, BH, kv_len, scale, num_splits, stream);
+        case 64:
+            return decode_typed<T, 64>(Q, K, V, O, L, BH, kv_len, scale, num_splits, stream);
+        case 128:
+            return decode_typed<T, 128>(Q, K, V, O, L, BH, kv_len, scale, num_splits, stream);
+        default:
+            return FlashAttentionError::UNSUPPORTED_HEAD_DIM;
+    }
+}
+
+template FlashAttentionError launch_decode<half>(const half*, const half*, const half*, half*,
+                                                 float*, int, int, int, int, float, int,
+                                                 cudaStream_t);
+template FlashAttentionError launch_decode<__nv_bfloat16>(const __nv_bfloat16*,
+                                                          const __nv_bfloat16*,
+                                                          const __nv_bfloat16*, __nv_bfloat16*,
+                                                          float*, int, int, int, int, float, int,
+                                                          cudaStream_t);
+
+FlashAttentionError launch_lse_merge(float* O_acc, float* L_acc, const float* O_part,
+                                     const float* L_part, long long rows, int D,
+                                     cudaStream_t stream) {
+    long long blocks = (rows * 32 + 255) / 256;
+    const long long cap = 16LL * current_sm_count();
+    if (blocks > cap) blocks = cap;
+    if (blocks < 1) blocks = 1;
+    lse_merge_kernel<<<static_cast<unsigned>(blocks), 256, 0, stream>>>(O_acc, L_acc, O_part,
+                                                                         L_part, rows, D);
+    return cudaGetLastError() == cudaSuccess ? FlashAttentionError::SUCCESS
+                                             : FlashAttentionError::CUDA_ERROR;
+}
+
+template <typename T>
+FlashAttentionError launch_convert_f32(const float* src, T* dst, long long count,
+                                       cudaStream_t stream) {
+    long long blocks = (count + 255) / 256;
+    const long long cap = 32LL * current_sm_count();
+    if (blocks > cap) blocks = cap;
+    convert_kernel<T><<<static_cast<unsigned>(blocks), 256, 0, stream>>>(src, dst, count);
+    return cudaGetLastError() == cudaSuccess ? FlashAttentionError::SUCCESS
+                                             : FlashAttentionError::CUDA_ERROR;
+}
+
+template FlashAttentionError launch_convert_f32<half>(const float*, half*, long long,
+                                                      cudaStream_t);
+template FlashAttentionError launch_convert_f32<__nv_bfloat16>(const float*, __nv_bfloat16*,
+                                                               long long, cudaStream_t);
+
+}  // namespace detail
+}  // namespace cuflash

@@ -1,0 +1,95 @@
+// Host-side helpers shared by the launchers: tensor-map encoding through the
+// driver entry point (no link-time dependency on libcuda), a per-device
+// cache of kernel shared-memory attributes and of the SM count.
+
+#include <cudaTypedefs.h>
+
+#include <mutex>
+#include <set>
+#include <utility>
+
+#include "common.cuh"
+
+namespace cuflash {
+namespace detail {
+
+namespace {
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* ptr = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) ==
+                cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+    });
+    return fn;
+}
+
+}  // namespace
+
+bool encode_tmap_3d(CUtensorMap* map, const void* base, CUtensorMapDataType dtype, int elem_bytes,
+                    uint64_t inner, uint64_t rows, uint64_t outer, uint32_t box_inner,
+                    uint32_t box_rows, CUtensorMapSwizzle swizzle) {
+    auto fn = encode_fn();
+    if (fn == nullptr) return false;
+    if ((reinterpret_cast<uintptr_t>(base) & 15u) != 0) return false;
+    cuuint64_t dims[3] = {inner, rows, outer};
+    cuuint64_t strides[2] = {inner * static_cast<uint64_t>(elem_bytes),
+                             inner * rows * static_cast<uint64_t>(elem_bytes)};
+    cuuint32_t box[3] = {box_inner, box_rows, 1};
+    cuuint32_t estr[3] = {1, 1, 1};
+    CUresult r = fn(map, dtype, 3, const_cast<void*>(base), dims, strides, box, estr,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS;
+}
+
+bool ensure_smem_attr(const void* kernel, int bytes) {
+    static std::mutex mu;
+    static std::set<std::pair<int, const void*>> done;
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return false;
+    std::lock_guard<std::mutex> lock(mu);
+    if (done.count({dev, kernel})) return true;
+    int optin = 0;
+    if (cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) !=
+        cudaSuccess)
+        return false;
+    if (bytes > optin) return false;
+    if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes) !=
+        cudaSuccess)
+        return false;
+    done.insert({dev, kernel});
+    return true;
+}
+
+int current_sm_count() {
+    static std::mutex mu;
+    static int cache[64] = {0};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+    std::lock_guard<std::mutex> lock(mu);
+    if (cache[dev] == 0) {
+        int n = 0;
+        if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
+            n <= 0)
+            n = 148;
+        cache[dev] = n;
+    }
+    return cache[dev];
+}
+
+int read_and_clear_device_status() {
+    if (cudaDeviceSynchronize() != cudaSuccess) return -1;
+    const int a = fwd_sm100_status();
+    const int b = bwd_sm100_status();
+    if (a < 0 || b < 0) return -1;
+    return a != 0 ? a : b;
+}
+
+}  // namespace detail
+}  // namespace cuflash

@@ -1,0 +1,207 @@
+#pragma once
+
+// cuflash B200: public API.
+//
+// The first half of this header is the drop-in surface of the reference
+// library (AICL-Lab/cuflash-attn, include/cuflash/flash_attention.h:10-118):
+// the same enum, the same C++ overloads with the same default stream
+// argument, and the same extern "C" entry points with the same argument
+// order and meaning.  A program built against the reference header links
+// against this library unchanged.
+//
+// The second half declares additive entry points that the reference does not
+// have (split-KV decode, the partial forward used by context parallelism and
+// the log-sum-exp merge).  They follow the same conventions: caller-owned
+// device buffers, fp32 log-sum-exp, int return code, stream last.
+//
+// Layout of every Q/K/V/O/dO/dQ/dK/dV tensor: contiguous row-major
+// [batch, heads, seq, head_dim]; element (b,h,i,d) lives at
+// ((b*H + h)*N + i)*D + d.  L is [batch, heads, seq] fp32 and holds
+// L_i = log(sum_j exp(scale * q_i.k_j)) over the unmasked keys (natural log).
+// Causal masking is top-left aligned: key j is masked for query i iff j > i.
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include "cuflash/export.h"
+
+#ifdef __cplusplus
+namespace cuflash {
+
+// Reference: include/cuflash/flash_attention.h:12-21 (values and order kept).
+enum class FlashAttentionError {
+    SUCCESS = 0,
+    INVALID_DIMENSION,
+    DIMENSION_MISMATCH,
+    NULL_POINTER,
+    CUDA_ERROR,
+    OUT_OF_MEMORY,
+    UNSUPPORTED_HEAD_DIM,
+    UNSUPPORTED_DTYPE
+};
+
+// Reference: flash_attention.h:24.  Strings are byte-identical to the
+// reference's src/api/flash_attention_api.cu:21-42.
+CUFLASH_EXPORT const char* get_error_string(FlashAttentionError error);
+
+// Reference: flash_attention.h:30-34 (fp32 forward).
+CUFLASH_EXPORT FlashAttentionError flash_attention_forward(const float* Q, const float* K,
+                                                           const float* V, float* O, float* L,
+                                                           int batch_size, int num_heads,
+                                                           int seq_len, int head_dim, float scale,
+                                                           bool causal, cudaStream_t stream = 0);
+
+// Reference: flash_attention.h:37-40 (fp32 backward).
+CUFLASH_EXPORT FlashAttentionError flash_attention_backward(
+    const float* Q, const float* K, const float* V, const float* O, const float* L, const float* dO,
+    float* dQ, float* dK, float* dV, int batch_size, int num_heads, int seq_len, int head_dim,
+    float scale, bool causal, cudaStream_t stream = 0);
+
+// Reference: flash_attention.h:48-57 (fp16).  L stays fp32.
+CUFLASH_EXPORT FlashAttentionError flash_attention_forward(const half* Q, const half* K,
+                                                           const half* V, half* O, float* L,
+                                                           int batch_size, int num_heads,
+                                                           int seq_len, int head_dim, float scale,
+                                                           bool causal, cudaStream_t stream = 0);
+
+CUFLASH_EXPORT FlashAttentionError flash_attention_backward(
+    const half* Q, const half* K, const half* V, const half* O, const float* L, const half* dO,
+    half* dQ, half* dK, half* dV, int batch_size, int num_heads, int seq_len, int head_dim,
+    float scale, bool causal, cudaStream_t stream = 0);
+
+// Reference: flash_attention.h:60-71 (bf16).  L stays fp32.
+CUFLASH_EXPORT FlashAttentionError flash_attention_forward(const __nv_bfloat16* Q,
+                                                           const __nv_bfloat16* K,
+                                                           const __nv_bfloat16* V, __nv_bfloat16* O,
+                                                           float* L, int batch_size, int num_heads,
+                                                           int seq_len, int head_dim, float scale,
+                                                           bool causal, cudaStream_t stream = 0);
+
+CUFLASH_EXPORT FlashAttentionError flash_attention_backward(
+    const __nv_bfloat16* Q, const __nv_bfloat16* K, const __nv_bfloat16* V, const __nv_bfloat16* O,
+    const float* L, const __nv_bfloat16* dO, __nv_bfloat16* dQ, __nv_bfloat16* dK,
+    __nv_bfloat16* dV, int batch_size, int num_heads, int seq_len, int head_dim, float scale,
+    bool causal, cudaStream_t stream = 0);
+
+}  // namespace cuflash
+#endif  // __cplusplus
+
+#ifdef __cplusplus
+extern "C" {
+#else
+#include <stdbool.h>
+#endif
+
+// ---------------------------------------------------------------------------
+// Reference C ABI (flash_attention.h:81-118).  Return value: integer value of
+// cuflash::FlashAttentionError.  Validation happens before any CUDA call, so
+// invalid arguments are reported on machines without a GPU.
+// ---------------------------------------------------------------------------
+
+// Replaces flash_attention.h:81-84.
+CUFLASH_EXPORT int cuflash_attention_forward_f32(const float* Q, const float* K, const float* V,
+                                                 float* O, float* L, int batch_size, int num_heads,
+                                                 int seq_len, int head_dim, float scale,
+                                                 bool causal, cudaStream_t stream);
+
+// Replaces flash_attention.h:86-90.
+CUFLASH_EXPORT int cuflash_attention_backward_f32(const float* Q, const float* K, const float* V,
+                                                  const float* O, const float* L, const float* dO,
+                                                  float* dQ, float* dK, float* dV, int batch_size,
+                                                  int num_heads, int seq_len, int head_dim,
+                                                  float scale, bool causal, cudaStream_t stream);
+
+// Replaces flash_attention.h:92-95.
+CUFLASH_EXPORT int cuflash_attention_forward_f16(const half* Q, const half* K, const half* V,
+                                                 half* O, float* L, int batch_size, int num_heads,
+                                                 int seq_len, int head_dim, float scale,
+                                                 bool causal, cudaStream_t stream);
+
+// Replaces flash_attention.h:97-101.
+CUFLASH_EXPORT int cuflash_attention_backward_f16(const half* Q, const half* K, const half* V,
+                                                  const half* O, const float* L, const half* dO,
+                                                  half* dQ, half* dK, half* dV, int batch_size,
+                                                  int num_heads, int seq_len, int head_dim,
+                                                  float scale, bool causal, cudaStream_t stream);
+
+// Replaces flash_attention.h:103-107.
+CUFLASH_EXPORT int cuflash_attention_forward_bf16(const __nv_bfloat16* Q, const __nv_bfloat16* K,
+                                                  const __nv_bfloat16* V, __nv_bfloat16* O,
+                                                  float* L, int batch_size, int num_heads,
+                                                  int seq_len, int head_dim, float scale,
+                                                  bool causal, cudaStream_t stream);
+
+// Replaces flash_attention.h:109-115.
+CUFLASH_EXPORT int cuflash_attention_backward_bf16(const __nv_bfloat16* Q, const __nv_bfloat16* K,
+                                                   const __nv_bfloat16* V, const __nv_bfloat16* O,
+                                                   const float* L, const __nv_bfloat16* dO,
+                                                   __nv_bfloat16* dQ, __nv_bfloat16* dK,
+                                                   __nv_bfloat16* dV, int batch_size, int num_heads,
+                                                   int seq_len, int head_dim, float scale,
+                                                   bool causal, cudaStream_t stream);
+
+// Replaces flash_attention.h:118.
+CUFLASH_EXPORT const char* cuflash_error_string(int error_code);
+
+// ---------------------------------------------------------------------------
+// Additive entry points (no reference counterpart; the reference lists
+// split-KV decoding as future work in ROADMAP.md:22-26 and has no
+// multi-GPU code).  Same conventions as above.
+// ---------------------------------------------------------------------------
+
+// Split-KV decode: one query token per (batch, head) against a KV cache of
+// length kv_len.  Q, O: [B,H,1,D]; K, V: [B,H,kv_len,D]; L: [B,H] fp32.
+// num_splits: 0 picks a split count from the problem size, 1..64 forces it;
+// anything else returns INVALID_DIMENSION.  The split partials live in a
+// stream-ordered workspace allocated and freed inside the call.
+CUFLASH_EXPORT int cuflash_attention_decode_f16(const half* Q, const half* K, const half* V,
+                                                half* O, float* L, int batch_size, int num_heads,
+                                                int kv_len, int head_dim, float scale,
+                                                int num_splits, cudaStream_t stream);
+CUFLASH_EXPORT int cuflash_attention_decode_bf16(const __nv_bfloat16* Q, const __nv_bfloat16* K,
+                                                 const __nv_bfloat16* V, __nv_bfloat16* O,
+                                                 float* L, int batch_size, int num_heads,
+                                                 int kv_len, int head_dim, float scale,
+                                                 int num_splits, cudaStream_t stream);
+
+// Partial forward for context parallelism: queries [B,H,seq_q,D] at global
+// positions q_offset.., keys/values [B,H,seq_k,D] at global positions
+// k_offset...  With causal, key g_k is masked for query g_q iff g_k > g_q.
+// Writes a normalised partial result: O_part fp32 [B,H,seq_q,D] divided by
+// its own row sum, and L_part fp32 [B,H,seq_q] (natural log; -inf for a row
+// whose keys are all masked, with O_part = 0).
+CUFLASH_EXPORT int cuflash_attention_forward_partial_bf16(
+    const __nv_bfloat16* Q, const __nv_bfloat16* K, const __nv_bfloat16* V, float* O_part,
+    float* L_part, int batch_size, int num_heads, int seq_q, int seq_k, int head_dim, float scale,
+    long long q_offset, long long k_offset, bool causal, cudaStream_t stream);
+CUFLASH_EXPORT int cuflash_attention_forward_partial_f16(
+    const half* Q, const half* K, const half* V, float* O_part, float* L_part, int batch_size,
+    int num_heads, int seq_q, int seq_k, int head_dim, float scale, long long q_offset,
+    long long k_offset, bool causal, cudaStream_t stream);
+
+// Log-sum-exp merge of a partial result into a running one, row by row:
+//   L = log(exp(L_acc) + exp(L_part));
+//   O_acc = exp(L_acc - L) * O_acc + exp(L_part - L) * O_part;  L_acc = L.
+// O_acc/O_part fp32 [rows, head_dim]; L_acc/L_part fp32 [rows].  -inf rows
+// contribute nothing.  Same algebra as the reference's online-softmax state
+// merge (src/kernels/impl/online_softmax.cuh:16-59).
+CUFLASH_EXPORT int cuflash_lse_merge_f32(float* O_acc, float* L_acc, const float* O_part,
+                                         const float* L_part, long long rows, int head_dim,
+                                         cudaStream_t stream);
+
+// Converts a merged fp32 result to the storage dtype (round to nearest).
+CUFLASH_EXPORT int cuflash_convert_f32_to_bf16(const float* src, __nv_bfloat16* dst,
+                                               long long count, cudaStream_t stream);
+CUFLASH_EXPORT int cuflash_convert_f32_to_f16(const float* src, half* dst, long long count,
+                                              cudaStream_t stream);
+
+// Device-side status word.  Every kernel with a bounded wait (mbarrier
+// polling) records a non-zero code here instead of hanging when a wait runs
+// out; the host reads and clears it with this call (synchronises the
+// current device).  Returns 0 when no kernel reported a timeout.
+CUFLASH_EXPORT int cuflash_device_status(void);
+
+#ifdef __cplusplus
+}
+#endif

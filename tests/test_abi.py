@@ -1,0 +1,172 @@
+"""C-ABI boundary tests that need no GPU (the reference's host-only smoke
+tests: tests/integration/test_api_smoke.cpp, tests/package_smoke/main.cpp,
+and the validation half of tests/unit/test_error_handling.cu).
+
+Argument validation runs before any CUDA call, so invalid calls return their
+error code on a machine without a GPU.  Where the reference library was
+built here (oracle/_ref), every invalid call is also made against it and the
+two return codes must agree.
+"""
+
+import ctypes
+import math
+import re
+from pathlib import Path
+
+import pytest
+
+import cuflash_attn as cf
+import oracle
+
+ROOT = Path(__file__).resolve().parents[1]
+HEADER = ROOT / "include" / "cuflash" / "flash_attention.h"
+
+FAKE = ctypes.c_void_p(0x1000)  # never dereferenced: validation fails first
+NUL = ctypes.c_void_p(0)
+STREAM = ctypes.c_void_p(0)
+
+
+def declared_c_symbols():
+    text = HEADER.read_text()
+    c_part = text[text.index('extern "C"'):]
+    return sorted(set(re.findall(r"CUFLASH_EXPORT\s+[\w\s\*]+?\b(cuflash_\w+)\s*\(", c_part)))
+
+
+def test_header_declares_reference_abi():
+    syms = declared_c_symbols()
+    for name in cf.REFERENCE_ABI:
+        assert name in syms
+    assert set(syms) == set(cf.SIGNATURES), "binding and header disagree"
+
+
+def test_library_exports_every_declared_symbol():
+    lib = ctypes.CDLL(cf.library_path(), mode=ctypes.RTLD_LOCAL)
+    for name in declared_c_symbols():
+        assert hasattr(lib, name), name
+
+
+def test_library_hides_internal_symbols():
+    import subprocess
+
+    out = subprocess.run(["nm", "-D", "--defined-only", cf.library_path()], capture_output=True,
+                         text=True, check=True).stdout
+    exported = {ln.split()[-1] for ln in out.splitlines() if " T " in ln}
+    internal = [s for s in exported if "detail" in s or "fa_fwd_kernel" in s]
+    assert not internal, internal
+
+
+EXPECTED_STRINGS = {
+    0: "Success",
+    1: "Invalid dimension: dimensions must be positive",
+    2: "Dimension mismatch: Q, K, V tensors have incompatible shapes",
+    3: "Null pointer: input or output pointer is null",
+    4: "CUDA error occurred",
+    5: "Out of memory: insufficient GPU memory",
+    6: "Unsupported head_dim: must be 32, 64, or 128",
+    7: "Unsupported data type",
+    99: "Unknown error",
+}
+
+
+def test_error_strings_byte_exact(lib):
+    # tests/unit/test_error_handling.cu:236-254 pins these strings
+    for code, s in EXPECTED_STRINGS.items():
+        assert lib.error_string(code) == s
+
+
+def _fwd(lib, sfx, q=FAKE, k=FAKE, v=FAKE, o=FAKE, l=FAKE, B=1, H=1, N=16, D=32, scale=0.125,
+         causal=False):
+    fn = getattr(lib.lib, f"cuflash_attention_forward_{sfx}")
+    return fn(q, k, v, o, l, B, H, N, D, scale, causal, STREAM)
+
+
+def _bwd(lib, sfx, ptrs=None, B=1, H=1, N=16, D=32, scale=0.125):
+    p = [FAKE] * 9 if ptrs is None else ptrs
+    fn = getattr(lib.lib, f"cuflash_attention_backward_{sfx}")
+    return fn(*p, B, H, N, D, scale, False, STREAM)
+
+
+INVALID_FWD = [
+    # (kwargs, expected) — tests/unit/test_error_handling.cu:21-233
+    (dict(q=NUL), 3), (dict(k=NUL), 3), (dict(v=NUL), 3), (dict(o=NUL), 3), (dict(l=NUL), 3),
+    (dict(B=0), 1), (dict(B=-1), 1), (dict(H=0), 1), (dict(N=0), 1), (dict(D=0), 1),
+    (dict(D=48), 6), (dict(D=256), 6), (dict(D=16), 6),
+    (dict(scale=float("nan")), 1), (dict(scale=float("inf")), 1), (dict(scale=-1.0), 1),
+    # order: null before dims, dims before head_dim, head_dim before scale
+    (dict(q=NUL, B=0), 3), (dict(B=0, D=48), 1), (dict(D=48, scale=float("nan")), 6),
+]
+
+
+@pytest.mark.parametrize("sfx", ["f32", "f16", "bf16"])
+@pytest.mark.parametrize("kwargs,expected", INVALID_FWD)
+def test_forward_validation(lib, sfx, kwargs, expected):
+    assert _fwd(lib, sfx, **kwargs) == expected
+
+
+@pytest.mark.parametrize("sfx", ["f32", "f16", "bf16"])
+def test_backward_validation(lib, sfx):
+    for idx in range(9):  # each of Q,K,V,O,L,dO,dQ,dK,dV null
+        ptrs = [FAKE] * 9
+        ptrs[idx] = NUL
+        assert _bwd(lib, sfx, ptrs) == 3
+    # gradient pointers are checked before the dimensions (:69-79)
+    ptrs = [FAKE] * 9
+    ptrs[6] = NUL
+    assert _bwd(lib, sfx, ptrs, B=0) == 3
+    assert _bwd(lib, sfx, B=0) == 1
+    assert _bwd(lib, sfx, D=48) == 6
+    assert _bwd(lib, sfx, scale=-0.5) == 1
+
+
+@pytest.mark.parametrize("sfx", ["f32", "f16", "bf16"])
+def test_validation_matches_reference_library(lib, ref_lib, sfx):
+    for kwargs, expected in INVALID_FWD:
+        assert _fwd(ref_lib, sfx, **kwargs) == _fwd(lib, sfx, **kwargs) == expected
+    for B, D, scale in [(0, 32, 0.1), (1, 48, 0.1), (1, 32, math.nan), (2, 100, -1.0)]:
+        assert _bwd(ref_lib, sfx, B=B, D=D, scale=scale) == _bwd(lib, sfx, B=B, D=D, scale=scale)
+    for s in EXPECTED_STRINGS:
+        assert ref_lib.error_string(s) == lib.error_string(s)
+
+
+@pytest.mark.parametrize("sfx", ["f16", "bf16"])
+def test_decode_validation(lib, sfx):
+    fn = getattr(lib.lib, f"cuflash_attention_decode_{sfx}")
+    args = lambda **kw: [kw.get(n, FAKE) for n in "qkvol"] + [
+        kw.get("B", 1), kw.get("H", 1), kw.get("N", 64), kw.get("D", 64),
+        kw.get("scale", 0.1), kw.get("splits", 0), STREAM]
+    assert fn(*args(q=NUL)) == 3
+    assert fn(*args(l=NUL)) == 3
+    assert fn(*args(N=0)) == 1
+    assert fn(*args(D=96)) == 6
+    assert fn(*args(scale=float("nan"))) == 1
+    assert fn(*args(splits=-1)) == 1
+    assert fn(*args(splits=65)) == 1
+
+
+@pytest.mark.parametrize("sfx", ["f16", "bf16"])
+def test_partial_and_merge_validation(lib, sfx):
+    fn = getattr(lib.lib, f"cuflash_attention_forward_partial_{sfx}")
+    base = [FAKE] * 5 + [1, 1, 16, 16, 64, 0.1, 0, 0, True, STREAM]
+    a = list(base)
+    a[11] = -1
+    assert fn(*a) == 1
+    a = list(base)
+    a[3] = NUL
+    assert fn(*a) == 3
+    a = list(base)
+    a[9] = 80
+    assert fn(*a) == 6
+    m = lib.lib.cuflash_lse_merge_f32
+    assert m(NUL, FAKE, FAKE, FAKE, 4, 64, STREAM) == 3
+    assert m(FAKE, FAKE, FAKE, FAKE, 0, 64, STREAM) == 1
+    assert m(FAKE, FAKE, FAKE, FAKE, 4, 0, STREAM) == 1
+
+
+def test_oracle_is_test_infrastructure_only():
+    """The product path must not import the oracle."""
+    pkg = ROOT / "cuflash-attn_b200"
+    for f in list(pkg.rglob("*.py")) + list(pkg.rglob("*.cu")) + list(pkg.rglob("*.cuh")):
+        text = f.read_text()
+        assert "import oracle" not in text and "liboracle" not in text, f
+    assert "TEST INFRASTRUCTURE ONLY" in (ROOT / "oracle" / "cpu_ref.cpp").read_text()
+    assert oracle.LIB_PATH.name == "liboracle.so"

@@ -1,0 +1,97 @@
+"""Backward parity on the GPU, through the C ABI (dQ, dK, dV).
+
+Bars: fp32 within 1e-4 of fp64; fp16/bf16 within 2e-2 of fp64 and no worse
+than the reference library on the same inputs; the reference tests' golden
+gradients within each test's tolerance.
+"""
+
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+import cases
+import oracle
+from helpers import host, max_err, round_to, to_dev
+
+pytestmark = pytest.mark.gpu
+
+GOLDEN = Path(__file__).resolve().parent / "golden" / "reference_outputs.npz"
+LOWP_TOL = 2e-2
+F32_TOL = 1e-4
+REF_SLACK = 2e-3
+
+
+def run_bwd(lib, arrs, dt, causal, scale):
+    import torch
+
+    Q, K, V, dO = (to_dev(a, dt) for a in arrs)
+    O, L = lib.forward(Q, K, V, causal=causal, scale=scale)
+    dQ, dK, dV = lib.backward(Q, K, V, O, L, dO, causal=causal, scale=scale)
+    torch.cuda.synchronize()
+    if hasattr(lib.lib, "cuflash_device_status"):
+        assert lib.device_status() == 0
+    return host(dQ), host(dK), host(dV)
+
+
+@pytest.mark.parametrize("case", [c for c in cases.as_dicts() if c["kind"] == "bwd"],
+                         ids=lambda c: c["name"])
+def test_backward_golden(lib, cuda, case):
+    arrs = cases.inputs(case)
+    scale = 1.0 / np.sqrt(case["D"])
+    got = run_bwd(lib, arrs, case["dtype"], case["causal"], scale)
+    want = oracle.backward_f64(*arrs, scale, case["causal"])
+    bar = F32_TOL if case["dtype"] == "f32" else LOWP_TOL
+    for g, w in zip(got, want):
+        assert max_err(g, w) < bar
+    if GOLDEN.exists():
+        gold = np.load(GOLDEN)
+        for name, g in zip(("dQ", "dK", "dV"), got):
+            gx = gold[case["name"] + "/" + name]
+            assert max_err(g[:, :gx.shape[1]], gx) < case["tol"], name
+
+
+SHAPES = [(1, 1, 1, 32), (1, 2, 128, 128), (2, 1, 129, 64), (1, 1, 255, 32), (1, 2, 384, 128),
+          (1, 1, 500, 64)]
+
+
+@pytest.mark.parametrize("dt", ["bf16", "f16"])
+@pytest.mark.parametrize("causal", [False, True])
+@pytest.mark.parametrize("shape", SHAPES, ids=lambda s: "x".join(map(str, s)))
+def test_backward_lowp_vs_f64_and_reference(lib, ref_lib, cuda, dt, causal, shape):
+    D = shape[3]
+    seed = 2000 + shape[2] * 3 + D + (1 if causal else 0)
+    arrs = [round_to(oracle.normal(shape, seed + i, std=0.5 if i < 3 else 1.0), dt)
+            for i in range(4)]
+    scale = 1.0 / np.sqrt(D)
+    got = run_bwd(lib, arrs, dt, causal, scale)
+    want = oracle.backward_f64(*arrs, scale, causal)
+    ref = run_bwd(ref_lib, arrs, dt, causal, scale)
+    for name, g, w, r in zip(("dQ", "dK", "dV"), got, want, ref):
+        e, er = max_err(g, w), max_err(r, w)
+        assert e < LOWP_TOL, (name, e)
+        assert e <= er + REF_SLACK, (name, e, er)
+
+
+@pytest.mark.parametrize("causal", [False, True])
+def test_backward_f32_within_1e4(lib, cuda, causal):
+    shape = (1, 2, 200, 64)
+    arrs = [oracle.uniform(shape, s) for s in (1, 2, 3, 4)]
+    got = run_bwd(lib, arrs, "f32", causal, 0.125)
+    want = oracle.backward_f64(*arrs, 0.125, causal)
+    for g, w in zip(got, want):
+        assert max_err(g, w) < F32_TOL
+
+
+def test_config2_backward_sampled_units(lib, cuda):
+    """BASELINE config 2 (fp16 non-causal B4 H16 N2048 D128, seeds 11-14)."""
+    shape = (4, 16, 2048, 128)
+    arrs = [round_to(oracle.normal(shape, s), "f16") for s in (11, 12, 13, 14)]
+    scale = 1.0 / np.sqrt(128)
+    got = run_bwd(lib, arrs, "f16", False, scale)
+    for u in (0, 63):
+        b, h = divmod(u, 16)
+        sub = [a[b:b + 1, h:h + 1] for a in arrs]
+        want = oracle.backward_f64(*sub, scale, False)
+        for g, w in zip(got, want):
+            assert max_err(g[b, h], w[0, 0]) < LOWP_TOL
