@@ -1,7 +1,39 @@
-// Backward attention for fp16/bf16 on sm_100a.
+// Backward attention for fp16/bf16 on sm_100a (tcgen05 + TMEM + TMA).
 //
 // Replaces the reference's three backward kernels
-// (src/backward/flash_attention_backward_typed.cu:13-288).
+//   compute_D_kernel                        backward_typed.cu:13-34
+//   flash_attention_backward_dq_kernel      backward_typed.cu:37-143
+//   flash_attention_backward_dkdv_kernel    backward_typed.cu:146-288
+// with the same math (P = exp(scale q.k - L), dP = dO V^T,
+// D_i = rowsum(dO_i * O_i), dS = P (dP - D), dV = P^T dO,
+// dK = scale dS^T Q, dQ = scale dS K) but one pass over the score matrix:
+// S and dP are computed once per (kv block, q block) pair instead of twice.
+//
+// Kernel 1 (preprocess): D_i and L_i*log2(e) into a padded workspace
+// (+inf / 0 in the padding rows so padded queries get P = 0), and zeroes the
+// fp32 dQ accumulator.
+// Kernel 2 (main): one CTA per (128-row K/V block j, batch*head); K_j and V_j
+// stay in shared memory while the CTA walks the query blocks i (all of them,
+// or i >= j when causal):
+//   warp 0      TMA producer: Q_i, dO_i (tiled, swizzled) and the 128 values
+//               of L and D for block i (1-D bulk copies), 2-stage ring.
+//   warp 1      tcgen05.mma issuer:
+//                 dP^T = V_j dO_i^T   -> TMEM [128,256)
+//                 S^T  = K_j Q_i^T    -> TMEM [0,128)
+//                 dV  += P^T dO_i     (A = P^T from TMEM)   -> TMEM [256,256+D)
+//                 dK  += dS^T Q_i     (A = dS^T from TMEM)  -> TMEM [384,384+D)
+//                 dQ_i = dS K_j       (A = dS from smem)    -> TMEM [0,D)
+//   warps 4-7   one thread per K/V row (TMEM lane): P^T, dS^T from S^T, dP^T;
+//               writes P^T and dS^T back into TMEM (fp16/bf16) and dS^T into
+//               shared memory for the dQ product; at the end stores dK, dV.
+//   warps 8-11  one thread per query row: drains dQ_i from TMEM into the fp32
+//               accumulator with vector reductions (red.global.add.v4.f32).
+// Kernel 3 (convert): dQ = scale * dQ_acc in the output dtype.
+//
+// CTAs of one (batch, head) are adjacent in launch order, so the dQ
+// accumulator tiles they reduce into stay resident in L2.
+
+#include <cmath>
 
 #include "common.cuh"
 
@@ -9,7 +41,533 @@ namespace cuflash {
 namespace detail {
 
 namespace {
+
 __device__ int g_bwd_status;
+
+constexpr float kLog2eB = 1.4426950408889634f;
+
+template <int D>
+struct BwdGeom {
+    static constexpr int kRows = 128;
+    static constexpr int kRowBytes = D * 2;
+    static constexpr int kSwz = kRowBytes >= 128 ? 128 : kRowBytes;
+    static constexpr int kCbElems = kSwz / 2;
+    static constexpr int kNumCb = D / kCbElems;
+    static constexpr int kCbBytes = kRows * kSwz;
+    static constexpr int kTileBytes = kRows * kRowBytes;
+    static constexpr uint32_t kLayout = kSwz == 128 ? sm100::kLayoutSw128 : sm100::kLayoutSw64;
+    static constexpr int kStages = 2;
+    static constexpr int kDsBytes = 128 * 256;  // 128 kv rows x 128 q (16-bit), SW128
+    static constexpr int kOffK = 0;
+    static constexpr int kOffV = kTileBytes;
+    static constexpr int kOffDs = 2 * kTileBytes;
+    static constexpr int kOffStage = kOffDs + kDsBytes;
+    static constexpr int kStageBytes = 2 * kTileBytes + 1024;  // Q, dO, L (512 B), D (512 B)
+    static constexpr int kOffBar = kOffStage + kStages * kStageBytes;
+    static constexpr int kNumBars = 1 + 2 * kStages + 6;
+    static constexpr int kSmemBytes = kOffBar + kNumBars * 8 + 16;
+    static_assert(kStageBytes % 1024 == 0, "stage must keep 1024-byte alignment");
+};
+
+struct BwdParams {
+    float* dq_acc;
+    void* dK;
+    void* dV;
+    const float* l2p;  // L * log2(e), padded to n_blk*128 per (b,h) with +inf
+    const float* dvp;  // rowsum(dO*O), padded with 0
+    int N;
+    int n_blk;
+    int causal;
+    float scale_log2;
+    float scale;
+};
+
+template <int D>
+__device__ __forceinline__ uint64_t bkmajor_desc(uint32_t tile_base, int kk) {
+    using G = BwdGeom<D>;
+    const uint32_t byte = static_cast<uint32_t>(kk) * 32u;
+    const uint32_t addr = tile_base + (byte / G::kSwz) * G::kCbBytes + (byte % G::kSwz);
+    return sm100::make_smem_desc(addr, 16, 8 * G::kSwz, G::kLayout);
+}
+
+template <int D>
+__device__ __forceinline__ uint64_t bmnmajor_desc(uint32_t tile_base, int kk) {
+    using G = BwdGeom<D>;
+    const uint32_t addr = tile_base + static_cast<uint32_t>(kk) * 16u * G::kSwz;
+    return sm100::make_smem_desc(addr, G::kCbBytes, 8 * G::kSwz, G::kLayout);
+}
+
+// dS tile: [128 kv rows][128 q], two 64-column SW128 blocks; as the MN-major
+// A operand of dQ = dS K (M = q, K = kv), k-step kk covers kv rows 16kk..
+__device__ __forceinline__ uint64_t ds_desc(uint32_t ds_base, int kk) {
+    return sm100::make_smem_desc(ds_base + static_cast<uint32_t>(kk) * 16u * 128u, 128 * 128, 1024,
+                                 sm100::kLayoutSw128);
+}
+
+__device__ __forceinline__ bool bwarp_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag) {
+    int ok = 0;
+    if ((threadIdx.x & 31) == 0) ok = sm100::mbar_wait(bar, parity, abort_flag, &g_bwd_status);
+    ok = __shfl_sync(0xffffffffu, ok, 0);
+    return ok != 0;
+}
+
+__device__ __forceinline__ void bdrain_wait(uint64_t* bar, uint32_t parity) {
+    volatile int never = 0;
+    sm100::mbar_wait(bar, parity, &never, &g_bwd_status);
+}
+
+__device__ __forceinline__ void bulk_load(void* smem_dst, const void* gsrc, uint32_t bytes,
+                                          uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+            sm100::smem_u32(smem_dst)),
+        "l"(gsrc), "r"(bytes), "r"(sm100::smem_u32(bar))
+        : "memory");
+}
+
+__device__ __forceinline__ void red_add_v4(float* gptr, float a, float b, float c, float d) {
+    asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(gptr), "f"(a), "f"(b),
+                 "f"(c), "f"(d)
+                 : "memory");
+}
+
+__device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c,
+                                             uint32_t d) {
+    asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c),
+                 "r"(d)
+                 : "memory");
+}
+
+__device__ __forceinline__ void fence_proxy_async_smem() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// ---------------------------------------------------------------- preprocess
+
+template <typename T, int D>
+__global__ void __launch_bounds__(256)
+    bwd_preprocess_kernel(const T* __restrict__ O, const T* __restrict__ dO,
+                          const float* __restrict__ L, float* __restrict__ l2p,
+                          float* __restrict__ dvp, float* __restrict__ dq_acc, int N, int N_pad,
+                          long long rows_pad) {
+    constexpr int E = D / 32;  // elements per lane
+    const int lane = threadIdx.x & 31;
+    const long long r = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+    if (r >= rows_pad) return;
+    const long long bh = r / N_pad;
+    const int q = static_cast<int>(r - bh * N_pad);
+    if (q >= N) {
+        if (lane == 0) {
+            l2p[r] = INFINITY;
+            dvp[r] = 0.f;
+        }
+        return;
+    }
+    const long long row = bh * N + q;
+    float acc = 0.f;
+#pragma unroll
+    for (int e = 0; e < E; ++e) {
+        const int d = lane * E + e;
+        acc = fmaf(DType<T>::to_float(O[row * D + d]), DType<T>::to_float(dO[row * D + d]), acc);
+        dq_acc[row * D + d] = 0.f;
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
+    if (lane == 0) {
+        l2p[r] = L[row] * kLog2eB;
+        dvp[r] = acc;
+    }
+}
+
+template <typename T>
+__global__ void __launch_bounds__(256)
+    bwd_convert_dq_kernel(const float* __restrict__ acc, T* __restrict__ dQ, float scale,
+                          long long n4) {
+    const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;
+    for (long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; i < n4;
+         i += stride) {
+        const float4 v = reinterpret_cast<const float4*>(acc)[i];
+        uint2 o;
+        o.x = DType<T>::pack2(v.x * scale, v.y * scale);
+        o.y = DType<T>::pack2(v.z * scale, v.w * scale);
+        reinterpret_cast<uint2*>(dQ)[i] = o;
+    }
+}
+
+// ---------------------------------------------------------------- main kernel
+
+template <typename T, int D>
+__global__ void __launch_bounds__(384, 1)
+    fa_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                  const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmdO,
+                  const BwdParams p) {
+    using G = BwdGeom<D>;
+    using namespace sm100;
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+
+    if (*reinterpret_cast<volatile int*>(&g_bwd_status) != 0) return;
+    const uint32_t sbase = smem_u32(smem_raw);
+    if ((sbase & 1023u) != 0) {  // swizzled operands need 1024-byte alignment
+        if (threadIdx.x == 0) atomicExch(&g_bwd_status, 2);
+        return;
+    }
+    uint8_t* sptr = smem_raw;
+    uint64_t* bars = reinterpret_cast<uint64_t*>(sptr + G::kOffBar);
+    uint64_t* bar_kv = bars;
+    uint64_t* full = bars + 1;
+    uint64_t* empty = full + G::kStages;
+    uint64_t* bar_sdp = empty + G::kStages;
+    uint64_t* bar_ds = bar_sdp + 1;
+    uint64_t* bar_dq = bar_ds + 1;
+    uint64_t* bar_dqfree = bar_dq + 1;
+    uint64_t* bar_acc = bar_dqfree + 1;
+    uint64_t* bar_done = bar_acc + 1;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar_done + 1);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const int j = blockIdx.x;  // kv block
+    const int bh = blockIdx.y;
+    const int i0 = p.causal ? j : 0;
+    const int n_it = p.n_blk - i0;
+
+    if (threadIdx.x == 0) {
+        mbar_init(bar_kv, 1);
+        for (int s = 0; s < G::kStages; ++s) {
+            mbar_init(full + s, 1);
+            mbar_init(empty + s, 1);
+        }
+        mbar_init(bar_sdp, 1);
+        mbar_init(bar_ds, 128);
+        mbar_init(bar_dq, 1);
+        mbar_init(bar_dqfree, 128);
+        mbar_init(bar_acc, 1);
+        mbar_init(bar_done, 1);
+        *abort_flag = 0;
+        fence_mbar_init();
+    }
+    if (warp == 1) {
+        tmem_alloc(tmem_slot, 512);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 0) {
+        // ------------------------------------------------ producer
+        if (lane == 0) {
+            prefetch_tmap(&tmQ);
+            prefetch_tmap(&tmK);
+            prefetch_tmap(&tmV);
+            prefetch_tmap(&tmdO);
+            mbar_arrive_expect_tx(bar_kv, 2 * G::kTileBytes);
+            for (int cb = 0; cb < G::kNumCb; ++cb) {
+                tma_load_3d(sptr + G::kOffK + cb * G::kCbBytes, &tmK, bar_kv, cb * G::kCbElems,
+                            j * 128, bh);
+                tma_load_3d(sptr + G::kOffV + cb * G::kCbBytes, &tmV, bar_kv, cb * G::kCbElems,
+                            j * 128, bh);
+            }
+            const size_t lrow = static_cast<size_t>(bh) * p.n_blk * 128;
+            int issued = 0;
+            for (int it = 0; it < n_it; ++it) {
+                const int i = i0 + it;
+                const int s = it % G::kStages;
+                if (it >= G::kStages &&
+                    !mbar_wait(empty + s, ((it / G::kStages) & 1) ^ 1, abort_flag, &g_bwd_status))
+                    break;
+                uint8_t* st = sptr + G::kOffStage + s * G::kStageBytes;
+                mbar_arrive_expect_tx(full + s, 2 * G::kTileBytes + 1024);
+                for (int cb = 0; cb < G::kNumCb; ++cb) {
+                    tma_load_3d(st + cb * G::kCbBytes, &tmQ, full + s, cb * G::kCbElems, i * 128,
+                                bh);
+                    tma_load_3d(st + G::kTileBytes + cb * G::kCbBytes, &tmdO, full + s,
+                                cb * G::kCbElems, i * 128, bh);
+                }
+                bulk_load(st + 2 * G::kTileBytes, p.l2p + lrow + i * 128, 512, full + s);
+                bulk_load(st + 2 * G::kTileBytes + 512, p.dvp + lrow + i * 128, 512, full + s);
+                ++issued;
+            }
+            bdrain_wait(bar_kv, 0);
+            for (int it = max(0, issued - G::kStages); it < issued; ++it)
+                bdrain_wait(full + it % G::kStages, (it / G::kStages) & 1);
+        }
+    } else if (warp == 1) {
+        // ------------------------------------------------ MMA issuer
+        if (lane == 0) {
+            constexpr uint32_t kFmt = DType<T>::kMmaFmt;
+            constexpr uint32_t idesc_ss = make_idesc(kFmt, 128, 128, false, false);
+            constexpr uint32_t idesc_acc = make_idesc(kFmt, 128, D, false, true);
+            constexpr uint32_t idesc_dq = make_idesc(kFmt, 128, D, true, true);
+            const uint32_t sK = sbase + G::kOffK, sV = sbase + G::kOffV, sDs = sbase + G::kOffDs;
+            bool ok = mbar_wait(bar_kv, 0, abort_flag, &g_bwd_status);
+            for (int it = 0; ok && it < n_it; ++it) {
+                const int s = it % G::kStages;
+                const uint32_t sQ = sbase + G::kOffStage + s * G::kStageBytes;
+                const uint32_t sdO = sQ + G::kTileBytes;
+                if (!mbar_wait(full + s, (it / G::kStages) & 1, abort_flag, &g_bwd_status)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                // dP^T = V_j dO_i^T (its TMEM columns were last read by dK of it-1)
+#pragma unroll
+                for (int kk = 0; kk < D / 16; ++kk)
+                    mma_f16_ss(tmem + 128, bkmajor_desc<D>(sV, kk), bkmajor_desc<D>(sdO, kk),
+                               idesc_ss, kk > 0 ? 1u : 0u);
+                if (it > 0) {
+                    // S columns hold dQ_{i-1} until the drain warps have read it
+                    if (!mbar_wait(bar_dqfree, (it - 1) & 1, abort_flag, &g_bwd_status)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                }
+#pragma unroll
+                for (int kk = 0; kk < D / 16; ++kk)
+                    mma_f16_ss(tmem, bkmajor_desc<D>(sK, kk), bkmajor_desc<D>(sQ, kk), idesc_ss,
+                               kk > 0 ? 1u : 0u);
+                tc_commit(bar_sdp);
+                if (!mbar_wait(bar_ds, it & 1, abort_flag, &g_bwd_status)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                // dV += P^T dO_i ; dK += dS^T Q_i  (K dimension = 128 query rows)
+#pragma unroll
+                for (int kk = 0; kk < 8; ++kk)
+                    mma_f16_ts(tmem + 256, tmem + kk * 8, bmnmajor_desc<D>(sdO, kk), idesc_acc,
+                               (it > 0 || kk > 0) ? 1u : 0u);
+#pragma unroll
+                for (int kk = 0; kk < 8; ++kk)
+                    mma_f16_ts(tmem + 384, tmem + 128 + kk * 8, bmnmajor_desc<D>(sQ, kk),
+                               idesc_acc, (it > 0 || kk > 0) ? 1u : 0u);
+                tc_commit(empty + s);
+                // dQ_i = dS K_j (K dimension = 128 kv rows) into the S columns
+#pragma unroll
+                for (int kk = 0; kk < 8; ++kk)
+                    mma_f16_ss(tmem, ds_desc(sDs, kk), bmnmajor_desc<D>(sK, kk), idesc_dq,
+                               kk > 0 ? 1u : 0u);
+                tc_commit(bar_dq);
+            }
+            tc_commit(bar_acc);
+            tc_commit(bar_done);
+            volatile int never = 0;
+            mbar_wait(bar_done, 0, &never, &g_bwd_status);
+        }
+        __syncwarp();
+    } else if (warp >= 4 && warp < 8) {
+        // ------------------------------------------------ P^T / dS^T, then dK/dV epilogue
+        const int wq = warp & 3;
+        const int r = wq * 32 + lane;  // kv row within block j
+        const uint32_t lane_addr = static_cast<uint32_t>(wq * 32) << 16;
+        const uint32_t t_s = tmem + lane_addr;
+        const uint32_t t_dp = tmem + lane_addr + 128;
+        const uint32_t sDs = sbase + G::kOffDs + r * 128;
+        const float c = p.scale_log2;
+        bool ok = true;
+        for (int it = 0; it < n_it; ++it) {
+            const int i = i0 + it;
+            if (!bwarp_wait(bar_sdp, it & 1, abort_flag)) {
+                ok = false;
+                break;
+            }
+            tc_fence_after();
+            const int s = it % G::kStages;
+            // L and D of block i arrived through the async proxy: observe the
+            // stage's own barrier before reading them
+            if (!bwarp_wait(full + s, (it / G::kStages) & 1, abort_flag)) {
+                ok = false;
+                break;
+            }
+            const float* sL = reinterpret_cast<const float*>(sptr + G::kOffStage +
+                                                             s * G::kStageBytes + 2 * G::kTileBytes);
+            const float* sD = sL + 128;
+            const bool diag = p.causal && (i == j);
+#pragma unroll
+            for (int cc = 0; cc < 4; ++cc) {
+                uint32_t sv[32], dv[32];
+                tmem_ld_x32(t_s + cc * 32, sv);
+                tmem_ld_x32(t_dp + cc * 32, dv);
+                uint32_t pp[16], dd[16];
+#pragma unroll
+                for (int e = 0; e < 16; ++e) {
+                    const int q0 = cc * 32 + 2 * e;
+                    float p0 = ex2_approx(fmaf(__uint_as_float(sv[2 * e]), c, -sL[q0]));
+                    float p1 = ex2_approx(fmaf(__uint_as_float(sv[2 * e + 1]), c, -sL[q0 + 1]));
+                    if (diag) {
+                        if (q0 < r) p0 = 0.f;
+                        if (q0 + 1 < r) p1 = 0.f;
+                    }
+                    const float d0 = p0 * (__uint_as_float(dv[2 * e]) - sD[q0]);
+                    const float d1 = p1 * (__uint_as_float(dv[2 * e + 1]) - sD[q0 + 1]);
+                    pp[e] = DType<T>::pack2(p0, p1);
+                    dd[e] = DType<T>::pack2(d0, d1);
+                }
+                // P^T and dS^T overwrite columns already consumed
+                tmem_st_x16(t_s + cc * 16, pp);
+                tmem_st_x16(t_dp + cc * 16, dd);
+                const int cb = cc >> 1;
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                    const int chunk = (cc & 1) * 4 + k;
+                    const uint32_t addr = sDs + cb * (128 * 128) + ((chunk ^ (r & 7)) << 4);
+                    st_shared_v4(addr, dd[4 * k], dd[4 * k + 1], dd[4 * k + 2], dd[4 * k + 3]);
+                }
+            }
+            fence_proxy_async_smem();
+            tc_fence_before();
+            mbar_arrive(bar_ds);
+        }
+        if (ok) {
+            ok = bwarp_wait(bar_acc, 0, abort_flag);
+            tc_fence_after();
+        }
+        const int kv = j * 128 + r;
+        const bool valid = kv < p.N;
+        const size_t row = (static_cast<size_t>(bh) * p.N + kv) * D;
+        T* dVp = static_cast<T*>(p.dV);
+        T* dKp = static_cast<T*>(p.dK);
+#pragma unroll
+        for (int cb = 0; cb < D / 32; ++cb) {
+            uint32_t a[32], b[32];
+            if (ok) {
+                tmem_ld_x32(tmem + lane_addr + 256 + cb * 32, a);
+                tmem_ld_x32(tmem + lane_addr + 384 + cb * 32, b);
+            } else {
+#pragma unroll
+                for (int e = 0; e < 32; ++e) a[e] = b[e] = 0u;
+            }
+            if (valid) {
+                uint4* dstv = reinterpret_cast<uint4*>(dVp + row + cb * 32);
+                uint4* dstk = reinterpret_cast<uint4*>(dKp + row + cb * 32);
+#pragma unroll
+                for (int q4 = 0; q4 < 4; ++q4) {
+                    uint4 v, k;
+                    v.x = DType<T>::pack2(__uint_as_float(a[8 * q4 + 0]), __uint_as_float(a[8 * q4 + 1]));
+                    v.y = DType<T>::pack2(__uint_as_float(a[8 * q4 + 2]), __uint_as_float(a[8 * q4 + 3]));
+                    v.z = DType<T>::pack2(__uint_as_float(a[8 * q4 + 4]), __uint_as_float(a[8 * q4 + 5]));
+                    v.w = DType<T>::pack2(__uint_as_float(a[8 * q4 + 6]), __uint_as_float(a[8 * q4 + 7]));
+                    k.x = DType<T>::pack2(__uint_as_float(b[8 * q4 + 0]) * p.scale,
+                                          __uint_as_float(b[8 * q4 + 1]) * p.scale);
+                    k.y = DType<T>::pack2(__uint_as_float(b[8 * q4 + 2]) * p.scale,
+                                          __uint_as_float(b[8 * q4 + 3]) * p.scale);
+                    k.z = DType<T>::pack2(__uint_as_float(b[8 * q4 + 4]) * p.scale,
+                                          __uint_as_float(b[8 * q4 + 5]) * p.scale);
+                    k.w = DType<T>::pack2(__uint_as_float(b[8 * q4 + 6]) * p.scale,
+                                          __uint_as_float(b[8 * q4 + 7]) * p.scale);
+                    dstv[q4] = v;
+                    dstk[q4] = k;
+                }
+            }
+        }
+    } else if (warp >= 8) {
+        // ------------------------------------------------ dQ drain
+        const int wq = warp & 3;
+        const int r = wq * 32 + lane;  // query row within block i
+        const uint32_t t_q = tmem + (static_cast<uint32_t>(wq * 32) << 16);
+        for (int it = 0; it < n_it; ++it) {
+            const int i = i0 + it;
+            if (!bwarp_wait(bar_dq, it & 1, abort_flag)) break;
+            tc_fence_after();
+            const int q = i * 128 + r;
+            float* dst = p.dq_acc + (static_cast<size_t>(bh) * p.N + q) * D;
+#pragma unroll
+            for (int cb = 0; cb < D / 32; ++cb) {
+                uint32_t v[32];
+                tmem_ld_x32(t_q + cb * 32, v);
+                if (q < p.N) {
+#pragma unroll
+                    for (int k = 0; k < 8; ++k)
+                        red_add_v4(dst + cb * 32 + 4 * k, __uint_as_float(v[4 * k]),
+                                   __uint_as_float(v[4 * k + 1]), __uint_as_float(v[4 * k + 2]),
+                                   __uint_as_float(v[4 * k + 3]));
+                }
+            }
+            tc_fence_before();
+            mbar_arrive(bar_dqfree);
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem, 512);
+    }
+}
+
+template <typename T, int D>
+FlashAttentionError bwd_typed(const T* Q, const T* K, const T* V, const T* O, const float* L,
+                              const T* dO, T* dQ, T* dK, T* dV, int BH, int N, float scale,
+                              bool causal, cudaStream_t stream) {
+    using G = BwdGeom<D>;
+    const int n_blk = (N + 127) / 128;
+    const long long n_pad = static_cast<long long>(n_blk) * 128;
+    const size_t acc_elems = static_cast<size_t>(BH) * N * D;
+    const size_t pad_elems = static_cast<size_t>(BH) * n_pad;
+    void* ws = nullptr;
+    FlashAttentionError e =
+        workspace_alloc(&ws, (acc_elems + 2 * pad_elems) * sizeof(float), stream);
+    if (e != FlashAttentionError::SUCCESS) return e;
+    float* dq_acc = static_cast<float*>(ws);
+    float* l2p = dq_acc + acc_elems;
+    float* dvp = l2p + pad_elems;
+
+    auto fail = [&](FlashAttentionError err) {
+        workspace_free(ws, stream);
+        return err;
+    };
+    const CUtensorMapSwizzle swz =
+        G::kSwz == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
+    CUtensorMap mq, mk, mv, mdo;
+    if (!encode_tmap_3d(&mq, Q, DType<T>::kTmaType, 2, D, N, BH, G::kCbElems, 128, swz) ||
+        !encode_tmap_3d(&mk, K, DType<T>::kTmaType, 2, D, N, BH, G::kCbElems, 128, swz) ||
+        !encode_tmap_3d(&mv, V, DType<T>::kTmaType, 2, D, N, BH, G::kCbElems, 128, swz) ||
+        !encode_tmap_3d(&mdo, dO, DType<T>::kTmaType, 2, D, N, BH, G::kCbElems, 128, swz))
+        return fail(FlashAttentionError::CUDA_ERROR);
+    for (const void* ptr : {static_cast<const void*>(O), static_cast<const void*>(dQ),
+                            static_cast<const void*>(dK), static_cast<const void*>(dV)})
+        if ((reinterpret_cast<uintptr_t>(ptr) & 15u) != 0)
+            return fail(FlashAttentionError::CUDA_ERROR);
+    auto kern = fa_bwd_kernel<T, D>;
+    if (!ensure_smem_attr(reinterpret_cast<const void*>(kern), G::kSmemBytes))
+        return fail(FlashAttentionError::CUDA_ERROR);
+    if (n_blk > 0x7fffffff / 1) return fail(FlashAttentionError::CUDA_ERROR);
+
+    const long long rows_pad = static_cast<long long>(BH) * n_pad;
+    const long long pre_blocks = (rows_pad * 32 + 255) / 256;
+    bwd_preprocess_kernel<T, D><<<static_cast<unsigned>(pre_blocks), 256, 0, stream>>>(
+        O, dO, L, l2p, dvp, dq_acc, N, static_cast<int>(n_pad), rows_pad);
+    if (cudaGetLastError() != cudaSuccess) return fail(FlashAttentionError::CUDA_ERROR);
+
+    BwdParams prm;
+    prm.dq_acc = dq_acc;
+    prm.dK = dK;
+    prm.dV = dV;
+    prm.l2p = l2p;
+    prm.dvp = dvp;
+    prm.N = N;
+    prm.n_blk = n_blk;
+    prm.causal = causal ? 1 : 0;
+    prm.scale_log2 = scale * kLog2eB;
+    prm.scale = scale;
+    kern<<<dim3(n_blk, BH), 384, G::kSmemBytes, stream>>>(mq, mk, mv, mdo, prm);
+    if (cudaGetLastError() != cudaSuccess) return fail(FlashAttentionError::CUDA_ERROR);
+
+    const long long n4 = static_cast<long long>(acc_elems / 4);
+    long long cblocks = (n4 + 255) / 256;
+    const long long cap = 32LL * current_sm_count();
+    if (cblocks > cap) cblocks = cap;
+    bwd_convert_dq_kernel<T><<<static_cast<unsigned>(cblocks), 256, 0, stream>>>(dq_acc, dQ, scale,
+                                                                                 n4);
+    if (cudaGetLastError() != cudaSuccess) return fail(FlashAttentionError::CUDA_ERROR);
+    workspace_free(ws, stream);
+    return FlashAttentionError::SUCCESS;
+}
+
 }  // namespace
 
 template <typename T>
@@ -17,7 +575,18 @@ FlashAttentionError launch_bwd_sm100(const T* Q, const T* K, const T* V, const T
                                      const float* L, const T* dO, T* dQ, T* dK, T* dV, int B,
                                      int H, int N, int D, float scale, bool causal,
                                      cudaStream_t stream) {
-    return launch_bwd_simt<T>(Q, K, V, O, L, dO, dQ, dK, dV, B, H, N, D, scale, causal, stream);
+    const int BH = B * H;
+    if (N > 65535 * 128) return FlashAttentionError::CUDA_ERROR;
+    switch (D) {
+        case 32:
+            return bwd_typed<T, 32>(Q, K, V, O, L, dO, dQ, dK, dV, BH, N, scale, causal, stream);
+        case 64:
+            return bwd_typed<T, 64>(Q, K, V, O, L, dO, dQ, dK, dV, BH, N, scale, causal, stream);
+        case 128:
+            return bwd_typed<T, 128>(Q, K, V, O, L, dO, dQ, dK, dV, BH, N, scale, causal, stream);
+        default:
+            return FlashAttentionError::UNSUPPORTED_HEAD_DIM;
+    }
 }
 
 template FlashAttentionError launch_bwd_sm100<half>(const half*, const half*, const half*,

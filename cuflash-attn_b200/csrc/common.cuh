@@ -69,6 +69,15 @@ bool ensure_smem_attr(const void* kernel, int bytes);
 
 int current_sm_count();
 
+// Stream-ordered workspace from a library-private memory pool on the current
+// device (created on first use; freed blocks stay cached in the pool so
+// repeated calls do not remap memory).  Returns OUT_OF_MEMORY when the pool
+// cannot grow.  Setting the environment variable
+// CUFLASH_FAULT_WORKSPACE_OOM=1 makes every request fail with OUT_OF_MEMORY
+// before any CUDA call (host-side fault injection for tests).
+FlashAttentionError workspace_alloc(void** ptr, size_t bytes, cudaStream_t stream);
+void workspace_free(void* ptr, cudaStream_t stream);
+
 // Launchers (defined in the kernel .cu files).  All pointers are device
 // pointers; validation has already happened.
 template <typename T>

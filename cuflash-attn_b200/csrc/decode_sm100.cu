@@ -263,15 +263,12 @@ FlashAttentionError decode_typed(const T* Q, const T* K, const T* V, T* O, float
         return cudaGetLastError() == cudaSuccess ? FlashAttentionError::SUCCESS
                                                  : FlashAttentionError::CUDA_ERROR;
     }
-    float* ws = nullptr;
     const size_t part_elems = static_cast<size_t>(BH) * S * D;
     const size_t bytes = (part_elems + static_cast<size_t>(BH) * S) * sizeof(float);
-    cudaError_t err = cudaMallocAsync(reinterpret_cast<void**>(&ws), bytes, stream);
-    if (err != cudaSuccess) {
-        cudaGetLastError();
-        return err == cudaErrorMemoryAllocation ? FlashAttentionError::OUT_OF_MEMORY
-                                                : FlashAttentionError::CUDA_ERROR;
-    }
+    void* wsv = nullptr;
+    FlashAttentionError werr = workspace_alloc(&wsv, bytes, stream);
+    if (werr != FlashAttentionError::SUCCESS) return werr;
+    float* ws = static_cast<float*>(wsv);
     float* o_part = ws;
     float* l_part = ws + part_elems;
     decode_split_kernel<T, D, false><<<dim3(S, BH), kDecodeThreads, 0, stream>>>(
@@ -279,7 +276,7 @@ FlashAttentionError decode_typed(const T* Q, const T* K, const T* V, T* O, float
     cudaError_t e1 = cudaGetLastError();
     decode_combine_kernel<T, D><<<BH, 128, 0, stream>>>(o_part, l_part, O, L, S);
     cudaError_t e2 = cudaGetLastError();
-    cudaFreeAsync(ws, stream);
+    workspace_free(ws, stream);
     return (e1 == cudaSuccess && e2 == cudaSuccess) ? FlashAttentionError::SUCCESS
                                                     : FlashAttentionError::CUDA_ERROR;
 }

@@ -4,6 +4,7 @@
 
 #include <cudaTypedefs.h>
 
+#include <cstdlib>
 #include <mutex>
 #include <set>
 #include <utility>
@@ -81,6 +82,46 @@ int current_sm_count() {
         cache[dev] = n;
     }
     return cache[dev];
+}
+
+FlashAttentionError workspace_alloc(void** ptr, size_t bytes, cudaStream_t stream) {
+    *ptr = nullptr;
+    const char* fault = std::getenv("CUFLASH_FAULT_WORKSPACE_OOM");
+    if (fault != nullptr && fault[0] != '\0' && fault[0] != '0')
+        return FlashAttentionError::OUT_OF_MEMORY;
+    static std::mutex mu;
+    static cudaMemPool_t pools[64] = {};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64)
+        return FlashAttentionError::CUDA_ERROR;
+    cudaMemPool_t pool;
+    {
+        std::lock_guard<std::mutex> lock(mu);
+        if (pools[dev] == nullptr) {
+            cudaMemPoolProps props = {};
+            props.allocType = cudaMemAllocationTypePinned;
+            props.location.type = cudaMemLocationTypeDevice;
+            props.location.id = dev;
+            cudaMemPool_t p = nullptr;
+            if (cudaMemPoolCreate(&p, &props) != cudaSuccess) return FlashAttentionError::CUDA_ERROR;
+            uint64_t keep = ~0ull;
+            cudaMemPoolSetAttribute(p, cudaMemPoolAttrReleaseThreshold, &keep);
+            pools[dev] = p;
+        }
+        pool = pools[dev];
+    }
+    cudaError_t err = cudaMallocFromPoolAsync(ptr, bytes, pool, stream);
+    if (err != cudaSuccess) {
+        cudaGetLastError();
+        *ptr = nullptr;
+        return err == cudaErrorMemoryAllocation ? FlashAttentionError::OUT_OF_MEMORY
+                                                : FlashAttentionError::CUDA_ERROR;
+    }
+    return FlashAttentionError::SUCCESS;
+}
+
+void workspace_free(void* ptr, cudaStream_t stream) {
+    if (ptr != nullptr) cudaFreeAsync(ptr, stream);
 }
 
 int read_and_clear_device_status() {

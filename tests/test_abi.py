@@ -170,3 +170,15 @@ def test_oracle_is_test_infrastructure_only():
         assert "import oracle" not in text and "liboracle" not in text, f
     assert "TEST INFRASTRUCTURE ONLY" in (ROOT / "oracle" / "cpu_ref.cpp").read_text()
     assert oracle.LIB_PATH.name == "liboracle.so"
+
+
+def test_workspace_oom_fault_injection(lib, monkeypatch):
+    """Host-side fault injection: a failing workspace allocation surfaces as
+    OUT_OF_MEMORY (the reference maps cudaMallocAsync failure the same way,
+    src/backward/flash_attention_backward_typed.cu:378-387).  The request
+    fails before any CUDA call, so no GPU is involved."""
+    monkeypatch.setenv("CUFLASH_FAULT_WORKSPACE_OOM", "1")
+    for sfx in ("f16", "bf16"):
+        assert _bwd(lib, sfx, N=256, D=64) == cf.OUT_OF_MEMORY
+        fn = getattr(lib.lib, f"cuflash_attention_decode_{sfx}")
+        assert fn(FAKE, FAKE, FAKE, FAKE, FAKE, 2, 2, 4096, 128, 0.1, 8, STREAM) == cf.OUT_OF_MEMORY
