@@ -311,6 +311,23 @@ int cuflash_convert_f32_to_f16(const float* src, half* dst, long long count,
     return static_cast<int>(cuflash::detail::launch_convert_f32<half>(src, dst, count, stream));
 }
 
+int cuflash_attention_decode_bf16_noalloc(const __nv_bfloat16* Q, const __nv_bfloat16* K,
+                                          const __nv_bfloat16* V, __nv_bfloat16* O, float* L,
+                                          int batch_size, int num_heads, int kv_len, int head_dim,
+                                          float scale, int num_splits, cudaStream_t stream) {
+    if (!Q || !K || !V || !O || !L) return static_cast<int>(FlashAttentionError::NULL_POINTER);
+    if (batch_size <= 0 || num_heads <= 0 || kv_len <= 0 || head_dim <= 0)
+        return static_cast<int>(FlashAttentionError::INVALID_DIMENSION);
+    if (!(head_dim == 32 || head_dim == 64 || head_dim == 128))
+        return static_cast<int>(FlashAttentionError::UNSUPPORTED_HEAD_DIM);
+    if (!std::isfinite(scale) || scale < 0.0f || num_splits < 0 || num_splits > 64)
+        return static_cast<int>(FlashAttentionError::INVALID_DIMENSION);
+    if (static_cast<long long>(batch_size) * num_heads > 0x7fffffffLL)
+        return static_cast<int>(FlashAttentionError::INVALID_DIMENSION);
+    return static_cast<int>(cuflash::detail::launch_decode_bf16_noalloc(
+        Q, K, V, O, L, batch_size, num_heads, kv_len, head_dim, scale, num_splits, stream));
+}
+
 int cuflash_device_status(void) { return cuflash::detail::read_and_clear_device_status(); }
 
 }  // extern "C"

@@ -117,6 +117,13 @@ FlashAttentionError launch_decode(const T* Q, const T* K, const T* V, T* O, floa
                                   int kv_len, int D, float scale, int num_splits,
                                   cudaStream_t stream);
 
+// Split-KV decode whose partials live in a fixed device buffer (no
+// allocation); see decode_sm100.cu.
+FlashAttentionError launch_decode_bf16_noalloc(const __nv_bfloat16* Q, const __nv_bfloat16* K,
+                                               const __nv_bfloat16* V, __nv_bfloat16* O, float* L,
+                                               int B, int H, int kv_len, int D, float scale,
+                                               int num_splits, cudaStream_t stream);
+
 FlashAttentionError launch_lse_merge(float* O_acc, float* L_acc, const float* O_part,
                                      const float* L_part, long long rows, int D,
                                      cudaStream_t stream);

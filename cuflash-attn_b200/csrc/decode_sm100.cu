@@ -18,6 +18,7 @@
 // (src/kernels/impl/online_softmax.cuh:16-59) in the log2 domain.
 
 #include <cmath>
+#include <mutex>
 
 #include "common.cuh"
 
@@ -337,6 +338,115 @@ template FlashAttentionError launch_convert_f32<half>(const float*, half*, long 
                                                       cudaStream_t);
 template FlashAttentionError launch_convert_f32<__nv_bfloat16>(const float*, __nv_bfloat16*,
                                                                long long, cudaStream_t);
+
+
+// ---------------------------------------------------------------------------
+// Split-KV decode without any allocation.
+//
+// Some callers cannot let a library allocate device memory: serving engines
+// that claim nearly all of HBM at start-up for their KV-cache pages and hand
+// memory out only through their own allocator (a stray cudaMalloc either
+// fails or fragments that reservation), and latency-critical decode loops that
+// keep allocation calls, whose cost is unpredictable, off the per-token path.
+// For them the split partials live in this fixed buffer instead of the
+// stream-ordered workspace.
+//
+// kNoAllocScratchFloats fp32 values (8 MiB) are reserved on every GPU that
+// loads the library and stay reserved until the process exits.  The buffer
+// is shared by all calls and keeps whatever the last call left in it; each
+// call overwrites every partial it reads, so nothing needs clearing first.
+// Two calls whose kernels overlap on the GPU (different streams, or
+// different host threads) race on the buffer and must be serialised by the
+// caller.
+// ---------------------------------------------------------------------------
+constexpr long long kNoAllocScratchFloats = 2LL * 1024 * 1024;  // 8 MiB
+static __device__ __align__(256) float g_noalloc_scratch[kNoAllocScratchFloats];
+
+namespace {
+
+// Device address of g_noalloc_scratch on the current device.  In host code
+// the symbol is only a host-side stand-in, so the address is looked up once
+// per device (with that device current) and cached.
+FlashAttentionError noalloc_scratch_ptr(float** out) {
+    static std::mutex mu;
+    static float* cache[64] = {};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64)
+        return FlashAttentionError::CUDA_ERROR;
+    std::lock_guard<std::mutex> lock(mu);
+    if (cache[dev] == nullptr) {
+        void* ptr = nullptr;
+        if (cudaGetSymbolAddress(&ptr, g_noalloc_scratch) != cudaSuccess || ptr == nullptr) {
+            cudaGetLastError();
+            return FlashAttentionError::CUDA_ERROR;
+        }
+        cache[dev] = static_cast<float*>(ptr);
+    }
+    *out = cache[dev];
+    return FlashAttentionError::SUCCESS;
+}
+
+template <int D>
+FlashAttentionError decode_noalloc_typed(const __nv_bfloat16* Q, const __nv_bfloat16* K,
+                                         const __nv_bfloat16* V, __nv_bfloat16* O, float* L,
+                                         int BH, int kv_len, float scale, int num_splits,
+                                         cudaStream_t stream) {
+    using T = __nv_bfloat16;
+    for (const void* p : {static_cast<const void*>(Q), static_cast<const void*>(K),
+                          static_cast<const void*>(V), static_cast<const void*>(O)})
+        if ((reinterpret_cast<uintptr_t>(p) & 15u) != 0) return FlashAttentionError::CUDA_ERROR;
+    const long long per_split = static_cast<long long>(BH) * (D + 1);  // partial O + its LSE
+    int S;
+    if (num_splits == 0) {
+        S = auto_splits(BH, kv_len);
+        const long long fit = kNoAllocScratchFloats / per_split;  // auto mode stays within it
+        if (S > fit) S = static_cast<int>(fit < 1 ? 1 : fit);
+    } else {
+        S = num_splits;
+    }
+    if (S > kv_len) S = kv_len;
+    const int chunk = (kv_len + S - 1) / S;
+    S = (kv_len + chunk - 1) / chunk;
+    const float sl2 = scale * kLog2ef;
+    if (S == 1) {
+        decode_split_kernel<T, D, true><<<dim3(1, BH), kDecodeThreads, 0, stream>>>(
+            Q, K, V, O, L, nullptr, nullptr, kv_len, chunk, sl2);
+        return cudaGetLastError() == cudaSuccess ? FlashAttentionError::SUCCESS
+                                                 : FlashAttentionError::CUDA_ERROR;
+    }
+    if (per_split * S > kNoAllocScratchFloats) return FlashAttentionError::OUT_OF_MEMORY;
+    float* scratch = nullptr;
+    FlashAttentionError e = noalloc_scratch_ptr(&scratch);
+    if (e != FlashAttentionError::SUCCESS) return e;
+    float* o_part = scratch;
+    float* l_part = scratch + static_cast<size_t>(BH) * S * D;
+    decode_split_kernel<T, D, false><<<dim3(S, BH), kDecodeThreads, 0, stream>>>(
+        Q, K, V, nullptr, nullptr, o_part, l_part, kv_len, chunk, sl2);
+    cudaError_t e1 = cudaGetLastError();
+    decode_combine_kernel<T, D><<<BH, 128, 0, stream>>>(o_part, l_part, O, L, S);
+    cudaError_t e2 = cudaGetLastError();
+    return (e1 == cudaSuccess && e2 == cudaSuccess) ? FlashAttentionError::SUCCESS
+                                                    : FlashAttentionError::CUDA_ERROR;
+}
+
+}  // namespace
+
+FlashAttentionError launch_decode_bf16_noalloc(const __nv_bfloat16* Q, const __nv_bfloat16* K,
+                                               const __nv_bfloat16* V, __nv_bfloat16* O, float* L,
+                                               int B, int H, int kv_len, int D, float scale,
+                                               int num_splits, cudaStream_t stream) {
+    const int BH = B * H;
+    switch (D) {
+        case 32:
+            return decode_noalloc_typed<32>(Q, K, V, O, L, BH, kv_len, scale, num_splits, stream);
+        case 64:
+            return decode_noalloc_typed<64>(Q, K, V, O, L, BH, kv_len, scale, num_splits, stream);
+        case 128:
+            return decode_noalloc_typed<128>(Q, K, V, O, L, BH, kv_len, scale, num_splits, stream);
+        default:
+            return FlashAttentionError::UNSUPPORTED_HEAD_DIM;
+    }
+}
 
 }  // namespace detail
 }  // namespace cuflash

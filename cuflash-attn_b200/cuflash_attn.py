@@ -52,6 +52,7 @@ SIGNATURES = {
     "cuflash_error_string": [_I],
     "cuflash_attention_decode_f16": [_P] * 5 + [_I] * 4 + [_F, _I, _P],
     "cuflash_attention_decode_bf16": [_P] * 5 + [_I] * 4 + [_F, _I, _P],
+    "cuflash_attention_decode_bf16_noalloc": [_P] * 5 + [_I] * 4 + [_F, _I, _P],
     "cuflash_attention_forward_partial_bf16": [_P] * 5 + [_I] * 5 + [_F, _LL, _LL, _B, _P],
     "cuflash_attention_forward_partial_f16": [_P] * 5 + [_I] * 5 + [_F, _LL, _LL, _B, _P],
     "cuflash_lse_merge_f32": [_P] * 4 + [_LL, _I, _P],

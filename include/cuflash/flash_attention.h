@@ -165,6 +165,25 @@ CUFLASH_EXPORT int cuflash_attention_decode_bf16(const __nv_bfloat16* Q, const _
                                                  int kv_len, int head_dim, float scale,
                                                  int num_splits, cudaStream_t stream);
 
+// Split-KV decode (bf16) that allocates nothing.  No counterpart in the
+// reference library.  For callers that must not have device memory
+// allocated behind their back: serving engines that reserve nearly all of
+// HBM for their KV cache and hand memory out only through their own
+// allocator, and decode loops that keep allocation calls off the per-token
+// path.  Same arguments and results as cuflash_attention_decode_bf16; the
+// split partials go to a fixed 8 MiB device buffer that every GPU loading the
+// library holds until exit (batch*heads*splits*(head_dim+1) fp32 values must
+// fit: with num_splits = 0 the split count is capped to fit, an explicit
+// num_splits that does not fit returns OUT_OF_MEMORY without launching).
+// The first call on a device looks up the buffer's device address (make that
+// first call before any stream capture on that device).  All calls share the
+// buffer: calls whose kernels may overlap on the GPU race and must be
+// serialised by the caller (one stream, or events between streams).
+CUFLASH_EXPORT int cuflash_attention_decode_bf16_noalloc(
+    const __nv_bfloat16* Q, const __nv_bfloat16* K, const __nv_bfloat16* V, __nv_bfloat16* O,
+    float* L, int batch_size, int num_heads, int kv_len, int head_dim, float scale,
+    int num_splits, cudaStream_t stream);
+
 // Partial forward for context parallelism: queries [B,H,seq_q,D] at global
 // positions q_offset.., keys/values [B,H,seq_k,D] at global positions
 // k_offset...  With causal, key g_k is masked for query g_q iff g_k > g_q.
