@@ -214,8 +214,7 @@ def run_ours(args):
     if args.workload == "decode":
         return run_decode(args, lib, dev, world, rank, pk, pk_kind)
 
-    c = TRAIN
-    B, H, N, D = c["B"], c["H"], c["N"], c["D"]
+    B, H, N, D = args.batch, args.heads, args.seq, args.head_dim
     scale = 1.0 / math.sqrt(D)
     g = torch.Generator(device=dev).manual_seed(21 + 1000 * rank)
     shape = (B, H, N, D)
@@ -332,11 +331,13 @@ def run_ours(args):
             "steps": args.steps, "warmup": max(args.warmup, 3), "ms_per_step": ms_step,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic (torch.randn, seeds 21+1000*rank; Q/K/V 0.5*N(0,1), dO N(0,1))",
-            "config": {"workload": "BASELINE config 3: bf16 causal attention fwd+bwd, "
-                                   "B8 H32 N4096 D128 per GPU",
-                       "global_batch": 8 * world, "heads": 32, "seq_len": N, "head_dim": D,
+            "config": {"workload": ("BASELINE config 3: " if (B, H, N, D) == (8, 32, 4096, 128)
+                                    else "custom shape: ") +
+                                   f"bf16 causal attention fwd+bwd, B{B} H{H} N{N} D{D} per GPU",
+                       "global_batch": B * world, "heads": 32, "seq_len": N, "head_dim": D,
                        "parallelism": f"(batch,head) sharding, {world} GPU(s), no collective",
-                       "l2": "inputs (1 GiB per GPU) larger than L2; no flush"},
+                       "l2": f"inputs ({4 * Q.numel() * 2 / 2**20:.0f} MiB per GPU) vs 126 MB L2; "
+                             "no flush"},
             "per_gpu_tflops": value / world,
             "pct_bf16_peak_per_gpu": 100.0 * (value / world) / peak,
             "fwd": {"ms": fwd_ms, "tflops": fwd_tflops,
@@ -419,6 +420,10 @@ def main():
     ap.add_argument("--workload", choices=["train", "decode"], default="train")
     ap.add_argument("--splits", type=int, nargs="*", default=[0, 1, 2, 4, 8, 16, 32, 64])
     ap.add_argument("--skip-cpu-baseline", action="store_true")
+    ap.add_argument("--batch", type=int, default=TRAIN["B"])
+    ap.add_argument("--heads", type=int, default=TRAIN["H"])
+    ap.add_argument("--seq", type=int, default=TRAIN["N"])
+    ap.add_argument("--head-dim", type=int, default=TRAIN["D"])
     args = ap.parse_args()
     if args.impl == "reference":
         return run_reference(args)

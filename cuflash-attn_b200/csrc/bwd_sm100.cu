@@ -26,8 +26,9 @@
 //   warps 4-7   one thread per K/V row (TMEM lane): P^T, dS^T from S^T, dP^T;
 //               writes P^T and dS^T back into TMEM (fp16/bf16) and dS^T into
 //               shared memory for the dQ product; at the end stores dK, dV.
-//   warps 8-11  one thread per query row: drains dQ_i from TMEM into the fp32
-//               accumulator with vector reductions (red.global.add.v4.f32).
+//   warps 8-11  one thread per query row: drains dQ_i from TMEM through
+//               swizzled shared-memory boxes into the fp32 accumulator with
+//               TMA reduce-add (cp.reduce.async.bulk.tensor).
 // Kernel 3 (convert): dQ = scale * dQ_acc in the output dtype.
 //
 // CTAs of one (batch, head) are adjacent in launch order, so the dQ
@@ -125,17 +126,29 @@ __device__ __forceinline__ void bulk_load(void* smem_dst, const void* gsrc, uint
         : "memory");
 }
 
-__device__ __forceinline__ void red_add_v4(float* gptr, float a, float b, float c, float d) {
-    asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(gptr), "f"(a), "f"(b),
-                 "f"(c), "f"(d)
-                 : "memory");
-}
-
 __device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c,
                                              uint32_t d) {
     asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c),
                  "r"(d)
                  : "memory");
+}
+
+// Element-wise add of a shared-memory box into global memory through the TMA
+// unit (no multicast); completion is tracked with bulk async-groups.
+__device__ __forceinline__ void tma_reduce_add_3d(const CUtensorMap* map, uint32_t smem_src, int c0,
+                                                  int c1, int c2) {
+    asm volatile(
+        "cp.reduce.async.bulk.tensor.3d.global.shared::cta.add.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(
+            reinterpret_cast<uint64_t>(map)),
+        "r"(smem_src), "r"(c0), "r"(c1), "r"(c2)
+        : "memory");
+}
+__device__ __forceinline__ void bulk_commit_group() {
+    asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+template <int N>
+__device__ __forceinline__ void bulk_wait_group_read() {
+    asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
 }
 
 __device__ __forceinline__ void fence_proxy_async_smem() {
@@ -200,7 +213,7 @@ template <typename T, int D>
 __global__ void __launch_bounds__(384, 1)
     fa_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                   const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmdO,
-                  const BwdParams p) {
+                  const __grid_constant__ CUtensorMap tmdQ, const BwdParams p) {
     using G = BwdGeom<D>;
     using namespace sm100;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -389,20 +402,27 @@ __global__ void __launch_bounds__(384, 1)
 #pragma unroll
             for (int cc = 0; cc < 4; ++cc) {
                 uint32_t sv[32], dv[32];
-                tmem_ld_x32(t_s + cc * 32, sv);
-                tmem_ld_x32(t_dp + cc * 32, dv);
+                tmem_ld2_x32(t_s + cc * 32, sv, t_dp + cc * 32, dv);
+                float lq[32], dq[32];
+#pragma unroll
+                for (int v = 0; v < 8; ++v) {
+                    const float4 a = reinterpret_cast<const float4*>(sL + cc * 32)[v];
+                    const float4 b = reinterpret_cast<const float4*>(sD + cc * 32)[v];
+                    lq[4 * v] = a.x; lq[4 * v + 1] = a.y; lq[4 * v + 2] = a.z; lq[4 * v + 3] = a.w;
+                    dq[4 * v] = b.x; dq[4 * v + 1] = b.y; dq[4 * v + 2] = b.z; dq[4 * v + 3] = b.w;
+                }
                 uint32_t pp[16], dd[16];
 #pragma unroll
                 for (int e = 0; e < 16; ++e) {
                     const int q0 = cc * 32 + 2 * e;
-                    float p0 = ex2_approx(fmaf(__uint_as_float(sv[2 * e]), c, -sL[q0]));
-                    float p1 = ex2_approx(fmaf(__uint_as_float(sv[2 * e + 1]), c, -sL[q0 + 1]));
+                    float p0 = ex2_approx(fmaf(__uint_as_float(sv[2 * e]), c, -lq[2 * e]));
+                    float p1 = ex2_approx(fmaf(__uint_as_float(sv[2 * e + 1]), c, -lq[2 * e + 1]));
                     if (diag) {
                         if (q0 < r) p0 = 0.f;
                         if (q0 + 1 < r) p1 = 0.f;
                     }
-                    const float d0 = p0 * (__uint_as_float(dv[2 * e]) - sD[q0]);
-                    const float d1 = p1 * (__uint_as_float(dv[2 * e + 1]) - sD[q0 + 1]);
+                    const float d0 = p0 * (__uint_as_float(dv[2 * e]) - dq[2 * e]);
+                    const float d1 = p1 * (__uint_as_float(dv[2 * e + 1]) - dq[2 * e + 1]);
                     pp[e] = DType<T>::pack2(p0, p1);
                     dd[e] = DType<T>::pack2(d0, d1);
                 }
@@ -465,27 +485,42 @@ __global__ void __launch_bounds__(384, 1)
         }
     } else if (warp >= 8) {
         // ------------------------------------------------ dQ drain
+        // Each warp owns 32 query rows.  Per 32-column chunk it copies its
+        // 32x32 fp32 block from TMEM into a 128-byte-swizzled staging box and
+        // the TMA unit adds the box into the fp32 accumulator in global
+        // memory.  Staging lives in the dS buffer, which is idle from the
+        // completion of dQ_i until the MMA issues S_{i+1} (after this drain
+        // signals bar_dqfree); two 4 KiB boxes per warp alternate.
         const int wq = warp & 3;
-        const int r = wq * 32 + lane;  // query row within block i
         const uint32_t t_q = tmem + (static_cast<uint32_t>(wq * 32) << 16);
+        const uint32_t stage0 = sbase + G::kOffDs + wq * 8192;
         for (int it = 0; it < n_it; ++it) {
             const int i = i0 + it;
             if (!bwarp_wait(bar_dq, it & 1, abort_flag)) break;
             tc_fence_after();
-            const int q = i * 128 + r;
-            float* dst = p.dq_acc + (static_cast<size_t>(bh) * p.N + q) * D;
 #pragma unroll
             for (int cb = 0; cb < D / 32; ++cb) {
+                const uint32_t box = stage0 + (cb & 1) * 4096;
+                if (cb >= 2) {
+                    if (lane == 0) bulk_wait_group_read<1>();
+                    __syncwarp();
+                }
                 uint32_t v[32];
                 tmem_ld_x32(t_q + cb * 32, v);
-                if (q < p.N) {
 #pragma unroll
-                    for (int k = 0; k < 8; ++k)
-                        red_add_v4(dst + cb * 32 + 4 * k, __uint_as_float(v[4 * k]),
-                                   __uint_as_float(v[4 * k + 1]), __uint_as_float(v[4 * k + 2]),
-                                   __uint_as_float(v[4 * k + 3]));
+                for (int k = 0; k < 8; ++k)
+                    st_shared_v4(box + lane * 128 + ((k ^ (lane & 7)) << 4), v[4 * k], v[4 * k + 1],
+                                 v[4 * k + 2], v[4 * k + 3]);
+                fence_proxy_async_smem();
+                __syncwarp();
+                if (lane == 0) {
+                    tma_reduce_add_3d(&tmdQ, box, cb * 32, i * 128 + wq * 32, bh);
+                    bulk_commit_group();
                 }
             }
+            // the staging boxes must be read out before dS_{i+1} overwrites them
+            if (lane == 0) bulk_wait_group_read<0>();
+            __syncwarp();
             tc_fence_before();
             mbar_arrive(bar_dqfree);
         }
@@ -522,11 +557,13 @@ FlashAttentionError bwd_typed(const T* Q, const T* K, const T* V, const T* O, co
     };
     const CUtensorMapSwizzle swz =
         G::kSwz == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
-    CUtensorMap mq, mk, mv, mdo;
+    CUtensorMap mq, mk, mv, mdo, mdq;
     if (!encode_tmap_3d(&mq, Q, DType<T>::kTmaType, 2, D, N, BH, G::kCbElems, 128, swz) ||
         !encode_tmap_3d(&mk, K, DType<T>::kTmaType, 2, D, N, BH, G::kCbElems, 128, swz) ||
         !encode_tmap_3d(&mv, V, DType<T>::kTmaType, 2, D, N, BH, G::kCbElems, 128, swz) ||
-        !encode_tmap_3d(&mdo, dO, DType<T>::kTmaType, 2, D, N, BH, G::kCbElems, 128, swz))
+        !encode_tmap_3d(&mdo, dO, DType<T>::kTmaType, 2, D, N, BH, G::kCbElems, 128, swz) ||
+        !encode_tmap_3d(&mdq, dq_acc, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, D, N, BH, 32, 32,
+                        CU_TENSOR_MAP_SWIZZLE_128B))
         return fail(FlashAttentionError::CUDA_ERROR);
     for (const void* ptr : {static_cast<const void*>(O), static_cast<const void*>(dQ),
                             static_cast<const void*>(dK), static_cast<const void*>(dV)})
@@ -554,7 +591,7 @@ FlashAttentionError bwd_typed(const T* Q, const T* K, const T* V, const T* O, co
     prm.causal = causal ? 1 : 0;
     prm.scale_log2 = scale * kLog2eB;
     prm.scale = scale;
-    kern<<<dim3(n_blk, BH), 384, G::kSmemBytes, stream>>>(mq, mk, mv, mdo, prm);
+    kern<<<dim3(n_blk, BH), 384, G::kSmemBytes, stream>>>(mq, mk, mv, mdo, mdq, prm);
     if (cudaGetLastError() != cudaSuccess) return fail(FlashAttentionError::CUDA_ERROR);
 
     const long long n4 = static_cast<long long>(acc_elems / 4);

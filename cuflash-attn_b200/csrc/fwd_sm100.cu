@@ -133,8 +133,10 @@ __global__ void __launch_bounds__(384, 1)
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
-    const int bh = blockIdx.x;
-    const int ct = p.num_ctiles - 1 - static_cast<int>(blockIdx.y);
+    // (q tile, b*h) grid with q tiles fastest: the CTAs running at the same
+    // time share few (b,h), so their K/V blocks are reused from L2.
+    const int bh = blockIdx.y;
+    const int ct = p.num_ctiles - 1 - static_cast<int>(blockIdx.x);
     const int q_row0 = ct * 256;
 
     // kv blocks needed by each 128-row tile
@@ -182,6 +184,11 @@ __global__ void __launch_bounds__(384, 1)
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
 
+    // Registers: launched with 168 per thread (384 x 168 = 64512); warpgroup 0
+    // (producer, MMA, 2 idle warps) gives back down to 56 and the two softmax
+    // warpgroups take 216 each: 128*56 + 256*216 = 62464 <= 64512.
+    if (warp < 4) {
+        setmaxnreg_dec<56>();
     if (warp == 0) {
         // ------------------------------------------------ TMA producer
         if (lane == 0 && n_max > 0) {
@@ -301,7 +308,9 @@ __global__ void __launch_bounds__(384, 1)
             mbar_wait(bar_done, 0, &never, &g_fwd_status);
         }
         __syncwarp();
-    } else if (warp >= 4) {
+    }
+    } else {
+        setmaxnreg_inc<216>();
         // ------------------------------------------------ softmax / epilogue
         const int t = (warp - 4) >> 2;
         const int wq = warp & 3;
@@ -329,7 +338,6 @@ __global__ void __launch_bounds__(384, 1)
             const int col0 = j * 128;
             const bool need_mask = (col0 + 128 > p.seq_k) ||
                                    (p.causal && (p.k_offset + col0 + 127 > tile_g0));
-            float mx = -INFINITY;
             if (need_mask) {
                 // largest visible local key column for this row (32-bit safe)
                 const long long lim64 = grow - p.k_offset;
@@ -337,15 +345,21 @@ __global__ void __launch_bounds__(384, 1)
                                          : 0x7fffffff;
                 const int vis_end = min(p.seq_k - 1, lim) - col0;  // visible iff i <= vis_end
 #pragma unroll
-                for (int i = 0; i < 128; ++i) {
-                    const float x = (i <= vis_end) ? __uint_as_float(sr[i]) * c : -INFINITY;
-                    sr[i] = __float_as_uint(x);
-                    mx = fmaxf(mx, x);
-                }
-            } else {
+                for (int i = 0; i < 128; ++i)
+                    if (i > vis_end) sr[i] = __float_as_uint(-INFINITY);
+            }
+            // row maximum: 3-input max over four independent chains
+            float mx;
+            {
+                float m0 = -INFINITY, m1 = -INFINITY, m2 = -INFINITY, m3 = -INFINITY;
 #pragma unroll
-                for (int i = 0; i < 128; ++i) mx = fmaxf(mx, __uint_as_float(sr[i]));
-                mx *= c;
+                for (int i = 0; i < 128; i += 8) {
+                    m0 = fmax3(m0, __uint_as_float(sr[i]), __uint_as_float(sr[i + 1]));
+                    m1 = fmax3(m1, __uint_as_float(sr[i + 2]), __uint_as_float(sr[i + 3]));
+                    m2 = fmax3(m2, __uint_as_float(sr[i + 4]), __uint_as_float(sr[i + 5]));
+                    m3 = fmax3(m3, __uint_as_float(sr[i + 6]), __uint_as_float(sr[i + 7]));
+                }
+                mx = fmaxf(fmaxf(m0, m1), fmaxf(m2, m3)) * c;  // c > 0
             }
             // Decide the new running maximum; O is rescaled after P is stored so
             // that the score registers are dead by then.
@@ -361,25 +375,34 @@ __global__ void __launch_bounds__(384, 1)
                 }
             }
             const float m_use = (m_run == -INFINITY) ? 0.f : m_run;
-            float sum = 0.f;
+            const uint64_t c2 = f2_pack(c, c);
+            const uint64_t nm2 = f2_pack(-m_use, -m_use);
+            uint64_t acc0 = 0, acc1 = 0, acc2 = 0, acc3 = 0;  // (0.f, 0.f) pairs
 #pragma unroll
             for (int h = 0; h < 2; ++h) {
                 uint32_t pk[32];
 #pragma unroll
                 for (int i = 0; i < 32; ++i) {
                     const int c0 = h * 64 + 2 * i;
-                    float p0, p1;
-                    if (need_mask) {
-                        p0 = ex2_approx(__uint_as_float(sr[c0]) - m_use);
-                        p1 = ex2_approx(__uint_as_float(sr[c0 + 1]) - m_use);
-                    } else {
-                        p0 = ex2_approx(fmaf(__uint_as_float(sr[c0]), c, -m_use));
-                        p1 = ex2_approx(fmaf(__uint_as_float(sr[c0 + 1]), c, -m_use));
+                    const float2 x = f2_unpack(
+                        f2_fma(f2_pack(__uint_as_float(sr[c0]), __uint_as_float(sr[c0 + 1])), c2, nm2));
+                    const float p0 = ex2_approx(x.x);
+                    const float p1 = ex2_approx(x.y);
+                    const uint64_t pp = f2_pack(p0, p1);
+                    switch (i & 3) {
+                        case 0: acc0 = f2_add(acc0, pp); break;
+                        case 1: acc1 = f2_add(acc1, pp); break;
+                        case 2: acc2 = f2_add(acc2, pp); break;
+                        default: acc3 = f2_add(acc3, pp); break;
                     }
-                    sum += p0 + p1;
                     pk[i] = DType<T>::pack2(p0, p1);
                 }
                 tmem_st_x32(s_tmem + h * 32, pk);
+            }
+            float sum;
+            {
+                const float2 a = f2_unpack(f2_add(f2_add(acc0, acc1), f2_add(acc2, acc3)));
+                sum = a.x + a.y;
             }
             l_run = l_run * alpha + sum;
             // PV_{j-1} has completed: S_t(j) was issued after it and its commit
@@ -481,11 +504,13 @@ FlashAttentionError launch_typed(const T* Q, const T* K, const T* V, void* O, fl
     prm.seq_k = seq_k;
     prm.num_ctiles = (seq_q + 255) / 256;
     prm.causal = causal ? 1 : 0;
-    prm.scale_log2 = scale * kLog2e;
+    // A zero scale is replaced by a tiny positive one so that masked scores
+    // (-inf) still map to -inf; the effect on results is below fp32 resolution.
+    prm.scale_log2 = fmaxf(scale * kLog2e, 1e-30f);
     prm.q_offset = q_offset;
     prm.k_offset = k_offset;
-    if (prm.num_ctiles > 65535) return FlashAttentionError::CUDA_ERROR;
-    dim3 grid(static_cast<unsigned>(BH), static_cast<unsigned>(prm.num_ctiles));
+    if (BH > 65535) return FlashAttentionError::CUDA_ERROR;
+    dim3 grid(static_cast<unsigned>(prm.num_ctiles), static_cast<unsigned>(BH));
     kern<<<grid, 384, G::kSmemBytes, stream>>>(mq, mk, mv, prm);
     return cudaGetLastError() == cudaSuccess ? FlashAttentionError::SUCCESS
                                              : FlashAttentionError::CUDA_ERROR;
