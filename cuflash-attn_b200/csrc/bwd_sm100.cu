@@ -22,13 +22,16 @@
 //                 S^T  = K_j Q_i^T    -> TMEM [0,128)
 //                 dV  += P^T dO_i     (A = P^T from TMEM)   -> TMEM [256,256+D)
 //                 dK  += dS^T Q_i     (A = dS^T from TMEM)  -> TMEM [384,384+D)
-//                 dQ_i = dS K_j       (A = dS from smem)    -> TMEM [0,D)
-//   warps 4-7   one thread per K/V row (TMEM lane): P^T, dS^T from S^T, dP^T;
-//               writes P^T and dS^T back into TMEM (fp16/bf16) and dS^T into
-//               shared memory for the dQ product; at the end stores dK, dV.
-//   warps 8-11  one thread per query row: drains dQ_i from TMEM through
-//               swizzled shared-memory boxes into the fp32 accumulator with
-//               TMA reduce-add (cp.reduce.async.bulk.tensor).
+//                 dQ_i = dS K_j (or dQ_i^T = K_j^T dS^T)    -> TMEM [0,128)
+//   warps 4-11  two warpgroups, one thread per K/V row (TMEM lane) each,
+//               splitting the 128 query columns in halves: P^T, dS^T from
+//               S^T, dP^T; P^T and dS^T go back into TMEM (fp16/bf16) and dS^T
+//               also into shared memory for the dQ product; at the end one
+//               warpgroup stores dV, the other dK.
+//   warps 12-15 drain dQ_i from TMEM into the fp32 accumulator: with
+//               head_dim 128 dQ is computed transposed and drained with
+//               coalesced red.global.add.f32, otherwise through swizzled
+//               shared-memory boxes and TMA reduce-add.
 // Kernel 3 (convert): dQ = scale * dQ_acc in the output dtype.
 //
 // CTAs of one (batch, head) are adjacent in launch order, so the dQ
@@ -106,10 +109,9 @@ __device__ __forceinline__ uint64_t ds_desc(uint32_t ds_base, int kk) {
 }
 
 __device__ __forceinline__ bool bwarp_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag) {
-    int ok = 0;
-    if ((threadIdx.x & 31) == 0) ok = sm100::mbar_wait(bar, parity, abort_flag, &g_bwd_status);
-    ok = __shfl_sync(0xffffffffu, ok, 0);
-    return ok != 0;
+    // Every lane polls the barrier itself: all lanes observe the same phase,
+    // timer and abort flag, so the warp stays converged without a shuffle.
+    return sm100::mbar_wait(bar, parity, abort_flag, &g_bwd_status);
 }
 
 __device__ __forceinline__ void bdrain_wait(uint64_t* bar, uint32_t parity) {
@@ -124,6 +126,10 @@ __device__ __forceinline__ void bulk_load(void* smem_dst, const void* gsrc, uint
             sm100::smem_u32(smem_dst)),
         "l"(gsrc), "r"(bytes), "r"(sm100::smem_u32(bar))
         : "memory");
+}
+
+__device__ __forceinline__ void red_add_f32(float* gptr, float v) {
+    asm volatile("red.global.add.f32 [%0], %1;" ::"l"(gptr), "f"(v) : "memory");
 }
 
 __device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c,
@@ -209,14 +215,20 @@ __global__ void __launch_bounds__(256)
 
 // ---------------------------------------------------------------- main kernel
 
+constexpr int kBwdThreads = 512;
+
 template <typename T, int D>
-__global__ void __launch_bounds__(384, 1)
+__global__ void __launch_bounds__(kBwdThreads, 1)
     fa_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                   const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmdO,
                   const __grid_constant__ CUtensorMap tmdQ, const BwdParams p) {
     using G = BwdGeom<D>;
     using namespace sm100;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
+    // With head_dim 128 dQ is produced transposed (TMEM lane = head_dim
+    // element), so a warp's reduction into the accumulator covers 32
+    // consecutive floats of one query row: fully coalesced, no staging.
+    constexpr bool kTransposedDq = (D == 128);
 
     if (*reinterpret_cast<volatile int*>(&g_bwd_status) != 0) return;
     const uint32_t sbase = smem_u32(smem_raw);
@@ -252,7 +264,7 @@ __global__ void __launch_bounds__(384, 1)
             mbar_init(empty + s, 1);
         }
         mbar_init(bar_sdp, 1);
-        mbar_init(bar_ds, 128);
+        mbar_init(bar_ds, 256);
         mbar_init(bar_dq, 1);
         mbar_init(bar_dqfree, 128);
         mbar_init(bar_acc, 1);
@@ -269,9 +281,20 @@ __global__ void __launch_bounds__(384, 1)
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
 
-    if (warp == 0) {
-        // ------------------------------------------------ producer
-        if (lane == 0) {
+    // TMEM columns: S^T [0,128), dP^T [128,256), dV [256,256+D), dK [384,384+D).
+    // Softmax warpgroup h (h = 0, 1) owns query columns [64h, 64h+64): it
+    // reads S^T / dP^T columns [64h, 64h+64) and writes P^T / dS^T (16-bit,
+    // two per column) into columns [64h, 64h+32) of the same regions, so the
+    // two warpgroups never touch each other's columns.  dQ (or dQ^T) is then
+    // written by an MMA over the S^T columns.
+    //
+    // Registers: launched with 128 per thread (512 x 128 = 65536).
+    // warpgroup 0 (producer, MMA, 2 idle) -> 56, the drain -> 152, the two
+    // softmax warpgroups -> 152: 128*56 + 128*152 + 256*152 = 65536.
+    if (warp < 4) {
+        setmaxnreg_dec<56>();
+        if (warp == 0 && lane == 0) {
+            // ------------------------------------------------ producer
             prefetch_tmap(&tmQ);
             prefetch_tmap(&tmK);
             prefetch_tmap(&tmV);
@@ -306,15 +329,16 @@ __global__ void __launch_bounds__(384, 1)
             bdrain_wait(bar_kv, 0);
             for (int it = max(0, issued - G::kStages); it < issued; ++it)
                 bdrain_wait(full + it % G::kStages, (it / G::kStages) & 1);
-        }
-    } else if (warp == 1) {
-        // ------------------------------------------------ MMA issuer
-        if (lane == 0) {
+        } else if (warp == 1 && lane == 0) {
+            // ------------------------------------------------ MMA issuer
             constexpr uint32_t kFmt = DType<T>::kMmaFmt;
             constexpr uint32_t idesc_ss = make_idesc(kFmt, 128, 128, false, false);
             constexpr uint32_t idesc_acc = make_idesc(kFmt, 128, D, false, true);
             constexpr uint32_t idesc_dq = make_idesc(kFmt, 128, D, true, true);
+            constexpr uint32_t idesc_dqt = make_idesc(kFmt, 128, 128, true, true);
             const uint32_t sK = sbase + G::kOffK, sV = sbase + G::kOffV, sDs = sbase + G::kOffDs;
+            // TMEM column of k-step kk (16 queries) of a P^T / dS^T operand
+            auto acol = [](int kk) { return static_cast<uint32_t>(kk < 4 ? kk * 8 : 64 + (kk - 4) * 8); };
             bool ok = mbar_wait(bar_kv, 0, abort_flag, &g_bwd_status);
             for (int it = 0; ok && it < n_it; ++it) {
                 const int s = it % G::kStages;
@@ -325,13 +349,13 @@ __global__ void __launch_bounds__(384, 1)
                     break;
                 }
                 tc_fence_after();
-                // dP^T = V_j dO_i^T (its TMEM columns were last read by dK of it-1)
+                // dP^T = V_j dO_i^T (its columns were last read by dK of it-1)
 #pragma unroll
                 for (int kk = 0; kk < D / 16; ++kk)
                     mma_f16_ss(tmem + 128, bkmajor_desc<D>(sV, kk), bkmajor_desc<D>(sdO, kk),
                                idesc_ss, kk > 0 ? 1u : 0u);
                 if (it > 0) {
-                    // S columns hold dQ_{i-1} until the drain warps have read it
+                    // S columns hold dQ of it-1 until the drain warps have read it
                     if (!mbar_wait(bar_dqfree, (it - 1) & 1, abort_flag, &g_bwd_status)) {
                         ok = false;
                         break;
@@ -351,18 +375,26 @@ __global__ void __launch_bounds__(384, 1)
                 // dV += P^T dO_i ; dK += dS^T Q_i  (K dimension = 128 query rows)
 #pragma unroll
                 for (int kk = 0; kk < 8; ++kk)
-                    mma_f16_ts(tmem + 256, tmem + kk * 8, bmnmajor_desc<D>(sdO, kk), idesc_acc,
+                    mma_f16_ts(tmem + 256, tmem + acol(kk), bmnmajor_desc<D>(sdO, kk), idesc_acc,
                                (it > 0 || kk > 0) ? 1u : 0u);
 #pragma unroll
                 for (int kk = 0; kk < 8; ++kk)
-                    mma_f16_ts(tmem + 384, tmem + 128 + kk * 8, bmnmajor_desc<D>(sQ, kk),
+                    mma_f16_ts(tmem + 384, tmem + 128 + acol(kk), bmnmajor_desc<D>(sQ, kk),
                                idesc_acc, (it > 0 || kk > 0) ? 1u : 0u);
                 tc_commit(empty + s);
-                // dQ_i = dS K_j (K dimension = 128 kv rows) into the S columns
+                if constexpr (kTransposedDq) {
+                    // dQ_i^T = K_j^T dS^T (M = head_dim lanes, N = 128 queries)
 #pragma unroll
-                for (int kk = 0; kk < 8; ++kk)
-                    mma_f16_ss(tmem, ds_desc(sDs, kk), bmnmajor_desc<D>(sK, kk), idesc_dq,
-                               kk > 0 ? 1u : 0u);
+                    for (int kk = 0; kk < 8; ++kk)
+                        mma_f16_ss(tmem, bmnmajor_desc<D>(sK, kk), ds_desc(sDs, kk), idesc_dqt,
+                                   kk > 0 ? 1u : 0u);
+                } else {
+                    // dQ_i = dS K_j (M = 128 query lanes, N = head_dim)
+#pragma unroll
+                    for (int kk = 0; kk < 8; ++kk)
+                        mma_f16_ss(tmem, ds_desc(sDs, kk), bmnmajor_desc<D>(sK, kk), idesc_dq,
+                                   kk > 0 ? 1u : 0u);
+                }
                 tc_commit(bar_dq);
             }
             tc_commit(bar_acc);
@@ -371,14 +403,16 @@ __global__ void __launch_bounds__(384, 1)
             mbar_wait(bar_done, 0, &never, &g_bwd_status);
         }
         __syncwarp();
-    } else if (warp >= 4 && warp < 8) {
+    } else if (warp < 12) {
+        setmaxnreg_inc<152>();
         // ------------------------------------------------ P^T / dS^T, then dK/dV epilogue
+        const int h = (warp - 4) >> 2;  // query half
         const int wq = warp & 3;
         const int r = wq * 32 + lane;  // kv row within block j
         const uint32_t lane_addr = static_cast<uint32_t>(wq * 32) << 16;
-        const uint32_t t_s = tmem + lane_addr;
-        const uint32_t t_dp = tmem + lane_addr + 128;
-        const uint32_t sDs = sbase + G::kOffDs + r * 128;
+        const uint32_t t_s = tmem + lane_addr + h * 64;
+        const uint32_t t_dp = tmem + lane_addr + 128 + h * 64;
+        const uint32_t sDs = sbase + G::kOffDs + h * (128 * 128) + r * 128;
         const float c = p.scale_log2;
         bool ok = true;
         for (int it = 0; it < n_it; ++it) {
@@ -396,47 +430,48 @@ __global__ void __launch_bounds__(384, 1)
                 break;
             }
             const float* sL = reinterpret_cast<const float*>(sptr + G::kOffStage +
-                                                             s * G::kStageBytes + 2 * G::kTileBytes);
+                                                             s * G::kStageBytes + 2 * G::kTileBytes) +
+                              h * 64;
             const float* sD = sL + 128;
             const bool diag = p.causal && (i == j);
 #pragma unroll
-            for (int cc = 0; cc < 4; ++cc) {
+            for (int cc = 0; cc < 2; ++cc) {
                 uint32_t sv[32], dv[32];
                 tmem_ld2_x32(t_s + cc * 32, sv, t_dp + cc * 32, dv);
-                float lq[32], dq[32];
-#pragma unroll
-                for (int v = 0; v < 8; ++v) {
-                    const float4 a = reinterpret_cast<const float4*>(sL + cc * 32)[v];
-                    const float4 b = reinterpret_cast<const float4*>(sD + cc * 32)[v];
-                    lq[4 * v] = a.x; lq[4 * v + 1] = a.y; lq[4 * v + 2] = a.z; lq[4 * v + 3] = a.w;
-                    dq[4 * v] = b.x; dq[4 * v + 1] = b.y; dq[4 * v + 2] = b.z; dq[4 * v + 3] = b.w;
-                }
                 uint32_t pp[16], dd[16];
 #pragma unroll
-                for (int e = 0; e < 16; ++e) {
-                    const int q0 = cc * 32 + 2 * e;
-                    float p0 = ex2_approx(fmaf(__uint_as_float(sv[2 * e]), c, -lq[2 * e]));
-                    float p1 = ex2_approx(fmaf(__uint_as_float(sv[2 * e + 1]), c, -lq[2 * e + 1]));
-                    if (diag) {
-                        if (q0 < r) p0 = 0.f;
-                        if (q0 + 1 < r) p1 = 0.f;
+                for (int v = 0; v < 8; ++v) {
+                    const float4 lq = reinterpret_cast<const float4*>(sL + cc * 32)[v];
+                    const float4 dq = reinterpret_cast<const float4*>(sD + cc * 32)[v];
+                    const float la[4] = {lq.x, lq.y, lq.z, lq.w};
+                    const float da[4] = {dq.x, dq.y, dq.z, dq.w};
+#pragma unroll
+                    for (int u = 0; u < 2; ++u) {
+                        const int e = 2 * v + u;                  // pair index in the chunk
+                        const int q0 = h * 64 + cc * 32 + 2 * e;  // query within block i
+                        float p0 = ex2_approx(fmaf(__uint_as_float(sv[2 * e]), c, -la[2 * u]));
+                        float p1 = ex2_approx(fmaf(__uint_as_float(sv[2 * e + 1]), c, -la[2 * u + 1]));
+                        if (diag) {
+                            if (q0 < r) p0 = 0.f;
+                            if (q0 + 1 < r) p1 = 0.f;
+                        }
+                        const float d0 = p0 * (__uint_as_float(dv[2 * e]) - da[2 * u]);
+                        const float d1 = p1 * (__uint_as_float(dv[2 * e + 1]) - da[2 * u + 1]);
+                        pp[e] = DType<T>::pack2(p0, p1);
+                        dd[e] = DType<T>::pack2(d0, d1);
                     }
-                    const float d0 = p0 * (__uint_as_float(dv[2 * e]) - dq[2 * e]);
-                    const float d1 = p1 * (__uint_as_float(dv[2 * e + 1]) - dq[2 * e + 1]);
-                    pp[e] = DType<T>::pack2(p0, p1);
-                    dd[e] = DType<T>::pack2(d0, d1);
                 }
-                // P^T and dS^T overwrite columns already consumed
-                tmem_st_x16(t_s + cc * 16, pp);
-                tmem_st_x16(t_dp + cc * 16, dd);
-                const int cb = cc >> 1;
+                // P^T and dS^T overwrite columns this thread has already read
+                tmem_st_x16_nw(t_s + cc * 16, pp);
+                tmem_st_x16_nw(t_dp + cc * 16, dd);
 #pragma unroll
                 for (int k = 0; k < 4; ++k) {
-                    const int chunk = (cc & 1) * 4 + k;
-                    const uint32_t addr = sDs + cb * (128 * 128) + ((chunk ^ (r & 7)) << 4);
+                    const int chunk = cc * 4 + k;
+                    const uint32_t addr = sDs + ((chunk ^ (r & 7)) << 4);
                     st_shared_v4(addr, dd[4 * k], dd[4 * k + 1], dd[4 * k + 2], dd[4 * k + 3]);
                 }
             }
+            tmem_wait_st();
             fence_proxy_async_smem();
             tc_fence_before();
             mbar_arrive(bar_ds);
@@ -445,84 +480,104 @@ __global__ void __launch_bounds__(384, 1)
             ok = bwarp_wait(bar_acc, 0, abort_flag);
             tc_fence_after();
         }
+        // warpgroup 0 stores dV, warpgroup 1 stores dK (scaled)
         const int kv = j * 128 + r;
         const bool valid = kv < p.N;
         const size_t row = (static_cast<size_t>(bh) * p.N + kv) * D;
-        T* dVp = static_cast<T*>(p.dV);
-        T* dKp = static_cast<T*>(p.dK);
+        T* dst_base = static_cast<T*>(h == 0 ? p.dV : p.dK);
+        const float mul = h == 0 ? 1.f : p.scale;
+        const uint32_t t_acc = tmem + lane_addr + (h == 0 ? 256 : 384);
 #pragma unroll
         for (int cb = 0; cb < D / 32; ++cb) {
-            uint32_t a[32], b[32];
+            uint32_t a[32];
             if (ok) {
-                tmem_ld_x32(tmem + lane_addr + 256 + cb * 32, a);
-                tmem_ld_x32(tmem + lane_addr + 384 + cb * 32, b);
+                tmem_ld_x32(t_acc + cb * 32, a);
             } else {
 #pragma unroll
-                for (int e = 0; e < 32; ++e) a[e] = b[e] = 0u;
+                for (int e = 0; e < 32; ++e) a[e] = 0u;
             }
             if (valid) {
-                uint4* dstv = reinterpret_cast<uint4*>(dVp + row + cb * 32);
-                uint4* dstk = reinterpret_cast<uint4*>(dKp + row + cb * 32);
+                uint4* dst = reinterpret_cast<uint4*>(dst_base + row + cb * 32);
 #pragma unroll
                 for (int q4 = 0; q4 < 4; ++q4) {
-                    uint4 v, k;
-                    v.x = DType<T>::pack2(__uint_as_float(a[8 * q4 + 0]), __uint_as_float(a[8 * q4 + 1]));
-                    v.y = DType<T>::pack2(__uint_as_float(a[8 * q4 + 2]), __uint_as_float(a[8 * q4 + 3]));
-                    v.z = DType<T>::pack2(__uint_as_float(a[8 * q4 + 4]), __uint_as_float(a[8 * q4 + 5]));
-                    v.w = DType<T>::pack2(__uint_as_float(a[8 * q4 + 6]), __uint_as_float(a[8 * q4 + 7]));
-                    k.x = DType<T>::pack2(__uint_as_float(b[8 * q4 + 0]) * p.scale,
-                                          __uint_as_float(b[8 * q4 + 1]) * p.scale);
-                    k.y = DType<T>::pack2(__uint_as_float(b[8 * q4 + 2]) * p.scale,
-                                          __uint_as_float(b[8 * q4 + 3]) * p.scale);
-                    k.z = DType<T>::pack2(__uint_as_float(b[8 * q4 + 4]) * p.scale,
-                                          __uint_as_float(b[8 * q4 + 5]) * p.scale);
-                    k.w = DType<T>::pack2(__uint_as_float(b[8 * q4 + 6]) * p.scale,
-                                          __uint_as_float(b[8 * q4 + 7]) * p.scale);
-                    dstv[q4] = v;
-                    dstk[q4] = k;
+                    uint4 v;
+                    v.x = DType<T>::pack2(__uint_as_float(a[8 * q4 + 0]) * mul, __uint_as_float(a[8 * q4 + 1]) * mul);
+                    v.y = DType<T>::pack2(__uint_as_float(a[8 * q4 + 2]) * mul, __uint_as_float(a[8 * q4 + 3]) * mul);
+                    v.z = DType<T>::pack2(__uint_as_float(a[8 * q4 + 4]) * mul, __uint_as_float(a[8 * q4 + 5]) * mul);
+                    v.w = DType<T>::pack2(__uint_as_float(a[8 * q4 + 6]) * mul, __uint_as_float(a[8 * q4 + 7]) * mul);
+                    dst[q4] = v;
                 }
             }
         }
-    } else if (warp >= 8) {
+    } else {
+        setmaxnreg_inc<152>();
         // ------------------------------------------------ dQ drain
-        // Each warp owns 32 query rows.  Per 32-column chunk it copies its
-        // 32x32 fp32 block from TMEM into a 128-byte-swizzled staging box and
-        // the TMA unit adds the box into the fp32 accumulator in global
-        // memory.  Staging lives in the dS buffer, which is idle from the
-        // completion of dQ_i until the MMA issues S_{i+1} (after this drain
-        // signals bar_dqfree); two 4 KiB boxes per warp alternate.
         const int wq = warp & 3;
         const uint32_t t_q = tmem + (static_cast<uint32_t>(wq * 32) << 16);
-        const uint32_t stage0 = sbase + G::kOffDs + wq * 8192;
-        for (int it = 0; it < n_it; ++it) {
-            const int i = i0 + it;
-            if (!bwarp_wait(bar_dq, it & 1, abort_flag)) break;
-            tc_fence_after();
+        if constexpr (kTransposedDq) {
+            // lane = head_dim element d; TMEM column = query row of block i
+            const int d = wq * 32 + lane;
+            for (int it = 0; it < n_it; ++it) {
+                const int i = i0 + it;
+                if (!bwarp_wait(bar_dq, it & 1, abort_flag)) break;
+                tc_fence_after();
+                uint32_t v0[32], v1[32], v2[32], v3[32];
+                tmem_ld2_x32(t_q, v0, t_q + 32, v1);
+                tmem_ld2_x32(t_q + 64, v2, t_q + 96, v3);
+                // TMEM columns are free once loaded: release them before the
+                // reductions so the next S MMA is not held up
+                tc_fence_before();
+                mbar_arrive(bar_dqfree);
+                float* dst = p.dq_acc + (static_cast<size_t>(bh) * p.N + i * 128) * D + d;
+                const int qn = min(128, p.N - i * 128);
+                auto flush = [&](const uint32_t(&v)[32], int q0) {
 #pragma unroll
-            for (int cb = 0; cb < D / 32; ++cb) {
-                const uint32_t box = stage0 + (cb & 1) * 4096;
-                if (cb >= 2) {
-                    if (lane == 0) bulk_wait_group_read<1>();
-                    __syncwarp();
-                }
-                uint32_t v[32];
-                tmem_ld_x32(t_q + cb * 32, v);
-#pragma unroll
-                for (int k = 0; k < 8; ++k)
-                    st_shared_v4(box + lane * 128 + ((k ^ (lane & 7)) << 4), v[4 * k], v[4 * k + 1],
-                                 v[4 * k + 2], v[4 * k + 3]);
-                fence_proxy_async_smem();
-                __syncwarp();
-                if (lane == 0) {
-                    tma_reduce_add_3d(&tmdQ, box, cb * 32, i * 128 + wq * 32, bh);
-                    bulk_commit_group();
-                }
+                    for (int e = 0; e < 32; ++e)
+                        if (q0 + e < qn)
+                            red_add_f32(dst + static_cast<size_t>(q0 + e) * D, __uint_as_float(v[e]));
+                };
+                flush(v0, 0);
+                flush(v1, 32);
+                flush(v2, 64);
+                flush(v3, 96);
             }
-            // the staging boxes must be read out before dS_{i+1} overwrites them
-            if (lane == 0) bulk_wait_group_read<0>();
-            __syncwarp();
-            tc_fence_before();
-            mbar_arrive(bar_dqfree);
+        } else {
+            // Each warp owns 32 query rows.  Per 32-column chunk it copies its
+            // 32x32 fp32 block from TMEM into a 128-byte-swizzled staging box
+            // and the TMA unit adds the box into the fp32 accumulator.  Staging
+            // lives in the dS buffer, idle from the completion of dQ_i until
+            // the MMA issues S_{i+1} (after this drain signals bar_dqfree).
+            const uint32_t stage0 = sbase + G::kOffDs + wq * 8192;
+            for (int it = 0; it < n_it; ++it) {
+                const int i = i0 + it;
+                if (!bwarp_wait(bar_dq, it & 1, abort_flag)) break;
+                tc_fence_after();
+#pragma unroll
+                for (int cb = 0; cb < D / 32; ++cb) {
+                    const uint32_t box = stage0 + (cb & 1) * 4096;
+                    if (cb >= 2) {
+                        if (lane == 0) bulk_wait_group_read<1>();
+                        __syncwarp();
+                    }
+                    uint32_t v[32];
+                    tmem_ld_x32(t_q + cb * 32, v);
+#pragma unroll
+                    for (int k = 0; k < 8; ++k)
+                        st_shared_v4(box + lane * 128 + ((k ^ (lane & 7)) << 4), v[4 * k],
+                                     v[4 * k + 1], v[4 * k + 2], v[4 * k + 3]);
+                    fence_proxy_async_smem();
+                    __syncwarp();
+                    if (lane == 0) {
+                        tma_reduce_add_3d(&tmdQ, box, cb * 32, i * 128 + wq * 32, bh);
+                        bulk_commit_group();
+                    }
+                }
+                // the staging boxes must be read out before dS_{i+1} overwrites them
+                if (lane == 0) bulk_wait_group_read<0>();
+                __syncwarp();
+                tc_fence_before();
+                mbar_arrive(bar_dqfree);
+            }
         }
     }
 
@@ -591,7 +646,7 @@ FlashAttentionError bwd_typed(const T* Q, const T* K, const T* V, const T* O, co
     prm.causal = causal ? 1 : 0;
     prm.scale_log2 = scale * kLog2eB;
     prm.scale = scale;
-    kern<<<dim3(n_blk, BH), 384, G::kSmemBytes, stream>>>(mq, mk, mv, mdo, mdq, prm);
+    kern<<<dim3(n_blk, BH), kBwdThreads, G::kSmemBytes, stream>>>(mq, mk, mv, mdo, mdq, prm);
     if (cudaGetLastError() != cudaSuccess) return fail(FlashAttentionError::CUDA_ERROR);
 
     const long long n4 = static_cast<long long>(acc_elems / 4);

@@ -90,12 +90,11 @@ __device__ __forceinline__ uint64_t mnmajor_desc(uint32_t tile_base, int kk) {
     return sm100::make_smem_desc(addr, G::kCbBytes, 8 * G::kSwz, G::kLayout);
 }
 
-// Warp-uniform bounded wait: lane 0 polls, the result is broadcast.
+// Warp-uniform bounded wait.
 __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag) {
-    int ok = 0;
-    if ((threadIdx.x & 31) == 0) ok = sm100::mbar_wait(bar, parity, abort_flag, &g_fwd_status);
-    ok = __shfl_sync(0xffffffffu, ok, 0);
-    return ok != 0;
+    // Every lane polls the barrier itself: all lanes observe the same phase,
+    // timer and abort flag, so the warp stays converged without a shuffle.
+    return sm100::mbar_wait(bar, parity, abort_flag, &g_fwd_status);
 }
 
 // Wait used by the producer at exit to make sure its TMA writes have landed;
