@@ -221,8 +221,9 @@ constexpr uint32_t kFmtTF32 = 2;
 // --------------------------------------------------------------- math
 
 // Per-warpgroup register re-allocation (every warp of the warpgroup executes
-// the same instruction).  The increases of all warpgroups must fit in what
-// the launch granted the block (threads x registers per thread at launch).
+// the same instruction).  inc must request more than the current count and
+// dec less; the increases of all warpgroups must fit in what the launch
+// granted the block (threads x registers per thread at launch).
 template <int N>
 __device__ __forceinline__ void setmaxnreg_inc() {
     asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N));
