@@ -371,7 +371,7 @@ def run_decode(args, lib, dev, world, rank, pk, pk_kind):
     import torch.distributed as dist
 
     c = DECODE
-    B, H, N, D = c["B"], c["H"], c["N"], c["D"]
+    B, H, N, D = (args.batch if args.batch_set else c["B"]), c["H"], c["N"], c["D"]
     g = torch.Generator(device=dev).manual_seed(31 + 1000 * rank)
     q = torch.randn((B, H, 1, D), device=dev, generator=g).to(torch.bfloat16)
     K = torch.randn((B, H, N, D), device=dev, generator=g).to(torch.bfloat16)
@@ -401,7 +401,8 @@ def run_decode(args, lib, dev, world, rank, pk, pk_kind):
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": results[best]["ms"], "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-            "config": {"workload": "BASELINE config 4: split-KV decode B64 H32 Nkv16384 D128",
+            "config": {"workload": ("BASELINE config 4: " if B == 64 else "custom: ") +
+                                   f"split-KV decode B{B} H{H} Nkv{N} D{D}",
                        "best_num_splits": best},
             "splits": results,
             "roofline": {"bound": "hbm", "achieved": results[best]["GBps"], "peak": peak,
@@ -425,6 +426,7 @@ def main():
     ap.add_argument("--seq", type=int, default=TRAIN["N"])
     ap.add_argument("--head-dim", type=int, default=TRAIN["D"])
     args = ap.parse_args()
+    args.batch_set = any(a == "--batch" or a.startswith("--batch=") for a in sys.argv[1:])
     if args.impl == "reference":
         return run_reference(args)
     return run_ours(args)
