@@ -93,11 +93,6 @@ FlashAttentionError launch_bwd_sm100(const T* Q, const T* K, const T* V, const T
                                      cudaStream_t stream);
 
 template <typename T>
-FlashAttentionError launch_fwd_simt(const T* Q, const T* K, const T* V, T* O, float* L, int B,
-                                    int H, int N, int D, float scale, bool causal,
-                                    cudaStream_t stream);
-
-template <typename T>
 FlashAttentionError launch_bwd_simt(const T* Q, const T* K, const T* V, const T* O,
                                     const float* L, const T* dO, T* dQ, T* dK, T* dV, int B,
                                     int H, int N, int D, float scale, bool causal,
@@ -136,6 +131,7 @@ FlashAttentionError launch_convert_f32(const float* src, T* dst, long long count
 int read_and_clear_device_status();
 int fwd_sm100_status();
 int bwd_sm100_status();
+int f32_sm100_status();
 
 }  // namespace detail
 }  // namespace cuflash

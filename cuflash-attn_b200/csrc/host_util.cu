@@ -128,8 +128,9 @@ int read_and_clear_device_status() {
     if (cudaDeviceSynchronize() != cudaSuccess) return -1;
     const int a = fwd_sm100_status();
     const int b = bwd_sm100_status();
-    if (a < 0 || b < 0) return -1;
-    return a != 0 ? a : b;
+    const int c = f32_sm100_status();
+    if (a < 0 || b < 0 || c < 0) return -1;
+    return a != 0 ? a : (b != 0 ? b : c);
 }
 
 }  // namespace detail

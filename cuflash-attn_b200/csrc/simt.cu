@@ -1,14 +1,8 @@
-// Warp-per-row CUDA-core attention (forward and backward) for any storage
-// dtype, computed in fp32.  This is the fp32 path of the library (the
-// reference's fp32 kernels are src/forward/flash_attention_forward_typed.cu
-// :16-152 and src/backward/flash_attention_backward_typed.cu:13-288) and,
-// for fp16/bf16, the backward used when a shape is outside the tcgen05
-// backward kernel's envelope.
+// Warp-per-row CUDA-core attention backward, computed in fp32: the fp32
+// backward of the library (the reference's fp32 backward is
+// src/backward/flash_attention_backward_typed.cu:13-288).
 //
-// Forward: one warp owns one query row; lanes split head_dim (D/32 elements
-// each), q.k is an xor-shuffle all-reduce, the online softmax runs in the
-// natural-log domain with expf, exactly one pass over the visible keys.
-// Backward: D_i = rowsum(dO_i * O_i) (as the reference's compute_D_kernel),
+// D_i = rowsum(dO_i * O_i) (as the reference's compute_D_kernel),
 // then a warp per query row accumulates dQ and a warp per key row
 // accumulates dK and dV, each recomputing P_ij = exp(scale q_i.k_j - L_i).
 
@@ -44,44 +38,6 @@ __device__ __forceinline__ float warp_sum(float v) {
 }
 
 constexpr int kRowsPerCta = 4;
-
-template <typename T, int D>
-__global__ void __launch_bounds__(128)
-    fwd_simt_kernel(const T* __restrict__ Q, const T* __restrict__ K, const T* __restrict__ V,
-                    T* __restrict__ O, float* __restrict__ L, int N, float scale, int causal) {
-    constexpr int E = D / 32;
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int i = blockIdx.x * kRowsPerCta + warp;
-    if (i >= N) return;
-    const long long bh = blockIdx.y;
-    const long long rowQ = (bh * N + i) * D;
-    float q[E], acc[E];
-#pragma unroll
-    for (int e = 0; e < E; ++e) {
-        q[e] = ld_f(Q + rowQ + lane + 32 * e);
-        acc[e] = 0.f;
-    }
-    float m = -INFINITY, l = 0.f;
-    const int jend = causal ? i + 1 : N;
-    for (int j = 0; j < jend; ++j) {
-        const long long rowK = (bh * N + j) * D;
-        float dot = 0.f;
-#pragma unroll
-        for (int e = 0; e < E; ++e) dot = fmaf(q[e], ld_f(K + rowK + lane + 32 * e), dot);
-        const float s = warp_sum(dot) * scale;
-        const float m_new = fmaxf(m, s);
-        const float alpha = expf(m - m_new);
-        const float pr = expf(s - m_new);
-        l = l * alpha + pr;
-#pragma unroll
-        for (int e = 0; e < E; ++e) acc[e] = fmaf(pr, ld_f(V + rowK + lane + 32 * e), acc[e] * alpha);
-        m = m_new;
-    }
-    const float inv = 1.f / l;
-#pragma unroll
-    for (int e = 0; e < E; ++e) st_f(O + rowQ + lane + 32 * e, acc[e] * inv);
-    if (lane == 0) L[bh * N + i] = m + logf(l);
-}
 
 template <typename T, int D>
 __global__ void __launch_bounds__(128)
@@ -189,17 +145,6 @@ __global__ void __launch_bounds__(128)
 }
 
 template <typename T, int D>
-FlashAttentionError fwd_simt_typed(const T* Q, const T* K, const T* V, T* O, float* L, int BH,
-                                   int N, float scale, bool causal, cudaStream_t stream) {
-    dim3 grid((N + kRowsPerCta - 1) / kRowsPerCta, BH);
-    if (grid.x > 0x7fffffffu) return FlashAttentionError::CUDA_ERROR;
-    fwd_simt_kernel<T, D><<<grid, 32 * kRowsPerCta, 0, stream>>>(Q, K, V, O, L, N, scale,
-                                                                 causal ? 1 : 0);
-    return cudaGetLastError() == cudaSuccess ? FlashAttentionError::SUCCESS
-                                             : FlashAttentionError::CUDA_ERROR;
-}
-
-template <typename T, int D>
 FlashAttentionError bwd_simt_typed(const T* Q, const T* K, const T* V, const T* O, const float* L,
                                    const T* dO, T* dQ, T* dK, T* dV, int BH, int N, float scale,
                                    bool causal, cudaStream_t stream) {
@@ -230,19 +175,6 @@ FlashAttentionError bwd_simt_typed(const T* Q, const T* K, const T* V, const T* 
 }  // namespace
 
 template <typename T>
-FlashAttentionError launch_fwd_simt(const T* Q, const T* K, const T* V, T* O, float* L, int B,
-                                    int H, int N, int D, float scale, bool causal,
-                                    cudaStream_t stream) {
-    const int BH = B * H;
-    switch (D) {
-        case 32: return fwd_simt_typed<T, 32>(Q, K, V, O, L, BH, N, scale, causal, stream);
-        case 64: return fwd_simt_typed<T, 64>(Q, K, V, O, L, BH, N, scale, causal, stream);
-        case 128: return fwd_simt_typed<T, 128>(Q, K, V, O, L, BH, N, scale, causal, stream);
-        default: return FlashAttentionError::UNSUPPORTED_HEAD_DIM;
-    }
-}
-
-template <typename T>
 FlashAttentionError launch_bwd_simt(const T* Q, const T* K, const T* V, const T* O,
                                     const float* L, const T* dO, T* dQ, T* dK, T* dV, int B,
                                     int H, int N, int D, float scale, bool causal,
@@ -264,9 +196,6 @@ FlashAttentionError launch_bwd_simt(const T* Q, const T* K, const T* V, const T*
 }
 
 #define CUFLASH_SIMT_INSTANTIATE(T)                                                          \
-    template FlashAttentionError launch_fwd_simt<T>(const T*, const T*, const T*, T*, float*, \
-                                                    int, int, int, int, float, bool,          \
-                                                    cudaStream_t);                            \
     template FlashAttentionError launch_bwd_simt<T>(const T*, const T*, const T*, const T*,   \
                                                     const float*, const T*, T*, T*, T*, int,  \
                                                     int, int, int, float, bool, cudaStream_t);
@@ -274,12 +203,6 @@ CUFLASH_SIMT_INSTANTIATE(float)
 CUFLASH_SIMT_INSTANTIATE(half)
 CUFLASH_SIMT_INSTANTIATE(__nv_bfloat16)
 #undef CUFLASH_SIMT_INSTANTIATE
-
-FlashAttentionError launch_fwd_f32(const float* Q, const float* K, const float* V, float* O,
-                                   float* L, int B, int H, int N, int D, float scale, bool causal,
-                                   cudaStream_t stream) {
-    return launch_fwd_simt<float>(Q, K, V, O, L, B, H, N, D, scale, causal, stream);
-}
 
 FlashAttentionError launch_bwd_f32(const float* Q, const float* K, const float* V,
                                    const float* O, const float* L, const float* dO, float* dQ,
