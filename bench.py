@@ -213,6 +213,8 @@ def run_ours(args):
 
     if args.workload == "decode":
         return run_decode(args, lib, dev, world, rank, pk, pk_kind)
+    if args.workload == "cp":
+        return run_cp(args, lib, dev, world, rank, pk, pk_kind)
 
     B, H, N, D = args.batch, args.heads, args.seq, args.head_dim
     scale = 1.0 / math.sqrt(D)
@@ -412,13 +414,76 @@ def run_decode(args, lib, dev, world, rank, pk, pk_kind):
     return 0
 
 
+def run_cp(args, lib, dev, world, rank, pk, pk_kind):
+    """causal forward over B1 H32 N131072 D128 with ring
+    context parallelism across the launched ranks (zigzag shards, NCCL P2P,
+    LSE merge)."""
+    import torch
+    import torch.distributed as dist
+
+    import ring_cp
+
+    B, H, N, D = 1, 32, args.cp_seq, 128
+    C = N // (2 * world)
+    scale = 1.0 / math.sqrt(D)
+    chunks = ring_cp.zigzag_chunks(rank, world)
+
+    def chunk_tensor(kind, c):
+        g = torch.Generator(device=dev).manual_seed(41 + 100 * kind + 7919 * c)
+        return torch.randn((B, H, C, D), device=dev, generator=g).to(torch.bfloat16)
+
+    q_ab = [chunk_tensor(0, c) for c in chunks]
+    k_ab = [chunk_tensor(1, c) for c in chunks]
+    v_ab = [chunk_tensor(2, c) for c in chunks]
+    ring = ring_cp.RingAttention(lib)
+    for _ in range(max(args.warmup, 3)):
+        ring.forward(q_ab, k_ab, v_ab, scale)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    stream = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with Clocks(dev.index) as clk:
+        e0.record(stream)
+        for _ in range(args.steps):
+            ring.forward(q_ab, k_ab, v_ab, scale)
+        e1.record(stream)
+        torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / args.steps
+    if world > 1:
+        t = torch.tensor([ms], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    flops = fwd_flops(B, H, N, D, True)
+    value = flops / (ms * 1e-3) / 1e12
+    peak = pk.get("bf16_tflops_sustained", FALLBACK_PEAKS["bf16_tflops_sustained"])
+    if rank == 0:
+        print(json.dumps({
+            "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world,
+            "steps": args.steps, "warmup": max(args.warmup, 3), "ms_per_step": ms,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": "bf16", "data": "synthetic (torch.randn per global chunk)",
+            "config": {"workload": f"BASELINE config 5: causal fwd B{B} H{H} N{N} D{D}, "
+                                   f"ring CP over {world} GPU(s), zigzag chunks of {C}",
+                       "global_batch": B, "seq_len": N, "parallelism": f"cp{world}"},
+            "per_gpu_tflops": value / world,
+            "pct_bf16_peak_per_gpu": 100.0 * value / world / peak,
+            "clocks": clk.summary(),
+        }), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["train", "decode"], default="train")
+    ap.add_argument("--workload", choices=["train", "decode", "cp"], default="train")
+    ap.add_argument("--cp-seq", type=int, default=131072)
     ap.add_argument("--splits", type=int, nargs="*", default=[0, 1, 2, 4, 8, 16, 32, 64])
     ap.add_argument("--skip-cpu-baseline", action="store_true")
     ap.add_argument("--batch", type=int, default=TRAIN["B"])

@@ -1,0 +1,142 @@
+"""Ring context-parallel causal attention forward.
+
+No counterpart in the reference library (single-device, no collectives).
+The sequence of length N is cut into 2P chunks of C = N / (2P) tokens and
+rank r of P holds chunks r and 2P-1-r ("zigzag"), which gives every rank the
+same amount of causal work.  Each rank keeps its two query chunks and passes
+its two K/V chunks around the ring: at step s it holds the K/V chunks of rank
+(r - s) mod P.  For every (query chunk c_q, K/V chunk c_k) pair with
+c_k <= c_q it runs the library's partial forward
+(``cuflash_attention_forward_partial_*``, causal on global positions) and
+folds the result into a running (O, L) with the log-sum-exp merge
+(``cuflash_lse_merge_f32``).  The next step's K/V travel over NCCL
+send/recv (``torch.distributed.batch_isend_irecv``) while the current step
+computes; every remote chunk lands in local HBM before a kernel reads it.
+
+The schedule (``ring_steps`` / ``visible_pairs``) is backend-independent
+and is exercised on CPU with gloo in the tests.
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass
+from typing import Callable, List, Sequence, Tuple
+
+
+def zigzag_chunks(rank: int, world: int) -> Tuple[int, int]:
+    """Global chunk indices held by `rank` (out of 2*world chunks)."""
+    return rank, 2 * world - 1 - rank
+
+
+def kv_owner(rank: int, step: int, world: int) -> int:
+    """Rank whose K/V chunks `rank` holds at ring step `step`."""
+    return (rank - step) % world
+
+
+def visible_pairs(q_chunks: Sequence[int], k_chunks: Sequence[int]) -> List[Tuple[int, int]]:
+    """(local query slot, local K/V slot) pairs with any unmasked key."""
+    return [(qi, ki) for qi, qc in enumerate(q_chunks) for ki, kc in enumerate(k_chunks)
+            if kc <= qc]
+
+
+@dataclass
+class RingStep:
+    step: int
+    owner: int
+    k_chunks: Tuple[int, int]
+    pairs: List[Tuple[int, int]]
+
+
+def ring_steps(rank: int, world: int) -> List[RingStep]:
+    q_chunks = zigzag_chunks(rank, world)
+    out = []
+    for s in range(world):
+        owner = kv_owner(rank, s, world)
+        k_chunks = zigzag_chunks(owner, world)
+        out.append(RingStep(s, owner, k_chunks, visible_pairs(q_chunks, k_chunks)))
+    return out
+
+
+def run_ring(rank: int, world: int, chunk: int, kv_local, compute_pair: Callable,
+             exchange: Callable):
+    """Drives the ring.  `kv_local` is this rank's K/V payload (opaque to the
+    schedule); `compute_pair(q_slot, q_chunk, kv, k_slot, k_chunk)` folds one
+    partial result into the caller's accumulators; `exchange(kv)` starts
+    sending `kv` to rank+1 and receiving rank-1's payload, returning a
+    callable that waits and yields the received payload."""
+    q_chunks = zigzag_chunks(rank, world)
+    cur = kv_local
+    for st in ring_steps(rank, world):
+        pending = exchange(cur) if st.step + 1 < world else None
+        for qi, ki in st.pairs:
+            compute_pair(qi, q_chunks[qi], cur, ki, st.k_chunks[ki])
+        if pending is not None:
+            cur = pending()
+    return q_chunks
+
+
+# ---------------------------------------------------------------------------
+# CUDA / NCCL backend
+# ---------------------------------------------------------------------------
+
+class RingAttention:
+    """Context-parallel causal forward over a torch.distributed NCCL group.
+
+    Each rank passes its zigzag shard as four contiguous tensors
+    [B, H, C, D] (query/key/value of its two chunks) and gets back its two
+    output chunks and their log-sum-exp.
+    """
+
+    def __init__(self, lib, group=None):
+        self.lib = lib
+        self.group = group
+
+    def forward(self, q_ab, k_ab, v_ab, scale: float):
+        """Runs on the current CUDA stream (the stream NCCL's P2P operations
+        are ordered against)."""
+        import torch
+        import torch.distributed as dist
+
+        world = dist.get_world_size(self.group) if dist.is_initialized() else 1
+        rank = dist.get_rank(self.group) if dist.is_initialized() else 0
+        Qa, Qb = q_ab
+        B, H, C, D = Qa.shape
+        dev = Qa.device
+        stream = torch.cuda.current_stream(dev)
+        O_acc = [torch.zeros((B, H, C, D), device=dev, dtype=torch.float32) for _ in range(2)]
+        L_acc = [torch.full((B, H, C), float("-inf"), device=dev, dtype=torch.float32)
+                 for _ in range(2)]
+        O_part = torch.empty((B, H, C, D), device=dev, dtype=torch.float32)
+        L_part = torch.empty((B, H, C), device=dev, dtype=torch.float32)
+        # K/V travel as one buffer [2 (k, v), 2 (chunks), B, H, C, D]
+        kv = torch.stack([torch.stack(list(k_ab)), torch.stack(list(v_ab))]).contiguous()
+        spare = torch.empty_like(kv)
+        state = {"spare": spare}
+
+        def compute_pair(qi, qc, kvbuf, ki, kc):
+            self.lib.forward_partial(q_ab[qi], kvbuf[0, ki], kvbuf[1, ki], qc * C, kc * C,
+                                     causal=True, scale=scale, O=O_part, L=L_part,
+                                     stream=stream)
+            self.lib.lse_merge(O_acc[qi], L_acc[qi], O_part, L_part, stream=stream)
+
+        def exchange(cur):
+            nxt = state["spare"]
+            ops = [dist.P2POp(dist.isend, cur, (rank + 1) % world, self.group),
+                   dist.P2POp(dist.irecv, nxt, (rank - 1) % world, self.group)]
+            reqs = dist.batch_isend_irecv(ops)
+
+            def wait():
+                for r in reqs:
+                    r.wait()
+                state["spare"] = cur  # the buffer just sent is free next step
+                return nxt
+
+            return wait
+
+        run_ring(rank, world, C, kv, compute_pair, exchange)
+        out = []
+        for qi in range(2):
+            o = torch.empty((B, H, C, D), device=dev, dtype=Qa.dtype)
+            self.lib.convert(O_acc[qi], o, stream=stream)
+            out.append(o)
+        return out, L_acc
