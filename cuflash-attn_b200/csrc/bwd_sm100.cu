@@ -49,6 +49,12 @@ namespace {
 __device__ int g_bwd_status;
 
 constexpr float kLog2eB = 1.4426950408889634f;
+// With kBwdExp2EmuEvery = k > 0, one pair of exponentials in k is computed on
+// the FMA pipe; measured not to pay on B200, so it is off.
+#ifndef CUFLASH_BWD_EXP2_EMU_EVERY
+#define CUFLASH_BWD_EXP2_EMU_EVERY 0
+#endif
+constexpr int kBwdExp2EmuEvery = CUFLASH_BWD_EXP2_EMU_EVERY;
 
 template <int D>
 struct BwdGeom {
@@ -417,18 +423,16 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         bool ok = true;
         for (int it = 0; it < n_it; ++it) {
             const int i = i0 + it;
-            if (!bwarp_wait(bar_sdp, it & 1, abort_flag)) {
+            const int s = it % G::kStages;
+            // L and D of block i arrived through the async proxy: observe the
+            // stage's own barrier before reading them (it completes before S
+            // is issued, so waiting for it first costs nothing)
+            if (!bwarp_wait(full + s, (it / G::kStages) & 1, abort_flag) ||
+                !bwarp_wait(bar_sdp, it & 1, abort_flag)) {
                 ok = false;
                 break;
             }
             tc_fence_after();
-            const int s = it % G::kStages;
-            // L and D of block i arrived through the async proxy: observe the
-            // stage's own barrier before reading them
-            if (!bwarp_wait(full + s, (it / G::kStages) & 1, abort_flag)) {
-                ok = false;
-                break;
-            }
             const float* sL = reinterpret_cast<const float*>(sptr + G::kOffStage +
                                                              s * G::kStageBytes + 2 * G::kTileBytes) +
                               h * 64;
@@ -449,8 +453,17 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
                     for (int u = 0; u < 2; ++u) {
                         const int e = 2 * v + u;                  // pair index in the chunk
                         const int q0 = h * 64 + cc * 32 + 2 * e;  // query within block i
-                        float p0 = ex2_approx(fmaf(__uint_as_float(sv[2 * e]), c, -la[2 * u]));
-                        float p1 = ex2_approx(fmaf(__uint_as_float(sv[2 * e + 1]), c, -la[2 * u + 1]));
+                        const float x0 = fmaf(__uint_as_float(sv[2 * e]), c, -la[2 * u]);
+                        const float x1 = fmaf(__uint_as_float(sv[2 * e + 1]), c, -la[2 * u + 1]);
+                        float p0, p1;
+                        if (kBwdExp2EmuEvery > 0 && (e % kBwdExp2EmuEvery) == kBwdExp2EmuEvery - 1) {
+                            const float2 ex = exp2_poly2(x0, x1);  // FMA pipe
+                            p0 = ex.x;
+                            p1 = ex.y;
+                        } else {
+                            p0 = ex2_approx(x0);  // MUFU
+                            p1 = ex2_approx(x1);
+                        }
                         if (diag) {
                             if (q0 < r) p0 = 0.f;
                             if (q0 + 1 < r) p1 = 0.f;

@@ -38,6 +38,13 @@ namespace {
 __device__ int g_fwd_status;
 
 constexpr float kRescaleThreshold = 8.0f;  // log2 units
+// With kExp2EmuEvery = k > 0, one pair of exponentials in k is computed on the
+// FMA pipe (exp2_poly2) instead of the MUFU unit.  Measured on B200 at
+// config 3 it does not pay (MUFU is not the binding limit), so it is off.
+#ifndef CUFLASH_FWD_EXP2_EMU_EVERY
+#define CUFLASH_FWD_EXP2_EMU_EVERY 0
+#endif
+constexpr int kExp2EmuEvery = CUFLASH_FWD_EXP2_EMU_EVERY;
 constexpr float kLn2 = 0.6931471805599453f;
 constexpr float kLog2e = 1.4426950408889634f;
 
@@ -385,8 +392,15 @@ __global__ void __launch_bounds__(384, 1)
                     const int c0 = h * 64 + 2 * i;
                     const float2 x = f2_unpack(
                         f2_fma(f2_pack(__uint_as_float(sr[c0]), __uint_as_float(sr[c0 + 1])), c2, nm2));
-                    const float p0 = ex2_approx(x.x);
-                    const float p1 = ex2_approx(x.y);
+                    float p0, p1;
+                    if (kExp2EmuEvery > 0 && (i % kExp2EmuEvery) == kExp2EmuEvery - 1) {
+                        const float2 e = exp2_poly2(x.x, x.y);  // FMA pipe
+                        p0 = e.x;
+                        p1 = e.y;
+                    } else {
+                        p0 = ex2_approx(x.x);  // MUFU
+                        p1 = ex2_approx(x.y);
+                    }
                     const uint64_t pp = f2_pack(p0, p1);
                     switch (i & 3) {
                         case 0: acc0 = f2_add(acc0, pp); break;
