@@ -8,8 +8,13 @@
 // the input dtype before the PV product (flash_attention_forward_wmma.cu:152),
 // fp32 accumulation, O rounded to nearest on store (type_adapter.cuh:24-32).
 //
-// CTA = 256 query rows of one (batch, head) = two 128-row tiles.
-//   warp 0      TMA producer: Q tiles once, then K/V blocks of 128 rows
+// Persistent kernel, one CTA per SM.  A work item is 256 query rows of one
+// (batch, head) = two 128-row tiles; each CTA walks a static list of items
+// (fwd_item) and keeps its barriers, TMEM and K/V ring across them, so the
+// next item's Q loads and first S products overlap the current item's last
+// softmax block and epilogue.
+//   warp 0      TMA producer: Q tiles per item (once the previous item's
+//               last QK on that slot retired), K/V blocks of 128 rows
 //               through a 2-stage ring (full/empty mbarriers).
 //   warp 1      TMEM allocator and tcgen05.mma issuer (one thread).
 //   warps 4-7   softmax for tile 0, warps 8-11 softmax for tile 1; one
@@ -26,6 +31,7 @@
 // Causal: kv blocks entirely above the diagonal are skipped, the diagonal
 // block is masked element-wise; CTAs are launched heaviest first.
 
+#include <algorithm>
 #include <cmath>
 
 #include "common.cuh"
@@ -45,6 +51,13 @@ constexpr float kRescaleThreshold = 8.0f;  // log2 units
 #define CUFLASH_FWD_EXP2_EMU_EVERY 0
 #endif
 constexpr int kExp2EmuEvery = CUFLASH_FWD_EXP2_EMU_EVERY;
+// P is handed to the MMA warp in two halves of 64 keys: the first half of
+// O += P V runs on the tensor pipe while the second half's exponentials are
+// computed.
+#ifndef CUFLASH_FWD_SPLIT_P
+#define CUFLASH_FWD_SPLIT_P 1
+#endif
+constexpr bool kSplitP = CUFLASH_FWD_SPLIT_P != 0;
 constexpr float kLn2 = 0.6931471805599453f;
 constexpr float kLog2e = 1.4426950408889634f;
 
@@ -63,7 +76,7 @@ struct FwdGeom {
     static constexpr int kOffK = 2 * kTileBytes;
     static constexpr int kOffV = kOffK + kStages * kTileBytes;
     static constexpr int kOffBar = kOffV + kStages * kTileBytes;
-    static constexpr int kNumBars = 1 + 4 * kStages + 2 + 2 + 2 + 1;
+    static constexpr int kNumBars = 2 + 4 * kStages + 2 + 2 + 2 + 2 + 2 + 1;
     static constexpr int kSmemBytes = kOffBar + kNumBars * 8 + 16 + 1024;
 };
 
@@ -72,7 +85,10 @@ struct FwdParams {
     float* L;
     int seq_q;
     int seq_k;
-    int num_ctiles;
+    int num_ctiles;  // 256-row query tiles per (b,h)
+    int npairs;      // (num_ctiles + 1) / 2
+    int paired;      // 1: a unit is a (heavy, light) item pair; 0: one item
+    int num_units;   // BH * npairs, or BH * num_ctiles when not paired
     int causal;
     float scale_log2;
     long long q_offset;
@@ -88,6 +104,19 @@ __device__ __forceinline__ uint64_t kmajor_desc(uint32_t tile_base, int kk) {
     return sm100::make_smem_desc(addr, 16, 8 * G::kSwz, G::kLayout);
 }
 
+// Descriptor of k-step kk = descriptor of k-step 0 + this (start address
+// field, in 16-byte units; shared addresses stay below 2^18 so no carry).
+template <int D>
+__host__ __device__ constexpr uint32_t kmajor_delta(int kk) {
+    using G = FwdGeom<D>;
+    return ((static_cast<uint32_t>(kk) * 32u / G::kSwz) * G::kCbBytes +
+            (static_cast<uint32_t>(kk) * 32u % G::kSwz)) >> 4;
+}
+template <int D>
+__host__ __device__ constexpr uint32_t mnmajor_delta(int kk) {
+    return (static_cast<uint32_t>(kk) * 16u * FwdGeom<D>::kSwz) >> 4;
+}
+
 // MN-major operand (kv rows = K dimension, D contiguous = N dimension) for
 // k-step kk (16 kv rows).
 template <int D>
@@ -95,6 +124,46 @@ __device__ __forceinline__ uint64_t mnmajor_desc(uint32_t tile_base, int kk) {
     using G = FwdGeom<D>;
     const uint32_t addr = tile_base + static_cast<uint32_t>(kk) * 16u * G::kSwz;
     return sm100::make_smem_desc(addr, G::kCbBytes, 8 * G::kSwz, G::kLayout);
+}
+
+// One work item = 256 query rows (two 128-row tiles) of one (b,h).  Unit u
+// of the persistent schedule holds two items of the same (b,h): q tile pair
+// ct = num_ctiles-1-k and ct = k.  Under a causal mask their costs add up to
+// about the same for every k, so a static round-robin of units over the CTAs
+// is balanced, and the second item re-reads K/V blocks the first one has just
+// brought into L2.  Problems with fewer units than SMs use one item per unit
+// instead (more CTAs, same per-item work as a non-persistent grid).
+struct FwdItem {
+    int bh;
+    int q_row0;
+};
+
+__device__ __forceinline__ bool fwd_item(const FwdParams& p, int u, int w, FwdItem& it) {
+    if (!p.paired) {  // one item per unit, heaviest first within a (b,h)
+        if (w == 1) return false;
+        const int bh = u / p.num_ctiles;
+        it.bh = bh;
+        it.q_row0 = (p.num_ctiles - 1 - (u - bh * p.num_ctiles)) * 256;
+        return true;
+    }
+    const int bh = u / p.npairs;
+    const int k = u - bh * p.npairs;
+    const int ct = w == 0 ? p.num_ctiles - 1 - k : k;
+    if (w == 1 && ct == p.num_ctiles - 1 - k) return false;  // middle tile of an odd count
+    it.bh = bh;
+    it.q_row0 = ct * 256;
+    return true;
+}
+
+// kv blocks the 128-row tile starting at query row r_lo visits.
+__device__ __forceinline__ int tile_blocks(const FwdParams& p, int r_lo) {
+    const int nkv_all = (p.seq_k + 127) / 128;
+    if (r_lo >= p.seq_q) return 0;
+    if (!p.causal) return nkv_all;
+    const int r_hi = min(r_lo + 127, p.seq_q - 1);
+    const long long lim = p.q_offset + r_hi - p.k_offset;  // largest visible local key
+    const long long nb = lim / 128 + 1;
+    return lim < 0 ? 0 : (nb < nkv_all ? static_cast<int>(nb) : nkv_all);
 }
 
 // Warp-uniform bounded wait.
@@ -125,47 +194,24 @@ __global__ void __launch_bounds__(384, 1)
     const uint32_t sbase = (raw_addr + 1023u) & ~1023u;
     uint8_t* sptr = smem_raw + (sbase - raw_addr);
     uint64_t* bars = reinterpret_cast<uint64_t*>(sptr + G::kOffBar);
-    uint64_t* bar_q = bars;
-    uint64_t* full_k = bars + 1;
+    uint64_t* bar_q = bars;  // [2] Q tile t landed
+    uint64_t* full_k = bar_q + 2;
     uint64_t* empty_k = full_k + G::kStages;
     uint64_t* full_v = empty_k + G::kStages;
     uint64_t* empty_v = full_v + G::kStages;
-    uint64_t* bar_s = empty_v + G::kStages;
-    uint64_t* bar_p = bar_s + 2;
-    uint64_t* bar_o = bar_p + 2;
-    uint64_t* bar_done = bar_o + 2;
+    uint64_t* bar_s = empty_v + G::kStages;  // [2] S_t in TMEM
+    uint64_t* bar_p = bar_s + 2;             // [2] P_t stored (128 arrivals)
+    uint64_t* bar_o = bar_p + 2;             // [2] O_t final for the item
+    uint64_t* bar_qfree = bar_o + 2;         // [2] last QK of the item's tile t retired
+    uint64_t* bar_p2 = bar_qfree + 2;        // [2] second half of P_t stored (split mode)
+    uint64_t* bar_done = bar_p2 + 2;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar_done + 1);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
-    // (q tile, b*h) grid with q tiles fastest: the CTAs running at the same
-    // time share few (b,h), so their K/V blocks are reused from L2.
-    const int bh = blockIdx.y;
-    const int ct = p.num_ctiles - 1 - static_cast<int>(blockIdx.x);
-    const int q_row0 = ct * 256;
-
-    // kv blocks needed by each 128-row tile
-    const int nkv_all = (p.seq_k + 127) / 128;
-    int n_t[2];
-#pragma unroll
-    for (int t = 0; t < 2; ++t) {
-        const int r_lo = q_row0 + t * 128;
-        if (r_lo >= p.seq_q) {
-            n_t[t] = 0;
-        } else if (!p.causal) {
-            n_t[t] = nkv_all;
-        } else {
-            const int r_hi = min(r_lo + 127, p.seq_q - 1);
-            const long long lim = p.q_offset + r_hi - p.k_offset;  // largest visible local key
-            const long long nb = lim / 128 + 1;
-            n_t[t] = lim < 0 ? 0 : (nb < nkv_all ? static_cast<int>(nb) : nkv_all);
-        }
-    }
-    const int n_max = max(n_t[0], n_t[1]);
 
     if (threadIdx.x == 0) {
-        mbar_init(bar_q, 1);
         for (int s = 0; s < G::kStages; ++s) {
             mbar_init(full_k + s, 1);
             mbar_init(empty_k + s, 1);
@@ -173,9 +219,12 @@ __global__ void __launch_bounds__(384, 1)
             mbar_init(empty_v + s, 1);
         }
         for (int t = 0; t < 2; ++t) {
+            mbar_init(bar_q + t, 1);
             mbar_init(bar_s + t, 1);
             mbar_init(bar_p + t, 128);
+            mbar_init(bar_p2 + t, 128);
             mbar_init(bar_o + t, 1);
+            mbar_init(bar_qfree + t, 1);
         }
         mbar_init(bar_done, 1);
         *abort_flag = 0;
@@ -191,122 +240,197 @@ __global__ void __launch_bounds__(384, 1)
     const uint32_t tmem = *tmem_slot;
 
     // Registers: launched with 168 per thread (384 x 168 = 64512); warpgroup 0
-    // (producer, MMA, 2 idle warps) gives back down to 56 and the two softmax
-    // warpgroups take 216 each: 128*56 + 256*216 = 62464 <= 64512.
+    // (producer, MMA, 2 idle warps) gives back down to 72 and the two softmax
+    // warpgroups take 216 each: 128*72 + 256*216 = 64512 <= 64512.
     if (warp < 4) {
-        setmaxnreg_dec<56>();
+        setmaxnreg_dec<72>();
     if (warp == 0) {
         // ------------------------------------------------ TMA producer
-        if (lane == 0 && n_max > 0) {
+        if (lane == 0) {
             prefetch_tmap(&tmQ);
             prefetch_tmap(&tmK);
             prefetch_tmap(&tmV);
-            const int ntiles_loaded = (n_t[0] > 0 ? 1 : 0) + (n_t[1] > 0 ? 1 : 0);
-            mbar_arrive_expect_tx(bar_q, ntiles_loaded * G::kTileBytes);
-            for (int t = 0; t < 2; ++t) {
-                if (n_t[t] == 0) continue;
-                for (int cb = 0; cb < G::kNumCb; ++cb)
-                    tma_load_3d(sptr + G::kOffQ + t * G::kTileBytes + cb * G::kCbBytes, &tmQ,
-                                bar_q, cb * G::kCbElems, q_row0 + t * 128, bh);
-            }
-            int issued_k = 0, issued_v = 0;
-            for (int j = 0; j < n_max; ++j) {
-                const int s = j % G::kStages;
-                const uint32_t ph = (j / G::kStages) & 1;
-                if (j >= G::kStages && !mbar_wait(empty_k + s, ph ^ 1, abort_flag, &g_fwd_status))
-                    break;
-                mbar_arrive_expect_tx(full_k + s, G::kTileBytes);
-                for (int cb = 0; cb < G::kNumCb; ++cb)
-                    tma_load_3d(sptr + G::kOffK + s * G::kTileBytes + cb * G::kCbBytes, &tmK,
-                                full_k + s, cb * G::kCbElems, j * 128, bh);
-                ++issued_k;
-                if (j >= G::kStages && !mbar_wait(empty_v + s, ph ^ 1, abort_flag, &g_fwd_status))
-                    break;
-                mbar_arrive_expect_tx(full_v + s, G::kTileBytes);
-                for (int cb = 0; cb < G::kNumCb; ++cb)
-                    tma_load_3d(sptr + G::kOffV + s * G::kTileBytes + cb * G::kCbBytes, &tmV,
-                                full_v + s, cb * G::kCbElems, j * 128, bh);
-                ++issued_v;
+            uint32_t q_cnt[2] = {0u, 0u};  // Q loads per tile slot
+            uint32_t issued_k = 0, issued_v = 0;  // K/V blocks through the ring
+            bool ok = true;
+            for (int u = blockIdx.x; ok && u < p.num_units; u += gridDim.x) {
+                for (int w = 0; ok && w < 2; ++w) {
+                    FwdItem it;
+                    if (!fwd_item(p, u, w, it)) continue;
+                    const int nt[2] = {tile_blocks(p, it.q_row0), tile_blocks(p, it.q_row0 + 128)};
+                    const int n_max = max(nt[0], nt[1]);
+#pragma unroll
+                    for (int t = 0; t < 2; ++t) {
+                        if (nt[t] == 0 || !ok) continue;
+                        // the slot is free once the previous item's last QK on it retired
+                        if (q_cnt[t] > 0 && !mbar_wait(bar_qfree + t, (q_cnt[t] - 1) & 1,
+                                                       abort_flag, &g_fwd_status)) {
+                            ok = false;
+                            break;
+                        }
+                        mbar_arrive_expect_tx(bar_q + t, G::kTileBytes);
+                        for (int cb = 0; cb < G::kNumCb; ++cb)
+                            tma_load_3d(sptr + G::kOffQ + t * G::kTileBytes + cb * G::kCbBytes,
+                                        &tmQ, bar_q + t, cb * G::kCbElems, it.q_row0 + t * 128,
+                                        it.bh);
+                        ++q_cnt[t];
+                    }
+                    for (int j = 0; ok && j < n_max; ++j) {
+                        const uint32_t g = issued_v;
+                        const int s = g % G::kStages;
+                        const uint32_t ph = (g / G::kStages) & 1;
+                        if (g >= G::kStages &&
+                            !mbar_wait(empty_k + s, ph ^ 1, abort_flag, &g_fwd_status)) {
+                            ok = false;
+                            break;
+                        }
+                        mbar_arrive_expect_tx(full_k + s, G::kTileBytes);
+                        for (int cb = 0; cb < G::kNumCb; ++cb)
+                            tma_load_3d(sptr + G::kOffK + s * G::kTileBytes + cb * G::kCbBytes,
+                                        &tmK, full_k + s, cb * G::kCbElems, j * 128, it.bh);
+                        ++issued_k;
+                        if (g >= G::kStages &&
+                            !mbar_wait(empty_v + s, ph ^ 1, abort_flag, &g_fwd_status)) {
+                            ok = false;
+                            break;
+                        }
+                        mbar_arrive_expect_tx(full_v + s, G::kTileBytes);
+                        for (int cb = 0; cb < G::kNumCb; ++cb)
+                            tma_load_3d(sptr + G::kOffV + s * G::kTileBytes + cb * G::kCbBytes,
+                                        &tmV, full_v + s, cb * G::kCbElems, j * 128, it.bh);
+                        ++issued_v;
+                    }
+                }
             }
             // every issued load must land before the CTA can exit
-            drain_wait(bar_q, 0);
-            for (int j = max(0, issued_k - G::kStages); j < issued_k; ++j)
-                drain_wait(full_k + j % G::kStages, (j / G::kStages) & 1);
-            for (int j = max(0, issued_v - G::kStages); j < issued_v; ++j)
-                drain_wait(full_v + j % G::kStages, (j / G::kStages) & 1);
+#pragma unroll
+            for (int t = 0; t < 2; ++t)
+                if (q_cnt[t] > 0) drain_wait(bar_q + t, (q_cnt[t] - 1) & 1);
+            for (uint32_t g = issued_k > G::kStages ? issued_k - G::kStages : 0; g < issued_k; ++g)
+                drain_wait(full_k + g % G::kStages, (g / G::kStages) & 1);
+            for (uint32_t g = issued_v > G::kStages ? issued_v - G::kStages : 0; g < issued_v; ++g)
+                drain_wait(full_v + g % G::kStages, (g / G::kStages) & 1);
         }
     } else if (warp == 1) {
         // ------------------------------------------------ MMA issuer
-        if (lane == 0 && n_max > 0) {
+        if (lane == 0) {
             constexpr uint32_t idesc_qk = make_idesc(DType<T>::kMmaFmt, 128, 128, false, false);
             constexpr uint32_t idesc_pv = make_idesc(DType<T>::kMmaFmt, 128, D, false, true);
             auto issue_qk = [&](int t, int s) {
                 const uint32_t d_tmem = tmem + t * 128;
                 const uint32_t a_base = sbase + G::kOffQ + t * G::kTileBytes;
                 const uint32_t b_base = sbase + G::kOffK + s * G::kTileBytes;
+                uint64_t a0 = kmajor_desc<D>(a_base, 0);
+                uint64_t b0 = kmajor_desc<D>(b_base, 0);
+                // opaque to the optimiser: keeps the 2 x D/16 descriptors from
+                // being hoisted out of the item loop into live registers
+                asm volatile("" : "+l"(a0), "+l"(b0));
 #pragma unroll
                 for (int kk = 0; kk < D / 16; ++kk)
-                    mma_f16_ss(d_tmem, kmajor_desc<D>(a_base, kk), kmajor_desc<D>(b_base, kk),
+                    mma_f16_ss(d_tmem, a0 + kmajor_delta<D>(kk), b0 + kmajor_delta<D>(kk),
                                idesc_qk, kk > 0 ? 1u : 0u);
             };
-            auto issue_pv = [&](int t, int s, bool acc) {
+            // O_t += P_t V over key k-steps [kk0, kk1)
+            auto issue_pv = [&](int t, int s, bool acc, int kk0, int kk1) {
                 const uint32_t d_tmem = tmem + 256 + t * 128;
                 const uint32_t p_tmem = tmem + t * 128;
-                const uint32_t v_base = sbase + G::kOffV + s * G::kTileBytes;
+                uint64_t v0 = mnmajor_desc<D>(sbase + G::kOffV + s * G::kTileBytes, 0);
+                asm volatile("" : "+l"(v0));
 #pragma unroll
                 for (int kk = 0; kk < 128 / 16; ++kk)
-                    mma_f16_ts(d_tmem, p_tmem + kk * 8, mnmajor_desc<D>(v_base, kk), idesc_pv,
-                               (acc || kk > 0) ? 1u : 0u);
+                    if (kk >= kk0 && kk < kk1)
+                        mma_f16_ts(d_tmem, p_tmem + kk * 8, v0 + mnmajor_delta<D>(kk), idesc_pv,
+                                   (acc || kk > 0) ? 1u : 0u);
             };
-            bool ok = mbar_wait(bar_q, 0, abort_flag, &g_fwd_status) &&
-                      mbar_wait(full_k, 0, abort_flag, &g_fwd_status);
-            if (ok) {
-                tc_fence_after();
-                for (int t = 0; t < 2; ++t) {
-                    if (n_t[t] > 0) {
-                        issue_qk(t, 0);
-                        tc_commit(bar_s + t);
+            uint32_t q_cnt[2] = {0u, 0u};  // bar_q phases consumed
+            uint32_t p_cnt[2] = {0u, 0u};  // bar_p phases consumed
+            uint32_t kv_g = 0;             // first ring slot of the current item
+            bool ok = true;
+            for (int u = blockIdx.x; ok && u < p.num_units; u += gridDim.x) {
+                for (int w = 0; ok && w < 2; ++w) {
+                    FwdItem it;
+                    if (!fwd_item(p, u, w, it)) continue;
+                    const int nt[2] = {tile_blocks(p, it.q_row0), tile_blocks(p, it.q_row0 + 128)};
+                    const int n_max = max(nt[0], nt[1]);
+                    if (n_max == 0) continue;
+                    // The item's first S tiles.  In-order issue keeps them
+                    // behind the previous item's last PV products, which
+                    // still read P from the same TMEM columns.
+                    {
+                        const int s0 = kv_g % G::kStages;
+                        const uint32_t ph0 = (kv_g / G::kStages) & 1;
+#pragma unroll
+                        for (int t = 0; t < 2; ++t)
+                            if (nt[t] > 0 && ok)
+                                ok = mbar_wait(bar_q + t, q_cnt[t] & 1, abort_flag, &g_fwd_status);
+                        ok = ok && mbar_wait(full_k + s0, ph0, abort_flag, &g_fwd_status);
+                        if (!ok) break;
+                        tc_fence_after();
+#pragma unroll
+                        for (int t = 0; t < 2; ++t) {
+                            if (nt[t] == 0) continue;
+                            issue_qk(t, s0);
+                            tc_commit(bar_s + t);
+                            if (nt[t] == 1) tc_commit(bar_qfree + t);
+                            ++q_cnt[t];
+                        }
+                        tc_commit(empty_k + s0);
                     }
-                }
-                tc_commit(empty_k);
-            }
-            for (int j = 0; ok && j < n_max; ++j) {
-                const int s = j % G::kStages;
-                const uint32_t ph = (j / G::kStages) & 1;
-                if (!mbar_wait(full_v + s, ph, abort_flag, &g_fwd_status)) {
-                    ok = false;
-                    break;
-                }
-                tc_fence_after();
-                const int jn = j + 1;
-                const int sn = jn % G::kStages;
-                const uint32_t phn = (jn / G::kStages) & 1;
-                bool k_next_ready = false;
-                for (int t = 0; t < 2 && ok; ++t) {
-                    if (j >= n_t[t]) continue;
-                    if (!mbar_wait(bar_p + t, j & 1, abort_flag, &g_fwd_status)) {
-                        ok = false;
-                        break;
-                    }
-                    tc_fence_after();
-                    issue_pv(t, s, j > 0);
-                    if (j == n_t[t] - 1) tc_commit(bar_o + t);
-                    if (jn < n_t[t]) {
-                        if (!k_next_ready) {
-                            if (!mbar_wait(full_k + sn, phn, abort_flag, &g_fwd_status)) {
+                    for (int j = 0; ok && j < n_max; ++j) {
+                        const uint32_t g = kv_g + j;
+                        const int s = g % G::kStages;
+                        const uint32_t ph = (g / G::kStages) & 1;
+                        if (!mbar_wait(full_v + s, ph, abort_flag, &g_fwd_status)) {
+                            ok = false;
+                            break;
+                        }
+                        tc_fence_after();
+                        const uint32_t gn = g + 1;
+                        const int sn = gn % G::kStages;
+                        const uint32_t phn = (gn / G::kStages) & 1;
+                        bool k_next_ready = false;
+#pragma unroll
+                        for (int t = 0; t < 2; ++t) {
+                            if (j >= nt[t] || !ok) continue;
+                            if (!mbar_wait(bar_p + t, p_cnt[t] & 1, abort_flag, &g_fwd_status)) {
                                 ok = false;
                                 break;
                             }
                             tc_fence_after();
-                            k_next_ready = true;
+                            if (kSplitP) {
+                                issue_pv(t, s, j > 0, 0, 4);
+                                if (!mbar_wait(bar_p2 + t, p_cnt[t] & 1, abort_flag,
+                                               &g_fwd_status)) {
+                                    ok = false;
+                                    break;
+                                }
+                                tc_fence_after();
+                                issue_pv(t, s, j > 0, 4, 8);
+                            } else {
+                                issue_pv(t, s, j > 0, 0, 8);
+                            }
+                            ++p_cnt[t];
+                            if (j == nt[t] - 1) tc_commit(bar_o + t);
+                            if (j + 1 < nt[t]) {
+                                if (!k_next_ready) {
+                                    if (!mbar_wait(full_k + sn, phn, abort_flag, &g_fwd_status)) {
+                                        ok = false;
+                                        break;
+                                    }
+                                    tc_fence_after();
+                                    k_next_ready = true;
+                                }
+                                issue_qk(t, sn);
+                                tc_commit(bar_s + t);
+                                if (j + 2 == nt[t]) tc_commit(bar_qfree + t);
+                            }
                         }
-                        issue_qk(t, sn);
-                        tc_commit(bar_s + t);
+                        if (!ok) break;
+                        tc_commit(empty_v + s);
+                        if (k_next_ready) tc_commit(empty_k + sn);
                     }
+                    kv_g += n_max;
                 }
-                if (!ok) break;
-                tc_commit(empty_v + s);
-                if (k_next_ready) tc_commit(empty_k + sn);
             }
             // all MMAs (and their commits) retire before teardown
             tc_commit(bar_done);
@@ -321,169 +445,193 @@ __global__ void __launch_bounds__(384, 1)
         const int t = (warp - 4) >> 2;
         const int wq = warp & 3;
         const int r = wq * 32 + lane;
-        const int row = q_row0 + t * 128 + r;
-        const long long grow = p.q_offset + row;
         const uint32_t lane_addr = static_cast<uint32_t>(wq * 32) << 16;
         const uint32_t s_tmem = tmem + lane_addr + t * 128;
         const uint32_t o_tmem = tmem + lane_addr + 256 + t * 128;
-        const int n = n_t[t];
         const float c = p.scale_log2;
-        const long long tile_g0 = p.q_offset + q_row0 + t * 128;
-
-        float m_run = -INFINITY;
-        float l_run = 0.f;
+        uint32_t s_cnt = 0, o_cnt = 0;  // bar_s / bar_o phases consumed
         bool ok = true;
-        for (int j = 0; j < n; ++j) {
-            if (!warp_wait(bar_s + t, j & 1, abort_flag)) {
-                ok = false;
-                break;
-            }
-            tc_fence_after();
-            uint32_t sr[128];
-            tmem_ld_x128(s_tmem, sr);
-            const int col0 = j * 128;
-            const bool need_mask = (col0 + 128 > p.seq_k) ||
-                                   (p.causal && (p.k_offset + col0 + 127 > tile_g0));
-            if (need_mask) {
-                // largest visible local key column for this row (32-bit safe)
-                const long long lim64 = grow - p.k_offset;
-                const int lim = p.causal ? static_cast<int>(lim64 < -1 ? -1 : (lim64 > 0x7fffffff ? 0x7fffffff : lim64))
-                                         : 0x7fffffff;
-                const int vis_end = min(p.seq_k - 1, lim) - col0;  // visible iff i <= vis_end
+        for (int u = blockIdx.x; ok && u < p.num_units; u += gridDim.x) {
+            for (int w = 0; ok && w < 2; ++w) {
+                FwdItem it;
+                if (!fwd_item(p, u, w, it)) continue;
+                const int row = it.q_row0 + t * 128 + r;
+                const long long grow = p.q_offset + row;
+                const int n = tile_blocks(p, it.q_row0 + t * 128);
+                const long long tile_g0 = p.q_offset + it.q_row0 + t * 128;
+
+                float m_run = -INFINITY;
+                float l_run = 0.f;
+                for (int j = 0; j < n; ++j) {
+                    if (!warp_wait(bar_s + t, s_cnt & 1, abort_flag)) {
+                        ok = false;
+                        break;
+                    }
+                    ++s_cnt;
+                    tc_fence_after();
+                    uint32_t sr[128];
+                    tmem_ld_x128(s_tmem, sr);
+                    const int col0 = j * 128;
+                    const bool need_mask = (col0 + 128 > p.seq_k) ||
+                                           (p.causal && (p.k_offset + col0 + 127 > tile_g0));
+                    if (need_mask) {
+                        // largest visible local key column for this row (32-bit safe)
+                        const long long lim64 = grow - p.k_offset;
+                        const int lim = p.causal ? static_cast<int>(lim64 < -1 ? -1 : (lim64 > 0x7fffffff ? 0x7fffffff : lim64))
+                                                 : 0x7fffffff;
+                        const int vis_end = min(p.seq_k - 1, lim) - col0;  // visible iff i <= vis_end
 #pragma unroll
-                for (int i = 0; i < 128; ++i)
-                    if (i > vis_end) sr[i] = __float_as_uint(-INFINITY);
-            }
-            // row maximum: 3-input max over four independent chains
-            float mx;
-            {
-                float m0 = -INFINITY, m1 = -INFINITY, m2 = -INFINITY, m3 = -INFINITY;
+                        for (int i = 0; i < 128; ++i)
+                            if (i > vis_end) sr[i] = __float_as_uint(-INFINITY);
+                    }
+                    // row maximum: 3-input max over four independent chains
+                    float mx;
+                    {
+                        float m0 = -INFINITY, m1 = -INFINITY, m2 = -INFINITY, m3 = -INFINITY;
 #pragma unroll
-                for (int i = 0; i < 128; i += 8) {
-                    m0 = fmax3(m0, __uint_as_float(sr[i]), __uint_as_float(sr[i + 1]));
-                    m1 = fmax3(m1, __uint_as_float(sr[i + 2]), __uint_as_float(sr[i + 3]));
-                    m2 = fmax3(m2, __uint_as_float(sr[i + 4]), __uint_as_float(sr[i + 5]));
-                    m3 = fmax3(m3, __uint_as_float(sr[i + 6]), __uint_as_float(sr[i + 7]));
-                }
-                mx = fmaxf(fmaxf(m0, m1), fmaxf(m2, m3)) * c;  // c > 0
-            }
-            // Decide the new running maximum; O is rescaled after P is stored so
-            // that the score registers are dead by then.
-            float alpha = 1.f;
-            bool need = false;
-            if (j == 0) {
-                m_run = mx;
-            } else {
-                need = mx > m_run + kRescaleThreshold;
-                if (need) {
-                    alpha = ex2_approx(m_run - mx);
-                    m_run = mx;
-                }
-            }
-            const float m_use = (m_run == -INFINITY) ? 0.f : m_run;
-            const uint64_t c2 = f2_pack(c, c);
-            const uint64_t nm2 = f2_pack(-m_use, -m_use);
-            uint64_t acc0 = 0, acc1 = 0, acc2 = 0, acc3 = 0;  // (0.f, 0.f) pairs
-#pragma unroll
-            for (int h = 0; h < 2; ++h) {
-                uint32_t pk[32];
-#pragma unroll
-                for (int i = 0; i < 32; ++i) {
-                    const int c0 = h * 64 + 2 * i;
-                    const float2 x = f2_unpack(
-                        f2_fma(f2_pack(__uint_as_float(sr[c0]), __uint_as_float(sr[c0 + 1])), c2, nm2));
-                    float p0, p1;
-                    if (kExp2EmuEvery > 0 && (i % kExp2EmuEvery) == kExp2EmuEvery - 1) {
-                        const float2 e = exp2_poly2(x.x, x.y);  // FMA pipe
-                        p0 = e.x;
-                        p1 = e.y;
+                        for (int i = 0; i < 128; i += 8) {
+                            m0 = fmax3(m0, __uint_as_float(sr[i]), __uint_as_float(sr[i + 1]));
+                            m1 = fmax3(m1, __uint_as_float(sr[i + 2]), __uint_as_float(sr[i + 3]));
+                            m2 = fmax3(m2, __uint_as_float(sr[i + 4]), __uint_as_float(sr[i + 5]));
+                            m3 = fmax3(m3, __uint_as_float(sr[i + 6]), __uint_as_float(sr[i + 7]));
+                        }
+                        mx = fmaxf(fmaxf(m0, m1), fmaxf(m2, m3)) * c;  // c > 0
+                    }
+                    // Decide the new running maximum.  O is rescaled before the first
+                    // P half is handed over (split mode) or after P is stored, when the
+                    // score registers are dead.
+                    float alpha = 1.f;
+                    bool need = false;
+                    if (j == 0) {
+                        m_run = mx;
                     } else {
-                        p0 = ex2_approx(x.x);  // MUFU
-                        p1 = ex2_approx(x.y);
+                        need = mx > m_run + kRescaleThreshold;
+                        if (need) {
+                            alpha = ex2_approx(m_run - mx);
+                            m_run = mx;
+                        }
                     }
-                    const uint64_t pp = f2_pack(p0, p1);
-                    switch (i & 3) {
-                        case 0: acc0 = f2_add(acc0, pp); break;
-                        case 1: acc1 = f2_add(acc1, pp); break;
-                        case 2: acc2 = f2_add(acc2, pp); break;
-                        default: acc3 = f2_add(acc3, pp); break;
+                    // PV_{j-1} has completed: S_t(j) was issued after it and its commit
+                    // covers every earlier tcgen05 operation.
+                    auto rescale_o = [&]() {
+                        if (__any_sync(0xffffffffu, need)) {
+#pragma unroll
+                            for (int cb = 0; cb < D / 16; ++cb) {
+                                uint32_t o[16];
+                                tmem_ld_x16(o_tmem + cb * 16, o);
+#pragma unroll
+                                for (int i = 0; i < 16; ++i)
+                                    o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+                                tmem_st_x16(o_tmem + cb * 16, o);
+                            }
+                        }
+                    };
+                    if (kSplitP) rescale_o();
+                    const float m_use = (m_run == -INFINITY) ? 0.f : m_run;
+                    const uint64_t c2 = f2_pack(c, c);
+                    const uint64_t nm2 = f2_pack(-m_use, -m_use);
+                    uint64_t acc0 = 0, acc1 = 0, acc2 = 0, acc3 = 0;  // (0.f, 0.f) pairs
+#pragma unroll
+                    for (int h = 0; h < 2; ++h) {
+                        uint32_t pk[32];
+#pragma unroll
+                        for (int i = 0; i < 32; ++i) {
+                            const int c0 = h * 64 + 2 * i;
+                            const float2 x = f2_unpack(
+                                f2_fma(f2_pack(__uint_as_float(sr[c0]), __uint_as_float(sr[c0 + 1])), c2, nm2));
+                            float p0, p1;
+                            if (kExp2EmuEvery > 0 &&
+                                (i % (kExp2EmuEvery > 0 ? kExp2EmuEvery : 1)) == kExp2EmuEvery - 1) {
+                                const float2 e = exp2_poly2(x.x, x.y);  // FMA pipe
+                                p0 = e.x;
+                                p1 = e.y;
+                            } else {
+                                p0 = ex2_approx(x.x);  // MUFU
+                                p1 = ex2_approx(x.y);
+                            }
+                            const uint64_t pp = f2_pack(p0, p1);
+                            switch (i & 3) {
+                                case 0: acc0 = f2_add(acc0, pp); break;
+                                case 1: acc1 = f2_add(acc1, pp); break;
+                                case 2: acc2 = f2_add(acc2, pp); break;
+                                default: acc3 = f2_add(acc3, pp); break;
+                            }
+                            pk[i] = DType<T>::pack2(p0, p1);
+                        }
+                        tmem_st_x32(s_tmem + h * 32, pk);
+                        if (kSplitP) {
+                            tc_fence_before();
+                            mbar_arrive((h == 0 ? bar_p : bar_p2) + t);
+                        }
                     }
-                    pk[i] = DType<T>::pack2(p0, p1);
+                    float sum;
+                    {
+                        const float2 a = f2_unpack(f2_add(f2_add(acc0, acc1), f2_add(acc2, acc3)));
+                        sum = a.x + a.y;
+                    }
+                    l_run = l_run * alpha + sum;
+                    if (!kSplitP) {
+                        rescale_o();
+                        tc_fence_before();
+                        mbar_arrive(bar_p + t);
+                    }
                 }
-                tmem_st_x32(s_tmem + h * 32, pk);
-            }
-            float sum;
-            {
-                const float2 a = f2_unpack(f2_add(f2_add(acc0, acc1), f2_add(acc2, acc3)));
-                sum = a.x + a.y;
-            }
-            l_run = l_run * alpha + sum;
-            // PV_{j-1} has completed: S_t(j) was issued after it and its commit
-            // covers every earlier tcgen05 operation.
-            if (__any_sync(0xffffffffu, need)) {
+
+                // epilogue
+                if (n > 0 && ok) {
+                    ok = warp_wait(bar_o + t, o_cnt & 1, abort_flag);
+                    ++o_cnt;
+                    tc_fence_after();
+                }
+                const bool valid_row = row < p.seq_q;
+                const float inv_l = l_run > 0.f ? 1.f / l_run : 0.f;
+                const size_t row_elem = (static_cast<size_t>(it.bh) * p.seq_q + row) * D;
 #pragma unroll
                 for (int cb = 0; cb < D / 32; ++cb) {
                     uint32_t o[32];
-                    tmem_ld_x32(o_tmem + cb * 32, o);
+                    if (n > 0 && ok) {
+                        tmem_ld_x32(o_tmem + cb * 32, o);
+                    } else {
 #pragma unroll
-                    for (int i = 0; i < 32; ++i)
-                        o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
-                    tmem_st_x32(o_tmem + cb * 32, o);
-                }
-            }
-            tc_fence_before();
-            mbar_arrive(bar_p + t);
-        }
-
-        // epilogue
-        if (n > 0 && ok) {
-            ok = warp_wait(bar_o + t, 0, abort_flag);
-            tc_fence_after();
-        }
-        const bool valid_row = row < p.seq_q;
-        const float inv_l = l_run > 0.f ? 1.f / l_run : 0.f;
-        const size_t row_elem = (static_cast<size_t>(bh) * p.seq_q + row) * D;
+                        for (int i = 0; i < 32; ++i) o[i] = 0u;
+                    }
+                    if (valid_row) {
+                        if constexpr (kF32Out) {
+                            float4* dst = reinterpret_cast<float4*>(static_cast<float*>(p.O) + row_elem +
+                                                                    cb * 32);
 #pragma unroll
-        for (int cb = 0; cb < D / 32; ++cb) {
-            uint32_t o[32];
-            if (n > 0 && ok) {
-                tmem_ld_x32(o_tmem + cb * 32, o);
-            } else {
+                            for (int i = 0; i < 8; ++i)
+                                dst[i] = make_float4(__uint_as_float(o[4 * i]) * inv_l,
+                                                     __uint_as_float(o[4 * i + 1]) * inv_l,
+                                                     __uint_as_float(o[4 * i + 2]) * inv_l,
+                                                     __uint_as_float(o[4 * i + 3]) * inv_l);
+                        } else {
+                            uint4* dst =
+                                reinterpret_cast<uint4*>(static_cast<T*>(p.O) + row_elem + cb * 32);
 #pragma unroll
-                for (int i = 0; i < 32; ++i) o[i] = 0u;
-            }
-            if (valid_row) {
-                if constexpr (kF32Out) {
-                    float4* dst = reinterpret_cast<float4*>(static_cast<float*>(p.O) + row_elem +
-                                                            cb * 32);
-#pragma unroll
-                    for (int i = 0; i < 8; ++i)
-                        dst[i] = make_float4(__uint_as_float(o[4 * i]) * inv_l,
-                                             __uint_as_float(o[4 * i + 1]) * inv_l,
-                                             __uint_as_float(o[4 * i + 2]) * inv_l,
-                                             __uint_as_float(o[4 * i + 3]) * inv_l);
-                } else {
-                    uint4* dst =
-                        reinterpret_cast<uint4*>(static_cast<T*>(p.O) + row_elem + cb * 32);
-#pragma unroll
-                    for (int i = 0; i < 4; ++i) {
-                        uint4 v;
-                        v.x = DType<T>::pack2(__uint_as_float(o[8 * i + 0]) * inv_l,
-                                              __uint_as_float(o[8 * i + 1]) * inv_l);
-                        v.y = DType<T>::pack2(__uint_as_float(o[8 * i + 2]) * inv_l,
-                                              __uint_as_float(o[8 * i + 3]) * inv_l);
-                        v.z = DType<T>::pack2(__uint_as_float(o[8 * i + 4]) * inv_l,
-                                              __uint_as_float(o[8 * i + 5]) * inv_l);
-                        v.w = DType<T>::pack2(__uint_as_float(o[8 * i + 6]) * inv_l,
-                                              __uint_as_float(o[8 * i + 7]) * inv_l);
-                        dst[i] = v;
+                            for (int i = 0; i < 4; ++i) {
+                                uint4 v;
+                                v.x = DType<T>::pack2(__uint_as_float(o[8 * i + 0]) * inv_l,
+                                                      __uint_as_float(o[8 * i + 1]) * inv_l);
+                                v.y = DType<T>::pack2(__uint_as_float(o[8 * i + 2]) * inv_l,
+                                                      __uint_as_float(o[8 * i + 3]) * inv_l);
+                                v.z = DType<T>::pack2(__uint_as_float(o[8 * i + 4]) * inv_l,
+                                                      __uint_as_float(o[8 * i + 5]) * inv_l);
+                                v.w = DType<T>::pack2(__uint_as_float(o[8 * i + 6]) * inv_l,
+                                                      __uint_as_float(o[8 * i + 7]) * inv_l);
+                                dst[i] = v;
+                            }
+                        }
                     }
                 }
+                if (valid_row) {
+                    p.L[static_cast<size_t>(it.bh) * p.seq_q + row] =
+                        l_run > 0.f ? (m_run + log2f(l_run)) * kLn2 : -INFINITY;
+                }
+                // The next item's first P store (and its bar_p arrival) follows
+                // these TMEM reads of O_t, so its PV product cannot overwrite
+                // O_t early.
             }
-        }
-        if (valid_row) {
-            p.L[static_cast<size_t>(bh) * p.seq_q + row] =
-                l_run > 0.f ? (m_run + log2f(l_run)) * kLn2 : -INFINITY;
         }
     }
 
@@ -522,8 +670,16 @@ FlashAttentionError launch_typed(const T* Q, const T* K, const T* V, void* O, fl
     prm.scale_log2 = fmaxf(scale * kLog2e, 1e-30f);
     prm.q_offset = q_offset;
     prm.k_offset = k_offset;
-    if (BH > 65535) return FlashAttentionError::CUDA_ERROR;
-    dim3 grid(static_cast<unsigned>(prm.num_ctiles), static_cast<unsigned>(BH));
+    prm.npairs = (prm.num_ctiles + 1) / 2;
+    const int sms = current_sm_count();
+    long long units = static_cast<long long>(BH) * prm.npairs;
+    prm.paired = units >= sms ? 1 : 0;
+    if (!prm.paired) units = static_cast<long long>(BH) * prm.num_ctiles;
+    if (units > 0x7fffffffLL) return FlashAttentionError::CUDA_ERROR;
+    prm.num_units = static_cast<int>(units);
+    // persistent: one CTA per SM (the shared-memory footprint allows one)
+    const int grid = static_cast<int>(std::min<long long>(units, sms));
+    if (grid <= 0) return FlashAttentionError::SUCCESS;
     kern<<<grid, 384, G::kSmemBytes, stream>>>(mq, mk, mv, prm);
     return cudaGetLastError() == cudaSuccess ? FlashAttentionError::SUCCESS
                                              : FlashAttentionError::CUDA_ERROR;
