@@ -22,7 +22,10 @@
 //                 S^T  = K_j Q_i^T    -> TMEM [0,128)
 //                 dV  += P^T dO_i     (A = P^T from TMEM)   -> TMEM [256,256+D)
 //                 dK  += dS^T Q_i     (A = dS^T from TMEM)  -> TMEM [384,384+D)
-//                 dQ_i = dS K_j (or dQ_i^T = K_j^T dS^T)    -> TMEM [0,128)
+//                 dQ_i = dS K_j (or dQ_i^T = K_j^T dS^T)    -> TMEM [128,256)
+//               in the order dV, dK, dQ_i, S^T_{i+1}, then (once the drain
+//               warps have read dQ_i) dP^T_{i+1}, so S^T_{i+1} runs while
+//               dQ_i is drained.
 //   warps 4-11  two warpgroups, one thread per K/V row (TMEM lane) each,
 //               splitting the 128 query columns in halves: P^T, dS^T from
 //               S^T, dP^T; P^T and dS^T go back into TMEM (fp16/bf16) and dS^T
@@ -105,6 +108,28 @@ __device__ __forceinline__ uint64_t bmnmajor_desc(uint32_t tile_base, int kk) {
     using G = BwdGeom<D>;
     const uint32_t addr = tile_base + static_cast<uint32_t>(kk) * 16u * G::kSwz;
     return sm100::make_smem_desc(addr, G::kCbBytes, 8 * G::kSwz, G::kLayout);
+}
+
+// Descriptor of k-step kk = descriptor of k-step 0 + these (start address
+// field, 16-byte units; shared addresses stay below 2^18, so no carry).
+template <int D>
+__host__ __device__ constexpr uint32_t bk_delta(int kk) {
+    using G = BwdGeom<D>;
+    return ((static_cast<uint32_t>(kk) * 32u / G::kSwz) * G::kCbBytes +
+            (static_cast<uint32_t>(kk) * 32u % G::kSwz)) >> 4;
+}
+template <int D>
+__host__ __device__ constexpr uint32_t bmn_delta(int kk) {
+    return (static_cast<uint32_t>(kk) * 16u * BwdGeom<D>::kSwz) >> 4;
+}
+__host__ __device__ constexpr uint32_t ds_delta(int kk) { return static_cast<uint32_t>(kk) * 128u; }
+
+// Keeps a descriptor opaque to the optimiser, so that the per-k-step
+// descriptors derived from it are not hoisted out of the loops into live
+// registers of the (register-starved) MMA warp.
+__device__ __forceinline__ uint64_t opaque(uint64_t d) {
+    asm volatile("" : "+l"(d));
+    return d;
 }
 
 // dS tile: [128 kv rows][128 q], two 64-column SW128 blocks; as the MN-major
@@ -292,7 +317,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     // reads S^T / dP^T columns [64h, 64h+64) and writes P^T / dS^T (16-bit,
     // two per column) into columns [64h, 64h+32) of the same regions, so the
     // two warpgroups never touch each other's columns.  dQ (or dQ^T) is then
-    // written by an MMA over the S^T columns.
+    // written by an MMA over the dP^T columns.
     //
     // Registers: launched with 128 per thread (512 x 128 = 65536).
     // warpgroup 0 (producer, MMA, 2 idle) -> 56, the drain -> 152, the two
@@ -345,63 +370,96 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
             const uint32_t sK = sbase + G::kOffK, sV = sbase + G::kOffV, sDs = sbase + G::kOffDs;
             // TMEM column of k-step kk (16 queries) of a P^T / dS^T operand
             auto acol = [](int kk) { return static_cast<uint32_t>(kk < 4 ? kk * 8 : 64 + (kk - 4) * 8); };
-            bool ok = mbar_wait(bar_kv, 0, abort_flag, &g_bwd_status);
+            auto stage_q = [&](int it) {
+                return sbase + G::kOffStage + static_cast<uint32_t>(it % G::kStages) * G::kStageBytes;
+            };
+            // dP^T = V_j dO_i^T -> TMEM [128, 256)
+            auto issue_dp = [&](uint32_t sdO) {
+                const uint64_t a0 = opaque(bkmajor_desc<D>(sV, 0));
+                const uint64_t b0 = opaque(bkmajor_desc<D>(sdO, 0));
+#pragma unroll
+                for (int kk = 0; kk < D / 16; ++kk)
+                    mma_f16_ss(tmem + 128, a0 + bk_delta<D>(kk), b0 + bk_delta<D>(kk), idesc_ss,
+                               kk > 0 ? 1u : 0u);
+            };
+            // S^T = K_j Q_i^T -> TMEM [0, 128)
+            auto issue_s = [&](uint32_t sQ) {
+                const uint64_t a0 = opaque(bkmajor_desc<D>(sK, 0));
+                const uint64_t b0 = opaque(bkmajor_desc<D>(sQ, 0));
+#pragma unroll
+                for (int kk = 0; kk < D / 16; ++kk)
+                    mma_f16_ss(tmem, a0 + bk_delta<D>(kk), b0 + bk_delta<D>(kk), idesc_ss,
+                               kk > 0 ? 1u : 0u);
+            };
+            bool ok = mbar_wait(bar_kv, 0, abort_flag, &g_bwd_status) &&
+                      mbar_wait(full, 0, abort_flag, &g_bwd_status);
+            if (ok && n_it > 0) {
+                tc_fence_after();
+                issue_dp(stage_q(0) + G::kTileBytes);
+                issue_s(stage_q(0));
+                tc_commit(bar_sdp);
+            }
             for (int it = 0; ok && it < n_it; ++it) {
                 const int s = it % G::kStages;
-                const uint32_t sQ = sbase + G::kOffStage + s * G::kStageBytes;
+                const uint32_t sQ = stage_q(it);
                 const uint32_t sdO = sQ + G::kTileBytes;
-                if (!mbar_wait(full + s, (it / G::kStages) & 1, abort_flag, &g_bwd_status)) {
-                    ok = false;
-                    break;
-                }
-                tc_fence_after();
-                // dP^T = V_j dO_i^T (its columns were last read by dK of it-1)
-#pragma unroll
-                for (int kk = 0; kk < D / 16; ++kk)
-                    mma_f16_ss(tmem + 128, bkmajor_desc<D>(sV, kk), bkmajor_desc<D>(sdO, kk),
-                               idesc_ss, kk > 0 ? 1u : 0u);
-                if (it > 0) {
-                    // S columns hold dQ of it-1 until the drain warps have read it
-                    if (!mbar_wait(bar_dqfree, (it - 1) & 1, abort_flag, &g_bwd_status)) {
-                        ok = false;
-                        break;
-                    }
-                    tc_fence_after();
-                }
-#pragma unroll
-                for (int kk = 0; kk < D / 16; ++kk)
-                    mma_f16_ss(tmem, bkmajor_desc<D>(sK, kk), bkmajor_desc<D>(sQ, kk), idesc_ss,
-                               kk > 0 ? 1u : 0u);
-                tc_commit(bar_sdp);
                 if (!mbar_wait(bar_ds, it & 1, abort_flag, &g_bwd_status)) {
                     ok = false;
                     break;
                 }
                 tc_fence_after();
                 // dV += P^T dO_i ; dK += dS^T Q_i  (K dimension = 128 query rows)
+                {
+                    const uint64_t bo = opaque(bmnmajor_desc<D>(sdO, 0));
 #pragma unroll
-                for (int kk = 0; kk < 8; ++kk)
-                    mma_f16_ts(tmem + 256, tmem + acol(kk), bmnmajor_desc<D>(sdO, kk), idesc_acc,
-                               (it > 0 || kk > 0) ? 1u : 0u);
+                    for (int kk = 0; kk < 8; ++kk)
+                        mma_f16_ts(tmem + 256, tmem + acol(kk), bo + bmn_delta<D>(kk), idesc_acc,
+                                   (it > 0 || kk > 0) ? 1u : 0u);
+                    const uint64_t bq = opaque(bmnmajor_desc<D>(sQ, 0));
 #pragma unroll
-                for (int kk = 0; kk < 8; ++kk)
-                    mma_f16_ts(tmem + 384, tmem + 128 + acol(kk), bmnmajor_desc<D>(sQ, kk),
-                               idesc_acc, (it > 0 || kk > 0) ? 1u : 0u);
+                    for (int kk = 0; kk < 8; ++kk)
+                        mma_f16_ts(tmem + 384, tmem + 128 + acol(kk), bq + bmn_delta<D>(kk),
+                                   idesc_acc, (it > 0 || kk > 0) ? 1u : 0u);
+                }
                 tc_commit(empty + s);
-                if constexpr (kTransposedDq) {
-                    // dQ_i^T = K_j^T dS^T (M = head_dim lanes, N = 128 queries)
+                // dQ_i goes into the dP^T columns, whose dS^T the dK product
+                // just read; the drain warps empty them before dP^T_{i+1}.
+                {
+                    const uint64_t kt0 = opaque(bmnmajor_desc<D>(sK, 0));
+                    const uint64_t ds0 = opaque(ds_desc(sDs, 0));
+                    if constexpr (kTransposedDq) {
+                        // dQ_i^T = K_j^T dS^T (M = head_dim lanes, N = 128 queries)
 #pragma unroll
-                    for (int kk = 0; kk < 8; ++kk)
-                        mma_f16_ss(tmem, bmnmajor_desc<D>(sK, kk), ds_desc(sDs, kk), idesc_dqt,
-                                   kk > 0 ? 1u : 0u);
-                } else {
-                    // dQ_i = dS K_j (M = 128 query lanes, N = head_dim)
+                        for (int kk = 0; kk < 8; ++kk)
+                            mma_f16_ss(tmem + 128, kt0 + bmn_delta<D>(kk), ds0 + ds_delta(kk),
+                                       idesc_dqt, kk > 0 ? 1u : 0u);
+                    } else {
+                        // dQ_i = dS K_j (M = 128 query lanes, N = head_dim)
 #pragma unroll
-                    for (int kk = 0; kk < 8; ++kk)
-                        mma_f16_ss(tmem, ds_desc(sDs, kk), bmnmajor_desc<D>(sK, kk), idesc_dq,
-                                   kk > 0 ? 1u : 0u);
+                        for (int kk = 0; kk < 8; ++kk)
+                            mma_f16_ss(tmem + 128, ds0 + ds_delta(kk), kt0 + bmn_delta<D>(kk),
+                                       idesc_dq, kk > 0 ? 1u : 0u);
+                    }
                 }
                 tc_commit(bar_dq);
+                if (it + 1 < n_it) {
+                    const uint32_t sQn = stage_q(it + 1);
+                    if (!mbar_wait(full + (it + 1) % G::kStages, ((it + 1) / G::kStages) & 1,
+                                   abort_flag, &g_bwd_status)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    // S^T columns: P^T was read by the dV product issued above
+                    issue_s(sQn);
+                    if (!mbar_wait(bar_dqfree, it & 1, abort_flag, &g_bwd_status)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    issue_dp(sQn + G::kTileBytes);
+                    tc_commit(bar_sdp);
+                }
             }
             tc_commit(bar_acc);
             tc_commit(bar_done);
@@ -526,7 +584,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         setmaxnreg_inc<152>();
         // ------------------------------------------------ dQ drain
         const int wq = warp & 3;
-        const uint32_t t_q = tmem + (static_cast<uint32_t>(wq * 32) << 16);
+        const uint32_t t_q = tmem + (static_cast<uint32_t>(wq * 32) << 16) + 128;
         if constexpr (kTransposedDq) {
             // lane = head_dim element d; TMEM column = query row of block i
             const int d = wq * 32 + lane;
@@ -538,7 +596,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
                 tmem_ld2_x32(t_q, v0, t_q + 32, v1);
                 tmem_ld2_x32(t_q + 64, v2, t_q + 96, v3);
                 // TMEM columns are free once loaded: release them before the
-                // reductions so the next S MMA is not held up
+                // reductions so the next dP MMA is not held up
                 tc_fence_before();
                 mbar_arrive(bar_dqfree);
                 float* dst = p.dq_acc + (static_cast<size_t>(bh) * p.N + i * 128) * D + d;
@@ -559,7 +617,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
             // 32x32 fp32 block from TMEM into a 128-byte-swizzled staging box
             // and the TMA unit adds the box into the fp32 accumulator.  Staging
             // lives in the dS buffer, idle from the completion of dQ_i until
-            // the MMA issues S_{i+1} (after this drain signals bar_dqfree).
+            // the softmax warps write dS_{i+1}, which they do only after
+            // dP^T_{i+1}, issued once this drain signals bar_dqfree.
             const uint32_t stage0 = sbase + G::kOffDs + wq * 8192;
             for (int it = 0; it < n_it; ++it) {
                 const int i = i0 + it;
