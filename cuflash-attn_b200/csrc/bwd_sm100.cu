@@ -53,9 +53,12 @@ __device__ int g_bwd_status;
 
 constexpr float kLog2eB = 1.4426950408889634f;
 // With kBwdExp2EmuEvery = k > 0, one pair of exponentials in k is computed on
-// the FMA pipe; measured not to pay on B200, so it is off.
+// the FMA pipe (exp2_poly2, relative error below 1e-4, far under the 16-bit
+// rounding that P and dS receive) instead of the MUFU unit, which the
+// pipelined softmax below saturates.  Measured on B200: k = 4 takes config 3
+// from 4.11 to 3.89 ms (k = 2: 3.99, k = 8: 3.97).
 #ifndef CUFLASH_BWD_EXP2_EMU_EVERY
-#define CUFLASH_BWD_EXP2_EMU_EVERY 0
+#define CUFLASH_BWD_EXP2_EMU_EVERY 4
 #endif
 constexpr int kBwdExp2EmuEvery = CUFLASH_BWD_EXP2_EMU_EVERY;
 
@@ -496,51 +499,67 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
                               h * 64;
             const float* sD = sL + 128;
             const bool diag = p.causal && (i == j);
+            const uint64_t c2 = f2_pack(c, c);
+            // 16-query sub-chunks; the next sub-chunk's S^T / dP^T columns are
+            // loaded while this one is computed.  P^T / dS^T of sub-chunk k
+            // go to columns [8k, 8k+8) of this warpgroup's S^T / dP^T range,
+            // which hold queries already loaded (sub-chunks 0..k/2).
+            uint32_t sA[16], dA[16], sB[16], dB[16];
+            tmem_ld2_x16_nw(t_s, sA, t_dp, dA);
+            tmem_wait_ld2_x16(sA, dA);
 #pragma unroll
-            for (int cc = 0; cc < 2; ++cc) {
-                uint32_t sv[32], dv[32];
-                tmem_ld2_x32(t_s + cc * 32, sv, t_dp + cc * 32, dv);
-                uint32_t pp[16], dd[16];
+            for (int k = 0; k < 4; ++k) {
+                uint32_t(&sv)[16] = (k & 1) ? sB : sA;
+                uint32_t(&dv)[16] = (k & 1) ? dB : dA;
+                uint32_t(&sn)[16] = (k & 1) ? sA : sB;
+                uint32_t(&dn)[16] = (k & 1) ? dA : dB;
+                if (k + 1 < 4) tmem_ld2_x16_nw(t_s + 16 * (k + 1), sn, t_dp + 16 * (k + 1), dn);
+                uint32_t pp[8], dd[8];
 #pragma unroll
-                for (int v = 0; v < 8; ++v) {
-                    const float4 lq = reinterpret_cast<const float4*>(sL + cc * 32)[v];
-                    const float4 dq = reinterpret_cast<const float4*>(sD + cc * 32)[v];
-                    const float la[4] = {lq.x, lq.y, lq.z, lq.w};
-                    const float da[4] = {dq.x, dq.y, dq.z, dq.w};
+                for (int v = 0; v < 4; ++v) {
+                    const float4 lq = reinterpret_cast<const float4*>(sL + 16 * k)[v];
+                    const float4 dq = reinterpret_cast<const float4*>(sD + 16 * k)[v];
 #pragma unroll
                     for (int u = 0; u < 2; ++u) {
-                        const int e = 2 * v + u;                  // pair index in the chunk
-                        const int q0 = h * 64 + cc * 32 + 2 * e;  // query within block i
-                        const float x0 = fmaf(__uint_as_float(sv[2 * e]), c, -la[2 * u]);
-                        const float x1 = fmaf(__uint_as_float(sv[2 * e + 1]), c, -la[2 * u + 1]);
+                        const int e = 2 * v + u;                 // pair index in the sub-chunk
+                        const int q0 = h * 64 + 16 * k + 2 * e;  // query within block i
+                        const float l0 = u ? lq.z : lq.x, l1 = u ? lq.w : lq.y;
+                        const float g0 = u ? dq.z : dq.x, g1 = u ? dq.w : dq.y;
+                        const float2 xx = f2_unpack(
+                            f2_fma(f2_pack(__uint_as_float(sv[2 * e]), __uint_as_float(sv[2 * e + 1])),
+                                   c2, f2_pack(-l0, -l1)));
                         float p0, p1;
-                        if (kBwdExp2EmuEvery > 0 && (e % kBwdExp2EmuEvery) == kBwdExp2EmuEvery - 1) {
-                            const float2 ex = exp2_poly2(x0, x1);  // FMA pipe
+                        if (kBwdExp2EmuEvery > 0 &&
+                            (e % (kBwdExp2EmuEvery > 0 ? kBwdExp2EmuEvery : 1)) == kBwdExp2EmuEvery - 1) {
+                            const float2 ex = exp2_poly2(xx.x, xx.y);  // FMA pipe
                             p0 = ex.x;
                             p1 = ex.y;
                         } else {
-                            p0 = ex2_approx(x0);  // MUFU
-                            p1 = ex2_approx(x1);
+                            p0 = ex2_approx(xx.x);  // MUFU
+                            p1 = ex2_approx(xx.y);
                         }
                         if (diag) {
                             if (q0 < r) p0 = 0.f;
                             if (q0 + 1 < r) p1 = 0.f;
                         }
-                        const float d0 = p0 * (__uint_as_float(dv[2 * e]) - da[2 * u]);
-                        const float d1 = p1 * (__uint_as_float(dv[2 * e + 1]) - da[2 * u + 1]);
+                        const uint64_t p2 = f2_pack(p0, p1);
+                        const float2 d = f2_unpack(f2_mul(
+                            p2, f2_add(f2_pack(__uint_as_float(dv[2 * e]), __uint_as_float(dv[2 * e + 1])),
+                                       f2_pack(-g0, -g1))));
                         pp[e] = DType<T>::pack2(p0, p1);
-                        dd[e] = DType<T>::pack2(d0, d1);
+                        dd[e] = DType<T>::pack2(d.x, d.y);
                     }
                 }
                 // P^T and dS^T overwrite columns this thread has already read
-                tmem_st_x16_nw(t_s + cc * 16, pp);
-                tmem_st_x16_nw(t_dp + cc * 16, dd);
+                tmem_st_x8_nw(t_s + 8 * k, pp);
+                tmem_st_x8_nw(t_dp + 8 * k, dd);
 #pragma unroll
-                for (int k = 0; k < 4; ++k) {
-                    const int chunk = cc * 4 + k;
+                for (int q = 0; q < 2; ++q) {
+                    const int chunk = 2 * k + q;
                     const uint32_t addr = sDs + ((chunk ^ (r & 7)) << 4);
-                    st_shared_v4(addr, dd[4 * k], dd[4 * k + 1], dd[4 * k + 2], dd[4 * k + 3]);
+                    st_shared_v4(addr, dd[4 * q], dd[4 * q + 1], dd[4 * q + 2], dd[4 * q + 3]);
                 }
+                if (k + 1 < 4) tmem_wait_ld2_x16(sn, dn);
             }
             tmem_wait_st();
             fence_proxy_async_smem();
