@@ -89,8 +89,8 @@ struct BwdParams {
     float* dq_acc;
     void* dK;
     void* dV;
-    const float* l2p;  // L * log2(e), padded to n_blk*128 per (b,h) with +inf
-    const float* dvp;  // rowsum(dO*O), padded with 0
+    const float* l2p;  // -L * log2(e), padded to n_blk*128 per (b,h) with -inf
+    const float* dvp;  // -rowsum(dO*O), padded with 0
     int N;
     int n_blk;
     int causal;
@@ -197,38 +197,46 @@ __device__ __forceinline__ void fence_proxy_async_smem() {
 
 // ---------------------------------------------------------------- preprocess
 
+// D/8 threads per query row, 16-byte loads of O and dO; writes -L*log2(e)
+// and -rowsum(dO*O) (the negated forms feed the softmax's fused multiply-adds
+// directly) and zeroes the row of the fp32 dQ accumulator.
 template <typename T, int D>
 __global__ void __launch_bounds__(256)
     bwd_preprocess_kernel(const T* __restrict__ O, const T* __restrict__ dO,
-                          const float* __restrict__ L, float* __restrict__ l2p,
-                          float* __restrict__ dvp, float* __restrict__ dq_acc, int N, int N_pad,
+                          const float* __restrict__ L, float* __restrict__ nl2,
+                          float* __restrict__ nd, float* __restrict__ dq_acc, int N, int N_pad,
                           long long rows_pad) {
-    constexpr int E = D / 32;  // elements per lane
-    const int lane = threadIdx.x & 31;
-    const long long r = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
-    if (r >= rows_pad) return;
-    const long long bh = r / N_pad;
-    const int q = static_cast<int>(r - bh * N_pad);
-    if (q >= N) {
-        if (lane == 0) {
-            l2p[r] = INFINITY;
-            dvp[r] = 0.f;
-        }
-        return;
-    }
+    constexpr int kTpr = D / 8;  // threads per row: 16, 8 or 4 (groups never straddle a warp)
+    const long long gt = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+    const long long r = gt / kTpr;
+    const int part = static_cast<int>(gt - r * kTpr);
+    const bool in_range = r < rows_pad;
+    const long long bh = in_range ? r / N_pad : 0;
+    const int q = in_range ? static_cast<int>(r - bh * N_pad) : 0;
+    const bool real = in_range && q < N;
     const long long row = bh * N + q;
     float acc = 0.f;
+    if (real) {
+        const uint4 o = *reinterpret_cast<const uint4*>(O + row * D + part * 8);
+        const uint4 g = *reinterpret_cast<const uint4*>(dO + row * D + part * 8);
+        const uint32_t ow[4] = {o.x, o.y, o.z, o.w};
+        const uint32_t gw[4] = {g.x, g.y, g.z, g.w};
 #pragma unroll
-    for (int e = 0; e < E; ++e) {
-        const int d = lane * E + e;
-        acc = fmaf(DType<T>::to_float(O[row * D + d]), DType<T>::to_float(dO[row * D + d]), acc);
-        dq_acc[row * D + d] = 0.f;
+        for (int e = 0; e < 4; ++e) {
+            const float2 of = DType<T>::unpack2(ow[e]);
+            const float2 gf = DType<T>::unpack2(gw[e]);
+            acc = fmaf(of.x, gf.x, acc);
+            acc = fmaf(of.y, gf.y, acc);
+        }
+        float4* z = reinterpret_cast<float4*>(dq_acc + row * D + part * 8);
+        z[0] = make_float4(0.f, 0.f, 0.f, 0.f);
+        z[1] = make_float4(0.f, 0.f, 0.f, 0.f);
     }
 #pragma unroll
-    for (int off = 16; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
-    if (lane == 0) {
-        l2p[r] = L[row] * kLog2eB;
-        dvp[r] = acc;
+    for (int off = kTpr / 2; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
+    if (in_range && part == 0) {
+        nl2[r] = real ? -L[row] * kLog2eB : -INFINITY;
+        nd[r] = -acc;
     }
 }
 
@@ -244,6 +252,76 @@ __global__ void __launch_bounds__(256)
         o.x = DType<T>::pack2(v.x * scale, v.y * scale);
         o.y = DType<T>::pack2(v.z * scale, v.w * scale);
         reinterpret_cast<uint2*>(dQ)[i] = o;
+    }
+}
+
+// P^T and dS^T of one (kv block, query block) pair for this thread's kv row r
+// (TMEM lane), warpgroup h covering queries [64h, 64h+64).  sL / sD hold
+// -L*log2(e) and -rowsum(dO*O) of those queries.  In 16-query sub-chunks, the
+// next sub-chunk's S^T / dP^T columns load while this one is computed.  P^T /
+// dS^T of sub-chunk k go to columns [8k, 8k+8) of the warpgroup's S^T / dP^T
+// range, which hold queries already loaded (sub-chunks 0..k/2).  kDiag masks
+// the keys above the causal diagonal (query < kv row).
+template <typename T, bool kDiag>
+__device__ __forceinline__ void bwd_softmax_block(uint32_t t_s, uint32_t t_dp, uint32_t sDs,
+                                                  const float* sL, const float* sD, float c,
+                                                  int h, int r) {
+    using namespace sm100;
+    const uint64_t c2 = f2_pack(c, c);
+    uint32_t sA[16], dA[16], sB[16], dB[16];
+    tmem_ld2_x16_nw(t_s, sA, t_dp, dA);
+    tmem_wait_ld2_x16(sA, dA);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        uint32_t(&sv)[16] = (k & 1) ? sB : sA;
+        uint32_t(&dv)[16] = (k & 1) ? dB : dA;
+        uint32_t(&sn)[16] = (k & 1) ? sA : sB;
+        uint32_t(&dn)[16] = (k & 1) ? dA : dB;
+        if (k + 1 < 4) tmem_ld2_x16_nw(t_s + 16 * (k + 1), sn, t_dp + 16 * (k + 1), dn);
+        uint32_t pp[8], dd[8];
+#pragma unroll
+        for (int v = 0; v < 4; ++v) {
+            const float4 lq = reinterpret_cast<const float4*>(sL + 16 * k)[v];
+            const float4 dq = reinterpret_cast<const float4*>(sD + 16 * k)[v];
+#pragma unroll
+            for (int u = 0; u < 2; ++u) {
+                const int e = 2 * v + u;                 // pair index in the sub-chunk
+                const int q0 = h * 64 + 16 * k + 2 * e;  // query within the block
+                const uint64_t nl = u ? f2_pack(lq.z, lq.w) : f2_pack(lq.x, lq.y);
+                const uint64_t ndv = u ? f2_pack(dq.z, dq.w) : f2_pack(dq.x, dq.y);
+                const float2 xx = f2_unpack(f2_fma(
+                    f2_pack(__uint_as_float(sv[2 * e]), __uint_as_float(sv[2 * e + 1])), c2, nl));
+                float p0, p1;
+                if (kBwdExp2EmuEvery > 0 &&
+                    (e % (kBwdExp2EmuEvery > 0 ? kBwdExp2EmuEvery : 1)) == kBwdExp2EmuEvery - 1) {
+                    const float2 ex = exp2_poly2(xx.x, xx.y);  // FMA pipe
+                    p0 = ex.x;
+                    p1 = ex.y;
+                } else {
+                    p0 = ex2_approx(xx.x);  // MUFU
+                    p1 = ex2_approx(xx.y);
+                }
+                if (kDiag) {
+                    if (q0 < r) p0 = 0.f;
+                    if (q0 + 1 < r) p1 = 0.f;
+                }
+                const float2 d = f2_unpack(f2_mul(
+                    f2_pack(p0, p1),
+                    f2_add(f2_pack(__uint_as_float(dv[2 * e]), __uint_as_float(dv[2 * e + 1])), ndv)));
+                pp[e] = DType<T>::pack2(p0, p1);
+                dd[e] = DType<T>::pack2(d.x, d.y);
+            }
+        }
+        // P^T and dS^T overwrite columns this thread has already read
+        tmem_st_x8_nw(t_s + 8 * k, pp);
+        tmem_st_x8_nw(t_dp + 8 * k, dd);
+#pragma unroll
+        for (int q = 0; q < 2; ++q) {
+            const int chunk = 2 * k + q;
+            st_shared_v4(sDs + ((chunk ^ (r & 7)) << 4), dd[4 * q], dd[4 * q + 1], dd[4 * q + 2],
+                         dd[4 * q + 3]);
+        }
+        if (k + 1 < 4) tmem_wait_ld2_x16(sn, dn);
     }
 }
 
@@ -498,69 +576,10 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
                                                              s * G::kStageBytes + 2 * G::kTileBytes) +
                               h * 64;
             const float* sD = sL + 128;
-            const bool diag = p.causal && (i == j);
-            const uint64_t c2 = f2_pack(c, c);
-            // 16-query sub-chunks; the next sub-chunk's S^T / dP^T columns are
-            // loaded while this one is computed.  P^T / dS^T of sub-chunk k
-            // go to columns [8k, 8k+8) of this warpgroup's S^T / dP^T range,
-            // which hold queries already loaded (sub-chunks 0..k/2).
-            uint32_t sA[16], dA[16], sB[16], dB[16];
-            tmem_ld2_x16_nw(t_s, sA, t_dp, dA);
-            tmem_wait_ld2_x16(sA, dA);
-#pragma unroll
-            for (int k = 0; k < 4; ++k) {
-                uint32_t(&sv)[16] = (k & 1) ? sB : sA;
-                uint32_t(&dv)[16] = (k & 1) ? dB : dA;
-                uint32_t(&sn)[16] = (k & 1) ? sA : sB;
-                uint32_t(&dn)[16] = (k & 1) ? dA : dB;
-                if (k + 1 < 4) tmem_ld2_x16_nw(t_s + 16 * (k + 1), sn, t_dp + 16 * (k + 1), dn);
-                uint32_t pp[8], dd[8];
-#pragma unroll
-                for (int v = 0; v < 4; ++v) {
-                    const float4 lq = reinterpret_cast<const float4*>(sL + 16 * k)[v];
-                    const float4 dq = reinterpret_cast<const float4*>(sD + 16 * k)[v];
-#pragma unroll
-                    for (int u = 0; u < 2; ++u) {
-                        const int e = 2 * v + u;                 // pair index in the sub-chunk
-                        const int q0 = h * 64 + 16 * k + 2 * e;  // query within block i
-                        const float l0 = u ? lq.z : lq.x, l1 = u ? lq.w : lq.y;
-                        const float g0 = u ? dq.z : dq.x, g1 = u ? dq.w : dq.y;
-                        const float2 xx = f2_unpack(
-                            f2_fma(f2_pack(__uint_as_float(sv[2 * e]), __uint_as_float(sv[2 * e + 1])),
-                                   c2, f2_pack(-l0, -l1)));
-                        float p0, p1;
-                        if (kBwdExp2EmuEvery > 0 &&
-                            (e % (kBwdExp2EmuEvery > 0 ? kBwdExp2EmuEvery : 1)) == kBwdExp2EmuEvery - 1) {
-                            const float2 ex = exp2_poly2(xx.x, xx.y);  // FMA pipe
-                            p0 = ex.x;
-                            p1 = ex.y;
-                        } else {
-                            p0 = ex2_approx(xx.x);  // MUFU
-                            p1 = ex2_approx(xx.y);
-                        }
-                        if (diag) {
-                            if (q0 < r) p0 = 0.f;
-                            if (q0 + 1 < r) p1 = 0.f;
-                        }
-                        const uint64_t p2 = f2_pack(p0, p1);
-                        const float2 d = f2_unpack(f2_mul(
-                            p2, f2_add(f2_pack(__uint_as_float(dv[2 * e]), __uint_as_float(dv[2 * e + 1])),
-                                       f2_pack(-g0, -g1))));
-                        pp[e] = DType<T>::pack2(p0, p1);
-                        dd[e] = DType<T>::pack2(d.x, d.y);
-                    }
-                }
-                // P^T and dS^T overwrite columns this thread has already read
-                tmem_st_x8_nw(t_s + 8 * k, pp);
-                tmem_st_x8_nw(t_dp + 8 * k, dd);
-#pragma unroll
-                for (int q = 0; q < 2; ++q) {
-                    const int chunk = 2 * k + q;
-                    const uint32_t addr = sDs + ((chunk ^ (r & 7)) << 4);
-                    st_shared_v4(addr, dd[4 * q], dd[4 * q + 1], dd[4 * q + 2], dd[4 * q + 3]);
-                }
-                if (k + 1 < 4) tmem_wait_ld2_x16(sn, dn);
-            }
+            if (p.causal && i == j)
+                bwd_softmax_block<T, true>(t_s, t_dp, sDs, sL, sD, c, h, r);
+            else
+                bwd_softmax_block<T, false>(t_s, t_dp, sDs, sL, sD, c, h, r);
             tmem_wait_st();
             fence_proxy_async_smem();
             tc_fence_before();
@@ -721,7 +740,7 @@ FlashAttentionError bwd_typed(const T* Q, const T* K, const T* V, const T* O, co
     if (n_blk > 0x7fffffff / 1) return fail(FlashAttentionError::CUDA_ERROR);
 
     const long long rows_pad = static_cast<long long>(BH) * n_pad;
-    const long long pre_blocks = (rows_pad * 32 + 255) / 256;
+    const long long pre_blocks = (rows_pad * (D / 8) + 255) / 256;
     bwd_preprocess_kernel<T, D><<<static_cast<unsigned>(pre_blocks), 256, 0, stream>>>(
         O, dO, L, l2p, dvp, dq_acc, N, static_cast<int>(n_pad), rows_pad);
     if (cudaGetLastError() != cudaSuccess) return fail(FlashAttentionError::CUDA_ERROR);
