@@ -40,6 +40,7 @@
 // CTAs of one (batch, head) are adjacent in launch order, so the dQ
 // accumulator tiles they reduce into stay resident in L2.
 
+#include <algorithm>
 #include <cmath>
 
 #include "common.cuh"
@@ -93,10 +94,41 @@ struct BwdParams {
     const float* dvp;  // -rowsum(dO*O), padded with 0
     int N;
     int n_blk;
+    int npairs;     // (n_blk + 1) / 2
+    int paired;     // 1: a unit is a (heavy, light) pair of kv blocks; 0: one kv block
+    int num_units;  // BH * npairs, or BH * n_blk when not paired
     int causal;
     float scale_log2;
     float scale;
 };
+
+// One work item = one 128-row K/V block j of one (b,h).  Unit u of the
+// persistent schedule holds two items of the same (b,h): kv blocks j = k and
+// j = n_blk-1-k.  Under a causal mask block j visits n_blk-j query blocks, so
+// every unit costs n_blk+1 blocks and a round-robin of units over the CTAs is
+// balanced; both items read the same Q, dO and dQ rows, which stay in L2.
+// Non-causal problems, and problems with fewer units than SMs, use one item
+// per unit instead.
+struct BwdItem {
+    int j;
+    int bh;
+};
+
+__device__ __forceinline__ bool bwd_item(const BwdParams& p, int u, int w, BwdItem& it) {
+    if (!p.paired) {
+        if (w == 1) return false;
+        it.bh = u / p.n_blk;
+        it.j = u - it.bh * p.n_blk;  // ascending j: heaviest first under a causal mask
+        return true;
+    }
+    const int bh = u / p.npairs;
+    const int k = u - bh * p.npairs;
+    const int j = w == 0 ? k : p.n_blk - 1 - k;
+    if (w == 1 && j == k) return false;  // middle block of an odd count
+    it.j = j;
+    it.bh = bh;
+    return true;
+}
 
 template <int D>
 __device__ __forceinline__ uint64_t bkmajor_desc(uint32_t tile_base, int kk) {
@@ -350,24 +382,20 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     }
     uint8_t* sptr = smem_raw;
     uint64_t* bars = reinterpret_cast<uint64_t*>(sptr + G::kOffBar);
-    uint64_t* bar_kv = bars;
+    uint64_t* bar_kv = bars;  // K_j, V_j of the current item landed
     uint64_t* full = bars + 1;
     uint64_t* empty = full + G::kStages;
     uint64_t* bar_sdp = empty + G::kStages;
     uint64_t* bar_ds = bar_sdp + 1;
     uint64_t* bar_dq = bar_ds + 1;
     uint64_t* bar_dqfree = bar_dq + 1;
-    uint64_t* bar_acc = bar_dqfree + 1;
+    uint64_t* bar_acc = bar_dqfree + 1;  // all MMAs of the item retired (dV, dK final; K, V free)
     uint64_t* bar_done = bar_acc + 1;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar_done + 1);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
-    const int j = blockIdx.x;  // kv block
-    const int bh = blockIdx.y;
-    const int i0 = p.causal ? j : 0;
-    const int n_it = p.n_blk - i0;
 
     if (threadIdx.x == 0) {
         mbar_init(bar_kv, 1);
@@ -393,6 +421,11 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
 
+    // Every role walks the same static list of work items (bwd_item).  The
+    // query-block counter g runs across items, so the stage ring and the
+    // per-block barrier phases continue from one item to the next; bar_kv and
+    // bar_acc complete once per item.
+    //
     // TMEM columns: S^T [0,128), dP^T [128,256), dV [256,256+D), dK [384,384+D).
     // Softmax warpgroup h (h = 0, 1) owns query columns [64h, 64h+64): it
     // reads S^T / dP^T columns [64h, 64h+64) and writes P^T / dS^T (16-bit,
@@ -411,22 +444,16 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
             prefetch_tmap(&tmK);
             prefetch_tmap(&tmV);
             prefetch_tmap(&tmdO);
-            mbar_arrive_expect_tx(bar_kv, 2 * G::kTileBytes);
-            for (int cb = 0; cb < G::kNumCb; ++cb) {
-                tma_load_3d(sptr + G::kOffK + cb * G::kCbBytes, &tmK, bar_kv, cb * G::kCbElems,
-                            j * 128, bh);
-                tma_load_3d(sptr + G::kOffV + cb * G::kCbBytes, &tmV, bar_kv, cb * G::kCbElems,
-                            j * 128, bh);
-            }
-            const size_t lrow = static_cast<size_t>(bh) * p.n_blk * 128;
-            int issued = 0;
-            for (int it = 0; it < n_it; ++it) {
-                const int i = i0 + it;
-                const int s = it % G::kStages;
-                if (it >= G::kStages &&
-                    !mbar_wait(empty + s, ((it / G::kStages) & 1) ^ 1, abort_flag, &g_bwd_status))
-                    break;
+            uint32_t g = 0;        // stage loads issued
+            uint32_t items = 0;    // K/V loads issued
+            bool ok = true;
+            auto load_stage = [&](int bh, int i) {
+                const int s = g % G::kStages;
+                if (g >= G::kStages &&
+                    !mbar_wait(empty + s, ((g / G::kStages) & 1) ^ 1, abort_flag, &g_bwd_status))
+                    return false;
                 uint8_t* st = sptr + G::kOffStage + s * G::kStageBytes;
+                const size_t lrow = static_cast<size_t>(bh) * p.n_blk * 128;
                 mbar_arrive_expect_tx(full + s, 2 * G::kTileBytes + 1024);
                 for (int cb = 0; cb < G::kNumCb; ++cb) {
                     tma_load_3d(st + cb * G::kCbBytes, &tmQ, full + s, cb * G::kCbElems, i * 128,
@@ -436,11 +463,39 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
                 }
                 bulk_load(st + 2 * G::kTileBytes, p.l2p + lrow + i * 128, 512, full + s);
                 bulk_load(st + 2 * G::kTileBytes + 512, p.dvp + lrow + i * 128, 512, full + s);
-                ++issued;
+                ++g;
+                return true;
+            };
+            for (int u = blockIdx.x; ok && u < p.num_units; u += gridDim.x) {
+                for (int w = 0; ok && w < 2; ++w) {
+                    BwdItem itm;
+                    if (!bwd_item(p, u, w, itm)) continue;
+                    const int i0 = p.causal ? itm.j : 0;
+                    const int n_it = p.n_blk - i0;
+                    // The item's first stages only need free ring slots, so they go
+                    // ahead of K_j, V_j, which wait for the previous item's MMAs
+                    // (the first item loads K_j, V_j first).
+                    const int pre = items == 0 ? 0 : min(n_it, G::kStages);
+                    for (int it = 0; ok && it < pre; ++it) ok = load_stage(itm.bh, i0 + it);
+                    // K_j, V_j: the previous item's MMAs must be done with the buffers
+                    if (ok && items > 0)
+                        ok = mbar_wait(bar_acc, (items - 1) & 1, abort_flag, &g_bwd_status);
+                    if (!ok) break;
+                    mbar_arrive_expect_tx(bar_kv, 2 * G::kTileBytes);
+                    for (int cb = 0; cb < G::kNumCb; ++cb) {
+                        tma_load_3d(sptr + G::kOffK + cb * G::kCbBytes, &tmK, bar_kv,
+                                    cb * G::kCbElems, itm.j * 128, itm.bh);
+                        tma_load_3d(sptr + G::kOffV + cb * G::kCbBytes, &tmV, bar_kv,
+                                    cb * G::kCbElems, itm.j * 128, itm.bh);
+                    }
+                    ++items;
+                    for (int it = pre; ok && it < n_it; ++it) ok = load_stage(itm.bh, i0 + it);
+                }
             }
-            bdrain_wait(bar_kv, 0);
-            for (int it = max(0, issued - G::kStages); it < issued; ++it)
-                bdrain_wait(full + it % G::kStages, (it / G::kStages) & 1);
+            // every issued load must land before the CTA can exit
+            if (items > 0) bdrain_wait(bar_kv, (items - 1) & 1);
+            for (uint32_t q = g > G::kStages ? g - G::kStages : 0; q < g; ++q)
+                bdrain_wait(full + q % G::kStages, (q / G::kStages) & 1);
         } else if (warp == 1 && lane == 0) {
             // ------------------------------------------------ MMA issuer
             constexpr uint32_t kFmt = DType<T>::kMmaFmt;
@@ -472,77 +527,98 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
                     mma_f16_ss(tmem, a0 + bk_delta<D>(kk), b0 + bk_delta<D>(kk), idesc_ss,
                                kk > 0 ? 1u : 0u);
             };
-            bool ok = mbar_wait(bar_kv, 0, abort_flag, &g_bwd_status) &&
-                      mbar_wait(full, 0, abort_flag, &g_bwd_status);
-            if (ok && n_it > 0) {
-                tc_fence_after();
-                issue_dp(stage_q(0) + G::kTileBytes);
-                issue_s(stage_q(0));
-                tc_commit(bar_sdp);
-            }
-            for (int it = 0; ok && it < n_it; ++it) {
-                const int s = it % G::kStages;
-                const uint32_t sQ = stage_q(it);
-                const uint32_t sdO = sQ + G::kTileBytes;
-                if (!mbar_wait(bar_ds, it & 1, abort_flag, &g_bwd_status)) {
-                    ok = false;
-                    break;
-                }
-                tc_fence_after();
-                // dV += P^T dO_i ; dK += dS^T Q_i  (K dimension = 128 query rows)
-                {
-                    const uint64_t bo = opaque(bmnmajor_desc<D>(sdO, 0));
-#pragma unroll
-                    for (int kk = 0; kk < 8; ++kk)
-                        mma_f16_ts(tmem + 256, tmem + acol(kk), bo + bmn_delta<D>(kk), idesc_acc,
-                                   (it > 0 || kk > 0) ? 1u : 0u);
-                    const uint64_t bq = opaque(bmnmajor_desc<D>(sQ, 0));
-#pragma unroll
-                    for (int kk = 0; kk < 8; ++kk)
-                        mma_f16_ts(tmem + 384, tmem + 128 + acol(kk), bq + bmn_delta<D>(kk),
-                                   idesc_acc, (it > 0 || kk > 0) ? 1u : 0u);
-                }
-                tc_commit(empty + s);
-                // dQ_i goes into the dP^T columns, whose dS^T the dK product
-                // just read; the drain warps empty them before dP^T_{i+1}.
-                {
-                    const uint64_t kt0 = opaque(bmnmajor_desc<D>(sK, 0));
-                    const uint64_t ds0 = opaque(ds_desc(sDs, 0));
-                    if constexpr (kTransposedDq) {
-                        // dQ_i^T = K_j^T dS^T (M = head_dim lanes, N = 128 queries)
-#pragma unroll
-                        for (int kk = 0; kk < 8; ++kk)
-                            mma_f16_ss(tmem + 128, kt0 + bmn_delta<D>(kk), ds0 + ds_delta(kk),
-                                       idesc_dqt, kk > 0 ? 1u : 0u);
-                    } else {
-                        // dQ_i = dS K_j (M = 128 query lanes, N = head_dim)
-#pragma unroll
-                        for (int kk = 0; kk < 8; ++kk)
-                            mma_f16_ss(tmem + 128, ds0 + ds_delta(kk), kt0 + bmn_delta<D>(kk),
-                                       idesc_dq, kk > 0 ? 1u : 0u);
-                    }
-                }
-                tc_commit(bar_dq);
-                if (it + 1 < n_it) {
-                    const uint32_t sQn = stage_q(it + 1);
-                    if (!mbar_wait(full + (it + 1) % G::kStages, ((it + 1) / G::kStages) & 1,
-                                   abort_flag, &g_bwd_status)) {
+            uint32_t g = 0;      // query blocks consumed
+            uint32_t items = 0;  // items finished
+            bool ok = true;
+            for (int u = blockIdx.x; ok && u < p.num_units; u += gridDim.x) {
+                for (int w = 0; ok && w < 2; ++w) {
+                    BwdItem itm;
+                    if (!bwd_item(p, u, w, itm)) continue;
+                    const int n_it = p.n_blk - (p.causal ? itm.j : 0);
+                    // K_j, V_j and the item's first query block
+                    ok = mbar_wait(bar_kv, items & 1, abort_flag, &g_bwd_status) &&
+                         mbar_wait(full + g % G::kStages, (g / G::kStages) & 1, abort_flag,
+                                   &g_bwd_status);
+                    if (!ok) break;
+                    tc_fence_after();
+                    // S^T columns: the previous item's P^T was read by its last
+                    // dV product (issued earlier, so ordered before this one)
+                    issue_s(stage_q(g));
+                    // dP^T columns hold the previous block's dQ until drained
+                    if (g > 0 && !mbar_wait(bar_dqfree, (g - 1) & 1, abort_flag, &g_bwd_status)) {
                         ok = false;
                         break;
                     }
                     tc_fence_after();
-                    // S^T columns: P^T was read by the dV product issued above
-                    issue_s(sQn);
-                    if (!mbar_wait(bar_dqfree, it & 1, abort_flag, &g_bwd_status)) {
-                        ok = false;
-                        break;
-                    }
-                    tc_fence_after();
-                    issue_dp(sQn + G::kTileBytes);
+                    issue_dp(stage_q(g) + G::kTileBytes);
                     tc_commit(bar_sdp);
+                    for (int it = 0; ok && it < n_it; ++it, ++g) {
+                        const int s = g % G::kStages;
+                        const uint32_t sQ = stage_q(g);
+                        const uint32_t sdO = sQ + G::kTileBytes;
+                        if (!mbar_wait(bar_ds, g & 1, abort_flag, &g_bwd_status)) {
+                            ok = false;
+                            break;
+                        }
+                        tc_fence_after();
+                        // dV += P^T dO_i ; dK += dS^T Q_i  (K dimension = 128 query rows)
+                        {
+                            const uint64_t bo = opaque(bmnmajor_desc<D>(sdO, 0));
+#pragma unroll
+                            for (int kk = 0; kk < 8; ++kk)
+                                mma_f16_ts(tmem + 256, tmem + acol(kk), bo + bmn_delta<D>(kk), idesc_acc,
+                                           (it > 0 || kk > 0) ? 1u : 0u);
+                            const uint64_t bq = opaque(bmnmajor_desc<D>(sQ, 0));
+#pragma unroll
+                            for (int kk = 0; kk < 8; ++kk)
+                                mma_f16_ts(tmem + 384, tmem + 128 + acol(kk), bq + bmn_delta<D>(kk),
+                                           idesc_acc, (it > 0 || kk > 0) ? 1u : 0u);
+                        }
+                        tc_commit(empty + s);
+                        // dQ_i goes into the dP^T columns, whose dS^T the dK product
+                        // just read; the drain warps empty them before dP^T_{i+1}.
+                        {
+                            const uint64_t kt0 = opaque(bmnmajor_desc<D>(sK, 0));
+                            const uint64_t ds0 = opaque(ds_desc(sDs, 0));
+                            if constexpr (kTransposedDq) {
+                                // dQ_i^T = K_j^T dS^T (M = head_dim lanes, N = 128 queries)
+#pragma unroll
+                                for (int kk = 0; kk < 8; ++kk)
+                                    mma_f16_ss(tmem + 128, kt0 + bmn_delta<D>(kk), ds0 + ds_delta(kk),
+                                               idesc_dqt, kk > 0 ? 1u : 0u);
+                            } else {
+                                // dQ_i = dS K_j (M = 128 query lanes, N = head_dim)
+#pragma unroll
+                                for (int kk = 0; kk < 8; ++kk)
+                                    mma_f16_ss(tmem + 128, ds0 + ds_delta(kk), kt0 + bmn_delta<D>(kk),
+                                               idesc_dq, kk > 0 ? 1u : 0u);
+                            }
+                        }
+                        tc_commit(bar_dq);
+                        if (it + 1 < n_it) {
+                            const uint32_t sQn = stage_q(g + 1);
+                            if (!mbar_wait(full + (g + 1) % G::kStages, ((g + 1) / G::kStages) & 1,
+                                           abort_flag, &g_bwd_status)) {
+                                ok = false;
+                                break;
+                            }
+                            tc_fence_after();
+                            // S^T columns: P^T was read by the dV product issued above
+                            issue_s(sQn);
+                            if (!mbar_wait(bar_dqfree, g & 1, abort_flag, &g_bwd_status)) {
+                                ok = false;
+                                break;
+                            }
+                            tc_fence_after();
+                            issue_dp(sQn + G::kTileBytes);
+                            tc_commit(bar_sdp);
+                        }
+                    }
+                    if (!ok) break;
+                    tc_commit(bar_acc);
+                    ++items;
                 }
             }
-            tc_commit(bar_acc);
             tc_commit(bar_done);
             volatile int never = 0;
             mbar_wait(bar_done, 0, &never, &g_bwd_status);
@@ -559,63 +635,77 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         const uint32_t t_dp = tmem + lane_addr + 128 + h * 64;
         const uint32_t sDs = sbase + G::kOffDs + h * (128 * 128) + r * 128;
         const float c = p.scale_log2;
+        uint32_t g = 0, items = 0;
         bool ok = true;
-        for (int it = 0; it < n_it; ++it) {
-            const int i = i0 + it;
-            const int s = it % G::kStages;
-            // L and D of block i arrived through the async proxy: observe the
-            // stage's own barrier before reading them (it completes before S
-            // is issued, so waiting for it first costs nothing)
-            if (!bwarp_wait(full + s, (it / G::kStages) & 1, abort_flag) ||
-                !bwarp_wait(bar_sdp, it & 1, abort_flag)) {
-                ok = false;
-                break;
-            }
-            tc_fence_after();
-            const float* sL = reinterpret_cast<const float*>(sptr + G::kOffStage +
-                                                             s * G::kStageBytes + 2 * G::kTileBytes) +
-                              h * 64;
-            const float* sD = sL + 128;
-            if (p.causal && i == j)
-                bwd_softmax_block<T, true>(t_s, t_dp, sDs, sL, sD, c, h, r);
-            else
-                bwd_softmax_block<T, false>(t_s, t_dp, sDs, sL, sD, c, h, r);
-            tmem_wait_st();
-            fence_proxy_async_smem();
-            tc_fence_before();
-            mbar_arrive(bar_ds);
-        }
-        if (ok) {
-            ok = bwarp_wait(bar_acc, 0, abort_flag);
-            tc_fence_after();
-        }
-        // warpgroup 0 stores dV, warpgroup 1 stores dK (scaled)
-        const int kv = j * 128 + r;
-        const bool valid = kv < p.N;
-        const size_t row = (static_cast<size_t>(bh) * p.N + kv) * D;
-        T* dst_base = static_cast<T*>(h == 0 ? p.dV : p.dK);
-        const float mul = h == 0 ? 1.f : p.scale;
-        const uint32_t t_acc = tmem + lane_addr + (h == 0 ? 256 : 384);
-#pragma unroll
-        for (int cb = 0; cb < D / 32; ++cb) {
-            uint32_t a[32];
-            if (ok) {
-                tmem_ld_x32(t_acc + cb * 32, a);
-            } else {
-#pragma unroll
-                for (int e = 0; e < 32; ++e) a[e] = 0u;
-            }
-            if (valid) {
-                uint4* dst = reinterpret_cast<uint4*>(dst_base + row + cb * 32);
-#pragma unroll
-                for (int q4 = 0; q4 < 4; ++q4) {
-                    uint4 v;
-                    v.x = DType<T>::pack2(__uint_as_float(a[8 * q4 + 0]) * mul, __uint_as_float(a[8 * q4 + 1]) * mul);
-                    v.y = DType<T>::pack2(__uint_as_float(a[8 * q4 + 2]) * mul, __uint_as_float(a[8 * q4 + 3]) * mul);
-                    v.z = DType<T>::pack2(__uint_as_float(a[8 * q4 + 4]) * mul, __uint_as_float(a[8 * q4 + 5]) * mul);
-                    v.w = DType<T>::pack2(__uint_as_float(a[8 * q4 + 6]) * mul, __uint_as_float(a[8 * q4 + 7]) * mul);
-                    dst[q4] = v;
+        for (int u = blockIdx.x; ok && u < p.num_units; u += gridDim.x) {
+            for (int w = 0; ok && w < 2; ++w) {
+                BwdItem itm;
+                if (!bwd_item(p, u, w, itm)) continue;
+                const int j = itm.j, bh = itm.bh;
+                const int i0 = p.causal ? j : 0;
+                const int n_it = p.n_blk - i0;
+                for (int it = 0; it < n_it; ++it, ++g) {
+                    const int i = i0 + it;
+                    const int s = g % G::kStages;
+                    // L and D of block i arrived through the async proxy: observe
+                    // the stage's own barrier before reading them (it completes
+                    // before S is issued, so waiting for it first costs nothing)
+                    if (!bwarp_wait(full + s, (g / G::kStages) & 1, abort_flag) ||
+                        !bwarp_wait(bar_sdp, g & 1, abort_flag)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const float* sL =
+                        reinterpret_cast<const float*>(sptr + G::kOffStage + s * G::kStageBytes +
+                                                       2 * G::kTileBytes) +
+                        h * 64;
+                    const float* sD = sL + 128;
+                    if (p.causal && i == j)
+                        bwd_softmax_block<T, true>(t_s, t_dp, sDs, sL, sD, c, h, r);
+                    else
+                        bwd_softmax_block<T, false>(t_s, t_dp, sDs, sL, sD, c, h, r);
+                    tmem_wait_st();
+                    fence_proxy_async_smem();
+                    tc_fence_before();
+                    mbar_arrive(bar_ds);
                 }
+                if (ok) {
+                    ok = bwarp_wait(bar_acc, items & 1, abort_flag);
+                    tc_fence_after();
+                }
+                ++items;
+                // warpgroup 0 stores dV, warpgroup 1 stores dK (scaled)
+                const int kv = j * 128 + r;
+                const bool valid = kv < p.N;
+                const size_t row = (static_cast<size_t>(bh) * p.N + kv) * D;
+                T* dst_base = static_cast<T*>(h == 0 ? p.dV : p.dK);
+                const float mul = h == 0 ? 1.f : p.scale;
+                const uint32_t t_acc = tmem + lane_addr + (h == 0 ? 256 : 384);
+#pragma unroll
+                for (int cb = 0; cb < D / 32; ++cb) {
+                    uint32_t a[32];
+                    if (ok) {
+                        tmem_ld_x32(t_acc + cb * 32, a);
+                    } else {
+#pragma unroll
+                        for (int e = 0; e < 32; ++e) a[e] = 0u;
+                    }
+                    if (valid) {
+                        uint4* dst = reinterpret_cast<uint4*>(dst_base + row + cb * 32);
+#pragma unroll
+                        for (int q4 = 0; q4 < 4; ++q4) {
+                            uint4 v;
+                            v.x = DType<T>::pack2(__uint_as_float(a[8 * q4 + 0]) * mul, __uint_as_float(a[8 * q4 + 1]) * mul);
+                            v.y = DType<T>::pack2(__uint_as_float(a[8 * q4 + 2]) * mul, __uint_as_float(a[8 * q4 + 3]) * mul);
+                            v.z = DType<T>::pack2(__uint_as_float(a[8 * q4 + 4]) * mul, __uint_as_float(a[8 * q4 + 5]) * mul);
+                            v.w = DType<T>::pack2(__uint_as_float(a[8 * q4 + 6]) * mul, __uint_as_float(a[8 * q4 + 7]) * mul);
+                            dst[q4] = v;
+                        }
+                    }
+                }
+                // The next item's first dS arrival follows these TMEM reads, so
+                // its dV / dK products cannot overwrite the accumulators early.
             }
         }
     } else {
@@ -623,70 +713,88 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         // ------------------------------------------------ dQ drain
         const int wq = warp & 3;
         const uint32_t t_q = tmem + (static_cast<uint32_t>(wq * 32) << 16) + 128;
-        if constexpr (kTransposedDq) {
-            // lane = head_dim element d; TMEM column = query row of block i
-            const int d = wq * 32 + lane;
-            for (int it = 0; it < n_it; ++it) {
-                const int i = i0 + it;
-                if (!bwarp_wait(bar_dq, it & 1, abort_flag)) break;
-                tc_fence_after();
-                uint32_t v0[32], v1[32], v2[32], v3[32];
-                tmem_ld2_x32(t_q, v0, t_q + 32, v1);
-                tmem_ld2_x32(t_q + 64, v2, t_q + 96, v3);
-                // TMEM columns are free once loaded: release them before the
-                // reductions so the next dP MMA is not held up
-                tc_fence_before();
-                mbar_arrive(bar_dqfree);
-                float* dst = p.dq_acc + (static_cast<size_t>(bh) * p.N + i * 128) * D + d;
-                const int qn = min(128, p.N - i * 128);
-                auto flush = [&](const uint32_t(&v)[32], int q0) {
+        uint32_t g = 0;
+        bool ok = true;
+        for (int u = blockIdx.x; ok && u < p.num_units; u += gridDim.x) {
+            for (int w = 0; ok && w < 2; ++w) {
+                BwdItem itm;
+                if (!bwd_item(p, u, w, itm)) continue;
+                const int bh = itm.bh;
+                const int i0 = p.causal ? itm.j : 0;
+                const int n_it = p.n_blk - i0;
+                if constexpr (kTransposedDq) {
+                    // lane = head_dim element d; TMEM column = query row of block i
+                    const int d = wq * 32 + lane;
+                    for (int it = 0; it < n_it; ++it, ++g) {
+                        const int i = i0 + it;
+                        if (!bwarp_wait(bar_dq, g & 1, abort_flag)) {
+                            ok = false;
+                            break;
+                        }
+                        tc_fence_after();
+                        uint32_t v0[32], v1[32], v2[32], v3[32];
+                        tmem_ld2_x32(t_q, v0, t_q + 32, v1);
+                        tmem_ld2_x32(t_q + 64, v2, t_q + 96, v3);
+                        // TMEM columns are free once loaded: release them before the
+                        // reductions so the next dP MMA is not held up
+                        tc_fence_before();
+                        mbar_arrive(bar_dqfree);
+                        float* dst = p.dq_acc + (static_cast<size_t>(bh) * p.N + i * 128) * D + d;
+                        const int qn = min(128, p.N - i * 128);
+                        auto flush = [&](const uint32_t(&v)[32], int q0) {
 #pragma unroll
-                    for (int e = 0; e < 32; ++e)
-                        if (q0 + e < qn)
-                            red_add_f32(dst + static_cast<size_t>(q0 + e) * D, __uint_as_float(v[e]));
-                };
-                flush(v0, 0);
-                flush(v1, 32);
-                flush(v2, 64);
-                flush(v3, 96);
-            }
-        } else {
-            // Each warp owns 32 query rows.  Per 32-column chunk it copies its
-            // 32x32 fp32 block from TMEM into a 128-byte-swizzled staging box
-            // and the TMA unit adds the box into the fp32 accumulator.  Staging
-            // lives in the dS buffer, idle from the completion of dQ_i until
-            // the softmax warps write dS_{i+1}, which they do only after
-            // dP^T_{i+1}, issued once this drain signals bar_dqfree.
-            const uint32_t stage0 = sbase + G::kOffDs + wq * 8192;
-            for (int it = 0; it < n_it; ++it) {
-                const int i = i0 + it;
-                if (!bwarp_wait(bar_dq, it & 1, abort_flag)) break;
-                tc_fence_after();
-#pragma unroll
-                for (int cb = 0; cb < D / 32; ++cb) {
-                    const uint32_t box = stage0 + (cb & 1) * 4096;
-                    if (cb >= 2) {
-                        if (lane == 0) bulk_wait_group_read<1>();
-                        __syncwarp();
+                            for (int e = 0; e < 32; ++e)
+                                if (q0 + e < qn)
+                                    red_add_f32(dst + static_cast<size_t>(q0 + e) * D, __uint_as_float(v[e]));
+                        };
+                        flush(v0, 0);
+                        flush(v1, 32);
+                        flush(v2, 64);
+                        flush(v3, 96);
                     }
-                    uint32_t v[32];
-                    tmem_ld_x32(t_q + cb * 32, v);
+                } else {
+                    // Each warp owns 32 query rows.  Per 32-column chunk it copies
+                    // its 32x32 fp32 block from TMEM into a 128-byte-swizzled
+                    // staging box and the TMA unit adds the box into the fp32
+                    // accumulator.  Staging lives in the dS buffer, idle from the
+                    // completion of dQ_i until the softmax warps write the next
+                    // dS, which they do only after the next dP^T, issued once
+                    // this drain signals bar_dqfree.
+                    const uint32_t stage0 = sbase + G::kOffDs + wq * 8192;
+                    for (int it = 0; it < n_it; ++it, ++g) {
+                        const int i = i0 + it;
+                        if (!bwarp_wait(bar_dq, g & 1, abort_flag)) {
+                            ok = false;
+                            break;
+                        }
+                        tc_fence_after();
 #pragma unroll
-                    for (int k = 0; k < 8; ++k)
-                        st_shared_v4(box + lane * 128 + ((k ^ (lane & 7)) << 4), v[4 * k],
-                                     v[4 * k + 1], v[4 * k + 2], v[4 * k + 3]);
-                    fence_proxy_async_smem();
-                    __syncwarp();
-                    if (lane == 0) {
-                        tma_reduce_add_3d(&tmdQ, box, cb * 32, i * 128 + wq * 32, bh);
-                        bulk_commit_group();
+                        for (int cb = 0; cb < D / 32; ++cb) {
+                            const uint32_t box = stage0 + (cb & 1) * 4096;
+                            if (cb >= 2) {
+                                if (lane == 0) bulk_wait_group_read<1>();
+                                __syncwarp();
+                            }
+                            uint32_t v[32];
+                            tmem_ld_x32(t_q + cb * 32, v);
+#pragma unroll
+                            for (int k = 0; k < 8; ++k)
+                                st_shared_v4(box + lane * 128 + ((k ^ (lane & 7)) << 4), v[4 * k],
+                                             v[4 * k + 1], v[4 * k + 2], v[4 * k + 3]);
+                            fence_proxy_async_smem();
+                            __syncwarp();
+                            if (lane == 0) {
+                                tma_reduce_add_3d(&tmdQ, box, cb * 32, i * 128 + wq * 32, bh);
+                                bulk_commit_group();
+                            }
+                        }
+                        // the staging boxes must be read out before dS_{i+1} overwrites them
+                        if (lane == 0) bulk_wait_group_read<0>();
+                        __syncwarp();
+                        tc_fence_before();
+                        mbar_arrive(bar_dqfree);
                     }
                 }
-                // the staging boxes must be read out before dS_{i+1} overwrites them
-                if (lane == 0) bulk_wait_group_read<0>();
-                __syncwarp();
-                tc_fence_before();
-                mbar_arrive(bar_dqfree);
             }
         }
     }
@@ -737,7 +845,6 @@ FlashAttentionError bwd_typed(const T* Q, const T* K, const T* V, const T* O, co
     auto kern = fa_bwd_kernel<T, D>;
     if (!ensure_smem_attr(reinterpret_cast<const void*>(kern), G::kSmemBytes))
         return fail(FlashAttentionError::CUDA_ERROR);
-    if (n_blk > 0x7fffffff / 1) return fail(FlashAttentionError::CUDA_ERROR);
 
     const long long rows_pad = static_cast<long long>(BH) * n_pad;
     const long long pre_blocks = (rows_pad * (D / 8) + 255) / 256;
@@ -753,10 +860,20 @@ FlashAttentionError bwd_typed(const T* Q, const T* K, const T* V, const T* O, co
     prm.dvp = dvp;
     prm.N = N;
     prm.n_blk = n_blk;
+    prm.npairs = (n_blk + 1) / 2;
+    const int sms = current_sm_count();
+    long long units = static_cast<long long>(BH) * prm.npairs;
+    // pairing only balances a causal walk (non-causal items all cost n_blk)
+    prm.paired = (causal && units >= sms) ? 1 : 0;
+    if (!prm.paired) units = static_cast<long long>(BH) * n_blk;
+    if (units > 0x7fffffffLL) return fail(FlashAttentionError::CUDA_ERROR);
+    prm.num_units = static_cast<int>(units);
     prm.causal = causal ? 1 : 0;
     prm.scale_log2 = scale * kLog2eB;
     prm.scale = scale;
-    kern<<<dim3(n_blk, BH), kBwdThreads, G::kSmemBytes, stream>>>(mq, mk, mv, mdo, mdq, prm);
+    // persistent: one CTA per SM (the shared-memory footprint allows one)
+    const int grid = static_cast<int>(std::min<long long>(units, sms));
+    kern<<<grid, kBwdThreads, G::kSmemBytes, stream>>>(mq, mk, mv, mdo, mdq, prm);
     if (cudaGetLastError() != cudaSuccess) return fail(FlashAttentionError::CUDA_ERROR);
 
     const long long n4 = static_cast<long long>(acc_elems / 4);
@@ -778,7 +895,6 @@ FlashAttentionError launch_bwd_sm100(const T* Q, const T* K, const T* V, const T
                                      int H, int N, int D, float scale, bool causal,
                                      cudaStream_t stream) {
     const int BH = B * H;
-    if (N > 65535 * 128) return FlashAttentionError::CUDA_ERROR;
     switch (D) {
         case 32:
             return bwd_typed<T, 32>(Q, K, V, O, L, dO, dQ, dK, dV, BH, N, scale, causal, stream);
