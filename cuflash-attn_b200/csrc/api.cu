@@ -193,6 +193,33 @@ FlashAttentionError partial_impl(const T* Q, const T* K, const T* V, float* O, f
                                                 causal, q_offset, k_offset, true, stream);
 }
 
+template <typename T>
+FlashAttentionError cp_step_impl(const T* Q, const T* K, const T* V, float* O_acc, float* L_acc,
+                                 int nq, int nk, int B, int H, int C, int D, float scale,
+                                 bool causal, int num_pairs, const int* q_slot, const int* kv_slot,
+                                 const long long* q_off, const long long* kv_off,
+                                 cudaStream_t stream) {
+    if (!Q || !K || !V || !O_acc || !L_acc || !q_slot || !kv_slot || !q_off || !kv_off)
+        return FlashAttentionError::NULL_POINTER;
+    if (nq <= 0 || nk <= 0 || B <= 0 || H <= 0 || C <= 0 || D <= 0)
+        return FlashAttentionError::INVALID_DIMENSION;
+    if (!(D == 32 || D == 64 || D == 128)) return FlashAttentionError::UNSUPPORTED_HEAD_DIM;
+    if (!std::isfinite(scale) || scale < 0.0f) return FlashAttentionError::INVALID_DIMENSION;
+    if (num_pairs < 1 || num_pairs > 4) return FlashAttentionError::INVALID_DIMENSION;
+    if (static_cast<long long>(B) * H * (nq > nk ? nq : nk) > 0x7fffffffLL)
+        return FlashAttentionError::INVALID_DIMENSION;
+    for (int i = 0; i < num_pairs; ++i) {
+        if (q_slot[i] < 0 || q_slot[i] >= nq || kv_slot[i] < 0 || kv_slot[i] >= nk ||
+            q_off[i] < 0 || kv_off[i] < 0)
+            return FlashAttentionError::INVALID_DIMENSION;
+        for (int k = 0; k < i; ++k)  // the merge writes each query slot once per launch
+            if (q_slot[k] == q_slot[i]) return FlashAttentionError::INVALID_DIMENSION;
+    }
+    return cuflash::detail::launch_fwd_cp_step_sm100<T>(Q, K, V, O_acc, L_acc, nq, nk, B, H, C, D,
+                                                        scale, causal, num_pairs, q_slot, kv_slot,
+                                                        q_off, kv_off, stream);
+}
+
 }  // namespace
 
 extern "C" {
@@ -285,6 +312,31 @@ int cuflash_attention_forward_partial_f16(const half* Q, const half* K, const ha
     return static_cast<int>(partial_impl<half>(Q, K, V, O_part, L_part, batch_size, num_heads,
                                                seq_q, seq_k, head_dim, scale, q_offset, k_offset,
                                                causal, stream));
+}
+
+int cuflash_attention_forward_cp_step_bf16(const __nv_bfloat16* Q, const __nv_bfloat16* K,
+                                           const __nv_bfloat16* V, float* O_acc, float* L_acc,
+                                           int num_q_slots, int num_kv_slots, int batch_size,
+                                           int num_heads, int chunk_len, int head_dim, float scale,
+                                           bool causal, int num_pairs, const int* q_slot,
+                                           const int* kv_slot, const long long* q_offset,
+                                           const long long* kv_offset, cudaStream_t stream) {
+    return static_cast<int>(cp_step_impl<__nv_bfloat16>(
+        Q, K, V, O_acc, L_acc, num_q_slots, num_kv_slots, batch_size, num_heads, chunk_len,
+        head_dim, scale, causal, num_pairs, q_slot, kv_slot, q_offset, kv_offset, stream));
+}
+
+int cuflash_attention_forward_cp_step_f16(const half* Q, const half* K, const half* V,
+                                          float* O_acc, float* L_acc, int num_q_slots,
+                                          int num_kv_slots, int batch_size, int num_heads,
+                                          int chunk_len, int head_dim, float scale, bool causal,
+                                          int num_pairs, const int* q_slot, const int* kv_slot,
+                                          const long long* q_offset, const long long* kv_offset,
+                                          cudaStream_t stream) {
+    return static_cast<int>(cp_step_impl<half>(Q, K, V, O_acc, L_acc, num_q_slots, num_kv_slots,
+                                               batch_size, num_heads, chunk_len, head_dim, scale,
+                                               causal, num_pairs, q_slot, kv_slot, q_offset,
+                                               kv_offset, stream));
 }
 
 int cuflash_lse_merge_f32(float* O_acc, float* L_acc, const float* O_part, const float* L_part,

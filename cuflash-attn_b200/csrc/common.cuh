@@ -86,6 +86,17 @@ FlashAttentionError launch_fwd_sm100(const T* Q, const T* K, const T* V, void* O
                                      long long q_offset, long long k_offset, bool out_f32_partial,
                                      cudaStream_t stream);
 
+// One context-parallel ring step: num_pairs (<= 4) partial forwards of query
+// slot q_slot[i] against K/V slot k_slot[i] (global offsets q_off/k_off), each
+// merged in place into O_acc / L_acc of its query slot; one launch.
+template <typename T>
+FlashAttentionError launch_fwd_cp_step_sm100(const T* Q, const T* K, const T* V, float* O_acc,
+                                             float* L_acc, int nq, int nk, int B, int H, int C,
+                                             int D, float scale, bool causal, int num_pairs,
+                                             const int* q_slot, const int* k_slot,
+                                             const long long* q_off, const long long* k_off,
+                                             cudaStream_t stream);
+
 template <typename T>
 FlashAttentionError launch_bwd_sm100(const T* Q, const T* K, const T* V, const T* O,
                                      const float* L, const T* dO, T* dQ, T* dK, T* dV, int B,

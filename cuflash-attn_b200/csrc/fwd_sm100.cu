@@ -88,12 +88,22 @@ struct FwdParams {
     int num_ctiles;  // 256-row query tiles per (b,h)
     int npairs;      // (num_ctiles + 1) / 2
     int paired;      // 1: a unit is a (heavy, light) item pair; 0: one item
-    int num_units;   // BH * npairs, or BH * num_ctiles when not paired
+    int num_units;   // units over all segments
     int causal;
+    int merge;       // fp32 output: log-sum-exp merge into O / L in place
     float scale_log2;
-    long long q_offset;
-    long long k_offset;
+    // Segments: one launch can run up to kMaxSegs (query slot, K/V slot)
+    // pairs, each over all B*H heads with its own global offsets.  Q / O / L
+    // hold the query slots stacked as [slot][B*H] along the outer dimension,
+    // K / V the K/V slots the same way.
+    int num_segs;
+    int seg_units;   // units of one segment
+    int q_base[4];   // outer index of the segment's first (b,h) in Q / O / L
+    int k_base[4];   // outer index of the segment's first (b,h) in K / V
+    long long q_off[4];
+    long long k_off[4];
 };
+constexpr int kMaxSegs = 4;
 
 // K-major operand (rows x D, D contiguous) for k-step kk (16 elements).
 template <int D>
@@ -134,34 +144,45 @@ __device__ __forceinline__ uint64_t mnmajor_desc(uint32_t tile_base, int kk) {
 // brought into L2.  Problems with fewer units than SMs use one item per unit
 // instead (more CTAs, same per-item work as a non-persistent grid).
 struct FwdItem {
-    int bh;
+    int bh;      // outer index in Q / O / L
+    int bhk;     // outer index in K / V
     int q_row0;
+    long long q_off;  // global position of query row 0 / key row 0
+    long long k_off;
 };
 
 __device__ __forceinline__ bool fwd_item(const FwdParams& p, int u, int w, FwdItem& it) {
+    int sg = 0;
+#pragma unroll
+    for (int i = 1; i < kMaxSegs; ++i)
+        if (i < p.num_segs && u >= i * p.seg_units) sg = i;
+    u -= sg * p.seg_units;
+    int bh, ct;
     if (!p.paired) {  // one item per unit, heaviest first within a (b,h)
         if (w == 1) return false;
-        const int bh = u / p.num_ctiles;
-        it.bh = bh;
-        it.q_row0 = (p.num_ctiles - 1 - (u - bh * p.num_ctiles)) * 256;
-        return true;
+        bh = u / p.num_ctiles;
+        ct = p.num_ctiles - 1 - (u - bh * p.num_ctiles);
+    } else {
+        bh = u / p.npairs;
+        const int k = u - bh * p.npairs;
+        ct = w == 0 ? p.num_ctiles - 1 - k : k;
+        if (w == 1 && ct == p.num_ctiles - 1 - k) return false;  // middle tile of an odd count
     }
-    const int bh = u / p.npairs;
-    const int k = u - bh * p.npairs;
-    const int ct = w == 0 ? p.num_ctiles - 1 - k : k;
-    if (w == 1 && ct == p.num_ctiles - 1 - k) return false;  // middle tile of an odd count
-    it.bh = bh;
+    it.bh = p.q_base[sg] + bh;
+    it.bhk = p.k_base[sg] + bh;
     it.q_row0 = ct * 256;
+    it.q_off = p.q_off[sg];
+    it.k_off = p.k_off[sg];
     return true;
 }
 
 // kv blocks the 128-row tile starting at query row r_lo visits.
-__device__ __forceinline__ int tile_blocks(const FwdParams& p, int r_lo) {
+__device__ __forceinline__ int tile_blocks(const FwdParams& p, const FwdItem& it, int r_lo) {
     const int nkv_all = (p.seq_k + 127) / 128;
     if (r_lo >= p.seq_q) return 0;
     if (!p.causal) return nkv_all;
     const int r_hi = min(r_lo + 127, p.seq_q - 1);
-    const long long lim = p.q_offset + r_hi - p.k_offset;  // largest visible local key
+    const long long lim = it.q_off + r_hi - it.k_off;  // largest visible local key
     const long long nb = lim / 128 + 1;
     return lim < 0 ? 0 : (nb < nkv_all ? static_cast<int>(nb) : nkv_all);
 }
@@ -257,7 +278,8 @@ __global__ void __launch_bounds__(384, 1)
                 for (int w = 0; ok && w < 2; ++w) {
                     FwdItem it;
                     if (!fwd_item(p, u, w, it)) continue;
-                    const int nt[2] = {tile_blocks(p, it.q_row0), tile_blocks(p, it.q_row0 + 128)};
+                    const int nt[2] = {tile_blocks(p, it, it.q_row0),
+                                       tile_blocks(p, it, it.q_row0 + 128)};
                     const int n_max = max(nt[0], nt[1]);
 #pragma unroll
                     for (int t = 0; t < 2; ++t) {
@@ -287,7 +309,7 @@ __global__ void __launch_bounds__(384, 1)
                         mbar_arrive_expect_tx(full_k + s, G::kTileBytes);
                         for (int cb = 0; cb < G::kNumCb; ++cb)
                             tma_load_3d(sptr + G::kOffK + s * G::kTileBytes + cb * G::kCbBytes,
-                                        &tmK, full_k + s, cb * G::kCbElems, j * 128, it.bh);
+                                        &tmK, full_k + s, cb * G::kCbElems, j * 128, it.bhk);
                         ++issued_k;
                         if (g >= G::kStages &&
                             !mbar_wait(empty_v + s, ph ^ 1, abort_flag, &g_fwd_status)) {
@@ -297,7 +319,7 @@ __global__ void __launch_bounds__(384, 1)
                         mbar_arrive_expect_tx(full_v + s, G::kTileBytes);
                         for (int cb = 0; cb < G::kNumCb; ++cb)
                             tma_load_3d(sptr + G::kOffV + s * G::kTileBytes + cb * G::kCbBytes,
-                                        &tmV, full_v + s, cb * G::kCbElems, j * 128, it.bh);
+                                        &tmV, full_v + s, cb * G::kCbElems, j * 128, it.bhk);
                         ++issued_v;
                     }
                 }
@@ -350,7 +372,8 @@ __global__ void __launch_bounds__(384, 1)
                 for (int w = 0; ok && w < 2; ++w) {
                     FwdItem it;
                     if (!fwd_item(p, u, w, it)) continue;
-                    const int nt[2] = {tile_blocks(p, it.q_row0), tile_blocks(p, it.q_row0 + 128)};
+                    const int nt[2] = {tile_blocks(p, it, it.q_row0),
+                                       tile_blocks(p, it, it.q_row0 + 128)};
                     const int n_max = max(nt[0], nt[1]);
                     if (n_max == 0) continue;
                     // The item's first S tiles.  In-order issue keeps them
@@ -456,9 +479,9 @@ __global__ void __launch_bounds__(384, 1)
                 FwdItem it;
                 if (!fwd_item(p, u, w, it)) continue;
                 const int row = it.q_row0 + t * 128 + r;
-                const long long grow = p.q_offset + row;
-                const int n = tile_blocks(p, it.q_row0 + t * 128);
-                const long long tile_g0 = p.q_offset + it.q_row0 + t * 128;
+                const long long grow = it.q_off + row;
+                const int n = tile_blocks(p, it, it.q_row0 + t * 128);
+                const long long tile_g0 = it.q_off + it.q_row0 + t * 128;
 
                 float m_run = -INFINITY;
                 float l_run = 0.f;
@@ -473,10 +496,10 @@ __global__ void __launch_bounds__(384, 1)
                     tmem_ld_x128(s_tmem, sr);
                     const int col0 = j * 128;
                     const bool need_mask = (col0 + 128 > p.seq_k) ||
-                                           (p.causal && (p.k_offset + col0 + 127 > tile_g0));
+                                           (p.causal && (it.k_off + col0 + 127 > tile_g0));
                     if (need_mask) {
                         // largest visible local key column for this row (32-bit safe)
-                        const long long lim64 = grow - p.k_offset;
+                        const long long lim64 = grow - it.k_off;
                         const int lim = p.causal ? static_cast<int>(lim64 < -1 ? -1 : (lim64 > 0x7fffffff ? 0x7fffffff : lim64))
                                                  : 0x7fffffff;
                         const int vis_end = min(p.seq_k - 1, lim) - col0;  // visible iff i <= vis_end
@@ -586,6 +609,26 @@ __global__ void __launch_bounds__(384, 1)
                 const bool valid_row = row < p.seq_q;
                 const float inv_l = l_run > 0.f ? 1.f / l_run : 0.f;
                 const size_t row_elem = (static_cast<size_t>(it.bh) * p.seq_q + row) * D;
+                const size_t l_idx = static_cast<size_t>(it.bh) * p.seq_q + row;
+                const float lse_part = l_run > 0.f ? (m_run + log2f(l_run)) * kLn2 : -INFINITY;
+                // Merge mode: (O, L) already hold a normalised result for these
+                // rows; fold this one in with the log-sum-exp weights (same
+                // algebra as cuflash_lse_merge_f32): wa * O + wb * O_part.
+                float wa = 0.f, wb = inv_l, lse_out = lse_part;
+                if (kF32Out && p.merge && valid_row) {
+                    const float la = p.L[l_idx];
+                    const float M = fmaxf(la, lse_part);
+                    wa = 0.f;
+                    wb = 0.f;
+                    lse_out = -INFINITY;
+                    if (M != -INFINITY) {
+                        const float ea = __expf(la - M), eb = __expf(lse_part - M);
+                        const float tot = ea + eb;
+                        wa = ea / tot;
+                        wb = eb / tot * inv_l;
+                        lse_out = M + logf(tot);
+                    }
+                }
 #pragma unroll
                 for (int cb = 0; cb < D / 32; ++cb) {
                     uint32_t o[32];
@@ -600,11 +643,14 @@ __global__ void __launch_bounds__(384, 1)
                             float4* dst = reinterpret_cast<float4*>(static_cast<float*>(p.O) + row_elem +
                                                                     cb * 32);
 #pragma unroll
-                            for (int i = 0; i < 8; ++i)
-                                dst[i] = make_float4(__uint_as_float(o[4 * i]) * inv_l,
-                                                     __uint_as_float(o[4 * i + 1]) * inv_l,
-                                                     __uint_as_float(o[4 * i + 2]) * inv_l,
-                                                     __uint_as_float(o[4 * i + 3]) * inv_l);
+                            for (int i = 0; i < 8; ++i) {
+                                float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
+                                if (wa != 0.f) a = dst[i];  // wa == 0: O may hold anything
+                                dst[i] = make_float4(fmaf(wa, a.x, __uint_as_float(o[4 * i]) * wb),
+                                                     fmaf(wa, a.y, __uint_as_float(o[4 * i + 1]) * wb),
+                                                     fmaf(wa, a.z, __uint_as_float(o[4 * i + 2]) * wb),
+                                                     fmaf(wa, a.w, __uint_as_float(o[4 * i + 3]) * wb));
+                            }
                         } else {
                             uint4* dst =
                                 reinterpret_cast<uint4*>(static_cast<T*>(p.O) + row_elem + cb * 32);
@@ -624,10 +670,7 @@ __global__ void __launch_bounds__(384, 1)
                         }
                     }
                 }
-                if (valid_row) {
-                    p.L[static_cast<size_t>(it.bh) * p.seq_q + row] =
-                        l_run > 0.f ? (m_run + log2f(l_run)) * kLn2 : -INFINITY;
-                }
+                if (valid_row) p.L[l_idx] = lse_out;
                 // The next item's first P store (and its bar_p arrival) follows
                 // these TMEM reads of O_t, so its PV product cannot overwrite
                 // O_t early.
@@ -643,17 +686,31 @@ __global__ void __launch_bounds__(384, 1)
     }
 }
 
+// Query/K-V slot layout and segment list of one launch (see FwdParams).
+struct FwdSegs {
+    int nq_slots = 1;  // Q / O / L hold nq_slots x B*H outer rows
+    int nk_slots = 1;  // K / V hold nk_slots x B*H outer rows
+    int num_segs = 1;
+    int q_slot[kMaxSegs] = {0, 0, 0, 0};
+    int k_slot[kMaxSegs] = {0, 0, 0, 0};
+    long long q_off[kMaxSegs] = {0, 0, 0, 0};
+    long long k_off[kMaxSegs] = {0, 0, 0, 0};
+    bool merge = false;
+};
+
 template <typename T, int D, bool kF32Out>
 FlashAttentionError launch_typed(const T* Q, const T* K, const T* V, void* O, float* L, int BH,
                                  int seq_q, int seq_k, float scale, bool causal,
-                                 long long q_offset, long long k_offset, cudaStream_t stream) {
+                                 const FwdSegs& sg, cudaStream_t stream) {
     using G = FwdGeom<D>;
     const CUtensorMapSwizzle swz =
         G::kSwz == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
     CUtensorMap mq, mk, mv;
-    if (!encode_tmap_3d(&mq, Q, DType<T>::kTmaType, 2, D, seq_q, BH, G::kCbElems, 128, swz) ||
-        !encode_tmap_3d(&mk, K, DType<T>::kTmaType, 2, D, seq_k, BH, G::kCbElems, 128, swz) ||
-        !encode_tmap_3d(&mv, V, DType<T>::kTmaType, 2, D, seq_k, BH, G::kCbElems, 128, swz))
+    const uint64_t q_outer = static_cast<uint64_t>(sg.nq_slots) * BH;
+    const uint64_t k_outer = static_cast<uint64_t>(sg.nk_slots) * BH;
+    if (!encode_tmap_3d(&mq, Q, DType<T>::kTmaType, 2, D, seq_q, q_outer, G::kCbElems, 128, swz) ||
+        !encode_tmap_3d(&mk, K, DType<T>::kTmaType, 2, D, seq_k, k_outer, G::kCbElems, 128, swz) ||
+        !encode_tmap_3d(&mv, V, DType<T>::kTmaType, 2, D, seq_k, k_outer, G::kCbElems, 128, swz))
         return FlashAttentionError::CUDA_ERROR;
     auto kern = fa_fwd_kernel<T, D, kF32Out>;
     if (!ensure_smem_attr(reinterpret_cast<const void*>(kern), G::kSmemBytes))
@@ -665,17 +722,25 @@ FlashAttentionError launch_typed(const T* Q, const T* K, const T* V, void* O, fl
     prm.seq_k = seq_k;
     prm.num_ctiles = (seq_q + 255) / 256;
     prm.causal = causal ? 1 : 0;
+    prm.merge = sg.merge ? 1 : 0;
     // A zero scale is replaced by a tiny positive one so that masked scores
     // (-inf) still map to -inf; the effect on results is below fp32 resolution.
     prm.scale_log2 = fmaxf(scale * kLog2e, 1e-30f);
-    prm.q_offset = q_offset;
-    prm.k_offset = k_offset;
+    prm.num_segs = sg.num_segs;
+    for (int i = 0; i < kMaxSegs; ++i) {
+        prm.q_base[i] = sg.q_slot[i] * BH;
+        prm.k_base[i] = sg.k_slot[i] * BH;
+        prm.q_off[i] = sg.q_off[i];
+        prm.k_off[i] = sg.k_off[i];
+    }
     prm.npairs = (prm.num_ctiles + 1) / 2;
     const int sms = current_sm_count();
-    long long units = static_cast<long long>(BH) * prm.npairs;
-    prm.paired = units >= sms ? 1 : 0;
-    if (!prm.paired) units = static_cast<long long>(BH) * prm.num_ctiles;
+    long long seg_units = static_cast<long long>(BH) * prm.npairs;
+    prm.paired = seg_units * sg.num_segs >= sms ? 1 : 0;
+    if (!prm.paired) seg_units = static_cast<long long>(BH) * prm.num_ctiles;
+    const long long units = seg_units * sg.num_segs;
     if (units > 0x7fffffffLL) return FlashAttentionError::CUDA_ERROR;
+    prm.seg_units = static_cast<int>(seg_units);
     prm.num_units = static_cast<int>(units);
     // persistent: one CTA per SM (the shared-memory footprint allows one)
     const int grid = static_cast<int>(std::min<long long>(units, sms));
@@ -688,17 +753,17 @@ FlashAttentionError launch_typed(const T* Q, const T* K, const T* V, void* O, fl
 template <typename T, bool kF32Out>
 FlashAttentionError dispatch_d(const T* Q, const T* K, const T* V, void* O, float* L, int BH,
                                int seq_q, int seq_k, int D, float scale, bool causal,
-                               long long q_offset, long long k_offset, cudaStream_t stream) {
+                               const FwdSegs& sg, cudaStream_t stream) {
     switch (D) {
         case 32:
-            return launch_typed<T, 32, kF32Out>(Q, K, V, O, L, BH, seq_q, seq_k, scale, causal,
-                                                q_offset, k_offset, stream);
+            return launch_typed<T, 32, kF32Out>(Q, K, V, O, L, BH, seq_q, seq_k, scale, causal, sg,
+                                                stream);
         case 64:
-            return launch_typed<T, 64, kF32Out>(Q, K, V, O, L, BH, seq_q, seq_k, scale, causal,
-                                                q_offset, k_offset, stream);
+            return launch_typed<T, 64, kF32Out>(Q, K, V, O, L, BH, seq_q, seq_k, scale, causal, sg,
+                                                stream);
         case 128:
-            return launch_typed<T, 128, kF32Out>(Q, K, V, O, L, BH, seq_q, seq_k, scale, causal,
-                                                 q_offset, k_offset, stream);
+            return launch_typed<T, 128, kF32Out>(Q, K, V, O, L, BH, seq_q, seq_k, scale, causal, sg,
+                                                 stream);
         default:
             return FlashAttentionError::UNSUPPORTED_HEAD_DIM;
     }
@@ -712,12 +777,43 @@ FlashAttentionError launch_fwd_sm100(const T* Q, const T* K, const T* V, void* O
                                      long long q_offset, long long k_offset, bool out_f32_partial,
                                      cudaStream_t stream) {
     const int BH = B * H;
+    FwdSegs sg;
+    sg.q_off[0] = q_offset;
+    sg.k_off[0] = k_offset;
     if (out_f32_partial)
-        return dispatch_d<T, true>(Q, K, V, O, L, BH, seq_q, seq_k, D, scale, causal, q_offset,
-                                   k_offset, stream);
-    return dispatch_d<T, false>(Q, K, V, O, L, BH, seq_q, seq_k, D, scale, causal, q_offset,
-                                k_offset, stream);
+        return dispatch_d<T, true>(Q, K, V, O, L, BH, seq_q, seq_k, D, scale, causal, sg, stream);
+    return dispatch_d<T, false>(Q, K, V, O, L, BH, seq_q, seq_k, D, scale, causal, sg, stream);
 }
+
+template <typename T>
+FlashAttentionError launch_fwd_cp_step_sm100(const T* Q, const T* K, const T* V, float* O_acc,
+                                             float* L_acc, int nq, int nk, int B, int H, int C,
+                                             int D, float scale, bool causal, int num_pairs,
+                                             const int* q_slot, const int* k_slot,
+                                             const long long* q_off, const long long* k_off,
+                                             cudaStream_t stream) {
+    if (num_pairs < 1 || num_pairs > kMaxSegs) return FlashAttentionError::INVALID_DIMENSION;
+    FwdSegs sg;
+    sg.nq_slots = nq;
+    sg.nk_slots = nk;
+    sg.num_segs = num_pairs;
+    sg.merge = true;
+    for (int i = 0; i < num_pairs; ++i) {
+        sg.q_slot[i] = q_slot[i];
+        sg.k_slot[i] = k_slot[i];
+        sg.q_off[i] = q_off[i];
+        sg.k_off[i] = k_off[i];
+    }
+    return dispatch_d<T, true>(Q, K, V, O_acc, L_acc, B * H, C, C, D, scale, causal, sg, stream);
+}
+
+template FlashAttentionError launch_fwd_cp_step_sm100<__nv_bfloat16>(
+    const __nv_bfloat16*, const __nv_bfloat16*, const __nv_bfloat16*, float*, float*, int, int,
+    int, int, int, int, float, bool, int, const int*, const int*, const long long*,
+    const long long*, cudaStream_t);
+template FlashAttentionError launch_fwd_cp_step_sm100<half>(
+    const half*, const half*, const half*, float*, float*, int, int, int, int, int, int, float,
+    bool, int, const int*, const int*, const long long*, const long long*, cudaStream_t);
 
 template FlashAttentionError launch_fwd_sm100<__nv_bfloat16>(const __nv_bfloat16*,
                                                              const __nv_bfloat16*,

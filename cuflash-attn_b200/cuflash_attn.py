@@ -55,6 +55,8 @@ SIGNATURES = {
     "cuflash_attention_decode_bf16_noalloc": [_P] * 5 + [_I] * 4 + [_F, _I, _P],
     "cuflash_attention_forward_partial_bf16": [_P] * 5 + [_I] * 5 + [_F, _LL, _LL, _B, _P],
     "cuflash_attention_forward_partial_f16": [_P] * 5 + [_I] * 5 + [_F, _LL, _LL, _B, _P],
+    "cuflash_attention_forward_cp_step_bf16": [_P] * 5 + [_I] * 6 + [_F, _B, _I] + [_P] * 5,
+    "cuflash_attention_forward_cp_step_f16": [_P] * 5 + [_I] * 6 + [_F, _B, _I] + [_P] * 5,
     "cuflash_lse_merge_f32": [_P] * 4 + [_LL, _I, _P],
     "cuflash_convert_f32_to_bf16": [_P, _P, _LL, _P],
     "cuflash_convert_f32_to_f16": [_P, _P, _LL, _P],
@@ -217,6 +219,27 @@ class CuFlashAttn:
                             float(scale), int(q_offset), int(k_offset), bool(causal),
                             _stream_handle(stream)))
         return O, L
+
+    def forward_cp_step(self, Q, K, V, O_acc, L_acc, pairs, causal: bool = True,
+                        scale: Optional[float] = None, stream=None) -> None:
+        """One context-parallel ring step in one launch.  Q [nq,B,H,C,D] and
+        K, V [nk,B,H,C,D] hold stacked chunks; O_acc fp32 [nq,B,H,C,D] and
+        L_acc fp32 [nq,B,H,C] are updated in place.  `pairs` lists up to four
+        (q_slot, kv_slot, q_offset, kv_offset) with distinct q_slot."""
+        nq, B, H, C, D = Q.shape
+        nk = K.shape[0]
+        if scale is None:
+            scale = 1.0 / math.sqrt(D)
+        n = len(pairs)
+        qs = (ctypes.c_int * max(n, 1))(*[int(x[0]) for x in pairs])
+        ks = (ctypes.c_int * max(n, 1))(*[int(x[1]) for x in pairs])
+        qo = (ctypes.c_longlong * max(n, 1))(*[int(x[2]) for x in pairs])
+        ko = (ctypes.c_longlong * max(n, 1))(*[int(x[3]) for x in pairs])
+        fn = getattr(self.lib, f"cuflash_attention_forward_cp_step_{_suffix(Q)}")
+        self.check_error(fn(_ptr(Q), _ptr(K), _ptr(V), _ptr(O_acc), _ptr(L_acc), nq, nk, B, H, C,
+                            D, float(scale), bool(causal), n, ctypes.cast(qs, _P),
+                            ctypes.cast(ks, _P), ctypes.cast(qo, _P), ctypes.cast(ko, _P),
+                            _stream_handle(stream)))
 
     def lse_merge(self, O_acc, L_acc, O_part, L_part, stream=None) -> None:
         rows = L_acc.numel()

@@ -13,8 +13,13 @@ folds the result into a running (O, L) with the log-sum-exp merge
 send/recv (``torch.distributed.batch_isend_irecv``) while the current step
 computes; every remote chunk lands in local HBM before a kernel reads it.
 
-The schedule (``ring_steps`` / ``visible_pairs``) is backend-independent
-and is exercised on CPU with gloo in the tests.
+On the CUDA path all visible pairs of one step run through
+``cuflash_attention_forward_cp_step_*``: one persistent launch per group of
+pairs with distinct query chunks (``distinct_q_groups``), with the
+log-sum-exp merge done in the kernel's epilogue.
+
+The schedule (``ring_steps`` / ``visible_pairs`` / ``distinct_q_groups``) is
+backend-independent and is exercised on CPU with gloo in the tests.
 """
 
 from __future__ import annotations
@@ -55,6 +60,22 @@ def ring_steps(rank: int, world: int) -> List[RingStep]:
         k_chunks = zigzag_chunks(owner, world)
         out.append(RingStep(s, owner, k_chunks, visible_pairs(q_chunks, k_chunks)))
     return out
+
+
+def distinct_q_groups(pairs: Sequence[Tuple]) -> List[List[Tuple]]:
+    """Splits a step's pairs (first element = query slot) into launch groups
+    in which every query slot appears at most once, keeping the order of the
+    pairs of each slot (the in-kernel merge updates each slot once per
+    launch)."""
+    groups: List[List[Tuple]] = []
+    for p in pairs:
+        for g in groups:
+            if all(x[0] != p[0] for x in g):
+                g.append(p)
+                break
+        else:
+            groups.append([p])
+    return groups
 
 
 def run_ring(rank: int, world: int, chunk: int, kv_local, compute_pair: Callable,
@@ -99,25 +120,18 @@ class RingAttention:
 
         world = dist.get_world_size(self.group) if dist.is_initialized() else 1
         rank = dist.get_rank(self.group) if dist.is_initialized() else 0
-        Qa, Qb = q_ab
+        Qa = q_ab[0]
         B, H, C, D = Qa.shape
         dev = Qa.device
         stream = torch.cuda.current_stream(dev)
-        O_acc = [torch.zeros((B, H, C, D), device=dev, dtype=torch.float32) for _ in range(2)]
-        L_acc = [torch.full((B, H, C), float("-inf"), device=dev, dtype=torch.float32)
-                 for _ in range(2)]
-        O_part = torch.empty((B, H, C, D), device=dev, dtype=torch.float32)
-        L_part = torch.empty((B, H, C), device=dev, dtype=torch.float32)
+        Qs = torch.stack(list(q_ab)).contiguous()  # [2, B, H, C, D]
+        O_acc = torch.zeros((2, B, H, C, D), device=dev, dtype=torch.float32)
+        L_acc = torch.full((2, B, H, C), float("-inf"), device=dev, dtype=torch.float32)
         # K/V travel as one buffer [2 (k, v), 2 (chunks), B, H, C, D]
         kv = torch.stack([torch.stack(list(k_ab)), torch.stack(list(v_ab))]).contiguous()
         spare = torch.empty_like(kv)
         state = {"spare": spare}
-
-        def compute_pair(qi, qc, kvbuf, ki, kc):
-            self.lib.forward_partial(q_ab[qi], kvbuf[0, ki], kvbuf[1, ki], qc * C, kc * C,
-                                     causal=True, scale=scale, O=O_part, L=L_part,
-                                     stream=stream)
-            self.lib.lse_merge(O_acc[qi], L_acc[qi], O_part, L_part, stream=stream)
+        q_chunks = zigzag_chunks(rank, world)
 
         def exchange(cur):
             nxt = state["spare"]
@@ -133,10 +147,18 @@ class RingAttention:
 
             return wait
 
-        run_ring(rank, world, C, kv, compute_pair, exchange)
+        cur = kv
+        for st in ring_steps(rank, world):
+            pending = exchange(cur) if st.step + 1 < world else None
+            pairs = [(qi, ki, q_chunks[qi] * C, st.k_chunks[ki] * C) for qi, ki in st.pairs]
+            for group in distinct_q_groups(pairs):
+                self.lib.forward_cp_step(Qs, cur[0], cur[1], O_acc, L_acc, group, causal=True,
+                                         scale=scale, stream=stream)
+            if pending is not None:
+                cur = pending()
         out = []
         for qi in range(2):
             o = torch.empty((B, H, C, D), device=dev, dtype=Qa.dtype)
             self.lib.convert(O_acc[qi], o, stream=stream)
             out.append(o)
-        return out, L_acc
+        return out, [L_acc[0], L_acc[1]]

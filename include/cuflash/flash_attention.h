@@ -199,6 +199,29 @@ CUFLASH_EXPORT int cuflash_attention_forward_partial_f16(
     int num_heads, int seq_q, int seq_k, int head_dim, float scale, long long q_offset,
     long long k_offset, bool causal, cudaStream_t stream);
 
+// One ring step of context-parallel attention in a single launch (no
+// reference counterpart: the reference has no multi-GPU path).  Q and the
+// running result hold num_q_slots query chunks stacked as [slot][B][H][C][D]
+// (O_acc fp32, L_acc fp32 [slot][B][H][C]); K and V hold num_kv_slots chunks
+// the same way.  For each of num_pairs (1..4) pairs i it runs the partial
+// forward of query slot q_slot[i] (global positions q_offset[i]..) against
+// K/V slot kv_slot[i] (global positions kv_offset[i]..), causal on global
+// positions when causal is set, and folds the result into O_acc / L_acc of
+// that slot with the log-sum-exp merge of cuflash_lse_merge_f32.  The pairs
+// of one call must name distinct query slots.  O_acc / L_acc start as 0 /
+// -inf; the slot-index and offset arrays are host memory.
+CUFLASH_EXPORT int cuflash_attention_forward_cp_step_bf16(
+    const __nv_bfloat16* Q, const __nv_bfloat16* K, const __nv_bfloat16* V, float* O_acc,
+    float* L_acc, int num_q_slots, int num_kv_slots, int batch_size, int num_heads,
+    int chunk_len, int head_dim, float scale, bool causal, int num_pairs, const int* q_slot,
+    const int* kv_slot, const long long* q_offset, const long long* kv_offset,
+    cudaStream_t stream);
+CUFLASH_EXPORT int cuflash_attention_forward_cp_step_f16(
+    const half* Q, const half* K, const half* V, float* O_acc, float* L_acc, int num_q_slots,
+    int num_kv_slots, int batch_size, int num_heads, int chunk_len, int head_dim, float scale,
+    bool causal, int num_pairs, const int* q_slot, const int* kv_slot,
+    const long long* q_offset, const long long* kv_offset, cudaStream_t stream);
+
 // Log-sum-exp merge of a partial result into a running one, row by row:
 //   L = log(exp(L_acc) + exp(L_part));
 //   O_acc = exp(L_acc - L) * O_acc + exp(L_part - L) * O_part;  L_acc = L.

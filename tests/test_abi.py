@@ -162,6 +162,35 @@ def test_partial_and_merge_validation(lib, sfx):
     assert m(FAKE, FAKE, FAKE, FAKE, 4, 0, STREAM) == 1
 
 
+@pytest.mark.parametrize("sfx", ["f16", "bf16"])
+def test_cp_step_validation(lib, sfx):
+    import ctypes
+
+    fn = getattr(lib.lib, f"cuflash_attention_forward_cp_step_{sfx}")
+
+    def arr(ct, vals):
+        return ctypes.cast((ct * len(vals))(*vals), ctypes.c_void_p)
+
+    def call(q=(0, 1), k=(0, 1), qo=(0, 64), ko=(0, 64), n=2, D=64, nq=2, nk=2, ptr=None):
+        args = [FAKE] * 5 + [nq, nk, 1, 2, 64, D, 0.1, True, n, arr(ctypes.c_int, q),
+                             arr(ctypes.c_int, k), arr(ctypes.c_longlong, qo),
+                             arr(ctypes.c_longlong, ko), STREAM]
+        if ptr is not None:
+            args[ptr] = NUL
+        return fn(*args)
+
+    assert call(ptr=0) == 3                       # Q null
+    assert call(ptr=4) == 3                       # L_acc null
+    assert call(ptr=14) == 3                      # q_slot array null
+    assert call(D=80) == 6
+    assert call(n=0) == 1 and call(n=5) == 1      # 1..4 pairs
+    assert call(q=(0, 0)) == 1                    # one launch merges each slot once
+    assert call(q=(0, 2)) == 1                    # slot out of range
+    assert call(k=(0, -1)) == 1
+    assert call(qo=(0, -64)) == 1                 # negative global offset
+    assert call(nq=0) == 1
+
+
 def test_oracle_is_test_infrastructure_only():
     """The product path must not import the oracle."""
     pkg = ROOT / "cuflash-attn_b200"

@@ -74,6 +74,77 @@ def test_ring_emulated_on_one_gpu(lib, cuda, world):
             assert max_err(host(L_acc[qi]), host(L_full[:, :, c * C:(c + 1) * C])) < 1e-4
 
 
+@pytest.mark.parametrize("D", [64, 128])
+@pytest.mark.parametrize("dt", ["bf16", "f16"])
+def test_cp_step_matches_partial_plus_merge(lib, cuda, D, dt):
+    """One multi-pair launch with the in-kernel merge equals separate partial
+    forwards folded in with cuflash_lse_merge_f32."""
+    import torch
+
+    B, H, C = 1, 4, 320  # C not a multiple of the 256-row q tile
+    tdt = torch.bfloat16 if dt == "bf16" else torch.float16
+    g = torch.Generator(device="cuda").manual_seed(5)
+    Q = torch.randn((2, B, H, C, D), device="cuda", generator=g).to(tdt)
+    K = torch.randn((3, B, H, C, D), device="cuda", generator=g).to(tdt)
+    V = torch.randn((3, B, H, C, D), device="cuda", generator=g).to(tdt)
+    scale = 1.0 / np.sqrt(D)
+    # running state from an earlier step: slot 0 holds a merged result, slot 1 is empty
+    O0 = torch.randn((2, B, H, C, D), device="cuda", generator=g) * 0.1
+    L0 = torch.randn((2, B, H, C), device="cuda", generator=g)
+    O0[1].zero_()
+    L0[1].fill_(float("-inf"))
+    steps = [
+        [(0, 2, 5 * C, 1 * C), (1, 0, 2 * C, 2 * C)],  # fully visible; diagonal
+        [(1, 1, 2 * C, 3 * C)],                         # fully masked (keys after queries)
+        [(0, 1, 5 * C, 5 * C), (1, 2, 2 * C, 0)],        # diagonal; fully visible
+    ]
+    Oa, La = O0.clone(), L0.clone()
+    Ob, Lb = O0.clone(), L0.clone()
+    for pairs in steps:
+        lib.forward_cp_step(Q, K, V, Oa, La, pairs, causal=True, scale=scale)
+        for qs, ks, qo, ko in pairs:
+            Op, Lp = lib.forward_partial(Q[qs], K[ks], V[ks], qo, ko, causal=True, scale=scale)
+            lib.lse_merge(Ob[qs], Lb[qs], Op, Lp)
+    torch.cuda.synchronize()
+    assert torch.allclose(Oa, Ob, rtol=1e-5, atol=1e-6), float((Oa - Ob).abs().max())
+    fin = torch.isfinite(Lb)
+    assert torch.equal(fin, torch.isfinite(La))
+    assert torch.allclose(La[fin], Lb[fin], rtol=1e-6, atol=1e-5)
+
+
+@pytest.mark.parametrize("world", [1, 2, 4])
+def test_ring_cp_step_emulated_on_one_gpu(lib, cuda, world):
+    """The ring schedule through the single-launch step entry, P ranks
+    emulated on one GPU, equals the single-GPU causal forward."""
+    import torch
+
+    B, H, D = 1, 4, 128
+    C = 256
+    N = 2 * world * C
+    Qh, Kh, Vh = (round_to(oracle.normal((B, H, N, D), s), "bf16") for s in (41, 42, 43))
+    Q, K, V = (to_dev(x, "bf16") for x in (Qh, Kh, Vh))
+    scale = 1.0 / np.sqrt(D)
+    O_full, L_full = _full_forward(lib, Q, K, V, scale)
+    sl = lambda x, c: x[:, :, c * C:(c + 1) * C].contiguous()
+    stack = lambda x, cs: torch.stack([sl(x, c) for c in cs]).contiguous()
+    for r in range(world):
+        chunks = ring_cp.zigzag_chunks(r, world)
+        Qs = stack(Q, chunks)
+        O_acc = torch.zeros((2, B, H, C, D), device="cuda")
+        L_acc = torch.full((2, B, H, C), float("-inf"), device="cuda")
+        for st in ring_cp.ring_steps(r, world):
+            Ks, Vs = stack(K, st.k_chunks), stack(V, st.k_chunks)
+            pairs = [(qi, ki, chunks[qi] * C, st.k_chunks[ki] * C) for qi, ki in st.pairs]
+            for grp in ring_cp.distinct_q_groups(pairs):
+                lib.forward_cp_step(Qs, Ks, Vs, O_acc, L_acc, grp, causal=True, scale=scale)
+        for qi, c in enumerate(chunks):
+            o = torch.empty((B, H, C, D), device="cuda", dtype=torch.bfloat16)
+            lib.convert(O_acc[qi], o)
+            torch.cuda.synchronize()
+            assert max_err(host(o), host(O_full[:, :, c * C:(c + 1) * C])) < 1e-2
+            assert max_err(host(L_acc[qi]), host(L_full[:, :, c * C:(c + 1) * C])) < 1e-4
+
+
 def _free_port():
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))

@@ -37,6 +37,20 @@ def test_schedule_covers_every_visible_pair_once(world):
     assert max(work) == min(work)
 
 
+def test_distinct_q_groups():
+    pairs = [(0, 0, "a"), (0, 1, "b"), (1, 0, "c"), (1, 1, "d")]
+    groups = ring_cp.distinct_q_groups(pairs)
+    assert groups == [[(0, 0, "a"), (1, 0, "c")], [(0, 1, "b"), (1, 1, "d")]]
+    for g in groups:
+        assert len({x[0] for x in g}) == len(g)
+    # every step of every schedule splits into at most two launches
+    for world in (1, 2, 3, 8):
+        for r in range(world):
+            for st in ring_cp.ring_steps(r, world):
+                gs = ring_cp.distinct_q_groups([(qi, ki) for qi, ki in st.pairs])
+                assert sum(len(g) for g in gs) == len(st.pairs) and len(gs) <= 2
+
+
 def _free_port():
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))
