@@ -743,7 +743,10 @@ FlashAttentionError launch_typed(const T* Q, const T* K, const T* V, void* O, fl
     prm.seg_units = static_cast<int>(seg_units);
     prm.num_units = static_cast<int>(units);
     // persistent: one CTA per SM (the shared-memory footprint allows one)
-    const int grid = static_cast<int>(std::min<long long>(units, sms));
+    // per wave; multi-segment (ring step) launches overlap NCCL transfers
+    const int grid = persistent_grid(
+        units, sg.num_segs > 1 || sg.merge ? env_waves("CUFLASH_CP_WAVES", 1)
+                                           : env_waves("CUFLASH_FWD_WAVES", 1));
     if (grid <= 0) return FlashAttentionError::SUCCESS;
     kern<<<grid, 384, G::kSmemBytes, stream>>>(mq, mk, mv, prm);
     return cudaGetLastError() == cudaSuccess ? FlashAttentionError::SUCCESS

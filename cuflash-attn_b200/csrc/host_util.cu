@@ -68,6 +68,22 @@ bool ensure_smem_attr(const void* kernel, int bytes) {
     return true;
 }
 
+// CTAs per launch of the persistent kernels: waves x SM count (capped by the
+// work).  One wave is the fastest when the kernel has the GPU to itself;
+// more waves let the block scheduler rebalance when other kernels (NCCL
+// transfers) hold SMs at launch time, at the price of more per-CTA setup.
+int persistent_grid(long long units, int waves) {
+    const long long cap = static_cast<long long>(current_sm_count()) * (waves > 0 ? waves : 1);
+    return static_cast<int>(units < cap ? units : cap);
+}
+
+int env_waves(const char* name, int dflt) {
+    const char* v = getenv(name);
+    if (!v || !*v) return dflt;
+    const int n = atoi(v);
+    return n >= 1 && n <= 16 ? n : dflt;
+}
+
 int current_sm_count() {
     static std::mutex mu;
     static int cache[64] = {0};
