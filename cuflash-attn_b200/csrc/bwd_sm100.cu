@@ -872,7 +872,7 @@ FlashAttentionError bwd_typed(const T* Q, const T* K, const T* V, const T* O, co
     prm.scale_log2 = scale * kLog2eB;
     prm.scale = scale;
     // persistent: one CTA per SM (the shared-memory footprint allows one)
-    const int grid = persistent_grid(units, env_waves("CUFLASH_BWD_WAVES", 1));
+    const int grid = persistent_grid(units, env_int("CUFLASH_BWD_WAVES", 1));
     kern<<<grid, kBwdThreads, G::kSmemBytes, stream>>>(mq, mk, mv, mdo, mdq, prm);
     if (cudaGetLastError() != cudaSuccess) return fail(FlashAttentionError::CUDA_ERROR);
 

@@ -69,7 +69,7 @@ bool ensure_smem_attr(const void* kernel, int bytes);
 
 int current_sm_count();
 int persistent_grid(long long units, int waves);
-int env_waves(const char* name, int dflt);
+int env_int(const char* name, int dflt);
 
 // Stream-ordered workspace from a library-private memory pool on the current
 // device (created on first use; freed blocks stay cached in the pool so

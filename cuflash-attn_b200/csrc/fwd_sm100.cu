@@ -744,9 +744,12 @@ FlashAttentionError launch_typed(const T* Q, const T* K, const T* V, void* O, fl
     prm.num_units = static_cast<int>(units);
     // persistent: one CTA per SM (the shared-memory footprint allows one)
     // per wave; multi-segment (ring step) launches overlap NCCL transfers
-    const int grid = persistent_grid(
-        units, sg.num_segs > 1 || sg.merge ? env_waves("CUFLASH_CP_WAVES", 1)
-                                           : env_waves("CUFLASH_FWD_WAVES", 1));
+    int grid = persistent_grid(units, sg.merge ? env_int("CUFLASH_CP_WAVES", 1)
+                                               : env_int("CUFLASH_FWD_WAVES", 1));
+    // A ring step runs while NCCL moves the next step's K/V; a CTA of this
+    // kernel fills an SM (registers and shared memory), so SMs left free let
+    // the transfer kernels run concurrently instead of after this launch.
+    if (sg.merge) grid = std::max(1, std::min(grid, sms - env_int("CUFLASH_CP_RESERVE_SMS", 0)));
     if (grid <= 0) return FlashAttentionError::SUCCESS;
     kern<<<grid, 384, G::kSmemBytes, stream>>>(mq, mk, mv, prm);
     return cudaGetLastError() == cudaSuccess ? FlashAttentionError::SUCCESS

@@ -77,11 +77,11 @@ int persistent_grid(long long units, int waves) {
     return static_cast<int>(units < cap ? units : cap);
 }
 
-int env_waves(const char* name, int dflt) {
+int env_int(const char* name, int dflt) {
     const char* v = getenv(name);
     if (!v || !*v) return dflt;
     const int n = atoi(v);
-    return n >= 1 && n <= 16 ? n : dflt;
+    return n >= 0 && n <= 64 ? n : dflt;
 }
 
 int current_sm_count() {
