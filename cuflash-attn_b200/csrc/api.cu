@@ -13,6 +13,7 @@
 // kernels; there is no CPU path.
 
 #include <cmath>
+#include <initializer_list>
 
 #include "common.cuh"
 
@@ -193,6 +194,42 @@ FlashAttentionError partial_impl(const T* Q, const T* K, const T* V, float* O, f
                                                 causal, q_offset, k_offset, true, stream);
 }
 
+// Grouped-query / unequal-length checks, in the reference's order (null
+// pointers, dimensions, head_dim, scale) plus the head-group relation.
+FlashAttentionError validate_gqa(std::initializer_list<const void*> ptrs, int B, int Hq, int Hkv,
+                                 int Nq, int Nk, int D, float scale) {
+    for (const void* ptr : ptrs)
+        if (!ptr) return FlashAttentionError::NULL_POINTER;
+    if (B <= 0 || Hq <= 0 || Hkv <= 0 || Nq <= 0 || Nk <= 0 || D <= 0)
+        return FlashAttentionError::INVALID_DIMENSION;
+    if (Hq % Hkv != 0) return FlashAttentionError::DIMENSION_MISMATCH;
+    if (!(D == 32 || D == 64 || D == 128)) return FlashAttentionError::UNSUPPORTED_HEAD_DIM;
+    if (!std::isfinite(scale) || scale < 0.0f) return FlashAttentionError::INVALID_DIMENSION;
+    if (static_cast<long long>(B) * Hq > 0x7fffffffLL) return FlashAttentionError::INVALID_DIMENSION;
+    return FlashAttentionError::SUCCESS;
+}
+
+template <typename T>
+FlashAttentionError fwd_gqa_impl(const T* Q, const T* K, const T* V, T* O, float* L, int B, int Hq,
+                                 int Hkv, int Nq, int Nk, int D, float scale, bool causal,
+                                 cudaStream_t stream) {
+    const FlashAttentionError e = validate_gqa({Q, K, V, O, L}, B, Hq, Hkv, Nq, Nk, D, scale);
+    if (e != FlashAttentionError::SUCCESS) return e;
+    return cuflash::detail::launch_fwd_gqa_sm100<T>(Q, K, V, O, L, B, Hq, Hkv, Nq, Nk, D, scale,
+                                                    causal, stream);
+}
+
+template <typename T>
+FlashAttentionError bwd_gqa_impl(const T* Q, const T* K, const T* V, const T* O, const float* L,
+                                 const T* dO, T* dQ, T* dK, T* dV, int B, int Hq, int Hkv, int Nq,
+                                 int Nk, int D, float scale, bool causal, cudaStream_t stream) {
+    const FlashAttentionError e =
+        validate_gqa({dO, dQ, dK, dV, Q, K, V, O, L}, B, Hq, Hkv, Nq, Nk, D, scale);
+    if (e != FlashAttentionError::SUCCESS) return e;
+    return cuflash::detail::launch_bwd_gqa_sm100<T>(Q, K, V, O, L, dO, dQ, dK, dV, B, Hq, Hkv, Nq,
+                                                    Nk, D, scale, causal, stream);
+}
+
 template <typename T>
 FlashAttentionError cp_step_impl(const T* Q, const T* K, const T* V, float* O_acc, float* L_acc,
                                  int nq, int nk, int B, int H, int C, int D, float scale,
@@ -312,6 +349,47 @@ int cuflash_attention_forward_partial_f16(const half* Q, const half* K, const ha
     return static_cast<int>(partial_impl<half>(Q, K, V, O_part, L_part, batch_size, num_heads,
                                                seq_q, seq_k, head_dim, scale, q_offset, k_offset,
                                                causal, stream));
+}
+
+int cuflash_attention_forward_gqa_bf16(const __nv_bfloat16* Q, const __nv_bfloat16* K,
+                                       const __nv_bfloat16* V, __nv_bfloat16* O, float* L,
+                                       int batch_size, int num_q_heads, int num_kv_heads,
+                                       int seq_len_q, int seq_len_k, int head_dim, float scale,
+                                       bool causal, cudaStream_t stream) {
+    return static_cast<int>(fwd_gqa_impl<__nv_bfloat16>(Q, K, V, O, L, batch_size, num_q_heads,
+                                                        num_kv_heads, seq_len_q, seq_len_k,
+                                                        head_dim, scale, causal, stream));
+}
+
+int cuflash_attention_forward_gqa_f16(const half* Q, const half* K, const half* V, half* O,
+                                      float* L, int batch_size, int num_q_heads, int num_kv_heads,
+                                      int seq_len_q, int seq_len_k, int head_dim, float scale,
+                                      bool causal, cudaStream_t stream) {
+    return static_cast<int>(fwd_gqa_impl<half>(Q, K, V, O, L, batch_size, num_q_heads,
+                                               num_kv_heads, seq_len_q, seq_len_k, head_dim,
+                                               scale, causal, stream));
+}
+
+int cuflash_attention_backward_gqa_bf16(const __nv_bfloat16* Q, const __nv_bfloat16* K,
+                                        const __nv_bfloat16* V, const __nv_bfloat16* O,
+                                        const float* L, const __nv_bfloat16* dO,
+                                        __nv_bfloat16* dQ, __nv_bfloat16* dK, __nv_bfloat16* dV,
+                                        int batch_size, int num_q_heads, int num_kv_heads,
+                                        int seq_len_q, int seq_len_k, int head_dim, float scale,
+                                        bool causal, cudaStream_t stream) {
+    return static_cast<int>(bwd_gqa_impl<__nv_bfloat16>(
+        Q, K, V, O, L, dO, dQ, dK, dV, batch_size, num_q_heads, num_kv_heads, seq_len_q,
+        seq_len_k, head_dim, scale, causal, stream));
+}
+
+int cuflash_attention_backward_gqa_f16(const half* Q, const half* K, const half* V, const half* O,
+                                       const float* L, const half* dO, half* dQ, half* dK,
+                                       half* dV, int batch_size, int num_q_heads, int num_kv_heads,
+                                       int seq_len_q, int seq_len_k, int head_dim, float scale,
+                                       bool causal, cudaStream_t stream) {
+    return static_cast<int>(bwd_gqa_impl<half>(Q, K, V, O, L, dO, dQ, dK, dV, batch_size,
+                                               num_q_heads, num_kv_heads, seq_len_q, seq_len_k,
+                                               head_dim, scale, causal, stream));
 }
 
 int cuflash_attention_forward_cp_step_bf16(const __nv_bfloat16* Q, const __nv_bfloat16* K,

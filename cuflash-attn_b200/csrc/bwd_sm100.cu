@@ -90,13 +90,19 @@ struct BwdParams {
     float* dq_acc;
     void* dK;
     void* dV;
-    const float* l2p;  // -L * log2(e), padded to n_blk*128 per (b,h) with -inf
+    const float* l2p;  // -L * log2(e), padded to n_blk_q*128 per query head with -inf
     const float* dvp;  // -rowsum(dO*O), padded with 0
-    int N;
-    int n_blk;
-    int npairs;     // (n_blk + 1) / 2
-    int paired;     // 1: a unit is a (heavy, light) pair of kv blocks; 0: one kv block
-    int num_units;  // BH * npairs, or BH * n_blk when not paired
+    int Nq;            // query length
+    int Nk;            // key length
+    int n_blk_q;
+    int n_blk_k;
+    long long q_off;   // global position of query 0 (keys start at 0); causal: key k visible
+                       // to query q iff k <= q_off + q
+    int hq;            // query heads per batch entry
+    int group;         // query heads per K/V head
+    int npairs;        // (n_blk_k + 1) / 2
+    int paired;        // 1: a unit is a (heavy, light) pair of kv blocks; 0: one kv block
+    int num_units;     // B*Hkv * npairs, or B*Hkv * n_blk_k when not paired
     int causal;
     float scale_log2;
     float scale;
@@ -111,23 +117,54 @@ struct BwdParams {
 // per unit instead.
 struct BwdItem {
     int j;
-    int bh;
+    int bh;  // K/V head: batch * Hkv + kv head
 };
 
 __device__ __forceinline__ bool bwd_item(const BwdParams& p, int u, int w, BwdItem& it) {
     if (!p.paired) {
         if (w == 1) return false;
-        it.bh = u / p.n_blk;
-        it.j = u - it.bh * p.n_blk;  // ascending j: heaviest first under a causal mask
+        it.bh = u / p.n_blk_k;
+        it.j = u - it.bh * p.n_blk_k;  // ascending j: heaviest first under a causal mask
         return true;
     }
     const int bh = u / p.npairs;
     const int k = u - bh * p.npairs;
-    const int j = w == 0 ? k : p.n_blk - 1 - k;
+    const int j = w == 0 ? k : p.n_blk_k - 1 - k;
     if (w == 1 && j == k) return false;  // middle block of an odd count
     it.j = j;
     it.bh = bh;
     return true;
+}
+
+// The query walk of an item: for each of the group's query heads, the query
+// blocks i0..n_blk_q-1 that see any key of block j (all of them unless causal).
+struct BwdWalk {
+    int i0;  // first visible query block
+    int ni;  // blocks per query head
+    int n;   // group * ni
+};
+
+__device__ __forceinline__ BwdWalk bwd_walk(const BwdParams& p, int j) {
+    BwdWalk w;
+    w.i0 = 0;
+    if (p.causal) {
+        // first query block with q_off + 128 i + 127 >= 128 j
+        const long long num = 128LL * j - p.q_off - 127;
+        const long long i0 = num <= 0 ? 0 : (num + 127) / 128;
+        w.i0 = static_cast<int>(i0 < p.n_blk_q ? i0 : p.n_blk_q);
+    }
+    w.ni = p.n_blk_q - w.i0;
+    w.n = p.group * w.ni;
+    return w;
+}
+
+// Query head and block of walk step `it`.
+__device__ __forceinline__ void bwd_step(const BwdParams& p, const BwdItem& itm, const BwdWalk& w,
+                                         int it, int& bh_q, int& i) {
+    const int gq = w.ni > 0 ? it / w.ni : 0;
+    i = w.i0 + (it - gq * w.ni);
+    const int hkv = p.hq / p.group;
+    bh_q = (itm.bh / hkv) * p.hq + (itm.bh % hkv) * p.group + gq;
 }
 
 template <int D>
@@ -293,11 +330,12 @@ __global__ void __launch_bounds__(256)
 // next sub-chunk's S^T / dP^T columns load while this one is computed.  P^T /
 // dS^T of sub-chunk k go to columns [8k, 8k+8) of the warpgroup's S^T / dP^T
 // range, which hold queries already loaded (sub-chunks 0..k/2).  kDiag masks
-// the keys above the causal diagonal (query < kv row).
+// the keys above the causal diagonal: query q of the block against kv row r
+// is hidden iff q < r + delta, delta = 128 (j - i) - q_off.
 template <typename T, bool kDiag>
 __device__ __forceinline__ void bwd_softmax_block(uint32_t t_s, uint32_t t_dp, uint32_t sDs,
                                                   const float* sL, const float* sD, float c,
-                                                  int h, int r) {
+                                                  int h, int r, int delta) {
     using namespace sm100;
     const uint64_t c2 = f2_pack(c, c);
     uint32_t sA[16], dA[16], sB[16], dB[16];
@@ -333,9 +371,9 @@ __device__ __forceinline__ void bwd_softmax_block(uint32_t t_s, uint32_t t_dp, u
                     p0 = ex2_approx(xx.x);  // MUFU
                     p1 = ex2_approx(xx.y);
                 }
-                if (kDiag) {
-                    if (q0 < r) p0 = 0.f;
-                    if (q0 + 1 < r) p1 = 0.f;
+                if (kDiag) {  // query q0 (global q_off + 128 i + q0) vs key 128 j + r
+                    if (q0 < r + delta) p0 = 0.f;
+                    if (q0 + 1 < r + delta) p1 = 0.f;
                 }
                 const float2 d = f2_unpack(f2_mul(
                     f2_pack(p0, p1),
@@ -447,13 +485,13 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
             uint32_t g = 0;        // stage loads issued
             uint32_t items = 0;    // K/V loads issued
             bool ok = true;
-            auto load_stage = [&](int bh, int i) {
+            auto load_stage = [&](int bh, int i) {  // bh: query head
                 const int s = g % G::kStages;
                 if (g >= G::kStages &&
                     !mbar_wait(empty + s, ((g / G::kStages) & 1) ^ 1, abort_flag, &g_bwd_status))
                     return false;
                 uint8_t* st = sptr + G::kOffStage + s * G::kStageBytes;
-                const size_t lrow = static_cast<size_t>(bh) * p.n_blk * 128;
+                const size_t lrow = static_cast<size_t>(bh) * p.n_blk_q * 128;
                 mbar_arrive_expect_tx(full + s, 2 * G::kTileBytes + 1024);
                 for (int cb = 0; cb < G::kNumCb; ++cb) {
                     tma_load_3d(st + cb * G::kCbBytes, &tmQ, full + s, cb * G::kCbElems, i * 128,
@@ -470,13 +508,18 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
                 for (int w = 0; ok && w < 2; ++w) {
                     BwdItem itm;
                     if (!bwd_item(p, u, w, itm)) continue;
-                    const int i0 = p.causal ? itm.j : 0;
-                    const int n_it = p.n_blk - i0;
+                    const BwdWalk wk = bwd_walk(p, itm.j);
+                    const int n_it = wk.n;
+                    auto load_step = [&](int it) {
+                        int bh_q, i;
+                        bwd_step(p, itm, wk, it, bh_q, i);
+                        return load_stage(bh_q, i);
+                    };
                     // The item's first stages only need free ring slots, so they go
                     // ahead of K_j, V_j, which wait for the previous item's MMAs
                     // (the first item loads K_j, V_j first).
                     const int pre = items == 0 ? 0 : min(n_it, G::kStages);
-                    for (int it = 0; ok && it < pre; ++it) ok = load_stage(itm.bh, i0 + it);
+                    for (int it = 0; ok && it < pre; ++it) ok = load_step(it);
                     // K_j, V_j: the previous item's MMAs must be done with the buffers
                     if (ok && items > 0)
                         ok = mbar_wait(bar_acc, (items - 1) & 1, abort_flag, &g_bwd_status);
@@ -489,7 +532,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
                                     cb * G::kCbElems, itm.j * 128, itm.bh);
                     }
                     ++items;
-                    for (int it = pre; ok && it < n_it; ++it) ok = load_stage(itm.bh, i0 + it);
+                    for (int it = pre; ok && it < n_it; ++it) ok = load_step(it);
                 }
             }
             // every issued load must land before the CTA can exit
@@ -534,7 +577,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
                 for (int w = 0; ok && w < 2; ++w) {
                     BwdItem itm;
                     if (!bwd_item(p, u, w, itm)) continue;
-                    const int n_it = p.n_blk - (p.causal ? itm.j : 0);
+                    const int n_it = bwd_walk(p, itm.j).n;
                     // K_j, V_j and the item's first query block
                     ok = mbar_wait(bar_kv, items & 1, abort_flag, &g_bwd_status) &&
                          mbar_wait(full + g % G::kStages, (g / G::kStages) & 1, abort_flag,
@@ -641,11 +684,12 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
             for (int w = 0; ok && w < 2; ++w) {
                 BwdItem itm;
                 if (!bwd_item(p, u, w, itm)) continue;
-                const int j = itm.j, bh = itm.bh;
-                const int i0 = p.causal ? j : 0;
-                const int n_it = p.n_blk - i0;
+                const int j = itm.j, bh = itm.bh;  // bh: K/V head (dK, dV rows)
+                const BwdWalk wk = bwd_walk(p, j);
+                const int n_it = wk.n;
                 for (int it = 0; it < n_it; ++it, ++g) {
-                    const int i = i0 + it;
+                    int bh_q, i;
+                    bwd_step(p, itm, wk, it, bh_q, i);
                     const int s = g % G::kStages;
                     // L and D of block i arrived through the async proxy: observe
                     // the stage's own barrier before reading them (it completes
@@ -661,10 +705,12 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
                                                        2 * G::kTileBytes) +
                         h * 64;
                     const float* sD = sL + 128;
-                    if (p.causal && i == j)
-                        bwd_softmax_block<T, true>(t_s, t_dp, sDs, sL, sD, c, h, r);
+                    const long long dl = 128LL * (j - i) - p.q_off;
+                    if (p.causal && dl > -127)
+                        bwd_softmax_block<T, true>(t_s, t_dp, sDs, sL, sD, c, h, r,
+                                                   static_cast<int>(dl));
                     else
-                        bwd_softmax_block<T, false>(t_s, t_dp, sDs, sL, sD, c, h, r);
+                        bwd_softmax_block<T, false>(t_s, t_dp, sDs, sL, sD, c, h, r, 0);
                     tmem_wait_st();
                     fence_proxy_async_smem();
                     tc_fence_before();
@@ -677,8 +723,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
                 ++items;
                 // warpgroup 0 stores dV, warpgroup 1 stores dK (scaled)
                 const int kv = j * 128 + r;
-                const bool valid = kv < p.N;
-                const size_t row = (static_cast<size_t>(bh) * p.N + kv) * D;
+                const bool valid = kv < p.Nk;
+                const size_t row = (static_cast<size_t>(bh) * p.Nk + kv) * D;
                 T* dst_base = static_cast<T*>(h == 0 ? p.dV : p.dK);
                 const float mul = h == 0 ? 1.f : p.scale;
                 const uint32_t t_acc = tmem + lane_addr + (h == 0 ? 256 : 384);
@@ -719,14 +765,14 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
             for (int w = 0; ok && w < 2; ++w) {
                 BwdItem itm;
                 if (!bwd_item(p, u, w, itm)) continue;
-                const int bh = itm.bh;
-                const int i0 = p.causal ? itm.j : 0;
-                const int n_it = p.n_blk - i0;
+                const BwdWalk wk = bwd_walk(p, itm.j);
+                const int n_it = wk.n;
                 if constexpr (kTransposedDq) {
                     // lane = head_dim element d; TMEM column = query row of block i
                     const int d = wq * 32 + lane;
                     for (int it = 0; it < n_it; ++it, ++g) {
-                        const int i = i0 + it;
+                        int bh, i;  // query head and block
+                        bwd_step(p, itm, wk, it, bh, i);
                         if (!bwarp_wait(bar_dq, g & 1, abort_flag)) {
                             ok = false;
                             break;
@@ -739,8 +785,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
                         // reductions so the next dP MMA is not held up
                         tc_fence_before();
                         mbar_arrive(bar_dqfree);
-                        float* dst = p.dq_acc + (static_cast<size_t>(bh) * p.N + i * 128) * D + d;
-                        const int qn = min(128, p.N - i * 128);
+                        float* dst = p.dq_acc + (static_cast<size_t>(bh) * p.Nq + i * 128) * D + d;
+                        const int qn = min(128, p.Nq - i * 128);
                         auto flush = [&](const uint32_t(&v)[32], int q0) {
 #pragma unroll
                             for (int e = 0; e < 32; ++e)
@@ -762,7 +808,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
                     // this drain signals bar_dqfree.
                     const uint32_t stage0 = sbase + G::kOffDs + wq * 8192;
                     for (int it = 0; it < n_it; ++it, ++g) {
-                        const int i = i0 + it;
+                        int bh, i;  // query head and block
+                        bwd_step(p, itm, wk, it, bh, i);
                         if (!bwarp_wait(bar_dq, g & 1, abort_flag)) {
                             ok = false;
                             break;
@@ -807,14 +854,18 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     }
 }
 
+// B*Hq query heads (BH) over Nq queries, B*Hkv = BH/group K/V heads over Nk keys.
 template <typename T, int D>
 FlashAttentionError bwd_typed(const T* Q, const T* K, const T* V, const T* O, const float* L,
-                              const T* dO, T* dQ, T* dK, T* dV, int BH, int N, float scale,
-                              bool causal, cudaStream_t stream) {
+                              const T* dO, T* dQ, T* dK, T* dV, int BH, int Hq, int group, int Nq,
+                              int Nk, long long q_off, float scale, bool causal,
+                              cudaStream_t stream) {
     using G = BwdGeom<D>;
-    const int n_blk = (N + 127) / 128;
-    const long long n_pad = static_cast<long long>(n_blk) * 128;
-    const size_t acc_elems = static_cast<size_t>(BH) * N * D;
+    const int BHk = BH / group;
+    const int n_blk_q = (Nq + 127) / 128;
+    const int n_blk_k = (Nk + 127) / 128;
+    const long long n_pad = static_cast<long long>(n_blk_q) * 128;
+    const size_t acc_elems = static_cast<size_t>(BH) * Nq * D;
     const size_t pad_elems = static_cast<size_t>(BH) * n_pad;
     void* ws = nullptr;
     FlashAttentionError e =
@@ -831,11 +882,11 @@ FlashAttentionError bwd_typed(const T* Q, const T* K, const T* V, const T* O, co
     const CUtensorMapSwizzle swz =
         G::kSwz == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
     CUtensorMap mq, mk, mv, mdo, mdq;
-    if (!encode_tmap_3d(&mq, Q, DType<T>::kTmaType, 2, D, N, BH, G::kCbElems, 128, swz) ||
-        !encode_tmap_3d(&mk, K, DType<T>::kTmaType, 2, D, N, BH, G::kCbElems, 128, swz) ||
-        !encode_tmap_3d(&mv, V, DType<T>::kTmaType, 2, D, N, BH, G::kCbElems, 128, swz) ||
-        !encode_tmap_3d(&mdo, dO, DType<T>::kTmaType, 2, D, N, BH, G::kCbElems, 128, swz) ||
-        !encode_tmap_3d(&mdq, dq_acc, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, D, N, BH, 32, 32,
+    if (!encode_tmap_3d(&mq, Q, DType<T>::kTmaType, 2, D, Nq, BH, G::kCbElems, 128, swz) ||
+        !encode_tmap_3d(&mk, K, DType<T>::kTmaType, 2, D, Nk, BHk, G::kCbElems, 128, swz) ||
+        !encode_tmap_3d(&mv, V, DType<T>::kTmaType, 2, D, Nk, BHk, G::kCbElems, 128, swz) ||
+        !encode_tmap_3d(&mdo, dO, DType<T>::kTmaType, 2, D, Nq, BH, G::kCbElems, 128, swz) ||
+        !encode_tmap_3d(&mdq, dq_acc, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, D, Nq, BH, 32, 32,
                         CU_TENSOR_MAP_SWIZZLE_128B))
         return fail(FlashAttentionError::CUDA_ERROR);
     for (const void* ptr : {static_cast<const void*>(O), static_cast<const void*>(dQ),
@@ -849,7 +900,7 @@ FlashAttentionError bwd_typed(const T* Q, const T* K, const T* V, const T* O, co
     const long long rows_pad = static_cast<long long>(BH) * n_pad;
     const long long pre_blocks = (rows_pad * (D / 8) + 255) / 256;
     bwd_preprocess_kernel<T, D><<<static_cast<unsigned>(pre_blocks), 256, 0, stream>>>(
-        O, dO, L, l2p, dvp, dq_acc, N, static_cast<int>(n_pad), rows_pad);
+        O, dO, L, l2p, dvp, dq_acc, Nq, static_cast<int>(n_pad), rows_pad);
     if (cudaGetLastError() != cudaSuccess) return fail(FlashAttentionError::CUDA_ERROR);
 
     BwdParams prm;
@@ -858,14 +909,19 @@ FlashAttentionError bwd_typed(const T* Q, const T* K, const T* V, const T* O, co
     prm.dV = dV;
     prm.l2p = l2p;
     prm.dvp = dvp;
-    prm.N = N;
-    prm.n_blk = n_blk;
-    prm.npairs = (n_blk + 1) / 2;
+    prm.Nq = Nq;
+    prm.Nk = Nk;
+    prm.n_blk_q = n_blk_q;
+    prm.n_blk_k = n_blk_k;
+    prm.q_off = q_off;
+    prm.hq = Hq;
+    prm.group = group;
+    prm.npairs = (n_blk_k + 1) / 2;
     const int sms = current_sm_count();
-    long long units = static_cast<long long>(BH) * prm.npairs;
-    // pairing only balances a causal walk (non-causal items all cost n_blk)
+    long long units = static_cast<long long>(BHk) * prm.npairs;
+    // pairing only balances a causal walk (non-causal items all cost n_blk_q)
     prm.paired = (causal && units >= sms) ? 1 : 0;
-    if (!prm.paired) units = static_cast<long long>(BH) * n_blk;
+    if (!prm.paired) units = static_cast<long long>(BHk) * n_blk_k;
     if (units > 0x7fffffffLL) return fail(FlashAttentionError::CUDA_ERROR);
     prm.num_units = static_cast<int>(units);
     prm.causal = causal ? 1 : 0;
@@ -887,6 +943,28 @@ FlashAttentionError bwd_typed(const T* Q, const T* K, const T* V, const T* O, co
     return FlashAttentionError::SUCCESS;
 }
 
+template <typename T>
+FlashAttentionError bwd_dispatch(const T* Q, const T* K, const T* V, const T* O, const float* L,
+                                 const T* dO, T* dQ, T* dK, T* dV, int B, int Hq, int Hkv, int Nq,
+                                 int Nk, int D, long long q_off, float scale, bool causal,
+                                 cudaStream_t stream) {
+    const int BH = B * Hq;
+    const int group = Hq / Hkv;
+    switch (D) {
+        case 32:
+            return bwd_typed<T, 32>(Q, K, V, O, L, dO, dQ, dK, dV, BH, Hq, group, Nq, Nk, q_off,
+                                    scale, causal, stream);
+        case 64:
+            return bwd_typed<T, 64>(Q, K, V, O, L, dO, dQ, dK, dV, BH, Hq, group, Nq, Nk, q_off,
+                                    scale, causal, stream);
+        case 128:
+            return bwd_typed<T, 128>(Q, K, V, O, L, dO, dQ, dK, dV, BH, Hq, group, Nq, Nk, q_off,
+                                     scale, causal, stream);
+        default:
+            return FlashAttentionError::UNSUPPORTED_HEAD_DIM;
+    }
+}
+
 }  // namespace
 
 template <typename T>
@@ -894,18 +972,28 @@ FlashAttentionError launch_bwd_sm100(const T* Q, const T* K, const T* V, const T
                                      const float* L, const T* dO, T* dQ, T* dK, T* dV, int B,
                                      int H, int N, int D, float scale, bool causal,
                                      cudaStream_t stream) {
-    const int BH = B * H;
-    switch (D) {
-        case 32:
-            return bwd_typed<T, 32>(Q, K, V, O, L, dO, dQ, dK, dV, BH, N, scale, causal, stream);
-        case 64:
-            return bwd_typed<T, 64>(Q, K, V, O, L, dO, dQ, dK, dV, BH, N, scale, causal, stream);
-        case 128:
-            return bwd_typed<T, 128>(Q, K, V, O, L, dO, dQ, dK, dV, BH, N, scale, causal, stream);
-        default:
-            return FlashAttentionError::UNSUPPORTED_HEAD_DIM;
-    }
+    return bwd_dispatch<T>(Q, K, V, O, L, dO, dQ, dK, dV, B, H, H, N, N, D, 0, scale, causal,
+                           stream);
 }
+
+template <typename T>
+FlashAttentionError launch_bwd_gqa_sm100(const T* Q, const T* K, const T* V, const T* O,
+                                         const float* L, const T* dO, T* dQ, T* dK, T* dV, int B,
+                                         int Hq, int Hkv, int seq_q, int seq_k, int D, float scale,
+                                         bool causal, cudaStream_t stream) {
+    // bottom-right causal alignment, as the grouped-query forward
+    return bwd_dispatch<T>(Q, K, V, O, L, dO, dQ, dK, dV, B, Hq, Hkv, seq_q, seq_k, D,
+                           static_cast<long long>(seq_k) - seq_q, scale, causal, stream);
+}
+
+template FlashAttentionError launch_bwd_gqa_sm100<half>(const half*, const half*, const half*,
+                                                        const half*, const float*, const half*,
+                                                        half*, half*, half*, int, int, int, int,
+                                                        int, int, float, bool, cudaStream_t);
+template FlashAttentionError launch_bwd_gqa_sm100<__nv_bfloat16>(
+    const __nv_bfloat16*, const __nv_bfloat16*, const __nv_bfloat16*, const __nv_bfloat16*,
+    const float*, const __nv_bfloat16*, __nv_bfloat16*, __nv_bfloat16*, __nv_bfloat16*, int, int,
+    int, int, int, int, float, bool, cudaStream_t);
 
 template FlashAttentionError launch_bwd_sm100<half>(const half*, const half*, const half*,
                                                     const half*, const float*, const half*, half*,

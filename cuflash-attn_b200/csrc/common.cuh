@@ -88,6 +88,20 @@ FlashAttentionError launch_fwd_sm100(const T* Q, const T* K, const T* V, void* O
                                      long long q_offset, long long k_offset, bool out_f32_partial,
                                      cudaStream_t stream);
 
+// Grouped-query backward, same layout and mask conventions as the forward.
+template <typename T>
+FlashAttentionError launch_bwd_gqa_sm100(const T* Q, const T* K, const T* V, const T* O,
+                                         const float* L, const T* dO, T* dQ, T* dK, T* dV, int B,
+                                         int Hq, int Hkv, int seq_q, int seq_k, int D, float scale,
+                                         bool causal, cudaStream_t stream);
+
+// Grouped-query forward: Q, O [B,Hq,seq_q,D], K, V [B,Hkv,seq_k,D], query head
+// h reads K/V head h / (Hq/Hkv); causal is aligned bottom-right.
+template <typename T>
+FlashAttentionError launch_fwd_gqa_sm100(const T* Q, const T* K, const T* V, T* O, float* L, int B,
+                                         int Hq, int Hkv, int seq_q, int seq_k, int D, float scale,
+                                         bool causal, cudaStream_t stream);
+
 // One context-parallel ring step: num_pairs (<= 4) partial forwards of query
 // slot q_slot[i] against K/V slot k_slot[i] (global offsets q_off/k_off), each
 // merged in place into O_acc / L_acc of its query slot; one launch.

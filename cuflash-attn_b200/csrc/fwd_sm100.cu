@@ -98,6 +98,8 @@ struct FwdParams {
     // K / V the K/V slots the same way.
     int num_segs;
     int seg_units;   // units of one segment
+    int hq;          // query heads per batch entry
+    int group;       // query heads per K/V head (grouped-query attention; 1 = MHA)
     int q_base[4];   // outer index of the segment's first (b,h) in Q / O / L
     int k_base[4];   // outer index of the segment's first (b,h) in K / V
     long long q_off[4];
@@ -169,7 +171,9 @@ __device__ __forceinline__ bool fwd_item(const FwdParams& p, int u, int w, FwdIt
         if (w == 1 && ct == p.num_ctiles - 1 - k) return false;  // middle tile of an odd count
     }
     it.bh = p.q_base[sg] + bh;
-    it.bhk = p.k_base[sg] + bh;
+    // K/V head of query head h = h / group within the same batch entry
+    it.bhk = p.k_base[sg] +
+             (p.group == 1 ? bh : (bh / p.hq) * (p.hq / p.group) + (bh % p.hq) / p.group);
     it.q_row0 = ct * 256;
     it.q_off = p.q_off[sg];
     it.k_off = p.k_off[sg];
@@ -696,6 +700,8 @@ struct FwdSegs {
     long long q_off[kMaxSegs] = {0, 0, 0, 0};
     long long k_off[kMaxSegs] = {0, 0, 0, 0};
     bool merge = false;
+    int hq = 1;     // query heads per batch entry (BH = batch * hq)
+    int group = 1;  // query heads per K/V head
 };
 
 template <typename T, int D, bool kF32Out>
@@ -707,7 +713,7 @@ FlashAttentionError launch_typed(const T* Q, const T* K, const T* V, void* O, fl
         G::kSwz == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
     CUtensorMap mq, mk, mv;
     const uint64_t q_outer = static_cast<uint64_t>(sg.nq_slots) * BH;
-    const uint64_t k_outer = static_cast<uint64_t>(sg.nk_slots) * BH;
+    const uint64_t k_outer = static_cast<uint64_t>(sg.nk_slots) * (BH / sg.group);
     if (!encode_tmap_3d(&mq, Q, DType<T>::kTmaType, 2, D, seq_q, q_outer, G::kCbElems, 128, swz) ||
         !encode_tmap_3d(&mk, K, DType<T>::kTmaType, 2, D, seq_k, k_outer, G::kCbElems, 128, swz) ||
         !encode_tmap_3d(&mv, V, DType<T>::kTmaType, 2, D, seq_k, k_outer, G::kCbElems, 128, swz))
@@ -727,9 +733,11 @@ FlashAttentionError launch_typed(const T* Q, const T* K, const T* V, void* O, fl
     // (-inf) still map to -inf; the effect on results is below fp32 resolution.
     prm.scale_log2 = fmaxf(scale * kLog2e, 1e-30f);
     prm.num_segs = sg.num_segs;
+    prm.hq = sg.hq;
+    prm.group = sg.group;
     for (int i = 0; i < kMaxSegs; ++i) {
         prm.q_base[i] = sg.q_slot[i] * BH;
-        prm.k_base[i] = sg.k_slot[i] * BH;
+        prm.k_base[i] = sg.k_slot[i] * (BH / sg.group);
         prm.q_off[i] = sg.q_off[i];
         prm.k_off[i] = sg.k_off[i];
     }
@@ -790,6 +798,26 @@ FlashAttentionError launch_fwd_sm100(const T* Q, const T* K, const T* V, void* O
         return dispatch_d<T, true>(Q, K, V, O, L, BH, seq_q, seq_k, D, scale, causal, sg, stream);
     return dispatch_d<T, false>(Q, K, V, O, L, BH, seq_q, seq_k, D, scale, causal, sg, stream);
 }
+
+template <typename T>
+FlashAttentionError launch_fwd_gqa_sm100(const T* Q, const T* K, const T* V, T* O, float* L, int B,
+                                         int Hq, int Hkv, int seq_q, int seq_k, int D, float scale,
+                                         bool causal, cudaStream_t stream) {
+    FwdSegs sg;
+    sg.hq = Hq;
+    sg.group = Hq / Hkv;
+    // bottom-right causal alignment: query i sits at global position
+    // seq_k - seq_q + i, keys at 0..seq_k-1
+    sg.q_off[0] = static_cast<long long>(seq_k) - seq_q;
+    return dispatch_d<T, false>(Q, K, V, O, L, B * Hq, seq_q, seq_k, D, scale, causal, sg, stream);
+}
+
+template FlashAttentionError launch_fwd_gqa_sm100<__nv_bfloat16>(
+    const __nv_bfloat16*, const __nv_bfloat16*, const __nv_bfloat16*, __nv_bfloat16*, float*, int,
+    int, int, int, int, int, float, bool, cudaStream_t);
+template FlashAttentionError launch_fwd_gqa_sm100<half>(const half*, const half*, const half*,
+                                                        half*, float*, int, int, int, int, int,
+                                                        int, float, bool, cudaStream_t);
 
 template <typename T>
 FlashAttentionError launch_fwd_cp_step_sm100(const T* Q, const T* K, const T* V, float* O_acc,

@@ -55,6 +55,10 @@ SIGNATURES = {
     "cuflash_attention_decode_bf16_noalloc": [_P] * 5 + [_I] * 4 + [_F, _I, _P],
     "cuflash_attention_forward_partial_bf16": [_P] * 5 + [_I] * 5 + [_F, _LL, _LL, _B, _P],
     "cuflash_attention_forward_partial_f16": [_P] * 5 + [_I] * 5 + [_F, _LL, _LL, _B, _P],
+    "cuflash_attention_forward_gqa_bf16": [_P] * 5 + [_I] * 6 + [_F, _B, _P],
+    "cuflash_attention_forward_gqa_f16": [_P] * 5 + [_I] * 6 + [_F, _B, _P],
+    "cuflash_attention_backward_gqa_bf16": [_P] * 9 + [_I] * 6 + [_F, _B, _P],
+    "cuflash_attention_backward_gqa_f16": [_P] * 9 + [_I] * 6 + [_F, _B, _P],
     "cuflash_attention_forward_cp_step_bf16": [_P] * 5 + [_I] * 6 + [_F, _B, _I] + [_P] * 5,
     "cuflash_attention_forward_cp_step_f16": [_P] * 5 + [_I] * 6 + [_F, _B, _I] + [_P] * 5,
     "cuflash_lse_merge_f32": [_P] * 4 + [_LL, _I, _P],
@@ -76,10 +80,8 @@ def library_path(lib_path: Optional[str] = None) -> str:
 
 
 # The entry points the reference library exports (flash_attention.h:81-118).
-REFERENCE_ABI = tuple(n for n in SIGNATURES if n.startswith(("cuflash_attention_forward_f",
-                                                             "cuflash_attention_forward_b",
-                                                             "cuflash_attention_backward_")))
-REFERENCE_ABI = REFERENCE_ABI + ("cuflash_error_string",)
+REFERENCE_ABI = tuple(f"cuflash_attention_{pass_}_{sfx}" for pass_ in ("forward", "backward")
+                      for sfx in ("f32", "f16", "bf16")) + ("cuflash_error_string",)
 
 
 def load_library(lib_path: Optional[str] = None, reference_abi_only: bool = False) -> ctypes.CDLL:
@@ -219,6 +221,40 @@ class CuFlashAttn:
                             float(scale), int(q_offset), int(k_offset), bool(causal),
                             _stream_handle(stream)))
         return O, L
+
+    def forward_gqa(self, Q, K, V, causal: bool = False, scale: Optional[float] = None, O=None,
+                    L=None, stream=None):
+        """Grouped-query forward: Q [B,Hq,Nq,D], K/V [B,Hkv,Nk,D]; causal is
+        aligned bottom-right."""
+        import torch
+
+        B, Hq, Nq, D = Q.shape
+        Hkv, Nk = K.shape[1], K.shape[2]
+        if scale is None:
+            scale = 1.0 / math.sqrt(D)
+        O = torch.empty_like(Q) if O is None else O
+        L = torch.empty((B, Hq, Nq), device=Q.device, dtype=torch.float32) if L is None else L
+        fn = getattr(self.lib, f"cuflash_attention_forward_gqa_{_suffix(Q)}")
+        self.check_error(fn(_ptr(Q), _ptr(K), _ptr(V), _ptr(O), _ptr(L), B, Hq, Hkv, Nq, Nk, D,
+                            float(scale), bool(causal), _stream_handle(stream)))
+        return O, L
+
+    def backward_gqa(self, Q, K, V, O, L, dO, causal: bool = False,
+                     scale: Optional[float] = None, dQ=None, dK=None, dV=None, stream=None):
+        import torch
+
+        B, Hq, Nq, D = Q.shape
+        Hkv, Nk = K.shape[1], K.shape[2]
+        if scale is None:
+            scale = 1.0 / math.sqrt(D)
+        dQ = torch.empty_like(Q) if dQ is None else dQ
+        dK = torch.empty_like(K) if dK is None else dK
+        dV = torch.empty_like(V) if dV is None else dV
+        fn = getattr(self.lib, f"cuflash_attention_backward_gqa_{_suffix(Q)}")
+        self.check_error(fn(_ptr(Q), _ptr(K), _ptr(V), _ptr(O), _ptr(L), _ptr(dO), _ptr(dQ),
+                            _ptr(dK), _ptr(dV), B, Hq, Hkv, Nq, Nk, D, float(scale),
+                            bool(causal), _stream_handle(stream)))
+        return dQ, dK, dV
 
     def forward_cp_step(self, Q, K, V, O_acc, L_acc, pairs, causal: bool = True,
                         scale: Optional[float] = None, stream=None) -> None:

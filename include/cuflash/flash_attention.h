@@ -199,6 +199,37 @@ CUFLASH_EXPORT int cuflash_attention_forward_partial_f16(
     int num_heads, int seq_q, int seq_k, int head_dim, float scale, long long q_offset,
     long long k_offset, bool causal, cudaStream_t stream);
 
+// Grouped-query (GQA / MQA) attention with separate query and key lengths
+// (no reference counterpart: the reference API has one seq_len and equal
+// head counts).  Q, O, dO, dQ [B, num_q_heads, seq_len_q, D]; K, V, dK, dV
+// [B, num_kv_heads, seq_len_k, D]; L fp32 [B, num_q_heads, seq_len_q].
+// num_q_heads must be a multiple of num_kv_heads (else DIMENSION_MISMATCH);
+// query head h reads K/V head h / (num_q_heads / num_kv_heads), and dK / dV
+// of a K/V head sum over its query heads.  causal aligns the mask
+// bottom-right: query i sees key j iff j <= i + seq_len_k - seq_len_q (the
+// KV-cache convention; with equal lengths it is the reference's top-left
+// mask).  Queries that see no key get O = 0 and L = -inf.  Validation order
+// and codes otherwise follow the reference entry points.
+CUFLASH_EXPORT int cuflash_attention_forward_gqa_bf16(
+    const __nv_bfloat16* Q, const __nv_bfloat16* K, const __nv_bfloat16* V, __nv_bfloat16* O,
+    float* L, int batch_size, int num_q_heads, int num_kv_heads, int seq_len_q, int seq_len_k,
+    int head_dim, float scale, bool causal, cudaStream_t stream);
+CUFLASH_EXPORT int cuflash_attention_forward_gqa_f16(const half* Q, const half* K, const half* V,
+                                                     half* O, float* L, int batch_size,
+                                                     int num_q_heads, int num_kv_heads,
+                                                     int seq_len_q, int seq_len_k, int head_dim,
+                                                     float scale, bool causal,
+                                                     cudaStream_t stream);
+CUFLASH_EXPORT int cuflash_attention_backward_gqa_bf16(
+    const __nv_bfloat16* Q, const __nv_bfloat16* K, const __nv_bfloat16* V,
+    const __nv_bfloat16* O, const float* L, const __nv_bfloat16* dO, __nv_bfloat16* dQ,
+    __nv_bfloat16* dK, __nv_bfloat16* dV, int batch_size, int num_q_heads, int num_kv_heads,
+    int seq_len_q, int seq_len_k, int head_dim, float scale, bool causal, cudaStream_t stream);
+CUFLASH_EXPORT int cuflash_attention_backward_gqa_f16(
+    const half* Q, const half* K, const half* V, const half* O, const float* L, const half* dO,
+    half* dQ, half* dK, half* dV, int batch_size, int num_q_heads, int num_kv_heads,
+    int seq_len_q, int seq_len_k, int head_dim, float scale, bool causal, cudaStream_t stream);
+
 // One ring step of context-parallel attention in a single launch (no
 // reference counterpart: the reference has no multi-GPU path).  Q and the
 // running result hold num_q_slots query chunks stacked as [slot][B][H][C][D]

@@ -201,6 +201,51 @@ void fwd_unit_f64(const float* Q, const float* K, const float* V, double* O, dou
 
 // fp64 backward of one unit, O(N^2) memory free: D_i from P and dP (as the
 // reference oracle does), recomputing the softmax row by row.
+// General fp64 backward: queries [Nq, D] at global positions q_off.., keys
+// [Nk, D] at k_off..; with causal, key j is visible to query i iff
+// k_off + j <= q_off + i.  Rows that see no key contribute nothing.
+void bwd_unit_gen_f64(const float* Q, const float* K, const float* V, const float* dO, double* dQ,
+                      double* dK, double* dV, int Nq, int Nk, int D, double scale, bool causal,
+                      long long q_off, long long k_off) {
+    std::vector<double> p(Nk), dp(Nk);
+    std::fill(dQ, dQ + (size_t)Nq * D, 0.0);
+    std::fill(dK, dK + (size_t)Nk * D, 0.0);
+    std::fill(dV, dV + (size_t)Nk * D, 0.0);
+    for (int i = 0; i < Nq; ++i) {
+        long long lim = causal ? q_off + i - k_off + 1 : Nk;  // visible keys: j < lim
+        const int jend = static_cast<int>(lim < 0 ? 0 : (lim > Nk ? Nk : lim));
+        if (jend == 0) continue;
+        double mx = -INFINITY;
+        for (int j = 0; j < jend; ++j) {
+            double dot = 0.0;
+            for (int d = 0; d < D; ++d) dot += (double)Q[(size_t)i * D + d] * K[(size_t)j * D + d];
+            p[j] = dot * scale;
+            mx = std::max(mx, p[j]);
+        }
+        double sum = 0.0;
+        for (int j = 0; j < jend; ++j) {
+            p[j] = std::exp(p[j] - mx);
+            sum += p[j];
+        }
+        double Di = 0.0;
+        for (int j = 0; j < jend; ++j) {
+            p[j] /= sum;
+            double g = 0.0;
+            for (int d = 0; d < D; ++d) g += (double)dO[(size_t)i * D + d] * V[(size_t)j * D + d];
+            dp[j] = g;
+            Di += p[j] * g;
+        }
+        for (int j = 0; j < jend; ++j) {
+            const double ds = p[j] * (dp[j] - Di);
+            for (int d = 0; d < D; ++d) {
+                dQ[(size_t)i * D + d] += ds * K[(size_t)j * D + d] * scale;
+                dK[(size_t)j * D + d] += ds * Q[(size_t)i * D + d] * scale;
+                dV[(size_t)j * D + d] += p[j] * dO[(size_t)i * D + d];
+            }
+        }
+    }
+}
+
 void bwd_unit_f64(const float* Q, const float* K, const float* V, const float* dO, double* dQ,
                   double* dK, double* dV, int N, int D, double scale, bool causal) {
     std::vector<double> p(N), dp(N);
@@ -377,6 +422,17 @@ void oracle_backward_f64(const float* Q, const float* K, const float* V, const f
     parallel_units(u0, u1, nthreads, [&](long long u) {
         bwd_unit_f64(Q + u * T, K + u * T, V + u * T, dO + u * T, dQ + u * T, dK + u * T,
                      dV + u * T, N, D, scale, causal != 0);
+    });
+}
+
+void oracle_backward_gen_f64(const float* Q, const float* K, const float* V, const float* dO,
+                             double* dQ, double* dK, double* dV, long long u0, long long u1,
+                             int Nq, int Nk, int D, double scale, int causal, long long q_off,
+                             long long k_off, int nthreads) {
+    const size_t Tq = (size_t)Nq * D, Tk = (size_t)Nk * D;
+    parallel_units(u0, u1, nthreads, [&](long long u) {
+        bwd_unit_gen_f64(Q + u * Tq, K + u * Tk, V + u * Tk, dO + u * Tq, dQ + u * Tq, dK + u * Tk,
+                         dV + u * Tk, Nq, Nk, D, scale, causal != 0, q_off, k_off);
     });
 }
 

@@ -54,12 +54,14 @@ def lib():
                                          _LL, _LL, _I, _I, _I, ctypes.c_double, _I, _LL, _LL, _I]
         L.oracle_backward_f64.argtypes = [_f32p] * 4 + [_f64p] * 3 + [
             _LL, _LL, _I, _I, ctypes.c_double, _I, _I]
+        L.oracle_backward_gen_f64.argtypes = [_f32p] * 4 + [ctypes.c_void_p] * 3 + [
+            _LL, _LL, _I, _I, _I, ctypes.c_double, _I, _LL, _LL, _I]
         L.oracle_train_step_rows_f32.argtypes = [_f32p] * 9 + [_LL, _LL, _I, _I, ctypes.c_float,
                                                    _I, _I, _I, _I]
         L.oracle_train_step_rows_f32.restype = ctypes.c_longlong
         for f in ("oracle_fill_interleaved_uniform", "oracle_fill_uniform", "oracle_fill_normal",
                   "oracle_forward_f32", "oracle_backward_f32", "oracle_forward_f64",
-                  "oracle_backward_f64"):
+                  "oracle_backward_f64", "oracle_backward_gen_f64"):
             getattr(L, f).restype = None
         _lib = L
     return _lib
@@ -154,6 +156,48 @@ def backward_f64(Q, K, V, dO, scale, causal, units=None, nthreads=8):
     dQ, dK, dV = (np.zeros(Q.shape, np.float64) for _ in range(3))
     lib().oracle_backward_f64(Q, K, V, dO, dQ, dK, dV, u0, u1, N, D, float(scale), int(causal),
                               int(nthreads))
+    return dQ, dK, dV
+
+
+def backward_gen_f64(Q, K, V, dO, scale, causal, q_offset=0, k_offset=0, units=None,
+                     nthreads=8):
+    """fp64 backward with separate lengths: Q, dO [B,H,Nq,D], K/V [B,H,Nk,D],
+    causal on global positions (key k_offset+j hidden from query q_offset+i
+    iff k_offset+j > q_offset+i)."""
+    Q, K, V, dO = (np.ascontiguousarray(x, np.float32) for x in (Q, K, V, dO))
+    B, H, Nq, D = Q.shape
+    Nk = K.shape[2]
+    u0, u1 = units if units is not None else (0, B * H)
+    dQ = np.zeros(Q.shape, np.float64)
+    dK, dV = (np.zeros(K.shape, np.float64) for _ in range(2))
+    lib().oracle_backward_gen_f64(Q, K, V, dO, _vp(dQ), _vp(dK), _vp(dV), u0, u1, Nq, Nk, D,
+                                  float(scale), int(causal), int(q_offset), int(k_offset),
+                                  int(nthreads))
+    return dQ, dK, dV
+
+
+def gqa_forward_f64(Q, K, V, scale, causal):
+    """Grouped-query forward: Q [B,Hq,Nq,D], K/V [B,Hkv,Nk,D], query head h
+    reads K/V head h // (Hq/Hkv); causal is bottom-right aligned (query i sees
+    key j iff j <= i + Nk - Nq)."""
+    g = Q.shape[1] // K.shape[1]
+    Kr, Vr = np.repeat(K, g, axis=1), np.repeat(V, g, axis=1)
+    return forward_f64(Q, Kr, Vr, scale, causal, q_offset=K.shape[2] - Q.shape[2], k_offset=0)
+
+
+def gqa_backward_f64(Q, K, V, dO, scale, causal):
+    """Grouped-query backward (same conventions); dK/dV of a K/V head sum its
+    query heads' contributions."""
+    B, Hq, Nq, D = Q.shape
+    Hkv, Nk = K.shape[1], K.shape[2]
+    g = Hq // Hkv
+    Kr, Vr = np.repeat(K, g, axis=1), np.repeat(V, g, axis=1)
+    qo = Nk - Nq
+    # q_offset may be negative (more queries than keys): shift both sides
+    dQ, dK, dV = backward_gen_f64(Q, Kr, Vr, dO, scale, causal, q_offset=max(qo, 0),
+                                  k_offset=max(-qo, 0))
+    dK = dK.reshape(B, Hkv, g, Nk, D).sum(axis=2)
+    dV = dV.reshape(B, Hkv, g, Nk, D).sum(axis=2)
     return dQ, dK, dV
 
 

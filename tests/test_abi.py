@@ -163,6 +163,32 @@ def test_partial_and_merge_validation(lib, sfx):
 
 
 @pytest.mark.parametrize("sfx", ["f16", "bf16"])
+def test_gqa_validation(lib, sfx):
+    fwd = getattr(lib.lib, f"cuflash_attention_forward_gqa_{sfx}")
+    bwd = getattr(lib.lib, f"cuflash_attention_backward_gqa_{sfx}")
+
+    def f(B=1, Hq=8, Hkv=2, Nq=16, Nk=32, D=64, scale=0.1, nul=None):
+        a = [FAKE] * 5 + [B, Hq, Hkv, Nq, Nk, D, scale, True, STREAM]
+        if nul is not None:
+            a[nul] = NUL
+        return fwd(*a)
+
+    def b(Hq=8, Hkv=2, nul=None):
+        a = [FAKE] * 9 + [1, Hq, Hkv, 16, 32, 64, 0.1, True, STREAM]
+        if nul is not None:
+            a[nul] = NUL
+        return bwd(*a)
+
+    assert f(nul=2) == 3 and f(nul=4) == 3
+    assert f(Nq=0) == 1 and f(Nk=-1) == 1 and f(Hkv=0) == 1
+    assert f(Hq=6, Hkv=4) == 2                 # heads not divisible: DIMENSION_MISMATCH
+    assert f(D=48) == 6
+    assert f(scale=float("inf")) == 1 and f(scale=-1.0) == 1
+    assert b(nul=5) == 3 and b(nul=8) == 3     # dO / dV checked like the reference
+    assert b(Hq=9, Hkv=2) == 2
+
+
+@pytest.mark.parametrize("sfx", ["f16", "bf16"])
 def test_cp_step_validation(lib, sfx):
     import ctypes
 
