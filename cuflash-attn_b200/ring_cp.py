@@ -24,6 +24,8 @@ backend-independent and is exercised on CPU with gloo in the tests.
 
 from __future__ import annotations
 
+import os
+
 from dataclasses import dataclass
 from typing import Callable, List, Sequence, Tuple
 
@@ -148,14 +150,27 @@ class RingAttention:
             return wait
 
         cur = kv
-        for st in ring_steps(rank, world):
-            pending = exchange(cur) if st.step + 1 < world else None
-            pairs = [(qi, ki, q_chunks[qi] * C, st.k_chunks[ki] * C) for qi, ki in st.pairs]
-            for group in distinct_q_groups(pairs):
-                self.lib.forward_cp_step(Qs, cur[0], cur[1], O_acc, L_acc, group, causal=True,
-                                         scale=scale, stream=stream)
-            if pending is not None:
-                cur = pending()
+        # The step launches leave SMs free for the concurrent NCCL transfer
+        # (CUFLASH_CP_RESERVE_SMS, 16 by default); a single rank has no
+        # transfer, so it gives them to the kernels.
+        saved = os.environ.get("CUFLASH_CP_RESERVE_SMS")
+        if world == 1:
+            os.environ["CUFLASH_CP_RESERVE_SMS"] = "0"
+        try:
+            for st in ring_steps(rank, world):
+                pending = exchange(cur) if st.step + 1 < world else None
+                pairs = [(qi, ki, q_chunks[qi] * C, st.k_chunks[ki] * C) for qi, ki in st.pairs]
+                for group in distinct_q_groups(pairs):
+                    self.lib.forward_cp_step(Qs, cur[0], cur[1], O_acc, L_acc, group,
+                                             causal=True, scale=scale, stream=stream)
+                if pending is not None:
+                    cur = pending()
+        finally:
+            if world == 1:
+                if saved is None:
+                    os.environ.pop("CUFLASH_CP_RESERVE_SMS", None)
+                else:
+                    os.environ["CUFLASH_CP_RESERVE_SMS"] = saved
         out = []
         for qi in range(2):
             o = torch.empty((B, H, C, D), device=dev, dtype=Qa.dtype)
