@@ -72,8 +72,15 @@ bool ensure_smem_attr(const void* kernel, int bytes) {
 // work).  One wave is the fastest when the kernel has the GPU to itself;
 // more waves let the block scheduler rebalance when other kernels (NCCL
 // transfers) hold SMs at launch time, at the price of more per-CTA setup.
+// CUFLASH_RESERVE_SMS=n keeps n SMs out of every persistent launch, for
+// callers that overlap collectives (a data-parallel gradient all-reduce)
+// with attention kernels: NCCL's kernels need SMs the persistent CTAs would
+// otherwise hold until the launch ends.
 int persistent_grid(long long units, int waves) {
-    const long long cap = static_cast<long long>(current_sm_count()) * (waves > 0 ? waves : 1);
+    const int sms = current_sm_count();
+    int reserve = env_int("CUFLASH_RESERVE_SMS", 0);
+    if (reserve >= sms) reserve = sms - 1;
+    const long long cap = static_cast<long long>(sms - reserve) * (waves > 0 ? waves : 1);
     return static_cast<int>(units < cap ? units : cap);
 }
 
