@@ -179,6 +179,30 @@ FlashAttentionError decode_impl(const T* Q, const T* K, const T* V, T* O, float*
 }
 
 template <typename T>
+FlashAttentionError decode_gqa_impl(const T* Q, const T* K, const T* V, T* O, float* L, int B,
+                                    int Hq, int Hkv, int kv_len, int D, float scale,
+                                    int num_splits, const int* block_table, const int* seq_lens,
+                                    int page_size, int max_pages, int num_pages,
+                                    cudaStream_t stream) {
+    const bool paged = block_table != nullptr || seq_lens != nullptr;
+    if (!Q || !K || !V || !O || !L) return FlashAttentionError::NULL_POINTER;
+    if (paged && (!block_table || !seq_lens)) return FlashAttentionError::NULL_POINTER;
+    if (B <= 0 || Hq <= 0 || Hkv <= 0 || D <= 0) return FlashAttentionError::INVALID_DIMENSION;
+    if (!paged && kv_len <= 0) return FlashAttentionError::INVALID_DIMENSION;
+    if (paged && (page_size <= 0 || (page_size & (page_size - 1)) != 0 || max_pages <= 0 ||
+                  num_pages <= 0 || static_cast<long long>(max_pages) * page_size > 0x7fffffffLL))
+        return FlashAttentionError::INVALID_DIMENSION;
+    if (Hq % Hkv != 0) return FlashAttentionError::DIMENSION_MISMATCH;
+    if (!(D == 32 || D == 64 || D == 128)) return FlashAttentionError::UNSUPPORTED_HEAD_DIM;
+    if (!std::isfinite(scale) || scale < 0.0f) return FlashAttentionError::INVALID_DIMENSION;
+    if (num_splits < 0 || num_splits > 64) return FlashAttentionError::INVALID_DIMENSION;
+    if (static_cast<long long>(B) * Hq > 0x7fffffffLL) return FlashAttentionError::INVALID_DIMENSION;
+    return cuflash::detail::launch_decode_gqa<T>(Q, K, V, O, L, B, Hq, Hkv, kv_len, D, scale,
+                                                 num_splits, block_table, seq_lens, page_size,
+                                                 max_pages, num_pages, stream);
+}
+
+template <typename T>
 FlashAttentionError partial_impl(const T* Q, const T* K, const T* V, float* O, float* L, int B,
                                  int H, int seq_q, int seq_k, int D, float scale,
                                  long long q_offset, long long k_offset, bool causal,
@@ -349,6 +373,48 @@ int cuflash_attention_forward_partial_f16(const half* Q, const half* K, const ha
     return static_cast<int>(partial_impl<half>(Q, K, V, O_part, L_part, batch_size, num_heads,
                                                seq_q, seq_k, head_dim, scale, q_offset, k_offset,
                                                causal, stream));
+}
+
+int cuflash_attention_decode_gqa_bf16(const __nv_bfloat16* Q, const __nv_bfloat16* K,
+                                      const __nv_bfloat16* V, __nv_bfloat16* O, float* L,
+                                      int batch_size, int num_q_heads, int num_kv_heads,
+                                      int kv_len, int head_dim, float scale, int num_splits,
+                                      cudaStream_t stream) {
+    return static_cast<int>(decode_gqa_impl<__nv_bfloat16>(
+        Q, K, V, O, L, batch_size, num_q_heads, num_kv_heads, kv_len, head_dim, scale,
+        num_splits, nullptr, nullptr, 0, 0, 0, stream));
+}
+
+int cuflash_attention_decode_gqa_f16(const half* Q, const half* K, const half* V, half* O,
+                                     float* L, int batch_size, int num_q_heads, int num_kv_heads,
+                                     int kv_len, int head_dim, float scale, int num_splits,
+                                     cudaStream_t stream) {
+    return static_cast<int>(decode_gqa_impl<half>(Q, K, V, O, L, batch_size, num_q_heads,
+                                                  num_kv_heads, kv_len, head_dim, scale,
+                                                  num_splits, nullptr, nullptr, 0, 0, 0, stream));
+}
+
+int cuflash_attention_decode_paged_bf16(const __nv_bfloat16* Q, const __nv_bfloat16* K_cache,
+                                        const __nv_bfloat16* V_cache, const int* block_table,
+                                        const int* seq_lens, __nv_bfloat16* O, float* L,
+                                        int batch_size, int num_q_heads, int num_kv_heads,
+                                        int head_dim, int page_size, int max_pages_per_seq,
+                                        int num_pages, float scale, int num_splits,
+                                        cudaStream_t stream) {
+    return static_cast<int>(decode_gqa_impl<__nv_bfloat16>(
+        Q, K_cache, V_cache, O, L, batch_size, num_q_heads, num_kv_heads, 0, head_dim, scale,
+        num_splits, block_table, seq_lens, page_size, max_pages_per_seq, num_pages, stream));
+}
+
+int cuflash_attention_decode_paged_f16(const half* Q, const half* K_cache, const half* V_cache,
+                                       const int* block_table, const int* seq_lens, half* O,
+                                       float* L, int batch_size, int num_q_heads,
+                                       int num_kv_heads, int head_dim, int page_size,
+                                       int max_pages_per_seq, int num_pages, float scale,
+                                       int num_splits, cudaStream_t stream) {
+    return static_cast<int>(decode_gqa_impl<half>(
+        Q, K_cache, V_cache, O, L, batch_size, num_q_heads, num_kv_heads, 0, head_dim, scale,
+        num_splits, block_table, seq_lens, page_size, max_pages_per_seq, num_pages, stream));
 }
 
 int cuflash_attention_forward_gqa_bf16(const __nv_bfloat16* Q, const __nv_bfloat16* K,

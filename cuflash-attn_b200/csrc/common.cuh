@@ -88,6 +88,17 @@ FlashAttentionError launch_fwd_sm100(const T* Q, const T* K, const T* V, void* O
                                      long long q_offset, long long k_offset, bool out_f32_partial,
                                      cudaStream_t stream);
 
+// Grouped-query split-KV decode.  Contiguous cache (block_table == nullptr):
+// K, V [B, Hkv, kv_len, D].  Paged cache: K, V [num_pages, page_size, Hkv, D],
+// block_table [B, max_pages] and seq_lens [B] in device memory, page_size a
+// power of two.  Q, O [B, Hq, 1, D], L [B, Hq].
+template <typename T>
+FlashAttentionError launch_decode_gqa(const T* Q, const T* K, const T* V, T* O, float* L, int B,
+                                      int Hq, int Hkv, int kv_len, int D, float scale,
+                                      int num_splits, const int* block_table,
+                                      const int* seq_lens, int page_size, int max_pages,
+                                      int num_pages, cudaStream_t stream);
+
 // Grouped-query backward, same layout and mask conventions as the forward.
 template <typename T>
 FlashAttentionError launch_bwd_gqa_sm100(const T* Q, const T* K, const T* V, const T* O,

@@ -174,6 +174,189 @@ __global__ void __launch_bounds__(kDecodeThreads)
     }
 }
 
+// ---------------------------------------------------------------------------
+// Grouped-query and paged decode.  A CTA serves TILE query heads that share
+// one K/V head, so every K/V row is read once for all of them (the point of
+// grouped-query attention in decode: the cache traffic shrinks by the group
+// size).  The K/V cache is either contiguous [B, Hkv, kv_len, D] or paged:
+// [num_pages, page_size, Hkv, D] with a block table [B, max_pages] of page
+// indices and per-sequence lengths seq_lens[B] (the layout of paged KV-cache
+// serving engines).  Page indices are clamped to [0, num_pages) so a bad
+// table entry reads the wrong page instead of faulting.
+// ---------------------------------------------------------------------------
+template <typename T>
+struct DecodeKv {
+    const T* K;
+    const T* V;
+    const int* block_table;  // paged: [B, max_pages]
+    const int* seq_lens;     // paged: [B]
+    int kv_len;              // contiguous: rows per K/V head
+    int hkv;
+    int page_shift;          // log2(page_size)
+    int max_pages;
+    int num_pages;
+};
+
+template <typename T, int D, int TILE, bool kPaged, bool kDirect>
+__global__ void __launch_bounds__(kDecodeThreads)
+    decode_group_kernel(const T* __restrict__ Q, const DecodeKv<T> kvp, T* __restrict__ O,
+                        float* __restrict__ L, float* __restrict__ O_part,
+                        float* __restrict__ L_part, int hq, int group, int chunk,
+                        float scale_log2) {
+    constexpr int LPR = D / 8;     // lanes per row
+    constexpr int RPW = 32 / LPR;  // rows per warp per load
+    constexpr int G = kDecodeWarps * RPW;
+    constexpr int STEP = G;
+    constexpr int U = (8 / TILE) > 2 ? (8 / TILE) : 2;  // rows in flight per lane group
+    extern __shared__ float dsm[];
+    float* s_m = dsm;                  // [G][TILE]
+    float* s_l = s_m + G * TILE;       // [G][TILE]
+    float* s_acc = s_l + G * TILE;     // [G][TILE][D]
+
+    const int split = blockIdx.x;
+    const int num_splits = gridDim.x;
+    const int tiles = group / TILE;
+    const int bhk = blockIdx.y / tiles;
+    const int tq = blockIdx.y - bhk * tiles;
+    const int b = bhk / kvp.hkv;
+    const int hk = bhk - b * kvp.hkv;
+    const long long bhq0 = static_cast<long long>(b) * hq + hk * group + tq * TILE;
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const int sub = lane / LPR;
+    const int li = lane % LPR;
+    const int grp = warp * RPW + sub;
+
+    float q[TILE][8];
+#pragma unroll
+    for (int t = 0; t < TILE; ++t) {
+        const uint4 qv = *reinterpret_cast<const uint4*>(Q + (bhq0 + t) * D + li * 8);
+        unpack8<T>(qv, q[t]);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) q[t][e] *= scale_log2;
+    }
+
+    // a paged length is clamped to what the block table can address
+    const int len = kPaged ? min(max(kvp.seq_lens[b], 0), kvp.max_pages << kvp.page_shift)
+                           : kvp.kv_len;
+    const int r_begin = split * chunk;
+    const int r_end = min(len, r_begin + chunk);
+    auto row_off = [&](int row) -> long long {  // element offset of (row, hk, li*8)
+        if constexpr (kPaged) {
+            int page = kvp.block_table[static_cast<long long>(b) * kvp.max_pages +
+                                       (row >> kvp.page_shift)];
+            page = min(max(page, 0), kvp.num_pages - 1);
+            const long long slot = (static_cast<long long>(page) << kvp.page_shift) +
+                                   (row & ((1 << kvp.page_shift) - 1));
+            return (slot * kvp.hkv + hk) * D + li * 8;
+        } else {
+            return (static_cast<long long>(bhk) * kvp.kv_len + row) * D + li * 8;
+        }
+    };
+
+    float m[TILE], l[TILE], acc[TILE][8];
+#pragma unroll
+    for (int t = 0; t < TILE; ++t) {
+        m[t] = -INFINITY;
+        l[t] = 0.f;
+#pragma unroll
+        for (int e = 0; e < 8; ++e) acc[t][e] = 0.f;
+    }
+
+    // The loop bound is warp-uniform so that every lane reaches the shuffles.
+    for (int rb = r_begin + warp * RPW; rb < r_end; rb += STEP * U) {
+        uint4 kv[U], vv[U];
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            const int row = rb + sub + u * STEP;
+            if (row < r_end) {
+                const long long off = row_off(row);
+                kv[u] = ld_stream(kvp.K + off);
+                vv[u] = ld_stream(kvp.V + off);
+            } else {
+                kv[u] = make_uint4(0, 0, 0, 0);
+                vv[u] = make_uint4(0, 0, 0, 0);
+            }
+        }
+        float sc[U][TILE];
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            float kf[8];
+            unpack8<T>(kv[u], kf);
+            const bool live = rb + sub + u * STEP < r_end;
+#pragma unroll
+            for (int t = 0; t < TILE; ++t) {
+                float dot = 0.f;
+#pragma unroll
+                for (int e = 0; e < 8; ++e) dot = fmaf(q[t][e], kf[e], dot);
+#pragma unroll
+                for (int off = LPR / 2; off > 0; off >>= 1)
+                    dot += __shfl_xor_sync(0xffffffffu, dot, off);
+                sc[u][t] = live ? dot : -INFINITY;
+            }
+        }
+#pragma unroll
+        for (int t = 0; t < TILE; ++t) {
+            float mx = sc[0][t];
+#pragma unroll
+            for (int u = 1; u < U; ++u) mx = fmaxf(mx, sc[u][t]);
+            const float m_new = fmaxf(m[t], mx);
+            if (m_new != -INFINITY) {
+                const float alpha = sm100::ex2_approx(m[t] - m_new);
+                l[t] *= alpha;
+#pragma unroll
+                for (int e = 0; e < 8; ++e) acc[t][e] *= alpha;
+#pragma unroll
+                for (int u = 0; u < U; ++u) {
+                    const float pr = sm100::ex2_approx(sc[u][t] - m_new);
+                    l[t] += pr;
+                    float vf[8];
+                    unpack8<T>(vv[u], vf);
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) acc[t][e] = fmaf(pr, vf[e], acc[t][e]);
+                }
+                m[t] = m_new;
+            }
+        }
+    }
+
+#pragma unroll
+    for (int t = 0; t < TILE; ++t) {
+        if (li == 0) {
+            s_m[grp * TILE + t] = m[t];
+            s_l[grp * TILE + t] = l[t];
+        }
+#pragma unroll
+        for (int e = 0; e < 8; ++e) s_acc[(grp * TILE + t) * D + li * 8 + e] = acc[t][e];
+    }
+    __syncthreads();
+
+    for (int idx = threadIdx.x; idx < TILE * D; idx += kDecodeThreads) {
+        const int t = idx / D;
+        const int d = idx - t * D;
+        float M = -INFINITY;
+        for (int g = 0; g < G; ++g) M = fmaxf(M, s_m[g * TILE + t]);
+        float lt = 0.f, o = 0.f;
+        if (M != -INFINITY) {
+            for (int g = 0; g < G; ++g) {
+                const float w = sm100::ex2_approx(s_m[g * TILE + t] - M);
+                lt = fmaf(w, s_l[g * TILE + t], lt);
+                o = fmaf(w, s_acc[(g * TILE + t) * D + d], o);
+            }
+        }
+        const float outv = lt > 0.f ? o / lt : 0.f;
+        const float lse = lt > 0.f ? (M + log2f(lt)) * kLn2f : -INFINITY;
+        const long long bhq = bhq0 + t;
+        if constexpr (kDirect) {
+            O[bhq * D + d] = DType<T>::from_float(outv);
+            if (d == 0) L[bhq] = lse;
+        } else {
+            O_part[(bhq * num_splits + split) * D + d] = outv;
+            if (d == 0) L_part[bhq * num_splits + split] = lse;
+        }
+    }
+}
+
 // grid (B*H); merges num_splits normalised partials by their log-sum-exp.
 template <typename T, int D>
 __global__ void __launch_bounds__(128)
@@ -282,6 +465,70 @@ FlashAttentionError decode_typed(const T* Q, const T* K, const T* V, T* O, float
                                                     : FlashAttentionError::CUDA_ERROR;
 }
 
+template <typename T, int D, int TILE, bool kPaged>
+FlashAttentionError decode_group_typed(const T* Q, const DecodeKv<T>& kvp, T* O, float* L, int B,
+                                       int hq, int max_len, float scale, int num_splits,
+                                       cudaStream_t stream) {
+    constexpr int G = kDecodeWarps * (32 / (D / 8));
+    const size_t smem = static_cast<size_t>(G) * TILE * (D + 2) * sizeof(float);
+    const int group = hq / kvp.hkv;
+    const int ctas_y = B * kvp.hkv * (group / TILE);
+    const int BHq = B * hq;
+    int S = num_splits == 0 ? auto_splits(ctas_y, max_len) : num_splits;
+    if (S > max_len) S = max_len;
+    if (S < 1) S = 1;
+    const int chunk = (max_len + S - 1) / S;
+    S = (max_len + chunk - 1) / chunk;
+    const float sl2 = scale * kLog2ef;
+    if (S == 1) {
+        auto k = decode_group_kernel<T, D, TILE, kPaged, true>;
+        if (!ensure_smem_attr(reinterpret_cast<const void*>(k), static_cast<int>(smem)))
+            return FlashAttentionError::CUDA_ERROR;
+        k<<<dim3(1, ctas_y), kDecodeThreads, smem, stream>>>(Q, kvp, O, L, nullptr, nullptr, hq,
+                                                              group, chunk, sl2);
+        return cudaGetLastError() == cudaSuccess ? FlashAttentionError::SUCCESS
+                                                 : FlashAttentionError::CUDA_ERROR;
+    }
+    const size_t part_elems = static_cast<size_t>(BHq) * S * D;
+    const size_t bytes = (part_elems + static_cast<size_t>(BHq) * S) * sizeof(float);
+    void* wsv = nullptr;
+    FlashAttentionError werr = workspace_alloc(&wsv, bytes, stream);
+    if (werr != FlashAttentionError::SUCCESS) return werr;
+    float* o_part = static_cast<float*>(wsv);
+    float* l_part = o_part + part_elems;
+    auto k = decode_group_kernel<T, D, TILE, kPaged, false>;
+    if (!ensure_smem_attr(reinterpret_cast<const void*>(k), static_cast<int>(smem))) {
+        workspace_free(wsv, stream);
+        return FlashAttentionError::CUDA_ERROR;
+    }
+    k<<<dim3(S, ctas_y), kDecodeThreads, smem, stream>>>(Q, kvp, nullptr, nullptr, o_part, l_part,
+                                                          hq, group, chunk, sl2);
+    cudaError_t e1 = cudaGetLastError();
+    decode_combine_kernel<T, D><<<BHq, 128, 0, stream>>>(o_part, l_part, O, L, S);
+    cudaError_t e2 = cudaGetLastError();
+    workspace_free(wsv, stream);
+    return (e1 == cudaSuccess && e2 == cudaSuccess) ? FlashAttentionError::SUCCESS
+                                                    : FlashAttentionError::CUDA_ERROR;
+}
+
+template <typename T, int D, bool kPaged>
+FlashAttentionError decode_group_tile(const T* Q, const DecodeKv<T>& kvp, T* O, float* L, int B,
+                                      int hq, int max_len, float scale, int num_splits,
+                                      cudaStream_t stream) {
+    const int group = hq / kvp.hkv;
+    if (group % 8 == 0)
+        return decode_group_typed<T, D, 8, kPaged>(Q, kvp, O, L, B, hq, max_len, scale,
+                                                   num_splits, stream);
+    if (group % 4 == 0)
+        return decode_group_typed<T, D, 4, kPaged>(Q, kvp, O, L, B, hq, max_len, scale,
+                                                   num_splits, stream);
+    if (group % 2 == 0)
+        return decode_group_typed<T, D, 2, kPaged>(Q, kvp, O, L, B, hq, max_len, scale,
+                                                   num_splits, stream);
+    return decode_group_typed<T, D, 1, kPaged>(Q, kvp, O, L, B, hq, max_len, scale, num_splits,
+                                               stream);
+}
+
 }  // namespace
 
 template <typename T>
@@ -309,6 +556,50 @@ template FlashAttentionError launch_decode<__nv_bfloat16>(const __nv_bfloat16*,
                                                           const __nv_bfloat16*, __nv_bfloat16*,
                                                           float*, int, int, int, int, float, int,
                                                           cudaStream_t);
+
+template <typename T>
+FlashAttentionError launch_decode_gqa(const T* Q, const T* K, const T* V, T* O, float* L, int B,
+                                      int Hq, int Hkv, int kv_len, int D, float scale,
+                                      int num_splits, const int* block_table,
+                                      const int* seq_lens, int page_size, int max_pages,
+                                      int num_pages, cudaStream_t stream) {
+    for (const void* p : {static_cast<const void*>(Q), static_cast<const void*>(K),
+                          static_cast<const void*>(V), static_cast<const void*>(O)})
+        if ((reinterpret_cast<uintptr_t>(p) & 15u) != 0) return FlashAttentionError::CUDA_ERROR;
+    DecodeKv<T> kvp;
+    kvp.K = K;
+    kvp.V = V;
+    kvp.block_table = block_table;
+    kvp.seq_lens = seq_lens;
+    kvp.kv_len = kv_len;
+    kvp.hkv = Hkv;
+    kvp.page_shift = 0;
+    while (page_size > 0 && (1 << kvp.page_shift) < page_size) ++kvp.page_shift;
+    kvp.max_pages = max_pages;
+    kvp.num_pages = num_pages;
+    const bool paged = block_table != nullptr;
+    const int max_len = paged ? max_pages * page_size : kv_len;
+#define CUFLASH_DECODE_GQA(DD)                                                                    \
+    return paged ? decode_group_tile<T, DD, true>(Q, kvp, O, L, B, Hq, max_len, scale,           \
+                                                  num_splits, stream)                            \
+                 : decode_group_tile<T, DD, false>(Q, kvp, O, L, B, Hq, max_len, scale,          \
+                                                   num_splits, stream)
+    switch (D) {
+        case 32: CUFLASH_DECODE_GQA(32);
+        case 64: CUFLASH_DECODE_GQA(64);
+        case 128: CUFLASH_DECODE_GQA(128);
+        default: return FlashAttentionError::UNSUPPORTED_HEAD_DIM;
+    }
+#undef CUFLASH_DECODE_GQA
+}
+
+template FlashAttentionError launch_decode_gqa<half>(const half*, const half*, const half*, half*,
+                                                     float*, int, int, int, int, int, float, int,
+                                                     const int*, const int*, int, int, int,
+                                                     cudaStream_t);
+template FlashAttentionError launch_decode_gqa<__nv_bfloat16>(
+    const __nv_bfloat16*, const __nv_bfloat16*, const __nv_bfloat16*, __nv_bfloat16*, float*,
+    int, int, int, int, int, float, int, const int*, const int*, int, int, int, cudaStream_t);
 
 FlashAttentionError launch_lse_merge(float* O_acc, float* L_acc, const float* O_part,
                                      const float* L_part, long long rows, int D,

@@ -55,6 +55,10 @@ SIGNATURES = {
     "cuflash_attention_decode_bf16_noalloc": [_P] * 5 + [_I] * 4 + [_F, _I, _P],
     "cuflash_attention_forward_partial_bf16": [_P] * 5 + [_I] * 5 + [_F, _LL, _LL, _B, _P],
     "cuflash_attention_forward_partial_f16": [_P] * 5 + [_I] * 5 + [_F, _LL, _LL, _B, _P],
+    "cuflash_attention_decode_gqa_bf16": [_P] * 5 + [_I] * 5 + [_F, _I, _P],
+    "cuflash_attention_decode_gqa_f16": [_P] * 5 + [_I] * 5 + [_F, _I, _P],
+    "cuflash_attention_decode_paged_bf16": [_P] * 7 + [_I] * 7 + [_F, _I, _P],
+    "cuflash_attention_decode_paged_f16": [_P] * 7 + [_I] * 7 + [_F, _I, _P],
     "cuflash_attention_forward_gqa_bf16": [_P] * 5 + [_I] * 6 + [_F, _B, _P],
     "cuflash_attention_forward_gqa_f16": [_P] * 5 + [_I] * 6 + [_F, _B, _P],
     "cuflash_attention_backward_gqa_bf16": [_P] * 9 + [_I] * 6 + [_F, _B, _P],
@@ -219,6 +223,42 @@ class CuFlashAttn:
         fn = getattr(self.lib, f"cuflash_attention_forward_partial_{_suffix(Q)}")
         self.check_error(fn(_ptr(Q), _ptr(K), _ptr(V), _ptr(O), _ptr(L), B, H, Nq, Nk, D,
                             float(scale), int(q_offset), int(k_offset), bool(causal),
+                            _stream_handle(stream)))
+        return O, L
+
+    def decode_gqa(self, q, K, V, scale: Optional[float] = None, num_splits: int = 0, O=None,
+                   L=None, stream=None):
+        """q [B,Hq,1,D] against a contiguous cache K/V [B,Hkv,Nkv,D]."""
+        import torch
+
+        B, Hq, _, D = q.shape
+        Hkv, Nkv = K.shape[1], K.shape[2]
+        if scale is None:
+            scale = 1.0 / math.sqrt(D)
+        O = torch.empty_like(q) if O is None else O
+        L = torch.empty((B, Hq), device=q.device, dtype=torch.float32) if L is None else L
+        fn = getattr(self.lib, f"cuflash_attention_decode_gqa_{_suffix(q)}")
+        self.check_error(fn(_ptr(q), _ptr(K), _ptr(V), _ptr(O), _ptr(L), B, Hq, Hkv, Nkv, D,
+                            float(scale), int(num_splits), _stream_handle(stream)))
+        return O, L
+
+    def decode_paged(self, q, K_cache, V_cache, block_table, seq_lens,
+                     scale: Optional[float] = None, num_splits: int = 0, O=None, L=None,
+                     stream=None):
+        """q [B,Hq,1,D] against a paged cache K/V [pages, page_size, Hkv, D]
+        with block_table int32 [B, max_pages] and seq_lens int32 [B]."""
+        import torch
+
+        B, Hq, _, D = q.shape
+        num_pages, page_size, Hkv, _ = K_cache.shape
+        if scale is None:
+            scale = 1.0 / math.sqrt(D)
+        O = torch.empty_like(q) if O is None else O
+        L = torch.empty((B, Hq), device=q.device, dtype=torch.float32) if L is None else L
+        fn = getattr(self.lib, f"cuflash_attention_decode_paged_{_suffix(q)}")
+        self.check_error(fn(_ptr(q), _ptr(K_cache), _ptr(V_cache), _ptr(block_table),
+                            _ptr(seq_lens), _ptr(O), _ptr(L), B, Hq, Hkv, D, page_size,
+                            block_table.shape[1], num_pages, float(scale), int(num_splits),
                             _stream_handle(stream)))
         return O, L
 

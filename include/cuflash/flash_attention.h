@@ -199,6 +199,42 @@ CUFLASH_EXPORT int cuflash_attention_forward_partial_f16(
     int num_heads, int seq_q, int seq_k, int head_dim, float scale, long long q_offset,
     long long k_offset, bool causal, cudaStream_t stream);
 
+// Grouped-query split-KV decode (no reference counterpart): one query token
+// per (batch, query head) against a contiguous cache K, V [B, num_kv_heads,
+// kv_len, D]; Q, O [B, num_q_heads, 1, D], L fp32 [B, num_q_heads].  Query
+// head h reads K/V head h / (num_q_heads / num_kv_heads); one CTA serves up
+// to 8 query heads of a group, so every cache row is read once for them.
+// num_splits: 0 = automatic, 1..64.
+CUFLASH_EXPORT int cuflash_attention_decode_gqa_bf16(
+    const __nv_bfloat16* Q, const __nv_bfloat16* K, const __nv_bfloat16* V, __nv_bfloat16* O,
+    float* L, int batch_size, int num_q_heads, int num_kv_heads, int kv_len, int head_dim,
+    float scale, int num_splits, cudaStream_t stream);
+CUFLASH_EXPORT int cuflash_attention_decode_gqa_f16(const half* Q, const half* K, const half* V,
+                                                    half* O, float* L, int batch_size,
+                                                    int num_q_heads, int num_kv_heads,
+                                                    int kv_len, int head_dim, float scale,
+                                                    int num_splits, cudaStream_t stream);
+
+// Split-KV decode over a paged KV cache (no reference counterpart).  K_cache,
+// V_cache [num_pages, page_size, num_kv_heads, D]; block_table int32
+// [B, max_pages_per_seq] and seq_lens int32 [B] in device memory: token t of
+// sequence b sits in page block_table[b][t / page_size], slot t % page_size.
+// page_size must be a power of two; page indices outside [0, num_pages) are
+// clamped (a bad table reads a wrong page instead of faulting); a sequence of
+// length 0 gets O = 0 and L = -inf.  Heads, Q / O / L and num_splits as in
+// cuflash_attention_decode_gqa_*; splits are planned over
+// max_pages_per_seq * page_size tokens.
+CUFLASH_EXPORT int cuflash_attention_decode_paged_bf16(
+    const __nv_bfloat16* Q, const __nv_bfloat16* K_cache, const __nv_bfloat16* V_cache,
+    const int* block_table, const int* seq_lens, __nv_bfloat16* O, float* L, int batch_size,
+    int num_q_heads, int num_kv_heads, int head_dim, int page_size, int max_pages_per_seq,
+    int num_pages, float scale, int num_splits, cudaStream_t stream);
+CUFLASH_EXPORT int cuflash_attention_decode_paged_f16(
+    const half* Q, const half* K_cache, const half* V_cache, const int* block_table,
+    const int* seq_lens, half* O, float* L, int batch_size, int num_q_heads, int num_kv_heads,
+    int head_dim, int page_size, int max_pages_per_seq, int num_pages, float scale,
+    int num_splits, cudaStream_t stream);
+
 // Grouped-query (GQA / MQA) attention with separate query and key lengths
 // (no reference counterpart: the reference API has one seq_len and equal
 // head counts).  Q, O, dO, dQ [B, num_q_heads, seq_len_q, D]; K, V, dK, dV

@@ -189,6 +189,31 @@ def test_gqa_validation(lib, sfx):
 
 
 @pytest.mark.parametrize("sfx", ["f16", "bf16"])
+def test_decode_gqa_paged_validation(lib, sfx):
+    g = getattr(lib.lib, f"cuflash_attention_decode_gqa_{sfx}")
+    pg = getattr(lib.lib, f"cuflash_attention_decode_paged_{sfx}")
+
+    def cg(Hq=8, Hkv=2, N=64, D=128, splits=0, nul=None):
+        a = [FAKE] * 5 + [1, Hq, Hkv, N, D, 0.1, splits, STREAM]
+        if nul is not None:
+            a[nul] = NUL
+        return g(*a)
+
+    def cp(Hq=8, Hkv=2, D=128, ps=16, mp=4, npg=8, splits=0, nul=None):
+        a = [FAKE] * 7 + [1, Hq, Hkv, D, ps, mp, npg, 0.1, splits, STREAM]
+        if nul is not None:
+            a[nul] = NUL
+        return pg(*a)
+
+    assert cg(nul=1) == 3 and cg(N=0) == 1 and cg(Hq=6, Hkv=4) == 2 and cg(D=80) == 6
+    assert cg(splits=65) == 1 and cg(splits=-1) == 1
+    assert cp(nul=3) == 3 and cp(nul=4) == 3        # block table / seq_lens
+    assert cp(ps=24) == 1 and cp(ps=0) == 1          # page size a power of two
+    assert cp(mp=0) == 1 and cp(npg=0) == 1
+    assert cp(Hq=9) == 2
+
+
+@pytest.mark.parametrize("sfx", ["f16", "bf16"])
 def test_cp_step_validation(lib, sfx):
     import ctypes
 
