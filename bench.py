@@ -435,9 +435,16 @@ def run_cp(args, lib, dev, world, rank, pk, pk_kind):
     q_ab = [chunk_tensor(0, c) for c in chunks]
     k_ab = [chunk_tensor(1, c) for c in chunks]
     v_ab = [chunk_tensor(2, c) for c in chunks]
+    do_ab = [chunk_tensor(3, c) for c in chunks] if args.cp_backward else None
     ring = ring_cp.RingAttention(lib)
+
+    def step():
+        outs, lses = ring.forward(q_ab, k_ab, v_ab, scale)
+        if args.cp_backward:  # the ring backward of the same step
+            ring.backward(q_ab, k_ab, v_ab, outs, lses, do_ab, scale)
+
     for _ in range(max(args.warmup, 3)):
-        ring.forward(q_ab, k_ab, v_ab, scale)
+        step()
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
@@ -446,7 +453,7 @@ def run_cp(args, lib, dev, world, rank, pk, pk_kind):
     with Clocks(dev.index) as clk:
         e0.record(stream)
         for _ in range(args.steps):
-            ring.forward(q_ab, k_ab, v_ab, scale)
+            step()
         e1.record(stream)
         torch.cuda.synchronize()
     ms = e0.elapsed_time(e1) / args.steps
@@ -454,7 +461,7 @@ def run_cp(args, lib, dev, world, rank, pk, pk_kind):
         t = torch.tensor([ms], device=dev, dtype=torch.float64)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = float(t.item())
-    flops = fwd_flops(B, H, N, D, True)
+    flops = fwd_flops(B, H, N, D, True) * (3.5 if args.cp_backward else 1.0)
     value = flops / (ms * 1e-3) / 1e12
     peak = pk.get("bf16_tflops_sustained", FALLBACK_PEAKS["bf16_tflops_sustained"])
     if rank == 0:
@@ -463,7 +470,9 @@ def run_cp(args, lib, dev, world, rank, pk, pk_kind):
             "steps": args.steps, "warmup": max(args.warmup, 3), "ms_per_step": ms,
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
             "dtype": "bf16", "data": "synthetic (torch.randn per global chunk)",
-            "config": {"workload": f"BASELINE config 5: causal fwd B{B} H{H} N{N} D{D}, "
+            "config": {"workload": f"BASELINE config 5: causal "
+                                   f"{'fwd+bwd' if args.cp_backward else 'fwd'} "
+                                   f"B{B} H{H} N{N} D{D}, "
                                    f"ring CP over {world} GPU(s), zigzag chunks of {C}",
                        "global_batch": B, "seq_len": N, "parallelism": f"cp{world}"},
             "per_gpu_tflops": value / world,
@@ -484,6 +493,8 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=["train", "decode", "cp"], default="train")
     ap.add_argument("--cp-seq", type=int, default=131072)
+    ap.add_argument("--cp-backward", action="store_true",
+                    help="cp workload: time the ring forward and backward of a training step")
     ap.add_argument("--splits", type=int, nargs="*", default=[0, 1, 2, 4, 8, 16, 32, 64])
     ap.add_argument("--skip-cpu-baseline", action="store_true")
     ap.add_argument("--batch", type=int, default=TRAIN["B"])

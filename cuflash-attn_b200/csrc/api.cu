@@ -281,6 +281,57 @@ FlashAttentionError cp_step_impl(const T* Q, const T* K, const T* V, float* O_ac
                                                         q_off, kv_off, stream);
 }
 
+FlashAttentionError cp_dims_check(int nq, int B, int H, int C, int D) {
+    if (nq <= 0 || B <= 0 || H <= 0 || C <= 0 || D <= 0)
+        return FlashAttentionError::INVALID_DIMENSION;
+    if (!(D == 32 || D == 64 || D == 128)) return FlashAttentionError::UNSUPPORTED_HEAD_DIM;
+    if (static_cast<long long>(B) * H * nq > 0x7fffffffLL) return FlashAttentionError::INVALID_DIMENSION;
+    return FlashAttentionError::SUCCESS;
+}
+
+template <typename T>
+FlashAttentionError cp_bwd_prepare_impl(const T* O, const T* dO, const float* L, void* ws, int nq,
+                                        int B, int H, int C, int D, cudaStream_t stream) {
+    if (!O || !dO || !L || !ws) return FlashAttentionError::NULL_POINTER;
+    const FlashAttentionError e = cp_dims_check(nq, B, H, C, D);
+    if (e != FlashAttentionError::SUCCESS) return e;
+    return cuflash::detail::launch_bwd_cp_prepare_sm100<T>(O, dO, L, ws, nq, B * H, C, D, stream);
+}
+
+template <typename T>
+FlashAttentionError cp_bwd_step_impl(const T* Q, const T* dO, const T* K, const T* V, void* ws,
+                                     float* dK_acc, float* dV_acc, int nq, int nk, int B, int H,
+                                     int C, int D, float scale, bool causal, int num_pairs,
+                                     const int* q_slot, const int* kv_slot,
+                                     const long long* q_off, const long long* kv_off,
+                                     cudaStream_t stream) {
+    if (!Q || !dO || !K || !V || !ws || !dK_acc || !dV_acc || !q_slot || !kv_slot || !q_off ||
+        !kv_off)
+        return FlashAttentionError::NULL_POINTER;
+    FlashAttentionError e = cp_dims_check(nq, B, H, C, D);
+    if (e == FlashAttentionError::SUCCESS) e = cp_dims_check(nk, B, H, C, D);
+    if (e != FlashAttentionError::SUCCESS) return e;
+    if (!std::isfinite(scale) || scale < 0.0f) return FlashAttentionError::INVALID_DIMENSION;
+    if (num_pairs < 1 || num_pairs > 4) return FlashAttentionError::INVALID_DIMENSION;
+    for (int i = 0; i < num_pairs; ++i)
+        if (q_slot[i] < 0 || q_slot[i] >= nq || kv_slot[i] < 0 || kv_slot[i] >= nk ||
+            q_off[i] < 0 || kv_off[i] < 0)
+            return FlashAttentionError::INVALID_DIMENSION;
+    return cuflash::detail::launch_bwd_cp_step_sm100<T>(Q, dO, K, V, ws, dK_acc, dV_acc, nq, nk,
+                                                        B * H, C, D, scale, causal, num_pairs,
+                                                        q_slot, kv_slot, q_off, kv_off, stream);
+}
+
+template <typename T>
+FlashAttentionError cp_bwd_finish_impl(const void* ws, T* dQ, int nq, int B, int H, int C, int D,
+                                       float scale, cudaStream_t stream) {
+    if (!ws || !dQ) return FlashAttentionError::NULL_POINTER;
+    const FlashAttentionError e = cp_dims_check(nq, B, H, C, D);
+    if (e != FlashAttentionError::SUCCESS) return e;
+    if (!std::isfinite(scale) || scale < 0.0f) return FlashAttentionError::INVALID_DIMENSION;
+    return cuflash::detail::launch_bwd_cp_finish_sm100<T>(ws, dQ, nq, B * H, C, D, scale, stream);
+}
+
 }  // namespace
 
 extern "C" {
@@ -481,6 +532,58 @@ int cuflash_attention_forward_cp_step_f16(const half* Q, const half* K, const ha
                                                batch_size, num_heads, chunk_len, head_dim, scale,
                                                causal, num_pairs, q_slot, kv_slot, q_offset,
                                                kv_offset, stream));
+}
+
+long long cuflash_attention_backward_cp_workspace_size(int num_q_slots, int batch_size,
+                                                       int num_heads, int chunk_len,
+                                                       int head_dim) {
+    if (cp_dims_check(num_q_slots, batch_size, num_heads, chunk_len, head_dim) !=
+        FlashAttentionError::SUCCESS)
+        return 0;
+    return cuflash::detail::bwd_cp_workspace_bytes(num_q_slots, batch_size * num_heads, chunk_len,
+                                                   head_dim);
+}
+
+#define CUFLASH_CP_BWD_ENTRIES(SUFFIX, T)                                                        \
+    int cuflash_attention_backward_cp_prepare_##SUFFIX(                                          \
+        const T* O, const T* dO, const float* L, void* workspace, int num_q_slots,               \
+        int batch_size, int num_heads, int chunk_len, int head_dim, cudaStream_t stream) {       \
+        return static_cast<int>(cp_bwd_prepare_impl<T>(O, dO, L, workspace, num_q_slots,         \
+                                                       batch_size, num_heads, chunk_len,         \
+                                                       head_dim, stream));                       \
+    }                                                                                            \
+    int cuflash_attention_backward_cp_step_##SUFFIX(                                             \
+        const T* Q, const T* dO, const T* K, const T* V, void* workspace, float* dK_acc,         \
+        float* dV_acc, int num_q_slots, int num_kv_slots, int batch_size, int num_heads,         \
+        int chunk_len, int head_dim, float scale, bool causal, int num_pairs, const int* q_slot, \
+        const int* kv_slot, const long long* q_offset, const long long* kv_offset,               \
+        cudaStream_t stream) {                                                                   \
+        return static_cast<int>(cp_bwd_step_impl<T>(                                             \
+            Q, dO, K, V, workspace, dK_acc, dV_acc, num_q_slots, num_kv_slots, batch_size,       \
+            num_heads, chunk_len, head_dim, scale, causal, num_pairs, q_slot, kv_slot, q_offset, \
+            kv_offset, stream));                                                                 \
+    }                                                                                            \
+    int cuflash_attention_backward_cp_finish_##SUFFIX(const void* workspace, T* dQ,              \
+                                                      int num_q_slots, int batch_size,           \
+                                                      int num_heads, int chunk_len,              \
+                                                      int head_dim, float scale,                 \
+                                                      cudaStream_t stream) {                     \
+        return static_cast<int>(cp_bwd_finish_impl<T>(workspace, dQ, num_q_slots, batch_size,    \
+                                                      num_heads, chunk_len, head_dim, scale,     \
+                                                      stream));                                  \
+    }
+CUFLASH_CP_BWD_ENTRIES(bf16, __nv_bfloat16)
+CUFLASH_CP_BWD_ENTRIES(f16, half)
+#undef CUFLASH_CP_BWD_ENTRIES
+
+int cuflash_accumulate_f32(float* dst, float* src, long long count, bool zero_src,
+                           cudaStream_t stream) {
+    if (!dst || !src) return static_cast<int>(FlashAttentionError::NULL_POINTER);
+    if (count <= 0 || count % 4 != 0 || (reinterpret_cast<uintptr_t>(dst) & 15u) != 0 ||
+        (reinterpret_cast<uintptr_t>(src) & 15u) != 0)
+        return static_cast<int>(FlashAttentionError::INVALID_DIMENSION);
+    return static_cast<int>(
+        cuflash::detail::launch_accumulate_f32(dst, src, count, zero_src, stream));
 }
 
 int cuflash_lse_merge_f32(float* O_acc, float* L_acc, const float* O_part, const float* L_part,

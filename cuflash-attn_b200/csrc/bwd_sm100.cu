@@ -106,6 +106,23 @@ struct BwdParams {
     int causal;
     float scale_log2;
     float scale;
+    // Context-parallel step (kernels instantiated with kCp): query tensors
+    // hold query slots and K/V tensors K/V slots, [slot][B*H][chunk][D] each,
+    // so query head q_slot * bh_slot + bh and K/V head kv_slot * bh_slot + bh.
+    // The step's (query slot, K/V slot) pairs are grouped by K/V slot into
+    // segments; an item is one 128-row block of one segment's K/V slot and
+    // walks the visible query blocks of every pair of the segment.  dK / dV
+    // of the step are added into fp32 accumulators [kv slot][B*H][chunk][D].
+    float* dk_acc;
+    float* dv_acc;
+    int bh_slot;            // B*H
+    int nkseg;              // segments (distinct K/V slots among the pairs)
+    int seg_units;          // units per segment
+    int kseg_slot[4];       // K/V slot of segment s
+    int kseg_first[4];      // its pairs: [kseg_first, kseg_first + kseg_count)
+    int kseg_count[4];
+    int pair_q_slot[4];     // query slot of pair k (pairs sorted by segment)
+    long long pair_rel[4];  // query offset - K/V offset of pair k (global positions)
 };
 
 // One work item = one 128-row K/V block j of one (b,h).  Unit u of the
@@ -117,54 +134,102 @@ struct BwdParams {
 // per unit instead.
 struct BwdItem {
     int j;
-    int bh;  // K/V head: batch * Hkv + kv head
+    int bh;   // K/V head: batch * Hkv + kv head (context-parallel: kv_slot * bh_slot + bh)
+    int seg;  // context-parallel segment
+    int bhl;  // context-parallel: bh within the slot
 };
-
-__device__ __forceinline__ bool bwd_item(const BwdParams& p, int u, int w, BwdItem& it) {
-    if (!p.paired) {
-        if (w == 1) return false;
-        it.bh = u / p.n_blk_k;
-        it.j = u - it.bh * p.n_blk_k;  // ascending j: heaviest first under a causal mask
-        return true;
-    }
-    const int bh = u / p.npairs;
-    const int k = u - bh * p.npairs;
-    const int j = w == 0 ? k : p.n_blk_k - 1 - k;
-    if (w == 1 && j == k) return false;  // middle block of an odd count
-    it.j = j;
-    it.bh = bh;
-    return true;
-}
 
 // The query walk of an item: for each of the group's query heads, the query
 // blocks i0..n_blk_q-1 that see any key of block j (all of them unless causal).
+// Context-parallel items walk, pair after pair of their segment, the visible
+// query blocks of each pair's query slot.
 struct BwdWalk {
     int i0;  // first visible query block
     int ni;  // blocks per query head
-    int n;   // group * ni
+    int n;   // group * ni (context-parallel: total over the segment's pairs)
 };
 
-__device__ __forceinline__ BwdWalk bwd_walk(const BwdParams& p, int j) {
+// First query block with rel + 128 i + 127 >= 128 j (the first that sees any
+// key of block j when query 0 sits at global position rel and key 0 at 0).
+__device__ __forceinline__ int bwd_first_block(const BwdParams& p, int j, long long rel) {
+    if (!p.causal) return 0;
+    const long long num = 128LL * j - rel - 127;
+    const long long i0 = num <= 0 ? 0 : (num + 127) / 128;
+    return static_cast<int>(i0 < p.n_blk_q ? i0 : p.n_blk_q);
+}
+
+template <bool kCp>
+__device__ __forceinline__ BwdWalk bwd_walk(const BwdParams& p, const BwdItem& itm) {
     BwdWalk w;
-    w.i0 = 0;
-    if (p.causal) {
-        // first query block with q_off + 128 i + 127 >= 128 j
-        const long long num = 128LL * j - p.q_off - 127;
-        const long long i0 = num <= 0 ? 0 : (num + 127) / 128;
-        w.i0 = static_cast<int>(i0 < p.n_blk_q ? i0 : p.n_blk_q);
+    if constexpr (kCp) {
+        w.i0 = 0;
+        w.ni = 0;
+        w.n = 0;
+        const int f = p.kseg_first[itm.seg], c = p.kseg_count[itm.seg];
+        for (int k = 0; k < c; ++k) w.n += p.n_blk_q - bwd_first_block(p, itm.j, p.pair_rel[f + k]);
+    } else {
+        w.i0 = bwd_first_block(p, itm.j, p.q_off);
+        w.ni = p.n_blk_q - w.i0;
+        w.n = p.group * w.ni;
     }
-    w.ni = p.n_blk_q - w.i0;
-    w.n = p.group * w.ni;
     return w;
 }
 
-// Query head and block of walk step `it`.
+template <bool kCp>
+__device__ __forceinline__ bool bwd_item(const BwdParams& p, int u, int w, BwdItem& it) {
+    int v = u, base = 0;
+    it.seg = 0;
+    if constexpr (kCp) {
+        it.seg = u / p.seg_units;
+        v = u - it.seg * p.seg_units;
+        base = p.kseg_slot[it.seg] * p.bh_slot;
+    }
+    if (!p.paired) {
+        if (w == 1) return false;
+        it.bhl = v / p.n_blk_k;
+        it.j = v - it.bhl * p.n_blk_k;  // ascending j: heaviest first under a causal mask
+    } else {
+        it.bhl = v / p.npairs;
+        const int k = v - it.bhl * p.npairs;
+        it.j = w == 0 ? k : p.n_blk_k - 1 - k;
+        if (w == 1 && it.j == k) return false;  // middle block of an odd count
+    }
+    it.bh = base + it.bhl;
+    // a context-parallel block that no query of the step sees adds nothing
+    if constexpr (kCp) return bwd_walk<true>(p, it).n > 0;
+    return true;
+}
+
+// Query head, query block and causal offset (global position of the block's
+// query 0 minus that of key 0) of walk step `it`.
+template <bool kCp>
 __device__ __forceinline__ void bwd_step(const BwdParams& p, const BwdItem& itm, const BwdWalk& w,
-                                         int it, int& bh_q, int& i) {
-    const int gq = w.ni > 0 ? it / w.ni : 0;
-    i = w.i0 + (it - gq * w.ni);
-    const int hkv = p.hq / p.group;
-    bh_q = (itm.bh / hkv) * p.hq + (itm.bh % hkv) * p.group + gq;
+                                         int it, int& bh_q, int& i, long long& rel) {
+    bh_q = 0;
+    i = 0;
+    rel = 0;
+    if constexpr (kCp) {
+        const int f = p.kseg_first[itm.seg], c = p.kseg_count[itm.seg];
+        int rest = it;
+        for (int k = 0; k < c; ++k) {
+            const long long r = p.pair_rel[f + k];
+            const int i0 = bwd_first_block(p, itm.j, r);
+            const int ni = p.n_blk_q - i0;
+            if (rest < ni || k == c - 1) {
+                i = i0 + rest;
+                rel = r;
+                bh_q = p.pair_q_slot[f + k] * p.bh_slot + itm.bhl;
+                return;
+            }
+            rest -= ni;
+        }
+    } else {
+        const int gq = w.ni > 0 ? it / w.ni : 0;
+        i = w.i0 + (it - gq * w.ni);
+        const int hkv = p.hq / p.group;
+        bh_q = (itm.bh / hkv) * p.hq + (itm.bh % hkv) * p.group + gq;
+        rel = p.q_off;
+    }
 }
 
 template <int D>
@@ -399,7 +464,7 @@ __device__ __forceinline__ void bwd_softmax_block(uint32_t t_s, uint32_t t_dp, u
 
 constexpr int kBwdThreads = 512;
 
-template <typename T, int D>
+template <typename T, int D, bool kCp>
 __global__ void __launch_bounds__(kBwdThreads, 1)
     fa_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                   const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmdO,
@@ -507,12 +572,13 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
             for (int u = blockIdx.x; ok && u < p.num_units; u += gridDim.x) {
                 for (int w = 0; ok && w < 2; ++w) {
                     BwdItem itm;
-                    if (!bwd_item(p, u, w, itm)) continue;
-                    const BwdWalk wk = bwd_walk(p, itm.j);
+                    if (!bwd_item<kCp>(p, u, w, itm)) continue;
+                    const BwdWalk wk = bwd_walk<kCp>(p, itm);
                     const int n_it = wk.n;
                     auto load_step = [&](int it) {
                         int bh_q, i;
-                        bwd_step(p, itm, wk, it, bh_q, i);
+                        long long rel;
+                        bwd_step<kCp>(p, itm, wk, it, bh_q, i, rel);
                         return load_stage(bh_q, i);
                     };
                     // The item's first stages only need free ring slots, so they go
@@ -576,8 +642,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
             for (int u = blockIdx.x; ok && u < p.num_units; u += gridDim.x) {
                 for (int w = 0; ok && w < 2; ++w) {
                     BwdItem itm;
-                    if (!bwd_item(p, u, w, itm)) continue;
-                    const int n_it = bwd_walk(p, itm.j).n;
+                    if (!bwd_item<kCp>(p, u, w, itm)) continue;
+                    const int n_it = bwd_walk<kCp>(p, itm).n;
                     // K_j, V_j and the item's first query block
                     ok = mbar_wait(bar_kv, items & 1, abort_flag, &g_bwd_status) &&
                          mbar_wait(full + g % G::kStages, (g / G::kStages) & 1, abort_flag,
@@ -683,13 +749,14 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         for (int u = blockIdx.x; ok && u < p.num_units; u += gridDim.x) {
             for (int w = 0; ok && w < 2; ++w) {
                 BwdItem itm;
-                if (!bwd_item(p, u, w, itm)) continue;
+                if (!bwd_item<kCp>(p, u, w, itm)) continue;
                 const int j = itm.j, bh = itm.bh;  // bh: K/V head (dK, dV rows)
-                const BwdWalk wk = bwd_walk(p, j);
+                const BwdWalk wk = bwd_walk<kCp>(p, itm);
                 const int n_it = wk.n;
                 for (int it = 0; it < n_it; ++it, ++g) {
                     int bh_q, i;
-                    bwd_step(p, itm, wk, it, bh_q, i);
+                    long long rel;
+                    bwd_step<kCp>(p, itm, wk, it, bh_q, i, rel);
                     const int s = g % G::kStages;
                     // L and D of block i arrived through the async proxy: observe
                     // the stage's own barrier before reading them (it completes
@@ -705,7 +772,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
                                                        2 * G::kTileBytes) +
                         h * 64;
                     const float* sD = sL + 128;
-                    const long long dl = 128LL * (j - i) - p.q_off;
+                    const long long dl = 128LL * (j - i) - rel;
                     if (p.causal && dl > -127)
                         bwd_softmax_block<T, true>(t_s, t_dp, sDs, sL, sD, c, h, r,
                                                    static_cast<int>(dl));
@@ -725,9 +792,33 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
                 const int kv = j * 128 + r;
                 const bool valid = kv < p.Nk;
                 const size_t row = (static_cast<size_t>(bh) * p.Nk + kv) * D;
-                T* dst_base = static_cast<T*>(h == 0 ? p.dV : p.dK);
                 const float mul = h == 0 ? 1.f : p.scale;
                 const uint32_t t_acc = tmem + lane_addr + (h == 0 ? 256 : 384);
+                if constexpr (kCp) {
+                    // add this step's dV / scale*dK of the row into the fp32 accumulator
+                    float* acc = (h == 0 ? p.dv_acc : p.dk_acc) + row;
+#pragma unroll
+                    for (int cb = 0; cb < D / 32; ++cb) {
+                        uint32_t a[32];
+                        if (ok) tmem_ld_x32(t_acc + cb * 32, a);
+                        if (ok && valid) {
+                            float4* dst = reinterpret_cast<float4*>(acc + cb * 32);
+                            float4 cur[8];
+#pragma unroll
+                            for (int q4 = 0; q4 < 8; ++q4) cur[q4] = dst[q4];
+#pragma unroll
+                            for (int q4 = 0; q4 < 8; ++q4) {
+                                cur[q4].x = fmaf(__uint_as_float(a[4 * q4 + 0]), mul, cur[q4].x);
+                                cur[q4].y = fmaf(__uint_as_float(a[4 * q4 + 1]), mul, cur[q4].y);
+                                cur[q4].z = fmaf(__uint_as_float(a[4 * q4 + 2]), mul, cur[q4].z);
+                                cur[q4].w = fmaf(__uint_as_float(a[4 * q4 + 3]), mul, cur[q4].w);
+                                dst[q4] = cur[q4];
+                            }
+                        }
+                    }
+                    continue;
+                }
+                T* dst_base = static_cast<T*>(h == 0 ? p.dV : p.dK);
 #pragma unroll
                 for (int cb = 0; cb < D / 32; ++cb) {
                     uint32_t a[32];
@@ -764,15 +855,16 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         for (int u = blockIdx.x; ok && u < p.num_units; u += gridDim.x) {
             for (int w = 0; ok && w < 2; ++w) {
                 BwdItem itm;
-                if (!bwd_item(p, u, w, itm)) continue;
-                const BwdWalk wk = bwd_walk(p, itm.j);
+                if (!bwd_item<kCp>(p, u, w, itm)) continue;
+                const BwdWalk wk = bwd_walk<kCp>(p, itm);
                 const int n_it = wk.n;
                 if constexpr (kTransposedDq) {
                     // lane = head_dim element d; TMEM column = query row of block i
                     const int d = wq * 32 + lane;
                     for (int it = 0; it < n_it; ++it, ++g) {
                         int bh, i;  // query head and block
-                        bwd_step(p, itm, wk, it, bh, i);
+                        long long rel;
+                        bwd_step<kCp>(p, itm, wk, it, bh, i, rel);
                         if (!bwarp_wait(bar_dq, g & 1, abort_flag)) {
                             ok = false;
                             break;
@@ -809,7 +901,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
                     const uint32_t stage0 = sbase + G::kOffDs + wq * 8192;
                     for (int it = 0; it < n_it; ++it, ++g) {
                         int bh, i;  // query head and block
-                        bwd_step(p, itm, wk, it, bh, i);
+                        long long rel;
+                        bwd_step<kCp>(p, itm, wk, it, bh, i, rel);
                         if (!bwarp_wait(bar_dq, g & 1, abort_flag)) {
                             ok = false;
                             break;
@@ -893,7 +986,7 @@ FlashAttentionError bwd_typed(const T* Q, const T* K, const T* V, const T* O, co
                             static_cast<const void*>(dK), static_cast<const void*>(dV)})
         if ((reinterpret_cast<uintptr_t>(ptr) & 15u) != 0)
             return fail(FlashAttentionError::CUDA_ERROR);
-    auto kern = fa_bwd_kernel<T, D>;
+    auto kern = fa_bwd_kernel<T, D, false>;
     if (!ensure_smem_attr(reinterpret_cast<const void*>(kern), G::kSmemBytes))
         return fail(FlashAttentionError::CUDA_ERROR);
 
@@ -965,7 +1058,222 @@ FlashAttentionError bwd_dispatch(const T* Q, const T* K, const T* V, const T* O,
     }
 }
 
+// ------------------------------------------------- context-parallel backward
+//
+// Workspace of the ring backward, kept across its steps: the fp32 dQ
+// accumulator [nq*BH][C][D], then -L*log2(e) and -rowsum(dO*O) per query
+// head, each padded to whole 128-row blocks.
+struct CpBwdWs {
+    float* dq_acc;
+    float* l2p;
+    float* dvp;
+};
+
+inline long long cp_bwd_pad(int C) { return (static_cast<long long>(C) + 127) / 128 * 128; }
+
+inline CpBwdWs cp_bwd_ws(void* ws, long long heads, int C, int D) {
+    CpBwdWs w;
+    w.dq_acc = static_cast<float*>(ws);
+    w.l2p = w.dq_acc + heads * C * D;
+    w.dvp = w.l2p + heads * cp_bwd_pad(C);
+    return w;
+}
+
+template <typename T, int D>
+FlashAttentionError bwd_cp_prepare_typed(const T* O, const T* dO, const float* L, void* ws,
+                                         long long heads, int C, cudaStream_t stream) {
+    const CpBwdWs w = cp_bwd_ws(ws, heads, C, D);
+    const long long n_pad = cp_bwd_pad(C);
+    const long long rows_pad = heads * n_pad;
+    const long long pre_blocks = (rows_pad * (D / 8) + 255) / 256;
+    bwd_preprocess_kernel<T, D><<<static_cast<unsigned>(pre_blocks), 256, 0, stream>>>(
+        O, dO, L, w.l2p, w.dvp, w.dq_acc, C, static_cast<int>(n_pad), rows_pad);
+    return cudaGetLastError() == cudaSuccess ? FlashAttentionError::SUCCESS
+                                             : FlashAttentionError::CUDA_ERROR;
+}
+
+template <typename T, int D>
+FlashAttentionError bwd_cp_step_typed(const T* Q, const T* dO, const T* K, const T* V, void* ws,
+                                      float* dk_acc, float* dv_acc, int nq, int nk, int BH, int C,
+                                      float scale, bool causal, int num_pairs, const int* q_slot,
+                                      const int* kv_slot, const long long* q_off,
+                                      const long long* kv_off, cudaStream_t stream) {
+    using G = BwdGeom<D>;
+    const long long qheads = static_cast<long long>(nq) * BH;
+    const long long kheads = static_cast<long long>(nk) * BH;
+    const CpBwdWs w = cp_bwd_ws(ws, qheads, C, D);
+    const CUtensorMapSwizzle swz =
+        G::kSwz == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
+    CUtensorMap mq, mk, mv, mdo, mdq;
+    if (!encode_tmap_3d(&mq, Q, DType<T>::kTmaType, 2, D, C, qheads, G::kCbElems, 128, swz) ||
+        !encode_tmap_3d(&mk, K, DType<T>::kTmaType, 2, D, C, kheads, G::kCbElems, 128, swz) ||
+        !encode_tmap_3d(&mv, V, DType<T>::kTmaType, 2, D, C, kheads, G::kCbElems, 128, swz) ||
+        !encode_tmap_3d(&mdo, dO, DType<T>::kTmaType, 2, D, C, qheads, G::kCbElems, 128, swz) ||
+        !encode_tmap_3d(&mdq, w.dq_acc, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, D, C, qheads, 32, 32,
+                        CU_TENSOR_MAP_SWIZZLE_128B))
+        return FlashAttentionError::CUDA_ERROR;
+    if ((reinterpret_cast<uintptr_t>(dk_acc) & 15u) != 0 ||
+        (reinterpret_cast<uintptr_t>(dv_acc) & 15u) != 0)
+        return FlashAttentionError::CUDA_ERROR;
+    auto kern = fa_bwd_kernel<T, D, true>;
+    if (!ensure_smem_attr(reinterpret_cast<const void*>(kern), G::kSmemBytes))
+        return FlashAttentionError::CUDA_ERROR;
+
+    BwdParams prm{};
+    prm.dq_acc = w.dq_acc;
+    prm.l2p = w.l2p;
+    prm.dvp = w.dvp;
+    prm.dk_acc = dk_acc;
+    prm.dv_acc = dv_acc;
+    prm.Nq = C;
+    prm.Nk = C;
+    prm.n_blk_q = (C + 127) / 128;
+    prm.n_blk_k = prm.n_blk_q;
+    prm.q_off = 0;
+    prm.hq = 1;
+    prm.group = 1;
+    prm.npairs = (prm.n_blk_k + 1) / 2;
+    prm.causal = causal ? 1 : 0;
+    prm.scale_log2 = scale * kLog2eB;
+    prm.scale = scale;
+    prm.bh_slot = BH;
+    // segments: the distinct K/V slots in order of first appearance, each
+    // with its pairs in call order
+    prm.nkseg = 0;
+    int np = 0;
+    for (int i = 0; i < num_pairs; ++i) {
+        bool seen = false;
+        for (int s = 0; s < prm.nkseg; ++s) seen = seen || prm.kseg_slot[s] == kv_slot[i];
+        if (seen) continue;
+        const int s = prm.nkseg++;
+        prm.kseg_slot[s] = kv_slot[i];
+        prm.kseg_first[s] = np;
+        for (int k = i; k < num_pairs; ++k) {
+            if (kv_slot[k] != kv_slot[i]) continue;
+            prm.pair_q_slot[np] = q_slot[k];
+            prm.pair_rel[np] = q_off[k] - kv_off[k];
+            ++np;
+        }
+        prm.kseg_count[s] = np - prm.kseg_first[s];
+    }
+    const int sms = current_sm_count();
+    long long seg_units = static_cast<long long>(BH) * prm.npairs;
+    prm.paired = (causal && seg_units * prm.nkseg >= sms) ? 1 : 0;
+    if (!prm.paired) seg_units = static_cast<long long>(BH) * prm.n_blk_k;
+    const long long units = seg_units * prm.nkseg;
+    if (units > 0x7fffffffLL) return FlashAttentionError::CUDA_ERROR;
+    prm.seg_units = static_cast<int>(seg_units);
+    prm.num_units = static_cast<int>(units);
+    // Leave SMs to the ring's concurrent transfers, as the forward step does.
+    int grid = persistent_grid(units, env_int("CUFLASH_BWD_WAVES", 1));
+    grid = std::max(1, std::min(grid, sms - env_int("CUFLASH_CP_RESERVE_SMS", 16)));
+    kern<<<grid, kBwdThreads, G::kSmemBytes, stream>>>(mq, mk, mv, mdo, mdq, prm);
+    return cudaGetLastError() == cudaSuccess ? FlashAttentionError::SUCCESS
+                                             : FlashAttentionError::CUDA_ERROR;
+}
+
+template <typename T>
+FlashAttentionError bwd_cp_finish_typed(const void* ws, T* dQ, long long heads, int C, int D,
+                                        float scale, cudaStream_t stream) {
+    const float* acc = static_cast<const float*>(ws);
+    const long long n4 = heads * C * D / 4;
+    long long cblocks = (n4 + 255) / 256;
+    const long long cap = 32LL * current_sm_count();
+    if (cblocks > cap) cblocks = cap;
+    if (cblocks < 1) cblocks = 1;
+    bwd_convert_dq_kernel<T><<<static_cast<unsigned>(cblocks), 256, 0, stream>>>(acc, dQ, scale,
+                                                                                 n4);
+    return cudaGetLastError() == cudaSuccess ? FlashAttentionError::SUCCESS
+                                             : FlashAttentionError::CUDA_ERROR;
+}
+
+__global__ void __launch_bounds__(256)
+    accumulate_f32_kernel(float* __restrict__ dst, float* __restrict__ src, long long n4,
+                          int zero_src) {
+    const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;
+    for (long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; i < n4;
+         i += stride) {
+        float4 a = reinterpret_cast<const float4*>(dst)[i];
+        const float4 b = reinterpret_cast<const float4*>(src)[i];
+        a.x += b.x;
+        a.y += b.y;
+        a.z += b.z;
+        a.w += b.w;
+        reinterpret_cast<float4*>(dst)[i] = a;
+        if (zero_src) reinterpret_cast<float4*>(src)[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+}
+
 }  // namespace
+
+long long bwd_cp_workspace_bytes(int nq, int BH, int C, int D) {
+    const long long heads = static_cast<long long>(nq) * BH;
+    return (heads * C * D + 2 * heads * cp_bwd_pad(C)) * static_cast<long long>(sizeof(float));
+}
+
+template <typename T>
+FlashAttentionError launch_bwd_cp_prepare_sm100(const T* O, const T* dO, const float* L, void* ws,
+                                                int nq, int BH, int C, int D,
+                                                cudaStream_t stream) {
+    const long long heads = static_cast<long long>(nq) * BH;
+    switch (D) {
+        case 32: return bwd_cp_prepare_typed<T, 32>(O, dO, L, ws, heads, C, stream);
+        case 64: return bwd_cp_prepare_typed<T, 64>(O, dO, L, ws, heads, C, stream);
+        case 128: return bwd_cp_prepare_typed<T, 128>(O, dO, L, ws, heads, C, stream);
+        default: return FlashAttentionError::UNSUPPORTED_HEAD_DIM;
+    }
+}
+
+template <typename T>
+FlashAttentionError launch_bwd_cp_step_sm100(const T* Q, const T* dO, const T* K, const T* V,
+                                             void* ws, float* dk_acc, float* dv_acc, int nq,
+                                             int nk, int BH, int C, int D, float scale,
+                                             bool causal, int num_pairs, const int* q_slot,
+                                             const int* kv_slot, const long long* q_off,
+                                             const long long* kv_off, cudaStream_t stream) {
+#define CUFLASH_CP_STEP(DD)                                                                    \
+    return bwd_cp_step_typed<T, DD>(Q, dO, K, V, ws, dk_acc, dv_acc, nq, nk, BH, C, scale,    \
+                                    causal, num_pairs, q_slot, kv_slot, q_off, kv_off, stream)
+    switch (D) {
+        case 32: CUFLASH_CP_STEP(32);
+        case 64: CUFLASH_CP_STEP(64);
+        case 128: CUFLASH_CP_STEP(128);
+        default: return FlashAttentionError::UNSUPPORTED_HEAD_DIM;
+    }
+#undef CUFLASH_CP_STEP
+}
+
+template <typename T>
+FlashAttentionError launch_bwd_cp_finish_sm100(const void* ws, T* dQ, int nq, int BH, int C, int D,
+                                               float scale, cudaStream_t stream) {
+    return bwd_cp_finish_typed<T>(ws, dQ, static_cast<long long>(nq) * BH, C, D, scale, stream);
+}
+
+FlashAttentionError launch_accumulate_f32(float* dst, float* src, long long count, bool zero_src,
+                                          cudaStream_t stream) {
+    const long long n4 = count / 4;
+    long long blocks = (n4 + 255) / 256;
+    const long long cap = 8LL * current_sm_count();
+    if (blocks > cap) blocks = cap;
+    if (blocks < 1) blocks = 1;
+    accumulate_f32_kernel<<<static_cast<unsigned>(blocks), 256, 0, stream>>>(dst, src, n4,
+                                                                             zero_src ? 1 : 0);
+    return cudaGetLastError() == cudaSuccess ? FlashAttentionError::SUCCESS
+                                             : FlashAttentionError::CUDA_ERROR;
+}
+
+#define CUFLASH_CP_INST(T)                                                                      \
+    template FlashAttentionError launch_bwd_cp_prepare_sm100<T>(                                \
+        const T*, const T*, const float*, void*, int, int, int, int, cudaStream_t);             \
+    template FlashAttentionError launch_bwd_cp_step_sm100<T>(                                   \
+        const T*, const T*, const T*, const T*, void*, float*, float*, int, int, int, int, int, \
+        float, bool, int, const int*, const int*, const long long*, const long long*,           \
+        cudaStream_t);                                                                          \
+    template FlashAttentionError launch_bwd_cp_finish_sm100<T>(const void*, T*, int, int, int, \
+                                                               int, float, cudaStream_t);
+CUFLASH_CP_INST(half)
+CUFLASH_CP_INST(__nv_bfloat16)
+#undef CUFLASH_CP_INST
 
 template <typename T>
 FlashAttentionError launch_bwd_sm100(const T* Q, const T* K, const T* V, const T* O,

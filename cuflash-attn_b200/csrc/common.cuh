@@ -124,6 +124,31 @@ FlashAttentionError launch_fwd_cp_step_sm100(const T* Q, const T* K, const T* V,
                                              const long long* q_off, const long long* k_off,
                                              cudaStream_t stream);
 
+// Context-parallel backward.  The workspace (bwd_cp_workspace_bytes) holds
+// the fp32 dQ accumulator and the per-query -L*log2(e) / -rowsum(dO*O) of nq
+// query slots; prepare fills it, each ring step adds its dQ into it and its
+// dK (scaled) / dV into fp32 accumulators [nk][BH][C][D], finish writes
+// dQ = scale * dQ_acc.
+long long bwd_cp_workspace_bytes(int nq, int BH, int C, int D);
+template <typename T>
+FlashAttentionError launch_bwd_cp_prepare_sm100(const T* O, const T* dO, const float* L, void* ws,
+                                                int nq, int BH, int C, int D,
+                                                cudaStream_t stream);
+template <typename T>
+FlashAttentionError launch_bwd_cp_step_sm100(const T* Q, const T* dO, const T* K, const T* V,
+                                             void* ws, float* dk_acc, float* dv_acc, int nq,
+                                             int nk, int BH, int C, int D, float scale,
+                                             bool causal, int num_pairs, const int* q_slot,
+                                             const int* kv_slot, const long long* q_off,
+                                             const long long* kv_off, cudaStream_t stream);
+template <typename T>
+FlashAttentionError launch_bwd_cp_finish_sm100(const void* ws, T* dQ, int nq, int BH, int C, int D,
+                                               float scale, cudaStream_t stream);
+// dst += src over count floats (count a multiple of 4, both 16-byte aligned);
+// zero_src also clears src.
+FlashAttentionError launch_accumulate_f32(float* dst, float* src, long long count, bool zero_src,
+                                          cudaStream_t stream);
+
 template <typename T>
 FlashAttentionError launch_bwd_sm100(const T* Q, const T* K, const T* V, const T* O,
                                      const float* L, const T* dO, T* dQ, T* dK, T* dV, int B,

@@ -65,12 +65,21 @@ SIGNATURES = {
     "cuflash_attention_backward_gqa_f16": [_P] * 9 + [_I] * 6 + [_F, _B, _P],
     "cuflash_attention_forward_cp_step_bf16": [_P] * 5 + [_I] * 6 + [_F, _B, _I] + [_P] * 5,
     "cuflash_attention_forward_cp_step_f16": [_P] * 5 + [_I] * 6 + [_F, _B, _I] + [_P] * 5,
+    "cuflash_attention_backward_cp_workspace_size": [_I] * 5,
+    "cuflash_attention_backward_cp_prepare_bf16": [_P] * 4 + [_I] * 5 + [_P],
+    "cuflash_attention_backward_cp_prepare_f16": [_P] * 4 + [_I] * 5 + [_P],
+    "cuflash_attention_backward_cp_step_bf16": [_P] * 7 + [_I] * 6 + [_F, _B, _I] + [_P] * 5,
+    "cuflash_attention_backward_cp_step_f16": [_P] * 7 + [_I] * 6 + [_F, _B, _I] + [_P] * 5,
+    "cuflash_attention_backward_cp_finish_bf16": [_P] * 2 + [_I] * 5 + [_F, _P],
+    "cuflash_attention_backward_cp_finish_f16": [_P] * 2 + [_I] * 5 + [_F, _P],
+    "cuflash_accumulate_f32": [_P, _P, _LL, _B, _P],
     "cuflash_lse_merge_f32": [_P] * 4 + [_LL, _I, _P],
     "cuflash_convert_f32_to_bf16": [_P, _P, _LL, _P],
     "cuflash_convert_f32_to_f16": [_P, _P, _LL, _P],
     "cuflash_device_status": [],
 }
-_RESTYPES = {"cuflash_error_string": ctypes.c_char_p}
+_RESTYPES = {"cuflash_error_string": ctypes.c_char_p,
+             "cuflash_attention_backward_cp_workspace_size": ctypes.c_longlong}
 
 
 def library_path(lib_path: Optional[str] = None) -> str:
@@ -316,6 +325,66 @@ class CuFlashAttn:
                             D, float(scale), bool(causal), n, ctypes.cast(qs, _P),
                             ctypes.cast(ks, _P), ctypes.cast(qo, _P), ctypes.cast(ko, _P),
                             _stream_handle(stream)))
+
+    @staticmethod
+    def _pair_arrays(pairs):
+        n = len(pairs)
+        qs = (ctypes.c_int * max(n, 1))(*[int(x[0]) for x in pairs])
+        ks = (ctypes.c_int * max(n, 1))(*[int(x[1]) for x in pairs])
+        qo = (ctypes.c_longlong * max(n, 1))(*[int(x[2]) for x in pairs])
+        ko = (ctypes.c_longlong * max(n, 1))(*[int(x[3]) for x in pairs])
+        return n, qs, ks, qo, ko
+
+    def backward_cp_workspace(self, Q):
+        """A byte workspace for the context-parallel backward of the stacked
+        query slots Q [nq,B,H,C,D] (kept across the ring steps)."""
+        import torch
+
+        nq, B, H, C, D = Q.shape
+        nbytes = int(self.lib.cuflash_attention_backward_cp_workspace_size(nq, B, H, C, D))
+        if nbytes <= 0:
+            raise CuFlashError(INVALID_DIMENSION, self.error_string(INVALID_DIMENSION))
+        return torch.empty(nbytes, dtype=torch.uint8, device=Q.device)
+
+    def backward_cp_prepare(self, O, dO, L, workspace, stream=None) -> None:
+        """O, dO [nq,B,H,C,D] (the forward's final output), L fp32 [nq,B,H,C]."""
+        nq, B, H, C, D = O.shape
+        fn = getattr(self.lib, f"cuflash_attention_backward_cp_prepare_{_suffix(O)}")
+        self.check_error(fn(_ptr(O), _ptr(dO), _ptr(L), _ptr(workspace), nq, B, H, C, D,
+                            _stream_handle(stream)))
+
+    def backward_cp_step(self, Q, dO, K, V, workspace, dK_acc, dV_acc, pairs,
+                         causal: bool = True, scale: Optional[float] = None,
+                         stream=None) -> None:
+        """One ring step of the context-parallel backward in one launch: Q, dO
+        [nq,B,H,C,D], K, V [nk,B,H,C,D]; scale*dK and dV of the step are added
+        into dK_acc / dV_acc fp32 [nk,B,H,C,D], dQ into the workspace.
+        `pairs` lists up to four (q_slot, kv_slot, q_offset, kv_offset)."""
+        nq, B, H, C, D = Q.shape
+        nk = K.shape[0]
+        if scale is None:
+            scale = 1.0 / math.sqrt(D)
+        n, qs, ks, qo, ko = self._pair_arrays(pairs)
+        fn = getattr(self.lib, f"cuflash_attention_backward_cp_step_{_suffix(Q)}")
+        self.check_error(fn(_ptr(Q), _ptr(dO), _ptr(K), _ptr(V), _ptr(workspace), _ptr(dK_acc),
+                            _ptr(dV_acc), nq, nk, B, H, C, D, float(scale), bool(causal), n,
+                            ctypes.cast(qs, _P), ctypes.cast(ks, _P), ctypes.cast(qo, _P),
+                            ctypes.cast(ko, _P), _stream_handle(stream)))
+
+    def backward_cp_finish(self, workspace, dQ, scale: Optional[float] = None,
+                           stream=None) -> None:
+        """dQ [nq,B,H,C,D] = scale * the accumulated dQ."""
+        nq, B, H, C, D = dQ.shape
+        if scale is None:
+            scale = 1.0 / math.sqrt(D)
+        fn = getattr(self.lib, f"cuflash_attention_backward_cp_finish_{_suffix(dQ)}")
+        self.check_error(fn(_ptr(workspace), _ptr(dQ), nq, B, H, C, D, float(scale),
+                            _stream_handle(stream)))
+
+    def accumulate(self, dst, src, zero_src: bool = False, stream=None) -> None:
+        """dst += src (fp32, same size); zero_src also clears src."""
+        self.check_error(self.lib.cuflash_accumulate_f32(_ptr(dst), _ptr(src), dst.numel(),
+                                                         bool(zero_src), _stream_handle(stream)))
 
     def lse_merge(self, O_acc, L_acc, O_part, L_part, stream=None) -> None:
         rows = L_acc.numel()

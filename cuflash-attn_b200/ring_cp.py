@@ -18,6 +18,16 @@ On the CUDA path all visible pairs of one step run through
 pairs with distinct query chunks (``distinct_q_groups``), with the
 log-sum-exp merge done in the kernel's epilogue.
 
+The backward (``RingAttention.backward``) walks the same ring.  dQ of the
+rank's query chunks accumulates locally in fp32; the dK/dV contributions of
+the K/V chunks held at step s belong to rank (r - s) and travel the ring in
+fp32 with them: the step's kernel (``cuflash_attention_backward_cp_step_*``,
+all of the step's pairs in one launch) adds them into a zeroed part buffer,
+and a side stream adds that part into the accumulator received from rank
+r - 1 (``cuflash_accumulate_f32``) and sends the sum to rank r + 1, while the
+next step computes.  After the last step one more hop brings every
+accumulator home (``dkv_hops``).
+
 The schedule (``ring_steps`` / ``visible_pairs`` / ``distinct_q_groups``) is
 backend-independent and is exercised on CPU with gloo in the tests.
 """
@@ -96,6 +106,35 @@ def run_ring(rank: int, world: int, chunk: int, kv_local, compute_pair: Callable
         if pending is not None:
             cur = pending()
     return q_chunks
+
+
+def dkv_hops(rank: int, world: int) -> List[int]:
+    """Owners of the dK/dV accumulators rank `rank` sends after each step
+    (step s: the owner of the K/V it held, (rank - s) mod world); the
+    accumulator sent after the last step arrives at its owner."""
+    return [kv_owner(rank, s, world) for s in range(world)]
+
+
+def run_ring_backward(rank: int, world: int, kv_local, compute_step: Callable,
+                      exchange: Callable, new_acc: Callable, add: Callable):
+    """Host-side schedule of the ring backward, independent of the backend.
+    `compute_step(step, kv, acc)` adds the step's dK/dV contributions of the
+    K/V chunks `kv` into `acc`; `exchange(payload)` sends to rank+1 and
+    returns a callable yielding rank-1's payload; `new_acc()` makes a zero
+    accumulator and `add(dst, src)` sums two.  Returns this rank's own final
+    dK/dV accumulator."""
+    cur = kv_local
+    acc_in = None
+    for st in ring_steps(rank, world):
+        pending = exchange(cur) if st.step + 1 < world else None
+        part = new_acc()
+        compute_step(st, cur, part)
+        if acc_in is not None:
+            part = add(acc_in(), part)
+        acc_in = exchange(part) if world > 1 else (lambda p=part: p)
+        if pending is not None:
+            cur = pending()
+    return acc_in()
 
 
 # ---------------------------------------------------------------------------
@@ -177,3 +216,110 @@ class RingAttention:
             self.lib.convert(O_acc[qi], o, stream=stream)
             out.append(o)
         return out, [L_acc[0], L_acc[1]]
+
+    def backward(self, q_ab, k_ab, v_ab, o_ab, l_ab, do_ab, scale: float):
+        """Ring backward of ``forward``: the same zigzag shard plus the
+        forward's outputs o_ab (two chunks), their log-sum-exp l_ab (fp32
+        [B, H, C] each) and the output gradients do_ab.  Returns
+        (dq_ab, dk_ab, dv_ab), two chunks each, in the input dtype."""
+        import torch
+        import torch.distributed as dist
+
+        world = dist.get_world_size(self.group) if dist.is_initialized() else 1
+        rank = dist.get_rank(self.group) if dist.is_initialized() else 0
+        Qa = q_ab[0]
+        B, H, C, D = Qa.shape
+        dev = Qa.device
+        lib = self.lib
+        stream = torch.cuda.current_stream(dev)
+        Qs = torch.stack(list(q_ab)).contiguous()
+        dOs = torch.stack(list(do_ab)).contiguous()
+        Os = torch.stack(list(o_ab)).contiguous()
+        Ls = torch.stack([x.float() for x in l_ab]).contiguous()
+        ws = lib.backward_cp_workspace(Qs)
+        lib.backward_cp_prepare(Os, dOs, Ls, ws, stream=stream)
+        kv = torch.stack([torch.stack(list(k_ab)), torch.stack(list(v_ab))]).contiguous()
+        spare = torch.empty_like(kv)
+        q_chunks = zigzag_chunks(rank, world)
+        shape = (2, 2, B, H, C, D)  # (dK, dV) x (K/V slot)
+        # Accumulators travelling the ring (one being sent, one receiving) and
+        # the steps' part buffers (one written by the step kernel, one being
+        # added on the side stream); the step kernel and the adds clear them.
+        accs = [torch.zeros(shape, device=dev, dtype=torch.float32) for _ in range(2)]
+        parts = ([torch.zeros(shape, device=dev, dtype=torch.float32) for _ in range(2)]
+                 if world > 1 else [])
+        side = torch.cuda.Stream(dev) if world > 1 else None
+        part_free = [None, None]  # side-stream event: part buffer cleared
+        state = {"spare": spare}
+
+        def exchange_kv(cur):
+            nxt = state["spare"]
+            ops = [dist.P2POp(dist.isend, cur, (rank + 1) % world, self.group),
+                   dist.P2POp(dist.irecv, nxt, (rank - 1) % world, self.group)]
+            reqs = dist.batch_isend_irecv(ops)
+
+            def wait():
+                for r in reqs:
+                    r.wait()
+                state["spare"] = cur
+                return nxt
+
+            return wait
+
+        saved = os.environ.get("CUFLASH_CP_RESERVE_SMS")
+        if world == 1:
+            os.environ["CUFLASH_CP_RESERVE_SMS"] = "0"
+        cur = kv
+        acc_reqs = None  # requests of the previous accumulator exchange
+        acc_cur = 0      # index of the accumulator this rank adds into next
+        try:
+            for st in ring_steps(rank, world):
+                pending = exchange_kv(cur) if st.step + 1 < world else None
+                pairs = [(qi, ki, q_chunks[qi] * C, st.k_chunks[ki] * C) for qi, ki in st.pairs]
+                if st.step == 0:
+                    target = accs[0]
+                else:
+                    target = parts[st.step % 2]
+                    ev = part_free[st.step % 2]
+                    if ev is not None:
+                        stream.wait_event(ev)
+                if pairs:
+                    lib.backward_cp_step(Qs, dOs, cur[0], cur[1], ws, target[0], target[1],
+                                         pairs, causal=True, scale=scale, stream=stream)
+                if world > 1:
+                    done = torch.cuda.Event()
+                    done.record(stream)
+                    with torch.cuda.stream(side):
+                        side.wait_event(done)
+                        if st.step > 0:
+                            for r in acc_reqs:
+                                r.wait()  # the accumulator of this owner has arrived
+                            lib.accumulate(accs[acc_cur], target, zero_src=True, stream=side)
+                            freed = torch.cuda.Event()
+                            freed.record(side)
+                            part_free[st.step % 2] = freed
+                        send, recv = accs[acc_cur], accs[1 - acc_cur]
+                        ops = [dist.P2POp(dist.isend, send, (rank + 1) % world, self.group),
+                               dist.P2POp(dist.irecv, recv, (rank - 1) % world, self.group)]
+                        acc_reqs = dist.batch_isend_irecv(ops)
+                        acc_cur = 1 - acc_cur
+                if pending is not None:
+                    cur = pending()
+            if world > 1:
+                for r in acc_reqs:
+                    r.wait()  # on the compute stream: this rank's own accumulator
+                stream.wait_stream(side)
+        finally:
+            if world == 1:
+                if saved is None:
+                    os.environ.pop("CUFLASH_CP_RESERVE_SMS", None)
+                else:
+                    os.environ["CUFLASH_CP_RESERVE_SMS"] = saved
+        final = accs[acc_cur] if world > 1 else accs[0]
+        dQs = torch.empty_like(Qs)
+        lib.backward_cp_finish(ws, dQs, scale=scale, stream=stream)
+        dk = torch.empty((2, B, H, C, D), device=dev, dtype=Qa.dtype)
+        dv = torch.empty_like(dk)
+        lib.convert(final[0], dk, stream=stream)
+        lib.convert(final[1], dv, stream=stream)
+        return [dQs[0], dQs[1]], [dk[0], dk[1]], [dv[0], dv[1]]

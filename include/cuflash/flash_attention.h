@@ -289,6 +289,62 @@ CUFLASH_EXPORT int cuflash_attention_forward_cp_step_f16(
     bool causal, int num_pairs, const int* q_slot, const int* kv_slot,
     const long long* q_offset, const long long* kv_offset, cudaStream_t stream);
 
+// Context-parallel backward, the ring counterpart of the step above (no
+// reference counterpart).  Per query slot q the caller holds the forward's
+// final O and L (natural-log LSE) and dO, stacked [slot][B][H][C][D] like Q.
+//   workspace_size  bytes of the workspace kept across the steps (0 for
+//                   invalid arguments);
+//   prepare         fills it from O, dO, L: -L*log2(e), -rowsum(dO*O) and a
+//                   zeroed fp32 dQ accumulator;
+//   step            for each of num_pairs (1..4) pairs i, the backward of query
+//                   slot q_slot[i] against K/V slot kv_slot[i] (global offsets
+//                   as in the forward step): dQ of the query slot is added into
+//                   the workspace, scale*dK and dV of the K/V slot are ADDED
+//                   into dK_acc / dV_acc, fp32 [kv slot][B][H][C][D].  Pairs
+//                   may share query or K/V slots;
+//   finish          writes dQ = scale * (accumulated dQ) for all query slots.
+// The slot-index and offset arrays are host memory.  dK_acc / dV_acc travel
+// the ring with the K/V they belong to; the final dK / dV are their values
+// converted to 16 bits (cuflash_convert_f32_to_*).
+CUFLASH_EXPORT long long cuflash_attention_backward_cp_workspace_size(int num_q_slots,
+                                                                      int batch_size,
+                                                                      int num_heads,
+                                                                      int chunk_len,
+                                                                      int head_dim);
+CUFLASH_EXPORT int cuflash_attention_backward_cp_prepare_bf16(
+    const __nv_bfloat16* O, const __nv_bfloat16* dO, const float* L, void* workspace,
+    int num_q_slots, int batch_size, int num_heads, int chunk_len, int head_dim,
+    cudaStream_t stream);
+CUFLASH_EXPORT int cuflash_attention_backward_cp_prepare_f16(
+    const half* O, const half* dO, const float* L, void* workspace, int num_q_slots,
+    int batch_size, int num_heads, int chunk_len, int head_dim, cudaStream_t stream);
+CUFLASH_EXPORT int cuflash_attention_backward_cp_step_bf16(
+    const __nv_bfloat16* Q, const __nv_bfloat16* dO, const __nv_bfloat16* K,
+    const __nv_bfloat16* V, void* workspace, float* dK_acc, float* dV_acc, int num_q_slots,
+    int num_kv_slots, int batch_size, int num_heads, int chunk_len, int head_dim, float scale,
+    bool causal, int num_pairs, const int* q_slot, const int* kv_slot,
+    const long long* q_offset, const long long* kv_offset, cudaStream_t stream);
+CUFLASH_EXPORT int cuflash_attention_backward_cp_step_f16(
+    const half* Q, const half* dO, const half* K, const half* V, void* workspace, float* dK_acc,
+    float* dV_acc, int num_q_slots, int num_kv_slots, int batch_size, int num_heads,
+    int chunk_len, int head_dim, float scale, bool causal, int num_pairs, const int* q_slot,
+    const int* kv_slot, const long long* q_offset, const long long* kv_offset,
+    cudaStream_t stream);
+CUFLASH_EXPORT int cuflash_attention_backward_cp_finish_bf16(const void* workspace,
+                                                             __nv_bfloat16* dQ, int num_q_slots,
+                                                             int batch_size, int num_heads,
+                                                             int chunk_len, int head_dim,
+                                                             float scale, cudaStream_t stream);
+CUFLASH_EXPORT int cuflash_attention_backward_cp_finish_f16(const void* workspace, half* dQ,
+                                                            int num_q_slots, int batch_size,
+                                                            int num_heads, int chunk_len,
+                                                            int head_dim, float scale,
+                                                            cudaStream_t stream);
+// dst += src over count fp32 values (count a multiple of 4, both pointers
+// 16-byte aligned); with zero_src, src is cleared as it is read.
+CUFLASH_EXPORT int cuflash_accumulate_f32(float* dst, float* src, long long count, bool zero_src,
+                                          cudaStream_t stream);
+
 // Log-sum-exp merge of a partial result into a running one, row by row:
 //   L = log(exp(L_acc) + exp(L_part));
 //   O_acc = exp(L_acc - L) * O_acc + exp(L_part - L) * O_part;  L_acc = L.

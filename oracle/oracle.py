@@ -176,6 +176,35 @@ def backward_gen_f64(Q, K, V, dO, scale, causal, q_offset=0, k_offset=0, units=N
     return dQ, dK, dV
 
 
+def backward_pair_f64(Q, K, V, dO, L, Dv, scale, causal, q_offset=0, k_offset=0):
+    """Contribution of one (query chunk, key chunk) pair to dQ, dK, dV, given
+    the statistics of the whole softmax row: L the natural-log LSE over every
+    key of the sequence, Dv = rowsum(dO * O) with the final output O.  Same
+    per-element algebra as the reference's CPU backward
+    (tests/unit/test_backward.cu:21-127: P = softmax row, dP = dO V^T,
+    dS = P (dP - D), dQ = scale dS K, dK = scale dS^T Q, dV = P^T dO), with P
+    taken as exp(scale q.k - L) so that the pairs of a sequence sum to the
+    full backward.  Causal on global positions (key k_offset+j hidden from
+    query q_offset+i iff k_offset+j > q_offset+i).  numpy fp64, [B,H,N,D]."""
+    Q, K, V, dO = (np.asarray(x, np.float64) for x in (Q, K, V, dO))
+    L = np.asarray(L, np.float64)
+    Dv = np.asarray(Dv, np.float64)
+    Nq, Nk = Q.shape[2], K.shape[2]
+    S = scale * np.einsum("bhid,bhjd->bhij", Q, K)
+    fin = np.isfinite(L)[..., None]
+    P = np.where(fin, np.exp(S - np.where(fin, L[..., None], 0.0)), 0.0)
+    if causal:
+        qpos = q_offset + np.arange(Nq)[:, None]
+        kpos = k_offset + np.arange(Nk)[None, :]
+        P = np.where(kpos > qpos, 0.0, P)
+    dV = np.einsum("bhij,bhid->bhjd", P, dO)
+    dP = np.einsum("bhid,bhjd->bhij", dO, V)
+    dS = P * (dP - Dv[..., None])
+    dQ = scale * np.einsum("bhij,bhjd->bhid", dS, K)
+    dK = scale * np.einsum("bhij,bhid->bhjd", dS, Q)
+    return dQ, dK, dV
+
+
 def gqa_forward_f64(Q, K, V, scale, causal):
     """Grouped-query forward: Q [B,Hq,Nq,D], K/V [B,Hkv,Nk,D], query head h
     reads K/V head h // (Hq/Hkv); causal is bottom-right aligned (query i sees

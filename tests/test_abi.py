@@ -242,6 +242,59 @@ def test_cp_step_validation(lib, sfx):
     assert call(nq=0) == 1
 
 
+@pytest.mark.parametrize("sfx", ["f16", "bf16"])
+def test_cp_backward_validation(lib, sfx):
+    import ctypes
+
+    L = lib.lib
+    assert L.cuflash_attention_backward_cp_workspace_size(2, 1, 2, 200, 64) == 4 * (
+        2 * 2 * 200 * 64 + 2 * 2 * 2 * 256)
+    assert L.cuflash_attention_backward_cp_workspace_size(2, 1, 2, 200, 80) == 0
+    assert L.cuflash_attention_backward_cp_workspace_size(0, 1, 2, 200, 64) == 0
+
+    prep = getattr(L, f"cuflash_attention_backward_cp_prepare_{sfx}")
+    assert prep(NUL, FAKE, FAKE, FAKE, 2, 1, 2, 64, 64, STREAM) == 3
+    assert prep(FAKE, FAKE, FAKE, NUL, 2, 1, 2, 64, 64, STREAM) == 3
+    assert prep(FAKE, FAKE, FAKE, FAKE, 2, 1, 2, 64, 48, STREAM) == 6
+    assert prep(FAKE, FAKE, FAKE, FAKE, 2, 0, 2, 64, 64, STREAM) == 1
+
+    fin = getattr(L, f"cuflash_attention_backward_cp_finish_{sfx}")
+    assert fin(NUL, FAKE, 2, 1, 2, 64, 64, 0.1, STREAM) == 3
+    assert fin(FAKE, FAKE, 2, 1, 2, 64, 64, float("nan"), STREAM) == 1
+    assert fin(FAKE, FAKE, 2, 1, 2, -1, 64, 0.1, STREAM) == 1
+
+    fn = getattr(L, f"cuflash_attention_backward_cp_step_{sfx}")
+
+    def arr(ct, vals):
+        return ctypes.cast((ct * len(vals))(*vals), ctypes.c_void_p)
+
+    def call(q=(0, 1), k=(0, 0), qo=(0, 64), ko=(0, 0), n=2, D=64, nq=2, nk=2, ptr=None,
+             scale=0.1):
+        args = [FAKE] * 7 + [nq, nk, 1, 2, 64, D, scale, True, n, arr(ctypes.c_int, q),
+                             arr(ctypes.c_int, k), arr(ctypes.c_longlong, qo),
+                             arr(ctypes.c_longlong, ko), STREAM]
+        if ptr is not None:
+            args[ptr] = NUL
+        return fn(*args)
+
+    assert call(ptr=0) == 3                       # Q null
+    assert call(ptr=4) == 3                       # workspace null
+    assert call(ptr=6) == 3                       # dV_acc null
+    assert call(ptr=18) == 3                      # kv_slot array null
+    assert call(D=96) == 6
+    assert call(n=0) == 1 and call(n=5) == 1      # 1..4 pairs
+    assert call(q=(0, 2)) == 1                    # query slot out of range
+    assert call(k=(0, 2)) == 1                    # K/V slot out of range
+    assert call(ko=(0, -1)) == 1                  # negative global offset
+    assert call(nk=0) == 1
+    assert call(scale=-1.0) == 1
+
+    acc = L.cuflash_accumulate_f32
+    assert acc(NUL, FAKE, 16, False, STREAM) == 3
+    assert acc(FAKE, FAKE, 6, False, STREAM) == 1              # count a multiple of 4
+    assert acc(ctypes.c_void_p(0x1004), FAKE, 16, False, STREAM) == 1  # 16-byte alignment
+
+
 def test_oracle_is_test_infrastructure_only():
     """The product path must not import the oracle."""
     pkg = ROOT / "cuflash-attn_b200"

@@ -1,7 +1,7 @@
 """Ring context parallelism on CPU: the schedule and the multi-process ring
 (world_size 2 and 3, gloo) with the fp64 oracle standing in for the GPU
-partial-attention kernel.  The assembled result must equal full causal
-attention over the whole sequence."""
+partial-attention kernels, forward and backward.  The assembled result must
+equal full causal attention (and its gradients) over the whole sequence."""
 
 import os
 import socket
@@ -120,3 +120,115 @@ def test_ring_over_gloo_equals_full_causal_attention(world, tmp_path):
                                        atol=1e-10)
             np.testing.assert_allclose(res[f"L{slot}"], L_full[:, :, c * C:(c + 1) * C],
                                        atol=1e-10)
+
+
+def test_backward_pairs_sum_to_full_backward():
+    """The per-pair backward with the full-row statistics, summed over the
+    zigzag ring's pairs, is the full causal backward."""
+    B, H, D, world = 1, 2, 16, 3
+    C = 10
+    N = 2 * world * C
+    Q, K, V, dO = (oracle.uniform((B, H, N, D), s) for s in (11, 12, 13, 14))
+    scale = 1.0 / np.sqrt(D)
+    O, L = oracle.forward_f64(Q, K, V, scale, True)
+    Dv = (dO.astype(np.float64) * O).sum(-1)
+    dQ = np.zeros((B, H, N, D))
+    dK = np.zeros((B, H, N, D))
+    dV = np.zeros((B, H, N, D))
+    sl = lambda c: slice(c * C, (c + 1) * C)
+    for r in range(world):
+        qc = ring_cp.zigzag_chunks(r, world)
+        for st in ring_cp.ring_steps(r, world):
+            for qi, ki in st.pairs:
+                a, b = qc[qi], st.k_chunks[ki]
+                gq, gk, gv = oracle.backward_pair_f64(
+                    Q[:, :, sl(a)], K[:, :, sl(b)], V[:, :, sl(b)], dO[:, :, sl(a)],
+                    L[:, :, sl(a)], Dv[:, :, sl(a)], scale, True, a * C, b * C)
+                dQ[:, :, sl(a)] += gq
+                dK[:, :, sl(b)] += gk
+                dV[:, :, sl(b)] += gv
+    rQ, rK, rV = oracle.backward_f64(Q, K, V, dO, scale, True)
+    for got, ref in ((dQ, rQ), (dK, rK), (dV, rV)):
+        np.testing.assert_allclose(got, ref, atol=1e-10)
+
+
+@pytest.mark.parametrize("world", [1, 2, 5])
+def test_dkv_hops_return_home(world):
+    for r in range(world):
+        hops = ring_cp.dkv_hops(r, world)
+        assert hops[0] == r                           # step 0: own K/V
+        assert (r + 1) % world == hops[-1]            # the last send reaches its owner
+    # every owner's accumulator visits every rank exactly once
+    for o in range(world):
+        visits = [r for r in range(world) for s, h in enumerate(ring_cp.dkv_hops(r, world))
+                  if h == o]
+        assert sorted(visits) == list(range(world))
+
+
+def _bwd_worker(rank, world, port, Q, K, V, dO, scale, out_path):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        B, H, N, D = Q.shape
+        C = N // (2 * world)
+        chunks = ring_cp.zigzag_chunks(rank, world)
+        sl = lambda x, c: np.ascontiguousarray(x[:, :, c * C:(c + 1) * C])
+        # the forward's statistics of this rank's rows (the ring forward's output)
+        O, L = oracle.forward_f64(Q, K, V, scale, True)
+        Dv = (dO.astype(np.float64) * O).sum(-1)
+        kv = torch.from_numpy(np.stack([np.stack([sl(K, c) for c in chunks]),
+                                        np.stack([sl(V, c) for c in chunks])]))
+        dq = [np.zeros((B, H, C, D)) for _ in range(2)]
+
+        def compute_step(st, kvbuf, acc):
+            kb = kvbuf.numpy()
+            for qi, ki in st.pairs:
+                qc, kc = chunks[qi], st.k_chunks[ki]
+                gq, gk, gv = oracle.backward_pair_f64(sl(Q, qc), kb[0, ki], kb[1, ki],
+                                                      sl(dO, qc), sl(L, qc), sl(Dv, qc), scale,
+                                                      True, qc * C, kc * C)
+                dq[qi] += gq
+                acc[0, ki] += torch.from_numpy(gk)
+                acc[1, ki] += torch.from_numpy(gv)
+
+        def exchange(cur):
+            nxt = torch.empty_like(cur)
+            reqs = [dist.isend(cur, (rank + 1) % world), dist.irecv(nxt, (rank - 1) % world)]
+
+            def wait():
+                for r in reqs:
+                    r.wait()
+                return nxt
+
+            return wait
+
+        acc = ring_cp.run_ring_backward(
+            rank, world, kv, compute_step, exchange,
+            lambda: torch.zeros((2, 2, B, H, C, D), dtype=torch.float64),
+            lambda a, b: a + b)
+        a = acc.numpy()
+        np.savez(out_path + f".{rank}.npz", dQ0=dq[0], dQ1=dq[1], dK0=a[0, 0], dK1=a[0, 1],
+                 dV0=a[1, 0], dV1=a[1, 1])
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [1, 2, 3])
+def test_ring_backward_over_gloo_equals_full_backward(world, tmp_path):
+    B, H, D = 1, 2, 16
+    N = 2 * world * 8
+    Q, K, V, dO = (oracle.uniform((B, H, N, D), s) for s in (21, 22, 23, 24))
+    scale = 1.0 / np.sqrt(D)
+    out = str(tmp_path / "ringb")
+    mp.start_processes(_bwd_worker, args=(world, _free_port(), Q, K, V, dO, scale, out),
+                       nprocs=world, join=True, start_method="spawn")
+    rQ, rK, rV = oracle.backward_f64(Q, K, V, dO, scale, True)
+    C = N // (2 * world)
+    for r in range(world):
+        res = np.load(out + f".{r}.npz")
+        for slot, c in enumerate(ring_cp.zigzag_chunks(r, world)):
+            sl = slice(c * C, (c + 1) * C)
+            np.testing.assert_allclose(res[f"dQ{slot}"], rQ[:, :, sl], atol=1e-10)
+            np.testing.assert_allclose(res[f"dK{slot}"], rK[:, :, sl], atol=1e-10)
+            np.testing.assert_allclose(res[f"dV{slot}"], rV[:, :, sl], atol=1e-10)
