@@ -6,7 +6,6 @@
 
 #include <cstdlib>
 #include <mutex>
-#include <set>
 #include <utility>
 
 #include "common.cuh"
@@ -50,12 +49,22 @@ bool encode_tmap_3d(CUtensorMap* map, const void* base, CUtensorMapDataType dtyp
 }
 
 bool ensure_smem_attr(const void* kernel, int bytes) {
+    // (device, kernel, bytes) already configured; a plain table keeps the
+    // library from exporting standard-container template instances.
+    struct Entry {
+        int dev;
+        int bytes;
+        const void* kernel;
+    };
+    constexpr int kCap = 512;
     static std::mutex mu;
-    static std::set<std::pair<int, const void*>> done;
+    static Entry done[kCap];
+    static int n_done = 0;
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess) return false;
     std::lock_guard<std::mutex> lock(mu);
-    if (done.count({dev, kernel})) return true;
+    for (int i = 0; i < n_done; ++i)
+        if (done[i].dev == dev && done[i].kernel == kernel && done[i].bytes >= bytes) return true;
     int optin = 0;
     if (cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) !=
         cudaSuccess)
@@ -64,7 +73,7 @@ bool ensure_smem_attr(const void* kernel, int bytes) {
     if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes) !=
         cudaSuccess)
         return false;
-    done.insert({dev, kernel});
+    if (n_done < kCap) done[n_done++] = Entry{dev, bytes, kernel};
     return true;
 }
 
