@@ -18,19 +18,21 @@
 //   warp 0      TMA producer: Q_i, dO_i (tiled, swizzled) and the 128 values
 //               of L and D for block i (1-D bulk copies), 2-stage ring.
 //   warp 1      tcgen05.mma issuer:
-//                 dP^T = V_j dO_i^T   -> TMEM [128,256)
 //                 S^T  = K_j Q_i^T    -> TMEM [0,128)
+//                 dP^T = V_j dO_i^T   -> TMEM [128,256)
 //                 dV  += P^T dO_i     (A = P^T from TMEM)   -> TMEM [256,256+D)
 //                 dK  += dS^T Q_i     (A = dS^T from TMEM)  -> TMEM [384,384+D)
 //                 dQ_i = dS K_j (or dQ_i^T = K_j^T dS^T)    -> TMEM [128,256)
-//               in the order dV, dK, dQ_i, S^T_{i+1}, then (once the drain
-//               warps have read dQ_i) dP^T_{i+1}, so S^T_{i+1} runs while
-//               dQ_i is drained.
+//               in the order dV (as soon as P^T is stored), dK, dQ_i,
+//               S^T_{i+1}, then (once the drain warps have read dQ_i)
+//               dP^T_{i+1}, so S^T_{i+1} runs while dQ_i is drained.
 //   warps 4-11  two warpgroups, one thread per K/V row (TMEM lane) each,
-//               splitting the 128 query columns in halves: P^T, dS^T from
-//               S^T, dP^T; P^T and dS^T go back into TMEM (fp16/bf16) and dS^T
-//               also into shared memory for the dQ product; at the end one
-//               warpgroup stores dV, the other dK.
+//               splitting the 128 query columns in halves, in two phases:
+//               P^T from S^T (stored back into TMEM as fp16/bf16, kept in
+//               fp32 registers), which releases the dV product, then dS^T
+//               from dP^T and P (into TMEM, and into shared memory for the dQ
+//               product), overlapping dV; at the end one warpgroup stores
+//               dV, the other dK.
 //   warps 12-15 drain dQ_i from TMEM into the fp32 accumulator: with
 //               head_dim 128 dQ is computed transposed and drained with
 //               coalesced red.global.add.f32, otherwise through swizzled
@@ -62,6 +64,12 @@ constexpr float kLog2eB = 1.4426950408889634f;
 #define CUFLASH_BWD_EXP2_EMU_EVERY 4
 #endif
 constexpr int kBwdExp2EmuEvery = CUFLASH_BWD_EXP2_EMU_EVERY;
+// head_dim 128: dQ produced transposed and reduced with red.global.add.f32
+// from registers (1), or produced row-major and reduced by the TMA unit from
+// shared-memory boxes as for the smaller head dims (0).
+#ifndef CUFLASH_BWD_DQ_TRANSPOSED
+#define CUFLASH_BWD_DQ_TRANSPOSED 1
+#endif
 
 template <int D>
 struct BwdGeom {
@@ -81,7 +89,7 @@ struct BwdGeom {
     static constexpr int kOffStage = kOffDs + kDsBytes;
     static constexpr int kStageBytes = 2 * kTileBytes + 1024;  // Q, dO, L (512 B), D (512 B)
     static constexpr int kOffBar = kOffStage + kStages * kStageBytes;
-    static constexpr int kNumBars = 1 + 2 * kStages + 6;
+    static constexpr int kNumBars = 1 + 2 * kStages + 8;
     static constexpr int kSmemBytes = kOffBar + kNumBars * 8 + 16;
     static_assert(kStageBytes % 1024 == 0, "stage must keep 1024-byte alignment");
 };
@@ -389,41 +397,41 @@ __global__ void __launch_bounds__(256)
     }
 }
 
-// P^T and dS^T of one (kv block, query block) pair for this thread's kv row r
-// (TMEM lane), warpgroup h covering queries [64h, 64h+64).  sL / sD hold
-// -L*log2(e) and -rowsum(dO*O) of those queries.  In 16-query sub-chunks, the
-// next sub-chunk's S^T / dP^T columns load while this one is computed.  P^T /
-// dS^T of sub-chunk k go to columns [8k, 8k+8) of the warpgroup's S^T / dP^T
-// range, which hold queries already loaded (sub-chunks 0..k/2).  kDiag masks
+// The softmax of one (kv block, query block) pair for this thread's kv row r
+// (TMEM lane), warpgroup h covering queries [64h, 64h+64), in two phases so
+// that the dV product can start before dS exists:
+//   bwd_softmax_p   P^T from S^T: p = exp2(scale*log2(e) * s - L*log2(e)),
+//                   kept in fp32 registers and stored (16-bit) over S^T;
+//   bwd_softmax_ds  dS^T = P^T (dP^T - D) from dP^T and the kept P, stored
+//                   (16-bit) over dP^T and into shared memory for dQ.
+// sL / sD hold -L*log2(e) and -rowsum(dO*O) of the warpgroup's queries.  Both
+// work in 16-query sub-chunks with the next sub-chunk's columns loading while
+// one is computed; the 16-bit results of sub-chunk k go to columns [8k, 8k+8)
+// of the warpgroup's range, which hold queries already loaded.  kDiag masks
 // the keys above the causal diagonal: query q of the block against kv row r
 // is hidden iff q < r + delta, delta = 128 (j - i) - q_off.
 template <typename T, bool kDiag>
-__device__ __forceinline__ void bwd_softmax_block(uint32_t t_s, uint32_t t_dp, uint32_t sDs,
-                                                  const float* sL, const float* sD, float c,
-                                                  int h, int r, int delta) {
+__device__ __forceinline__ void bwd_softmax_p(uint32_t t_s, const float* sL, float c, int h, int r,
+                                              int delta, float (&pf)[64]) {
     using namespace sm100;
     const uint64_t c2 = f2_pack(c, c);
-    uint32_t sA[16], dA[16], sB[16], dB[16];
-    tmem_ld2_x16_nw(t_s, sA, t_dp, dA);
-    tmem_wait_ld2_x16(sA, dA);
+    uint32_t sA[16], sB[16];
+    tmem_ld_x16_nw(t_s, sA);
+    tmem_wait_ld_x16(sA);
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
         uint32_t(&sv)[16] = (k & 1) ? sB : sA;
-        uint32_t(&dv)[16] = (k & 1) ? dB : dA;
         uint32_t(&sn)[16] = (k & 1) ? sA : sB;
-        uint32_t(&dn)[16] = (k & 1) ? dA : dB;
-        if (k + 1 < 4) tmem_ld2_x16_nw(t_s + 16 * (k + 1), sn, t_dp + 16 * (k + 1), dn);
-        uint32_t pp[8], dd[8];
+        if (k + 1 < 4) tmem_ld_x16_nw(t_s + 16 * (k + 1), sn);
+        uint32_t pp[8];
 #pragma unroll
         for (int v = 0; v < 4; ++v) {
             const float4 lq = reinterpret_cast<const float4*>(sL + 16 * k)[v];
-            const float4 dq = reinterpret_cast<const float4*>(sD + 16 * k)[v];
 #pragma unroll
             for (int u = 0; u < 2; ++u) {
                 const int e = 2 * v + u;                 // pair index in the sub-chunk
                 const int q0 = h * 64 + 16 * k + 2 * e;  // query within the block
                 const uint64_t nl = u ? f2_pack(lq.z, lq.w) : f2_pack(lq.x, lq.y);
-                const uint64_t ndv = u ? f2_pack(dq.z, dq.w) : f2_pack(dq.x, dq.y);
                 const float2 xx = f2_unpack(f2_fma(
                     f2_pack(__uint_as_float(sv[2 * e]), __uint_as_float(sv[2 * e + 1])), c2, nl));
                 float p0, p1;
@@ -440,15 +448,44 @@ __device__ __forceinline__ void bwd_softmax_block(uint32_t t_s, uint32_t t_dp, u
                     if (q0 < r + delta) p0 = 0.f;
                     if (q0 + 1 < r + delta) p1 = 0.f;
                 }
-                const float2 d = f2_unpack(f2_mul(
-                    f2_pack(p0, p1),
-                    f2_add(f2_pack(__uint_as_float(dv[2 * e]), __uint_as_float(dv[2 * e + 1])), ndv)));
+                pf[16 * k + 2 * e] = p0;
+                pf[16 * k + 2 * e + 1] = p1;
                 pp[e] = DType<T>::pack2(p0, p1);
+            }
+        }
+        // P^T overwrites columns this thread has already read
+        tmem_st_x8_nw(t_s + 8 * k, pp);
+        if (k + 1 < 4) tmem_wait_ld_x16(sn);
+    }
+}
+
+template <typename T>
+__device__ __forceinline__ void bwd_softmax_ds(uint32_t t_dp, uint32_t sDs, const float* sD, int r,
+                                               const float (&pf)[64]) {
+    using namespace sm100;
+    uint32_t dA[16], dB[16];
+    tmem_ld_x16_nw(t_dp, dA);
+    tmem_wait_ld_x16(dA);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        uint32_t(&dv)[16] = (k & 1) ? dB : dA;
+        uint32_t(&dn)[16] = (k & 1) ? dA : dB;
+        if (k + 1 < 4) tmem_ld_x16_nw(t_dp + 16 * (k + 1), dn);
+        uint32_t dd[8];
+#pragma unroll
+        for (int v = 0; v < 4; ++v) {
+            const float4 dq = reinterpret_cast<const float4*>(sD + 16 * k)[v];
+#pragma unroll
+            for (int u = 0; u < 2; ++u) {
+                const int e = 2 * v + u;
+                const uint64_t ndv = u ? f2_pack(dq.z, dq.w) : f2_pack(dq.x, dq.y);
+                const float2 d = f2_unpack(f2_mul(
+                    f2_pack(pf[16 * k + 2 * e], pf[16 * k + 2 * e + 1]),
+                    f2_add(f2_pack(__uint_as_float(dv[2 * e]), __uint_as_float(dv[2 * e + 1])), ndv)));
                 dd[e] = DType<T>::pack2(d.x, d.y);
             }
         }
-        // P^T and dS^T overwrite columns this thread has already read
-        tmem_st_x8_nw(t_s + 8 * k, pp);
+        // dS^T overwrites columns this thread has already read
         tmem_st_x8_nw(t_dp + 8 * k, dd);
 #pragma unroll
         for (int q = 0; q < 2; ++q) {
@@ -456,7 +493,7 @@ __device__ __forceinline__ void bwd_softmax_block(uint32_t t_s, uint32_t t_dp, u
             st_shared_v4(sDs + ((chunk ^ (r & 7)) << 4), dd[4 * q], dd[4 * q + 1], dd[4 * q + 2],
                          dd[4 * q + 3]);
         }
-        if (k + 1 < 4) tmem_wait_ld2_x16(sn, dn);
+        if (k + 1 < 4) tmem_wait_ld_x16(dn);
     }
 }
 
@@ -475,7 +512,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     // With head_dim 128 dQ is produced transposed (TMEM lane = head_dim
     // element), so a warp's reduction into the accumulator covers 32
     // consecutive floats of one query row: fully coalesced, no staging.
-    constexpr bool kTransposedDq = (D == 128);
+    constexpr bool kTransposedDq = (D == 128) && (CUFLASH_BWD_DQ_TRANSPOSED != 0);
 
     if (*reinterpret_cast<volatile int*>(&g_bwd_status) != 0) return;
     const uint32_t sbase = smem_u32(smem_raw);
@@ -488,8 +525,10 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     uint64_t* bar_kv = bars;  // K_j, V_j of the current item landed
     uint64_t* full = bars + 1;
     uint64_t* empty = full + G::kStages;
-    uint64_t* bar_sdp = empty + G::kStages;
-    uint64_t* bar_ds = bar_sdp + 1;
+    uint64_t* bar_s = empty + G::kStages;  // S^T in TMEM
+    uint64_t* bar_dp = bar_s + 1;          // dP^T in TMEM
+    uint64_t* bar_p = bar_dp + 1;          // P^T stored (256 arrivals)
+    uint64_t* bar_ds = bar_p + 1;          // dS^T stored in TMEM and shared memory (256)
     uint64_t* bar_dq = bar_ds + 1;
     uint64_t* bar_dqfree = bar_dq + 1;
     uint64_t* bar_acc = bar_dqfree + 1;  // all MMAs of the item retired (dV, dK final; K, V free)
@@ -506,7 +545,9 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
             mbar_init(full + s, 1);
             mbar_init(empty + s, 1);
         }
-        mbar_init(bar_sdp, 1);
+        mbar_init(bar_s, 1);
+        mbar_init(bar_dp, 1);
+        mbar_init(bar_p, 256);
         mbar_init(bar_ds, 256);
         mbar_init(bar_dq, 1);
         mbar_init(bar_dqfree, 128);
@@ -653,6 +694,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
                     // S^T columns: the previous item's P^T was read by its last
                     // dV product (issued earlier, so ordered before this one)
                     issue_s(stage_q(g));
+                    tc_commit(bar_s);
                     // dP^T columns hold the previous block's dQ until drained
                     if (g > 0 && !mbar_wait(bar_dqfree, (g - 1) & 1, abort_flag, &g_bwd_status)) {
                         ok = false;
@@ -660,23 +702,32 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
                     }
                     tc_fence_after();
                     issue_dp(stage_q(g) + G::kTileBytes);
-                    tc_commit(bar_sdp);
+                    tc_commit(bar_dp);
                     for (int it = 0; ok && it < n_it; ++it, ++g) {
                         const int s = g % G::kStages;
                         const uint32_t sQ = stage_q(g);
                         const uint32_t sdO = sQ + G::kTileBytes;
-                        if (!mbar_wait(bar_ds, g & 1, abort_flag, &g_bwd_status)) {
+                        // dV += P^T dO_i as soon as P^T is stored (the softmax warps
+                        // compute dS^T meanwhile)
+                        if (!mbar_wait(bar_p, g & 1, abort_flag, &g_bwd_status)) {
                             ok = false;
                             break;
                         }
                         tc_fence_after();
-                        // dV += P^T dO_i ; dK += dS^T Q_i  (K dimension = 128 query rows)
                         {
                             const uint64_t bo = opaque(bmnmajor_desc<D>(sdO, 0));
 #pragma unroll
                             for (int kk = 0; kk < 8; ++kk)
                                 mma_f16_ts(tmem + 256, tmem + acol(kk), bo + bmn_delta<D>(kk), idesc_acc,
                                            (it > 0 || kk > 0) ? 1u : 0u);
+                        }
+                        // dK += dS^T Q_i  (K dimension = 128 query rows)
+                        if (!mbar_wait(bar_ds, g & 1, abort_flag, &g_bwd_status)) {
+                            ok = false;
+                            break;
+                        }
+                        tc_fence_after();
+                        {
                             const uint64_t bq = opaque(bmnmajor_desc<D>(sQ, 0));
 #pragma unroll
                             for (int kk = 0; kk < 8; ++kk)
@@ -714,13 +765,14 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
                             tc_fence_after();
                             // S^T columns: P^T was read by the dV product issued above
                             issue_s(sQn);
+                            tc_commit(bar_s);
                             if (!mbar_wait(bar_dqfree, g & 1, abort_flag, &g_bwd_status)) {
                                 ok = false;
                                 break;
                             }
                             tc_fence_after();
                             issue_dp(sQn + G::kTileBytes);
-                            tc_commit(bar_sdp);
+                            tc_commit(bar_dp);
                         }
                     }
                     if (!ok) break;
@@ -762,7 +814,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
                     // the stage's own barrier before reading them (it completes
                     // before S is issued, so waiting for it first costs nothing)
                     if (!bwarp_wait(full + s, (g / G::kStages) & 1, abort_flag) ||
-                        !bwarp_wait(bar_sdp, g & 1, abort_flag)) {
+                        !bwarp_wait(bar_s, g & 1, abort_flag)) {
                         ok = false;
                         break;
                     }
@@ -773,11 +825,23 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
                         h * 64;
                     const float* sD = sL + 128;
                     const long long dl = 128LL * (j - i) - rel;
+                    float pf[64];  // this row's P for the warpgroup's 64 queries
                     if (p.causal && dl > -127)
-                        bwd_softmax_block<T, true>(t_s, t_dp, sDs, sL, sD, c, h, r,
-                                                   static_cast<int>(dl));
+                        bwd_softmax_p<T, true>(t_s, sL, c, h, r, static_cast<int>(dl), pf);
                     else
-                        bwd_softmax_block<T, false>(t_s, t_dp, sDs, sL, sD, c, h, r, 0);
+                        bwd_softmax_p<T, false>(t_s, sL, c, h, r, 0, pf);
+                    tmem_wait_st();
+                    tc_fence_before();
+                    mbar_arrive(bar_p);
+                    // dP^T: issued after S^T, once the previous block's dQ left
+                    // its columns; its commit also covers that dQ product, which
+                    // read the shared-memory dS this phase overwrites
+                    if (!bwarp_wait(bar_dp, g & 1, abort_flag)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    bwd_softmax_ds<T>(t_dp, sDs, sD, r, pf);
                     tmem_wait_st();
                     fence_proxy_async_smem();
                     tc_fence_before();
