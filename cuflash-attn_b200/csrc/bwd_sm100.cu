@@ -64,11 +64,18 @@ constexpr float kLog2eB = 1.4426950408889634f;
 #define CUFLASH_BWD_EXP2_EMU_EVERY 4
 #endif
 constexpr int kBwdExp2EmuEvery = CUFLASH_BWD_EXP2_EMU_EVERY;
-// head_dim 128: dQ produced transposed and reduced with red.global.add.f32
-// from registers (1), or produced row-major and reduced by the TMA unit from
-// shared-memory boxes as for the smaller head dims (0).
-#ifndef CUFLASH_BWD_DQ_TRANSPOSED
-#define CUFLASH_BWD_DQ_TRANSPOSED 1
+// How dQ_i leaves TMEM for the fp32 accumulator:
+//   0  dQ_i^T (TMEM lane = head_dim element), one red.global.add.f32 per
+//      element from registers (head_dim 128 only: M = head_dim);
+//   1  dQ_i row-major (TMEM lane = query), staged through swizzled
+//      shared-memory boxes and added by the TMA unit;
+//   2  dQ_i row-major, red.global.add.v4.f32 from registers (four
+//      consecutive elements of a row per instruction).
+#ifndef CUFLASH_BWD_DQ_MODE_128
+#define CUFLASH_BWD_DQ_MODE_128 0
+#endif
+#ifndef CUFLASH_BWD_DQ_MODE_SMALL
+#define CUFLASH_BWD_DQ_MODE_SMALL 1
 #endif
 
 template <int D>
@@ -307,6 +314,14 @@ __device__ __forceinline__ void bulk_load(void* smem_dst, const void* gsrc, uint
 __device__ __forceinline__ void red_add_f32(float* gptr, float v) {
     asm volatile("red.global.add.f32 [%0], %1;" ::"l"(gptr), "f"(v) : "memory");
 }
+// Element-wise add of four consecutive floats (16-byte aligned address).
+__device__ __forceinline__ void red_add_v4_f32(float* gptr, uint32_t a, uint32_t b, uint32_t c,
+                                               uint32_t d) {
+    asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(gptr),
+                 "f"(__uint_as_float(a)), "f"(__uint_as_float(b)), "f"(__uint_as_float(c)),
+                 "f"(__uint_as_float(d))
+                 : "memory");
+}
 
 __device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c,
                                              uint32_t d) {
@@ -512,7 +527,9 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     // With head_dim 128 dQ is produced transposed (TMEM lane = head_dim
     // element), so a warp's reduction into the accumulator covers 32
     // consecutive floats of one query row: fully coalesced, no staging.
-    constexpr bool kTransposedDq = (D == 128) && (CUFLASH_BWD_DQ_TRANSPOSED != 0);
+    constexpr int kDqMode = (D == 128) ? CUFLASH_BWD_DQ_MODE_128
+                                       : (CUFLASH_BWD_DQ_MODE_SMALL == 0 ? 1 : CUFLASH_BWD_DQ_MODE_SMALL);
+    constexpr bool kTransposedDq = (kDqMode == 0);
 
     if (*reinterpret_cast<volatile int*>(&g_bwd_status) != 0) return;
     const uint32_t sbase = smem_u32(smem_raw);
@@ -953,6 +970,44 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
                         flush(v1, 32);
                         flush(v2, 64);
                         flush(v3, 96);
+                    }
+                } else if constexpr (kDqMode == 2) {
+                    // lane = query row of block i; TMEM columns = head_dim elements
+                    const int qr = wq * 32 + lane;
+                    for (int it = 0; it < n_it; ++it, ++g) {
+                        int bh, i;  // query head and block
+                        long long rel;
+                        bwd_step<kCp>(p, itm, wk, it, bh, i, rel);
+                        if (!bwarp_wait(bar_dq, g & 1, abort_flag)) {
+                            ok = false;
+                            break;
+                        }
+                        tc_fence_after();
+                        uint32_t v0[32], v1[32], v2[32], v3[32];
+                        if constexpr (D == 32) {
+                            tmem_ld_x32(t_q, v0);
+                        } else {
+                            tmem_ld2_x32(t_q, v0, t_q + 32, v1);
+                            if constexpr (D == 128) tmem_ld2_x32(t_q + 64, v2, t_q + 96, v3);
+                        }
+                        // TMEM columns are free once loaded
+                        tc_fence_before();
+                        mbar_arrive(bar_dqfree);
+                        if (i * 128 + qr < p.Nq) {
+                            float* dst = p.dq_acc + (static_cast<size_t>(bh) * p.Nq + i * 128 + qr) * D;
+                            auto flush = [&](const uint32_t(&v)[32], int c0) {
+#pragma unroll
+                                for (int m = 0; m < 8; ++m)
+                                    red_add_v4_f32(dst + c0 + 4 * m, v[4 * m], v[4 * m + 1], v[4 * m + 2],
+                                                   v[4 * m + 3]);
+                            };
+                            flush(v0, 0);
+                            if constexpr (D >= 64) flush(v1, 32);
+                            if constexpr (D == 128) {
+                                flush(v2, 64);
+                                flush(v3, 96);
+                            }
+                        }
                     }
                 } else {
                     // Each warp owns 32 query rows.  Per 32-column chunk it copies
