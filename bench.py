@@ -22,7 +22,6 @@ import json
 import math
 import os
 import statistics
-import subprocess
 import sys
 import time
 from pathlib import Path
@@ -58,64 +57,79 @@ def dist_env():
 
 
 class Clocks:
-    """Samples SM clocks / throttle reasons of one GPU during the timed region."""
+    """Samples SM clock, power and clock-event reasons of one GPU every 10 ms
+    during the timed region, through NVML (read-only queries) in a background
+    thread; without NVML the summary says so instead of reporting clocks."""
 
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    REASONS = (("hw_slowdown", "nvmlClocksEventReasonHwSlowdown"),
+               ("hw_thermal_slowdown", "nvmlClocksEventReasonHwThermalSlowdown"),
+               ("sw_thermal_slowdown", "nvmlClocksEventReasonSwThermalSlowdown"),
+               ("sw_power_cap", "nvmlClocksEventReasonSwPowerCap"),
+               ("hw_power_brake", "nvmlClocksEventReasonHwPowerBrakeSlowdown"))
 
     def __init__(self, device_index):
         self.idx = device_index
-        self.proc = None
-        self.path = Path(f"/tmp/cuflash_clocks_{os.getpid()}.csv")
+        self.rows = []
+        self.err = None
+        self.thread = None
+
+    def _handle(self, nv):
+        try:
+            import torch
+
+            prop = torch.cuda.get_device_properties(self.idx)
+            bus = "%08X:%02X:%02X.0" % (prop.pci_domain_id, prop.pci_bus_id, prop.pci_device_id)
+            return nv.nvmlDeviceGetHandleByPciBusId(bus)
+        except Exception:
+            return nv.nvmlDeviceGetHandleByIndex(self.idx)
 
     def __enter__(self):
+        import threading
+
         try:
-            self.fh = open(self.path, "w")
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-lms", "25", "-i", str(self.idx)], stdout=self.fh, stderr=subprocess.DEVNULL)
-        except OSError:
-            self.proc = None
+            import pynvml as nv
+
+            nv.nvmlInit()
+            h = self._handle(nv)
+            self.max_mhz = nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM)
+            masks = [(name, getattr(nv, const, 0)) for name, const in self.REASONS]
+        except Exception as e:  # no NVML: report that instead of clocks
+            self.err = f"nvml unavailable: {type(e).__name__}"
             return self
-        # the timed region starts once the sampler is producing rows (its
-        # start-up takes longer than a short timed region)
+        self.stop = threading.Event()
+
+        def run():
+            while not self.stop.is_set():
+                try:
+                    mhz = nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)
+                    mw = nv.nvmlDeviceGetPowerUsage(h)
+                    bits = nv.nvmlDeviceGetCurrentClocksEventReasons(h)
+                    self.rows.append((mhz, mw / 1000.0, [n for n, m in masks if m and bits & m]))
+                except Exception as e:
+                    self.err = f"nvml query failed: {type(e).__name__}"
+                    return
+                self.stop.wait(0.01)
+
+        self.thread = threading.Thread(target=run, daemon=True)
+        self.thread.start()
         t0 = time.time()
-        while time.time() - t0 < 5.0 and self.proc.poll() is None:
-            if self.path.stat().st_size > 0:
-                break
-            time.sleep(0.01)
-        self.t_start = time.time()
+        while not self.rows and self.err is None and time.time() - t0 < 2.0:
+            time.sleep(0.002)
         return self
 
     def __exit__(self, *exc):
-        if self.proc is not None:
-            self.proc.terminate()
-            try:
-                self.proc.wait(timeout=5)
-            except subprocess.TimeoutExpired:
-                self.proc.kill()
-            self.fh.close()
+        if self.thread is not None:
+            self.stop.set()
+            self.thread.join(timeout=2)
 
     def summary(self):
-        if self.proc is None or not self.path.exists():
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
-        rows = []
-        for ln in self.path.read_text().splitlines():
-            parts = [x.strip() for x in ln.split(",")]
-            if len(parts) < 9:
-                continue
-            try:
-                rows.append((float(parts[1]), float(parts[2]), float(parts[3]), parts[5:9]))
-            except ValueError:
-                continue
-        self.path.unlink(missing_ok=True)
-        if not rows:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({names[i] for r in rows for i, v in enumerate(r[3]) if v == "Active"})
-        return {"sm_mhz": statistics.median(r[0] for r in rows), "sm_max_mhz": rows[0][1],
-                "power_w_max": max(r[2] for r in rows), "samples": len(rows),
+        if not self.rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "samples": 0,
+                    "reasons": [self.err or "no samples"]}
+        reasons = sorted({r for row in self.rows for r in row[2]})
+        return {"sm_mhz": statistics.median(r[0] for r in self.rows), "sm_max_mhz": self.max_mhz,
+                "sm_mhz_min": min(r[0] for r in self.rows),
+                "power_w_max": max(r[1] for r in self.rows), "samples": len(self.rows),
                 "reasons": reasons}
 
 
@@ -294,7 +308,7 @@ def run_ours(args):
     # step k computes and step k-1's outputs travel device->host (PCIe is full
     # duplex): three streams, device tensors double-buffered, ordered with
     # events.
-    e2e_steps = max(3, min(args.steps, 6))
+    e2e_steps = max(10, min(args.steps, 20))
     hQ, hK, hV, hdO = (x.cpu().pin_memory() for x in (Q, K, V, dO))
     hO = torch.empty_like(hQ, device="cpu").pin_memory()
     hL = torch.empty(L.shape, dtype=L.dtype).pin_memory()
