@@ -52,8 +52,12 @@ __device__ __forceinline__ void unpack8(const uint4& v, float (&f)[8]) {
 // grid (num_splits, B*H); one CTA streams rows [split*chunk, min(kv_len, (split+1)*chunk)).
 // kDirect: num_splits == 1, write the final O (dtype) and L; else write the
 // normalised split partial (fp32) and its log-sum-exp.
+// The explicit minimum of one block per SM changes ptxas' register target:
+// measured on sm_100a, it compiles this kernel into 127 registers instead of
+// 143-149 (no spills), so two CTAs fit on an SM, and config 4 goes from 5.35
+// to 7.2 TB/s.
 template <typename T, int D, bool kDirect>
-__global__ void __launch_bounds__(kDecodeThreads)
+__global__ void __launch_bounds__(kDecodeThreads, 1)
     decode_split_kernel(const T* __restrict__ Q, const T* __restrict__ K, const T* __restrict__ V,
                         T* __restrict__ O, float* __restrict__ L, float* __restrict__ O_part,
                         float* __restrict__ L_part, int kv_len, int chunk, float scale_log2) {
@@ -198,7 +202,7 @@ struct DecodeKv {
 };
 
 template <typename T, int D, int TILE, bool kPaged, bool kDirect>
-__global__ void __launch_bounds__(kDecodeThreads)
+__global__ void __launch_bounds__(kDecodeThreads, 1)
     decode_group_kernel(const T* __restrict__ Q, const DecodeKv<T> kvp, T* __restrict__ O,
                         float* __restrict__ L, float* __restrict__ O_part,
                         float* __restrict__ L_part, int hq, int group, int chunk,
@@ -515,11 +519,14 @@ template <typename T, int D, bool kPaged>
 FlashAttentionError decode_group_tile(const T* Q, const DecodeKv<T>& kvp, T* O, float* L, int B,
                                       int hq, int max_len, float scale, int num_splits,
                                       cudaStream_t stream) {
+    // Query heads per CTA: at most 4 on a contiguous cache and 2 on a paged
+    // one.  Larger tiles read each cache row once for more heads but hold more
+    // registers (8 heads: 216 per thread, one CTA per SM) and have too few
+    // bytes in flight; measured on B200 at B64 Hq32 Nkv16384 D128 (group 4 /
+    // 8): contiguous 1.31 / 1.26 ms with 4 heads per CTA against 1.31 / 1.96
+    // with 8; paged 1.67 / 1.62 ms with 2 against 2.91 / 2.76 with 4.
     const int group = hq / kvp.hkv;
-    if (group % 8 == 0)
-        return decode_group_typed<T, D, 8, kPaged>(Q, kvp, O, L, B, hq, max_len, scale,
-                                                   num_splits, stream);
-    if (group % 4 == 0)
+    if (group % 4 == 0 && !kPaged)
         return decode_group_typed<T, D, 4, kPaged>(Q, kvp, O, L, B, hq, max_len, scale,
                                                    num_splits, stream);
     if (group % 2 == 0)
