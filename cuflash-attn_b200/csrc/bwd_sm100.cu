@@ -23,9 +23,10 @@
 //                 dV  += P^T dO_i     (A = P^T from TMEM)   -> TMEM [256,256+D)
 //                 dK  += dS^T Q_i     (A = dS^T from TMEM)  -> TMEM [384,384+D)
 //                 dQ_i = dS K_j (or dQ_i^T = K_j^T dS^T)    -> TMEM [128,256)
-//               in the order dV (as soon as P^T is stored), dK, dQ_i,
-//               S^T_{i+1}, then (once the drain warps have read dQ_i)
-//               dP^T_{i+1}, so S^T_{i+1} runs while dQ_i is drained.
+//               in the order dV (as soon as P^T is stored), S^T_{i+1} (head
+//               dim 128; otherwise after dQ_i), dK, dQ_i, then (once the drain
+//               warps have read dQ_i) dP^T_{i+1}, so the next block's P phase
+//               overlaps dK and dQ_i.
 //   warps 4-11  two warpgroups, one thread per K/V row (TMEM lane) each,
 //               splitting the 128 query columns in halves, in two phases:
 //               P^T from S^T (stored back into TMEM as fp16/bf16, kept in
@@ -738,6 +739,30 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
                                 mma_f16_ts(tmem + 256, tmem + acol(kk), bo + bmn_delta<D>(kk), idesc_acc,
                                            (it > 0 || kk > 0) ? 1u : 0u);
                         }
+                        // head_dim 128: S^T_{i+1} right behind dV (the last reader of
+                        // P^T in the S^T columns), so the next block's P phase runs
+                        // while the tensor pipe does dK_i and dQ_i (config 3: 3.39 ->
+                        // 3.27 ms).  Smaller head dims issue it after dQ_i: their
+                        // shorter dK / dQ products leave little to overlap, and
+                        // holding dQ_i back delays dP^T_{i+1} (head_dim 64: 2.53 ->
+                        // 2.78 ms when issued early).
+                        constexpr bool kEarlyS = (D == 128);
+                        const bool more = it + 1 < n_it;
+                        auto issue_next_s = [&]() {
+                            if (!mbar_wait(full + (g + 1) % G::kStages, ((g + 1) / G::kStages) & 1,
+                                           abort_flag, &g_bwd_status))
+                                return false;
+                            tc_fence_after();
+                            issue_s(stage_q(g + 1));
+                            tc_commit(bar_s);
+                            return true;
+                        };
+                        if (kEarlyS && more) {
+                            if (!issue_next_s()) {
+                                ok = false;
+                                break;
+                            }
+                        }
                         // dK += dS^T Q_i  (K dimension = 128 query rows)
                         if (!mbar_wait(bar_ds, g & 1, abort_flag, &g_bwd_status)) {
                             ok = false;
@@ -772,23 +797,18 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
                             }
                         }
                         tc_commit(bar_dq);
-                        if (it + 1 < n_it) {
-                            const uint32_t sQn = stage_q(g + 1);
-                            if (!mbar_wait(full + (g + 1) % G::kStages, ((g + 1) / G::kStages) & 1,
-                                           abort_flag, &g_bwd_status)) {
+                        if (more) {
+                            if (!kEarlyS && !issue_next_s()) {
                                 ok = false;
                                 break;
                             }
-                            tc_fence_after();
-                            // S^T columns: P^T was read by the dV product issued above
-                            issue_s(sQn);
-                            tc_commit(bar_s);
+                            // dP^T_{i+1} once the drain warps have read dQ_i
                             if (!mbar_wait(bar_dqfree, g & 1, abort_flag, &g_bwd_status)) {
                                 ok = false;
                                 break;
                             }
                             tc_fence_after();
-                            issue_dp(sQn + G::kTileBytes);
+                            issue_dp(stage_q(g + 1) + G::kTileBytes);
                             tc_commit(bar_dp);
                         }
                     }
