@@ -61,6 +61,11 @@ struct DType<half> {
 bool encode_tmap_3d(CUtensorMap* map, const void* base, CUtensorMapDataType dtype, int elem_bytes,
                     uint64_t inner, uint64_t rows, uint64_t outer, uint32_t box_inner,
                     uint32_t box_rows, CUtensorMapSwizzle swizzle);
+// Same with explicit dimensions {inner, mid, outer}, byte strides of mid and
+// outer, and box {inner, mid, outer}.
+bool encode_tmap_3d_strided(CUtensorMap* map, const void* base, CUtensorMapDataType dtype,
+                            const uint64_t dims[3], const uint64_t stride_bytes[2],
+                            const uint32_t box[3], CUtensorMapSwizzle swizzle);
 
 // Raises the dynamic shared memory limit of `kernel` to `bytes` on the
 // current device once (thread-safe, per device and kernel).  Returns false
@@ -194,6 +199,7 @@ FlashAttentionError launch_convert_f32(const float* src, T* dst, long long count
 int read_and_clear_device_status();
 int fwd_sm100_status();
 int bwd_sm100_status();
+int dec_sm100_status();
 int f32_sm100_status();
 
 }  // namespace detail

@@ -17,6 +17,7 @@
 // The merge algebra is the reference's OnlineSoftmaxState merge
 // (src/kernels/impl/online_softmax.cuh:16-59) in the log2 domain.
 
+#include <algorithm>
 #include <cmath>
 #include <mutex>
 
@@ -515,6 +516,508 @@ FlashAttentionError decode_group_typed(const T* Q, const DecodeKv<T>& kvp, T* O,
                                                     : FlashAttentionError::CUDA_ERROR;
 }
 
+// ---------------------------------------------------------------------------
+// Grouped-query decode on the tensor cores (head_dim 128).  The SIMT kernel
+// above reduces every (cache row, query head) dot product across 16 lanes
+// with shuffles, and that chain, not the cache bytes, sets its speed.  Here a
+// CTA serves up to 16 query heads of one K/V head over a range of cache rows,
+// 128 rows at a time:
+//   S^T = K Q^T    tcgen05 M = 128 cache rows, N = 16 heads, K = head_dim
+//                  (A = the K block, B = the padded query tile; both K-major);
+//   softmax        one thread per cache row: per-head block maxima by warp
+//                  shuffles and a 4-warp exchange, running maxima raised only
+//                  when they grow by more than 2^8 (then O^T is rescaled),
+//                  P^T (16-bit) written to shared memory;
+//   O^T += V^T P^T M = head_dim, N = 16 heads, K = 128 cache rows (A = the V
+//                  block read MN-major, B = P^T K-major).
+// K/V blocks arrive by TMA through a 3-stage ring (contiguous cache: one box
+// per 64 columns; paged cache: one box per page and 64 columns, pages of 8 or
+// more rows).  MMA order S0, S1, O0, S2, O1, ...: S_j is issued right behind
+// O_{j-2}, so the completion of S_j (which the softmax waits for) also means
+// O_{j-2} has read the P^T buffer the softmax is about to overwrite.  TMEM:
+// S^T double-buffered in columns [0,32), O^T in [32,48).
+// ---------------------------------------------------------------------------
+__device__ int g_dec_status;
+
+constexpr int kTcHeads = 16;
+constexpr int kTcRows = 128;
+constexpr int kTcStages = 3;
+constexpr int kTcThreads = 192;  // warp 0 TMA, warp 1 MMA, warps 2-5 softmax / epilogue
+
+struct TcGeom {  // head_dim 128
+    static constexpr int kKvCbBytes = kTcRows * 128;      // 128 rows x 64 elements
+    static constexpr int kKvTileBytes = 2 * kKvCbBytes;   // one K or V block
+    static constexpr int kStageBytes = 2 * kKvTileBytes;  // K + V
+    static constexpr int kQCbBytes = kTcHeads * 128;
+    static constexpr int kQBytes = 2 * kQCbBytes;
+    static constexpr int kPCbBytes = kTcHeads * 128;      // 16 heads x 64 cache rows (16-bit)
+    static constexpr int kPBytes = 2 * kPCbBytes;
+    static constexpr int kOffQ = kTcStages * kStageBytes;
+    static constexpr int kOffP = kOffQ + kQBytes;
+    static constexpr int kOffRed = kOffP + 2 * kPBytes;
+    static constexpr int kRedFloats = 4 * kTcHeads;
+    static constexpr int kOffBar = kOffRed + 3 * kRedFloats * 4;
+    static constexpr int kNumBars = 1 + 2 * kTcStages + 2 + 2 + 2 + 1 + 1;
+    static constexpr int kSmemBytes = kOffBar + kNumBars * 8 + 16 + 1024;
+    static_assert(kOffQ % 1024 == 0 && kOffP % 1024 == 0, "swizzled tiles need 1024-byte alignment");
+};
+
+struct TcParams {
+    void* O;
+    float* L;
+    float* O_part;
+    float* L_part;
+    const int* block_table;
+    const int* seq_lens;
+    int kv_len;
+    int hkv;
+    int hq;
+    int group;
+    int head_tiles;
+    int chunk;  // rows per split, a multiple of 128
+    int page_shift;
+    int max_pages;
+    int num_pages;
+    float scale_log2;
+};
+
+// K-major operand of 64-element (128-byte) swizzled rows, `cb_bytes` per
+// 64-column block: descriptor of k-step kk (16 elements).
+__device__ __forceinline__ uint64_t tc_kmajor(uint32_t base, uint32_t cb_bytes, int kk) {
+    const uint32_t byte = static_cast<uint32_t>(kk) * 32u;
+    return sm100::make_smem_desc(base + (byte >> 7) * cb_bytes + (byte & 127u), 16, 1024,
+                                 sm100::kLayoutSw128);
+}
+// MN-major operand (K dimension = rows of 128 bytes): k-step kk covers 16 rows.
+__device__ __forceinline__ uint64_t tc_mnmajor(uint32_t base, uint32_t cb_bytes, int kk) {
+    return sm100::make_smem_desc(base + static_cast<uint32_t>(kk) * 16u * 128u, cb_bytes, 1024,
+                                 sm100::kLayoutSw128);
+}
+
+__device__ __forceinline__ void st_shared_u16(uint32_t addr, uint16_t v) {
+    asm volatile("st.shared.u16 [%0], %1;" ::"r"(addr), "h"(v) : "memory");
+}
+
+__device__ __forceinline__ void fence_proxy_async_smem_dec() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+__device__ __forceinline__ void softmax_group_sync() {
+    asm volatile("bar.sync 1, 128;" ::: "memory");
+}
+
+template <typename T, bool kPaged, bool kDirect>
+__global__ void __launch_bounds__(kTcThreads, 1)
+    decode_gqa_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
+                         const __grid_constant__ CUtensorMap tmK,
+                         const __grid_constant__ CUtensorMap tmV, const TcParams p) {
+    using G = TcGeom;
+    using namespace sm100;
+    extern __shared__ uint8_t smem_raw[];
+    if (*reinterpret_cast<volatile int*>(&g_dec_status) != 0) return;
+    const uint32_t raw = smem_u32(smem_raw);
+    const uint32_t sbase = (raw + 1023u) & ~1023u;
+    uint8_t* sptr = smem_raw + (sbase - raw);
+    uint64_t* bars = reinterpret_cast<uint64_t*>(sptr + G::kOffBar);
+    uint64_t* bar_q = bars;
+    uint64_t* full = bar_q + 1;
+    uint64_t* empty = full + kTcStages;
+    uint64_t* bar_s = empty + kTcStages;  // [2] S^T_j in TMEM
+    uint64_t* bar_sfree = bar_s + 2;      // [2] S^T_j read by the softmax (128 arrivals)
+    uint64_t* bar_p = bar_sfree + 2;      // [2] P^T_j in shared memory (128 arrivals)
+    uint64_t* bar_ofin = bar_p + 2;       // one completion per O^T product
+    uint64_t* bar_done = bar_ofin + 1;    // every MMA retired
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar_done + 1);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+    float* red = reinterpret_cast<float*>(sptr + G::kOffRed);  // 3 x [4 warps][16 heads]
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const int split = blockIdx.x;
+    const int tile = blockIdx.y % p.head_tiles;
+    const int bhk = blockIdx.y / p.head_tiles;
+    const int b = bhk / p.hkv;
+    const int hk = bhk - b * p.hkv;
+    const int g0 = tile * kTcHeads;
+    const int nh = min(kTcHeads, p.group - g0);
+    const long long bhq0 = static_cast<long long>(b) * p.hq + static_cast<long long>(hk) * p.group + g0;
+    // a paged length is clamped to what the block table can address
+    const int len = kPaged ? min(max(p.seq_lens[b], 0), p.max_pages << p.page_shift) : p.kv_len;
+    const int r_begin = split * p.chunk;
+    const int r_end = min(len, r_begin + p.chunk);
+    const int nb = r_end > r_begin ? (r_end - r_begin + kTcRows - 1) / kTcRows : 0;
+
+    if (threadIdx.x == 0) {
+        mbar_init(bar_q, 1);
+        for (int s = 0; s < kTcStages; ++s) {
+            mbar_init(full + s, 1);
+            mbar_init(empty + s, 1);
+        }
+        for (int t = 0; t < 2; ++t) {
+            mbar_init(bar_s + t, 1);
+            mbar_init(bar_sfree + t, 128);
+            mbar_init(bar_p + t, 128);
+        }
+        mbar_init(bar_ofin, 1);
+        mbar_init(bar_done, 1);
+        *abort_flag = 0;
+        fence_mbar_init();
+    }
+    if (warp == 1) {
+        tmem_alloc(tmem_slot, 64);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 0) {
+        // ------------------------------------------------ TMA producer
+        if (lane == 0 && nb > 0) {
+            prefetch_tmap(&tmQ);
+            prefetch_tmap(&tmK);
+            prefetch_tmap(&tmV);
+            // query rows bhq0 .. bhq0+15; rows of the next group or past the
+            // tensor end fill heads this CTA does not report
+            mbar_arrive_expect_tx(bar_q, G::kQBytes);
+            for (int cb = 0; cb < 2; ++cb)
+                tma_load_3d(sptr + G::kOffQ + cb * G::kQCbBytes, &tmQ, bar_q, cb * 64,
+                            static_cast<int>(bhq0), 0);
+            int issued = 0;
+            for (int j = 0; j < nb; ++j) {
+                const int s = j % kTcStages;
+                if (j >= kTcStages &&
+                    !mbar_wait(empty + s, ((j / kTcStages) - 1) & 1, abort_flag, &g_dec_status))
+                    break;
+                ++issued;
+                uint8_t* st = sptr + s * G::kStageBytes;
+                mbar_arrive_expect_tx(full + s, G::kStageBytes);
+                const int r0 = r_begin + j * kTcRows;
+                if constexpr (!kPaged) {
+                    for (int cb = 0; cb < 2; ++cb) {
+                        tma_load_3d(st + cb * G::kKvCbBytes, &tmK, full + s, cb * 64, r0, bhk);
+                        tma_load_3d(st + G::kKvTileBytes + cb * G::kKvCbBytes, &tmV, full + s,
+                                    cb * 64, r0, bhk);
+                    }
+                } else {
+                    const int ps = 1 << p.page_shift;
+                    const int per = ps < kTcRows ? ps : kTcRows;
+                    for (int rr = 0; rr < kTcRows; rr += per) {
+                        const int row = r0 + rr;
+                        const int pi = min(row >> p.page_shift, p.max_pages - 1);
+                        int page = p.block_table[static_cast<long long>(b) * p.max_pages + pi];
+                        page = min(max(page, 0), p.num_pages - 1);
+                        const int slot = (page << p.page_shift) + (row & (ps - 1));
+                        for (int cb = 0; cb < 2; ++cb) {
+                            tma_load_3d(st + cb * G::kKvCbBytes + rr * 128, &tmK, full + s, cb * 64,
+                                        hk, slot);
+                            tma_load_3d(st + G::kKvTileBytes + cb * G::kKvCbBytes + rr * 128, &tmV,
+                                        full + s, cb * 64, hk, slot);
+                        }
+                    }
+                }
+            }
+            // every issued copy lands before the CTA can exit, also after an abort
+            volatile int never = 0;
+            mbar_wait(bar_q, 0, &never, &g_dec_status);
+            for (int j = issued > kTcStages ? issued - kTcStages : 0; j < issued; ++j)
+                mbar_wait(full + j % kTcStages, (j / kTcStages) & 1, &never, &g_dec_status);
+        }
+    } else if (warp == 1) {
+        // ------------------------------------------------ MMA issuer
+        if (lane == 0 && nb > 0) {
+            constexpr uint32_t kFmt = DType<T>::kMmaFmt;
+            constexpr uint32_t idesc_s = make_idesc(kFmt, 128, kTcHeads, false, false);
+            constexpr uint32_t idesc_o = make_idesc(kFmt, 128, kTcHeads, true, false);
+            const uint32_t sQ = sbase + G::kOffQ;
+            bool ok = mbar_wait(bar_q, 0, abort_flag, &g_dec_status);
+            auto issue_s = [&](int j) {
+                const int s = j % kTcStages;
+                if (!mbar_wait(full + s, (j / kTcStages) & 1, abort_flag, &g_dec_status)) return false;
+                if (j >= 2 &&
+                    !mbar_wait(bar_sfree + (j & 1), ((j >> 1) - 1) & 1, abort_flag, &g_dec_status))
+                    return false;
+                tc_fence_after();
+                const uint32_t sK = sbase + s * G::kStageBytes;
+#pragma unroll
+                for (int kk = 0; kk < 8; ++kk)
+                    mma_f16_ss(tmem + (j & 1) * kTcHeads, tc_kmajor(sK, G::kKvCbBytes, kk),
+                               tc_kmajor(sQ, G::kQCbBytes, kk), idesc_s, kk > 0 ? 1u : 0u);
+                tc_commit(bar_s + (j & 1));
+                return true;
+            };
+            auto issue_o = [&](int j) {
+                if (!mbar_wait(bar_p + (j & 1), (j >> 1) & 1, abort_flag, &g_dec_status)) return false;
+                tc_fence_after();
+                const uint32_t sV = sbase + (j % kTcStages) * G::kStageBytes + G::kKvTileBytes;
+                const uint32_t sP = sbase + G::kOffP + (j & 1) * G::kPBytes;
+#pragma unroll
+                for (int kk = 0; kk < 8; ++kk)
+                    mma_f16_ss(tmem + 2 * kTcHeads, tc_mnmajor(sV, G::kKvCbBytes, kk),
+                               tc_kmajor(sP, G::kPCbBytes, kk), idesc_o,
+                               (j > 0 || kk > 0) ? 1u : 0u);
+                tc_commit(empty + (j % kTcStages));
+                tc_commit(bar_ofin);
+                return true;
+            };
+            ok = ok && issue_s(0);
+            if (nb > 1) ok = ok && issue_s(1);
+            for (int j = 0; ok && j < nb; ++j) {
+                ok = issue_o(j);
+                if (ok && j + 2 < nb) ok = issue_s(j + 2);
+            }
+            tc_commit(bar_done);
+        }
+        __syncwarp();
+    } else {
+        // ------------------------------------------------ softmax and epilogue
+        const int q4 = warp & 3;     // TMEM lane quarter of this warp
+        const int wsm = warp - 2;    // index in the cross-warp exchange
+        const int r = q4 * 32 + lane;  // cache row of the block (S^T) / head_dim element (O^T)
+        const uint32_t lane_addr = static_cast<uint32_t>(q4 * 32) << 16;
+        const float c = p.scale_log2;
+        float m_run[kTcHeads], l_part[kTcHeads];
+#pragma unroll
+        for (int g = 0; g < kTcHeads; ++g) {
+            m_run[g] = -INFINITY;
+            l_part[g] = 0.f;
+        }
+        // Every softmax thread runs all nb iterations and both group barriers
+        // per iteration whatever happens; after a failed (timed-out or
+        // aborted) wait, `ok` turns false warp-uniformly and the warp skips
+        // its TMEM and barrier traffic, so no thread is left in bar.sync.
+        bool ok = true;
+        for (int j = 0; j < nb; ++j) {
+            if (ok) ok = mbar_wait(bar_s + (j & 1), (j >> 1) & 1, abort_flag, &g_dec_status);
+            ok = __all_sync(0xffffffffu, ok);
+            uint32_t sv[16];
+            if (ok) {
+                tc_fence_after();
+                tmem_ld_x16(tmem + lane_addr + (j & 1) * kTcHeads, sv);
+                tc_fence_before();
+                mbar_arrive(bar_sfree + (j & 1));
+            } else {
+#pragma unroll
+                for (int g = 0; g < kTcHeads; ++g) sv[g] = 0u;
+            }
+            const bool live = r_begin + j * kTcRows + r < r_end;
+            float x[kTcHeads];
+#pragma unroll
+            for (int g = 0; g < kTcHeads; ++g) x[g] = live ? __uint_as_float(sv[g]) * c : -INFINITY;
+            // per-head block maxima: warp shuffles, then the four warps
+            float* rm = red + (j & 1) * G::kRedFloats;
+#pragma unroll
+            for (int g = 0; g < kTcHeads; ++g) {
+                float v = x[g];
+#pragma unroll
+                for (int off = 16; off > 0; off >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, off));
+                if (lane == 0) rm[wsm * kTcHeads + g] = v;
+            }
+            softmax_group_sync();
+            bool resc = false;
+            float alpha[kTcHeads];
+#pragma unroll
+            for (int g = 0; g < kTcHeads; ++g) {
+                const float bm = fmaxf(fmaxf(rm[g], rm[kTcHeads + g]),
+                                       fmaxf(rm[2 * kTcHeads + g], rm[3 * kTcHeads + g]));
+                float mn = m_run[g];
+                if (mn == -INFINITY || bm > mn + 8.f) mn = fmaxf(mn, bm);
+                alpha[g] = (m_run[g] == -INFINITY || mn == m_run[g]) ? 1.f : ex2_approx(m_run[g] - mn);
+                resc = resc || alpha[g] != 1.f;
+                m_run[g] = mn;
+            }
+            if (resc && ok) {  // resc is uniform: every thread saw the same maxima
+                // O^T_{j-1} must be complete (j >= 1 here: the first block never rescales)
+                ok = mbar_wait(bar_ofin, (j - 1) & 1, abort_flag, &g_dec_status);
+                ok = __all_sync(0xffffffffu, ok);
+            }
+            if (resc && ok) {
+                tc_fence_after();
+                uint32_t ov[16];
+                tmem_ld_x16(tmem + lane_addr + 2 * kTcHeads, ov);
+#pragma unroll
+                for (int g = 0; g < kTcHeads; ++g) {
+                    ov[g] = __float_as_uint(__uint_as_float(ov[g]) * alpha[g]);
+                    l_part[g] *= alpha[g];
+                }
+                tmem_st_x16(tmem + lane_addr + 2 * kTcHeads, ov);
+                tc_fence_before();
+            }
+            // P^T (head g, cache row r) into buffer j & 1, 128-byte swizzled K-major
+            const uint32_t pb = sbase + G::kOffP + (j & 1) * G::kPBytes + (r >> 6) * G::kPCbBytes;
+            const int kr = r & 63;
+#pragma unroll
+            for (int g = 0; g < kTcHeads; ++g) {
+                const float pv = m_run[g] == -INFINITY ? 0.f : ex2_approx(x[g] - m_run[g]);
+                l_part[g] += pv;
+                const uint32_t addr = pb + g * 128 + ((((kr >> 3) ^ (g & 7))) << 4) + (kr & 7) * 2;
+                const T h = DType<T>::from_float(pv);
+                st_shared_u16(addr, *reinterpret_cast<const uint16_t*>(&h));
+            }
+            if constexpr (kPaged) {
+                // rows past the sequence end hold whatever the cache page has;
+                // zero their V so that P = 0 cannot meet a non-finite value
+                if (!live) {
+                    const uint32_t vrow = sbase + (j % kTcStages) * G::kStageBytes + G::kKvTileBytes +
+                                          r * 128;
+#pragma unroll
+                    for (int cb = 0; cb < 2; ++cb)
+#pragma unroll
+                        for (int q = 0; q < 8; ++q)
+                            asm volatile("st.shared.v4.b32 [%0], {%1, %1, %1, %1};" ::"r"(
+                                             vrow + cb * G::kKvCbBytes + q * 16),
+                                         "r"(0u)
+                                         : "memory");
+                }
+            }
+            if (ok) {
+                fence_proxy_async_smem_dec();
+                mbar_arrive(bar_p + (j & 1));
+            }
+        }
+        // ---- epilogue: normalise, write the split's result
+        if (ok && nb > 0) {
+            ok = mbar_wait(bar_done, 0, abort_flag, &g_dec_status);
+            tc_fence_after();
+        }
+        ok = __all_sync(0xffffffffu, ok);
+        float* rs = red + 2 * G::kRedFloats;
+#pragma unroll
+        for (int g = 0; g < kTcHeads; ++g) {
+            float v = l_part[g];
+#pragma unroll
+            for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+            if (lane == 0) rs[wsm * kTcHeads + g] = v;
+        }
+        softmax_group_sync();
+        uint32_t ov[16];
+        if (ok && nb > 0) {
+            tmem_ld_x16(tmem + lane_addr + 2 * kTcHeads, ov);
+        } else {
+#pragma unroll
+            for (int g = 0; g < kTcHeads; ++g) ov[g] = 0u;
+        }
+        const int d = r;
+#pragma unroll
+        for (int g = 0; g < kTcHeads; ++g) {
+            if (g >= nh) continue;
+            const float lt = rs[g] + rs[kTcHeads + g] + rs[2 * kTcHeads + g] + rs[3 * kTcHeads + g];
+            const float outv = lt > 0.f ? __uint_as_float(ov[g]) / lt : 0.f;
+            const float lse = lt > 0.f ? (m_run[g] + log2f(lt)) * kLn2f : -INFINITY;
+            const long long bhq = bhq0 + g;
+            if constexpr (kDirect) {
+                static_cast<T*>(p.O)[bhq * 128 + d] = DType<T>::from_float(outv);
+                if (d == 0) p.L[bhq] = lse;
+            } else {
+                p.O_part[(bhq * gridDim.x + split) * 128 + d] = outv;
+                if (d == 0) p.L_part[bhq * gridDim.x + split] = lse;
+            }
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem, 64);
+    }
+}
+
+// Tensor-core grouped-query decode for head_dim 128 (see the kernel above).
+template <typename T, bool kPaged>
+FlashAttentionError decode_gqa_tc(const T* Q, const DecodeKv<T>& kvp, T* O, float* L, int B,
+                                  int hq, int max_len, float scale, int num_splits,
+                                  cudaStream_t stream) {
+    using G = TcGeom;
+    const int group = hq / kvp.hkv;
+    const int tiles = (group + kTcHeads - 1) / kTcHeads;
+    const long long units = static_cast<long long>(B) * kvp.hkv * tiles;
+    if (units > 65535) return FlashAttentionError::INVALID_DIMENSION;  // grid.y limit
+    const int blocks_total = (max_len + kTcRows - 1) / kTcRows;
+    int S = num_splits;
+    if (S == 0) {
+        // One wave of CTAs (one per SM, each streaming its rows): measured on
+        // B200 over B 8-64, Nkv 4k-32k, groups 2-16, the best split count is
+        // about SMs / units (units 16 / 32 / 64 / >= 128 -> 8 / 4 / 2 / 1);
+        // at least two blocks per split.
+        S = static_cast<int>(std::max<long long>(1, current_sm_count() / units));
+        S = std::min(S, std::max(1, blocks_total / 2));
+    }
+    S = std::max(1, std::min(S, std::min(64, std::max(1, blocks_total))));
+    const int chunk = ((blocks_total + S - 1) / S) * kTcRows;
+    S = (max_len + chunk - 1) / chunk;
+    if (S < 1) S = 1;
+
+    const CUtensorMapDataType dt = DType<T>::kTmaType;
+    CUtensorMap mq, mk, mv;
+    if (!encode_tmap_3d(&mq, Q, dt, 2, 128, static_cast<uint64_t>(B) * hq, 1, 64, kTcHeads,
+                        CU_TENSOR_MAP_SWIZZLE_128B))
+        return FlashAttentionError::CUDA_ERROR;
+    if (!kPaged) {
+        if (!encode_tmap_3d(&mk, kvp.K, dt, 2, 128, kvp.kv_len, static_cast<uint64_t>(B) * kvp.hkv,
+                            64, kTcRows, CU_TENSOR_MAP_SWIZZLE_128B) ||
+            !encode_tmap_3d(&mv, kvp.V, dt, 2, 128, kvp.kv_len, static_cast<uint64_t>(B) * kvp.hkv,
+                            64, kTcRows, CU_TENSOR_MAP_SWIZZLE_128B))
+            return FlashAttentionError::CUDA_ERROR;
+    } else {
+        const int ps = 1 << kvp.page_shift;
+        const uint64_t dims[3] = {128, static_cast<uint64_t>(kvp.hkv),
+                                  static_cast<uint64_t>(kvp.num_pages) << kvp.page_shift};
+        const uint64_t strides[2] = {128 * 2, static_cast<uint64_t>(kvp.hkv) * 128 * 2};
+        const uint32_t box[3] = {64, 1, static_cast<uint32_t>(ps < kTcRows ? ps : kTcRows)};
+        if (!encode_tmap_3d_strided(&mk, kvp.K, dt, dims, strides, box,
+                                    CU_TENSOR_MAP_SWIZZLE_128B) ||
+            !encode_tmap_3d_strided(&mv, kvp.V, dt, dims, strides, box,
+                                    CU_TENSOR_MAP_SWIZZLE_128B))
+            return FlashAttentionError::CUDA_ERROR;
+    }
+    TcParams prm{};
+    prm.block_table = kvp.block_table;
+    prm.seq_lens = kvp.seq_lens;
+    prm.kv_len = kvp.kv_len;
+    prm.hkv = kvp.hkv;
+    prm.hq = hq;
+    prm.group = group;
+    prm.head_tiles = tiles;
+    prm.chunk = chunk;
+    prm.page_shift = kvp.page_shift;
+    prm.max_pages = kvp.max_pages;
+    prm.num_pages = kvp.num_pages;
+    prm.scale_log2 = scale * kLog2ef;
+    const dim3 grid(S, static_cast<unsigned>(units));
+    if (S == 1) {
+        auto k = decode_gqa_tc_kernel<T, kPaged, true>;
+        if (!ensure_smem_attr(reinterpret_cast<const void*>(k), G::kSmemBytes))
+            return FlashAttentionError::CUDA_ERROR;
+        prm.O = O;
+        prm.L = L;
+        k<<<grid, kTcThreads, G::kSmemBytes, stream>>>(mq, mk, mv, prm);
+        return cudaGetLastError() == cudaSuccess ? FlashAttentionError::SUCCESS
+                                                 : FlashAttentionError::CUDA_ERROR;
+    }
+    const int BHq = B * hq;
+    const size_t part_elems = static_cast<size_t>(BHq) * S * 128;
+    const size_t bytes = (part_elems + static_cast<size_t>(BHq) * S) * sizeof(float);
+    void* wsv = nullptr;
+    FlashAttentionError werr = workspace_alloc(&wsv, bytes, stream);
+    if (werr != FlashAttentionError::SUCCESS) return werr;
+    prm.O_part = static_cast<float*>(wsv);
+    prm.L_part = prm.O_part + part_elems;
+    auto k = decode_gqa_tc_kernel<T, kPaged, false>;
+    if (!ensure_smem_attr(reinterpret_cast<const void*>(k), G::kSmemBytes)) {
+        workspace_free(wsv, stream);
+        return FlashAttentionError::CUDA_ERROR;
+    }
+    k<<<grid, kTcThreads, G::kSmemBytes, stream>>>(mq, mk, mv, prm);
+    cudaError_t e1 = cudaGetLastError();
+    decode_combine_kernel<T, 128><<<BHq, 128, 0, stream>>>(prm.O_part, prm.L_part, O, L, S);
+    cudaError_t e2 = cudaGetLastError();
+    workspace_free(wsv, stream);
+    return (e1 == cudaSuccess && e2 == cudaSuccess) ? FlashAttentionError::SUCCESS
+                                                    : FlashAttentionError::CUDA_ERROR;
+}
+
 template <typename T, int D, bool kPaged>
 FlashAttentionError decode_group_tile(const T* Q, const DecodeKv<T>& kvp, T* O, float* L, int B,
                                       int hq, int max_len, float scale, int num_splits,
@@ -526,6 +1029,12 @@ FlashAttentionError decode_group_tile(const T* Q, const DecodeKv<T>& kvp, T* O, 
     // 8): contiguous 1.31 / 1.26 ms with 4 heads per CTA against 1.31 / 1.96
     // with 8; paged 1.67 / 1.62 ms with 2 against 2.91 / 2.76 with 4.
     const int group = hq / kvp.hkv;
+    if constexpr (D == 128) {
+        // tensor-core kernel from two heads per K/V head up (pages of 8+ rows)
+        if (group >= 2 && (!kPaged || kvp.page_shift >= 3) && env_int("CUFLASH_DECODE_GQA_TC", 1) != 0)
+            return decode_gqa_tc<T, kPaged>(Q, kvp, O, L, B, hq, max_len, scale, num_splits,
+                                            stream);
+    }
     if (group % 4 == 0 && !kPaged)
         return decode_group_typed<T, D, 4, kPaged>(Q, kvp, O, L, B, hq, max_len, scale,
                                                    num_splits, stream);
@@ -598,6 +1107,16 @@ FlashAttentionError launch_decode_gqa(const T* Q, const T* K, const T* V, T* O, 
         default: return FlashAttentionError::UNSUPPORTED_HEAD_DIM;
     }
 #undef CUFLASH_DECODE_GQA
+}
+
+int dec_sm100_status() {
+    int v = 0;
+    if (cudaMemcpyFromSymbol(&v, g_dec_status, sizeof(int)) != cudaSuccess) return -1;
+    if (v != 0) {
+        const int zero = 0;
+        cudaMemcpyToSymbol(g_dec_status, &zero, sizeof(int));
+    }
+    return v;
 }
 
 template FlashAttentionError launch_decode_gqa<half>(const half*, const half*, const half*, half*,

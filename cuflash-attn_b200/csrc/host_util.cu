@@ -48,6 +48,22 @@ bool encode_tmap_3d(CUtensorMap* map, const void* base, CUtensorMapDataType dtyp
     return r == CUDA_SUCCESS;
 }
 
+bool encode_tmap_3d_strided(CUtensorMap* map, const void* base, CUtensorMapDataType dtype,
+                            const uint64_t dims[3], const uint64_t stride_bytes[2],
+                            const uint32_t box[3], CUtensorMapSwizzle swizzle) {
+    auto fn = encode_fn();
+    if (fn == nullptr) return false;
+    if ((reinterpret_cast<uintptr_t>(base) & 15u) != 0) return false;
+    cuuint64_t d[3] = {dims[0], dims[1], dims[2]};
+    cuuint64_t st[2] = {stride_bytes[0], stride_bytes[1]};
+    cuuint32_t bx[3] = {box[0], box[1], box[2]};
+    cuuint32_t estr[3] = {1, 1, 1};
+    CUresult r = fn(map, dtype, 3, const_cast<void*>(base), d, st, bx, estr,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS;
+}
+
 bool ensure_smem_attr(const void* kernel, int bytes) {
     // (device, kernel, bytes) already configured; a plain table keeps the
     // library from exporting standard-container template instances.
@@ -161,8 +177,9 @@ int read_and_clear_device_status() {
     const int a = fwd_sm100_status();
     const int b = bwd_sm100_status();
     const int c = f32_sm100_status();
-    if (a < 0 || b < 0 || c < 0) return -1;
-    return a != 0 ? a : (b != 0 ? b : c);
+    const int d = dec_sm100_status();
+    if (a < 0 || b < 0 || c < 0 || d < 0) return -1;
+    return a != 0 ? a : (b != 0 ? b : (c != 0 ? c : d));
 }
 
 }  // namespace detail

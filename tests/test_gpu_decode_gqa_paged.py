@@ -108,3 +108,30 @@ def test_decode_paged_vs_fp64(lib, cuda, dt, page_size, Hq, Hkv, splits):
         O64, L64 = _ref_decode(q[b:b + 1], Kb, Vb, scale)
         assert max_err(Og[b:b + 1], O64) < TOL_O, b
         assert max_err(Lg[b:b + 1], L64) < TOL_L, b
+
+
+@pytest.mark.parametrize("tc", ["1", "0"])
+@pytest.mark.parametrize("Hq,Hkv", [(48, 2), (64, 2), (4, 2)])
+def test_decode_gqa_large_groups_and_rescale(lib, cuda, monkeypatch, tc, Hq, Hkv):
+    """Groups above 16 heads (several head tiles per K/V head on the tensor-
+    core path) and scores that grow along the cache (later rows dominate,
+    so running maxima rise across blocks and O is rescaled), on both the
+    tensor-core kernel (CUFLASH_DECODE_GQA_TC=1, head_dim 128) and the SIMT
+    kernel (=0)."""
+    import torch
+
+    monkeypatch.setenv("CUFLASH_DECODE_GQA_TC", tc)
+    B, N, D, dt = 2, 1500, 128, "bf16"
+    scale = 1.0 / np.sqrt(D)
+    q = round_to(oracle.normal((B, Hq, 1, D), 21), dt)
+    ramp = (1.0 + 4.0 * np.arange(N, dtype=np.float32) / N)[None, None, :, None]
+    K = round_to(oracle.normal((B, Hkv, N, D), 22) * ramp, dt)
+    V = round_to(oracle.normal((B, Hkv, N, D), 23), dt)
+    for splits in (0, 1):
+        O, L = lib.decode_gqa(to_dev(q, dt), to_dev(K, dt), to_dev(V, dt), scale=scale,
+                              num_splits=splits)
+        torch.cuda.synchronize()
+        assert lib.device_status() == 0
+        O64, L64 = _ref_decode(q, K, V, scale)
+        assert max_err(host(O), O64) < TOL_O
+        assert max_err(host(L), L64) < TOL_L
