@@ -685,15 +685,30 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 tma_load_3d(sptr + G::kOffQ + cb * G::kQCbBytes, &tmQ, bar_q, cb * 64,
                             static_cast<int>(bhq0), 0);
             int issued = 0;
+            const int ps = 1 << p.page_shift;
+            const int per = ps < kTcRows ? ps : kTcRows;  // rows per TMA box (paged)
+            const int npb = kTcRows / per;                // boxes per block (paged, <= 16)
             for (int j = 0; j < nb; ++j) {
                 const int s = j % kTcStages;
+                const int r0 = r_begin + j * kTcRows;
+                // paged: the block's page indices, loaded before the ring wait
+                // so their latency overlaps it
+                int page[kTcRows / 8];
+                if constexpr (kPaged) {
+#pragma unroll
+                    for (int q = 0; q < kTcRows / 8; ++q) {
+                        if (q < npb) {
+                            const int pi = min((r0 + q * per) >> p.page_shift, p.max_pages - 1);
+                            page[q] = p.block_table[static_cast<long long>(b) * p.max_pages + pi];
+                        }
+                    }
+                }
                 if (j >= kTcStages &&
                     !mbar_wait(empty + s, ((j / kTcStages) - 1) & 1, abort_flag, &g_dec_status))
                     break;
                 ++issued;
                 uint8_t* st = sptr + s * G::kStageBytes;
                 mbar_arrive_expect_tx(full + s, G::kStageBytes);
-                const int r0 = r_begin + j * kTcRows;
                 if constexpr (!kPaged) {
                     for (int cb = 0; cb < 2; ++cb) {
                         tma_load_3d(st + cb * G::kKvCbBytes, &tmK, full + s, cb * 64, r0, bhk);
@@ -701,14 +716,12 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                                     cb * 64, r0, bhk);
                     }
                 } else {
-                    const int ps = 1 << p.page_shift;
-                    const int per = ps < kTcRows ? ps : kTcRows;
-                    for (int rr = 0; rr < kTcRows; rr += per) {
-                        const int row = r0 + rr;
-                        const int pi = min(row >> p.page_shift, p.max_pages - 1);
-                        int page = p.block_table[static_cast<long long>(b) * p.max_pages + pi];
-                        page = min(max(page, 0), p.num_pages - 1);
-                        const int slot = (page << p.page_shift) + (row & (ps - 1));
+#pragma unroll
+                    for (int q = 0; q < kTcRows / 8; ++q) {
+                        if (q >= npb) break;
+                        const int rr = q * per;
+                        const int pg = min(max(page[q], 0), p.num_pages - 1);
+                        const int slot = (pg << p.page_shift) + ((r0 + rr) & (ps - 1));
                         for (int cb = 0; cb < 2; ++cb) {
                             tma_load_3d(st + cb * G::kKvCbBytes + rr * 128, &tmK, full + s, cb * 64,
                                         hk, slot);
