@@ -427,23 +427,25 @@ def run_decode(args, lib, dev, world, rank, pk, pk_kind):
 
     c = DECODE
     B, H, N, D = (args.batch if args.batch_set else c["B"]), c["H"], c["N"], c["D"]
+    Hkv = args.kv_heads or H  # fewer K/V heads than query heads: grouped-query decode
     g = torch.Generator(device=dev).manual_seed(31 + 1000 * rank)
     q = torch.randn((B, H, 1, D), device=dev, generator=g).to(torch.bfloat16)
-    K = torch.randn((B, H, N, D), device=dev, generator=g).to(torch.bfloat16)
-    V = torch.randn((B, H, N, D), device=dev, generator=g).to(torch.bfloat16)
+    K = torch.randn((B, Hkv, N, D), device=dev, generator=g).to(torch.bfloat16)
+    V = torch.randn((B, Hkv, N, D), device=dev, generator=g).to(torch.bfloat16)
     O = torch.empty_like(q)
     L = torch.empty((B, H), device=dev, dtype=torch.float32)
     stream = torch.cuda.current_stream()
-    nbytes = 2 * B * H * N * D * 2 + 2 * B * H * D * 2 + B * H * 4
+    nbytes = 2 * B * Hkv * N * D * 2 + 2 * B * H * D * 2 + B * H * 4
+    call = lib.decode if Hkv == H else lib.decode_gqa
     results = {}
     for splits in args.splits:
         for _ in range(max(args.warmup, 3)):
-            lib.decode(q, K, V, num_splits=splits, O=O, L=L, stream=stream)
+            call(q, K, V, num_splits=splits, O=O, L=L, stream=stream)
         torch.cuda.synchronize()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(stream)
         for _ in range(args.steps):
-            lib.decode(q, K, V, num_splits=splits, O=O, L=L, stream=stream)
+            call(q, K, V, num_splits=splits, O=O, L=L, stream=stream)
         e1.record(stream)
         torch.cuda.synchronize()
         ms = e0.elapsed_time(e1) / args.steps
@@ -456,8 +458,9 @@ def run_decode(args, lib, dev, world, rank, pk, pk_kind):
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": results[best]["ms"], "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-            "config": {"workload": ("BASELINE config 4: " if B == 64 else "custom: ") +
-                                   f"split-KV decode B{B} H{H} Nkv{N} D{D}",
+            "config": {"workload": ("BASELINE config 4: " if B == 64 and Hkv == H else "custom: ") +
+                                   (f"split-KV decode B{B} H{H} Nkv{N} D{D}" if Hkv == H else
+                                    f"grouped-query split-KV decode B{B} Hq{H} Hkv{Hkv} Nkv{N} D{D}"),
                        "best_num_splits": best},
             "splits": results,
             "roofline": {"bound": "hbm", "achieved": results[best]["GBps"], "peak": peak,
@@ -549,6 +552,8 @@ def main():
     ap.add_argument("--cp-backward", action="store_true",
                     help="cp workload: time the ring forward and backward of a training step")
     ap.add_argument("--splits", type=int, nargs="*", default=[0, 1, 2, 4, 8, 16, 32, 64])
+    ap.add_argument("--kv-heads", type=int, default=0,
+                    help="decode workload: K/V heads (fewer than the 32 query heads: grouped-query)")
     ap.add_argument("--skip-cpu-baseline", action="store_true")
     ap.add_argument("--batch", type=int, default=TRAIN["B"])
     ap.add_argument("--heads", type=int, default=TRAIN["H"])
