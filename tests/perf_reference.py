@@ -26,6 +26,8 @@ import oracle  # noqa: E402
 CONFIGS = [
     # name, dtype, B, H, N, D, causal, backward
     ("config1_f32_causal_fwd", torch.float32, 2, 8, 1024, 64, True, False),
+    ("f32_causal_fwd_bwd_b2h8n1024d64", torch.float32, 2, 8, 1024, 64, True, True),
+    ("f32_fwd_bwd_b4h16n2048d128", torch.float32, 4, 16, 2048, 128, False, True),
     ("config2_f16_fwd_bwd", torch.float16, 4, 16, 2048, 128, False, True),
     ("config3_bf16_causal_fwd_bwd", torch.bfloat16, 8, 32, 4096, 128, True, True),
     ("config5_bf16_causal_fwd_1gpu", torch.bfloat16, 1, 32, 131072, 128, True, False),
@@ -47,11 +49,14 @@ def timed(fn, iters):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--quick", action="store_true")
+    ap.add_argument("--only", default="", help="substring of the config names to run")
     args = ap.parse_args()
     ours = cuflash_attn.CuFlashAttn()
     ref = cuflash_attn.CuFlashAttn(str(oracle.REF_LIB_PATH), reference_abi_only=True)
     for name, dt, B, H, N, D, causal, bwd in CONFIGS:
         if args.quick and N > 4096:
+            continue
+        if args.only and args.only not in name:
             continue
         g = torch.Generator(device="cuda").manual_seed(1)
         Q, K, V, dO = (torch.randn((B, H, N, D), device="cuda", generator=g).to(dt)
