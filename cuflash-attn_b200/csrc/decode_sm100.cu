@@ -50,7 +50,7 @@ __device__ __forceinline__ void unpack8(const uint4& v, float (&f)[8]) {
     f[4] = c.x; f[5] = c.y; f[6] = d.x; f[7] = d.y;
 }
 
-// grid (num_splits, B*H); one CTA streams rows [split*chunk, min(kv_len, (split+1)*chunk)).
+// grid (B*H, num_splits); one CTA streams rows [split*chunk, min(kv_len, (split+1)*chunk)).
 // kDirect: num_splits == 1, write the final O (dtype) and L; else write the
 // normalised split partial (fp32) and its log-sum-exp.
 // The explicit minimum of one block per SM changes ptxas' register target:
@@ -71,9 +71,9 @@ __global__ void __launch_bounds__(kDecodeThreads, 1)
     __shared__ float s_l[G];
     __shared__ float s_acc[G][D];
 
-    const int split = blockIdx.x;
-    const int num_splits = gridDim.x;
-    const long long bh = blockIdx.y;
+    const int split = blockIdx.y;
+    const int num_splits = gridDim.y;
+    const long long bh = blockIdx.x;
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
     const int sub = lane / LPR;
@@ -218,11 +218,11 @@ __global__ void __launch_bounds__(kDecodeThreads, 1)
     float* s_l = s_m + G * TILE;       // [G][TILE]
     float* s_acc = s_l + G * TILE;     // [G][TILE][D]
 
-    const int split = blockIdx.x;
-    const int num_splits = gridDim.x;
+    const int split = blockIdx.y;
+    const int num_splits = gridDim.y;
     const int tiles = group / TILE;
-    const int bhk = blockIdx.y / tiles;
-    const int tq = blockIdx.y - bhk * tiles;
+    const int bhk = blockIdx.x / tiles;
+    const int tq = blockIdx.x - bhk * tiles;
     const int b = bhk / kvp.hkv;
     const int hk = bhk - b * kvp.hkv;
     const long long bhq0 = static_cast<long long>(b) * hq + hk * group + tq * TILE;
@@ -447,7 +447,7 @@ FlashAttentionError decode_typed(const T* Q, const T* K, const T* V, T* O, float
     S = (kv_len + chunk - 1) / chunk;  // no empty splits
     const float sl2 = scale * kLog2ef;
     if (S == 1) {
-        decode_split_kernel<T, D, true><<<dim3(1, BH), kDecodeThreads, 0, stream>>>(
+        decode_split_kernel<T, D, true><<<dim3(BH, 1), kDecodeThreads, 0, stream>>>(
             Q, K, V, O, L, nullptr, nullptr, kv_len, chunk, sl2);
         return cudaGetLastError() == cudaSuccess ? FlashAttentionError::SUCCESS
                                                  : FlashAttentionError::CUDA_ERROR;
@@ -460,7 +460,7 @@ FlashAttentionError decode_typed(const T* Q, const T* K, const T* V, T* O, float
     float* ws = static_cast<float*>(wsv);
     float* o_part = ws;
     float* l_part = ws + part_elems;
-    decode_split_kernel<T, D, false><<<dim3(S, BH), kDecodeThreads, 0, stream>>>(
+    decode_split_kernel<T, D, false><<<dim3(BH, S), kDecodeThreads, 0, stream>>>(
         Q, K, V, nullptr, nullptr, o_part, l_part, kv_len, chunk, sl2);
     cudaError_t e1 = cudaGetLastError();
     decode_combine_kernel<T, D><<<BH, 128, 0, stream>>>(o_part, l_part, O, L, S);
@@ -489,7 +489,7 @@ FlashAttentionError decode_group_typed(const T* Q, const DecodeKv<T>& kvp, T* O,
         auto k = decode_group_kernel<T, D, TILE, kPaged, true>;
         if (!ensure_smem_attr(reinterpret_cast<const void*>(k), static_cast<int>(smem)))
             return FlashAttentionError::CUDA_ERROR;
-        k<<<dim3(1, ctas_y), kDecodeThreads, smem, stream>>>(Q, kvp, O, L, nullptr, nullptr, hq,
+        k<<<dim3(ctas_y, 1), kDecodeThreads, smem, stream>>>(Q, kvp, O, L, nullptr, nullptr, hq,
                                                               group, chunk, sl2);
         return cudaGetLastError() == cudaSuccess ? FlashAttentionError::SUCCESS
                                                  : FlashAttentionError::CUDA_ERROR;
@@ -506,7 +506,7 @@ FlashAttentionError decode_group_typed(const T* Q, const DecodeKv<T>& kvp, T* O,
         workspace_free(wsv, stream);
         return FlashAttentionError::CUDA_ERROR;
     }
-    k<<<dim3(S, ctas_y), kDecodeThreads, smem, stream>>>(Q, kvp, nullptr, nullptr, o_part, l_part,
+    k<<<dim3(ctas_y, S), kDecodeThreads, smem, stream>>>(Q, kvp, nullptr, nullptr, o_part, l_part,
                                                           hq, group, chunk, sl2);
     cudaError_t e1 = cudaGetLastError();
     decode_combine_kernel<T, D><<<BHq, 128, 0, stream>>>(o_part, l_part, O, L, S);
@@ -633,9 +633,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
-    const int split = blockIdx.x;
-    const int tile = blockIdx.y % p.head_tiles;
-    const int bhk = blockIdx.y / p.head_tiles;
+    const int split = blockIdx.y;
+    const int tile = blockIdx.x % p.head_tiles;
+    const int bhk = blockIdx.x / p.head_tiles;
     const int b = bhk / p.hkv;
     const int hk = bhk - b * p.hkv;
     const int g0 = tile * kTcHeads;
@@ -923,8 +923,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 static_cast<T*>(p.O)[bhq * 128 + d] = DType<T>::from_float(outv);
                 if (d == 0) p.L[bhq] = lse;
             } else {
-                p.O_part[(bhq * gridDim.x + split) * 128 + d] = outv;
-                if (d == 0) p.L_part[bhq * gridDim.x + split] = lse;
+                p.O_part[(bhq * gridDim.y + split) * 128 + d] = outv;
+                if (d == 0) p.L_part[bhq * gridDim.y + split] = lse;
             }
         }
     }
@@ -946,7 +946,7 @@ FlashAttentionError decode_gqa_tc(const T* Q, const DecodeKv<T>& kvp, T* O, floa
     const int group = hq / kvp.hkv;
     const int tiles = (group + kTcHeads - 1) / kTcHeads;
     const long long units = static_cast<long long>(B) * kvp.hkv * tiles;
-    if (units > 65535) return FlashAttentionError::INVALID_DIMENSION;  // grid.y limit
+    if (units > 0x7fffffffLL) return FlashAttentionError::INVALID_DIMENSION;
     const int blocks_total = (max_len + kTcRows - 1) / kTcRows;
     int S = num_splits;
     if (S == 0) {
@@ -998,7 +998,7 @@ FlashAttentionError decode_gqa_tc(const T* Q, const DecodeKv<T>& kvp, T* O, floa
     prm.max_pages = kvp.max_pages;
     prm.num_pages = kvp.num_pages;
     prm.scale_log2 = scale * kLog2ef;
-    const dim3 grid(S, static_cast<unsigned>(units));
+    const dim3 grid(static_cast<unsigned>(units), S);
     if (S == 1) {
         auto k = decode_gqa_tc_kernel<T, kPaged, true>;
         if (!ensure_smem_attr(reinterpret_cast<const void*>(k), G::kSmemBytes))
@@ -1239,7 +1239,7 @@ FlashAttentionError decode_noalloc_typed(const __nv_bfloat16* Q, const __nv_bflo
     S = (kv_len + chunk - 1) / chunk;
     const float sl2 = scale * kLog2ef;
     if (S == 1) {
-        decode_split_kernel<T, D, true><<<dim3(1, BH), kDecodeThreads, 0, stream>>>(
+        decode_split_kernel<T, D, true><<<dim3(BH, 1), kDecodeThreads, 0, stream>>>(
             Q, K, V, O, L, nullptr, nullptr, kv_len, chunk, sl2);
         return cudaGetLastError() == cudaSuccess ? FlashAttentionError::SUCCESS
                                                  : FlashAttentionError::CUDA_ERROR;
@@ -1250,7 +1250,7 @@ FlashAttentionError decode_noalloc_typed(const __nv_bfloat16* Q, const __nv_bflo
     if (e != FlashAttentionError::SUCCESS) return e;
     float* o_part = scratch;
     float* l_part = scratch + static_cast<size_t>(BH) * S * D;
-    decode_split_kernel<T, D, false><<<dim3(S, BH), kDecodeThreads, 0, stream>>>(
+    decode_split_kernel<T, D, false><<<dim3(BH, S), kDecodeThreads, 0, stream>>>(
         Q, K, V, nullptr, nullptr, o_part, l_part, kv_len, chunk, sl2);
     cudaError_t e1 = cudaGetLastError();
     decode_combine_kernel<T, D><<<BH, 128, 0, stream>>>(o_part, l_part, O, L, S);
