@@ -128,8 +128,10 @@ __global__ void __launch_bounds__(384, 1)
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
     const int nq = (p.N + G::kBM - 1) / G::kBM;
-    const int qt = nq - 1 - static_cast<int>(blockIdx.x);  // heaviest first
-    const int bh = blockIdx.y;
+    // one-dimensional grid, query tile major: every (b,h)'s heaviest tile first
+    const int BHn = static_cast<int>(gridDim.x / nq);
+    const int qt = nq - 1 - static_cast<int>(blockIdx.x / BHn);
+    const int bh = static_cast<int>(blockIdx.x % BHn);
     const int q0 = qt * G::kBM;
     const int row_hi = min(q0 + G::kBM, p.N) - 1;
     const int nkv_all = (p.N + BN - 1) / BN;
@@ -479,14 +481,15 @@ FlashAttentionError fwd_f32_typed(const float* Q, const float* K, const float* V
     if (!ensure_smem_attr(reinterpret_cast<const void*>(kern), G::kSmemBytes))
         return FlashAttentionError::CUDA_ERROR;
     const int nq = (N + G::kBM - 1) / G::kBM;
-    if (BH > 65535) return FlashAttentionError::CUDA_ERROR;
+    if (static_cast<long long>(nq) * BH > 0x7fffffffLL) return FlashAttentionError::INVALID_DIMENSION;
     F32Params prm;
     prm.O = O;
     prm.L = L;
     prm.N = N;
     prm.causal = causal ? 1 : 0;
     prm.scale_log2 = fmaxf(scale * kLog2eF, 1e-30f);
-    kern<<<dim3(nq, BH), 384, G::kSmemBytes, stream>>>(mq, mk, mv, prm);
+    kern<<<dim3(static_cast<unsigned>(static_cast<long long>(nq) * BH)), 384, G::kSmemBytes,
+           stream>>>(mq, mk, mv, prm);
     return cudaGetLastError() == cudaSuccess ? FlashAttentionError::SUCCESS
                                              : FlashAttentionError::CUDA_ERROR;
 }

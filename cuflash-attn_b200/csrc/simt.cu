@@ -63,9 +63,11 @@ __global__ void __launch_bounds__(128)
                        int causal) {
     constexpr int E = D / 32;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int i = blockIdx.x * kRowsPerCta + warp;
+    // one-dimensional grid: (b,h) major, row block minor (no 65535 bound on b*h)
+    const int nrb = (N + kRowsPerCta - 1) / kRowsPerCta;
+    const long long bh = blockIdx.x / nrb;
+    const int i = static_cast<int>(blockIdx.x - bh * nrb) * kRowsPerCta + warp;
     if (i >= N) return;
-    const long long bh = blockIdx.y;
     const long long rowQ = (bh * N + i) * D;
     float q[E], g[E], acc[E];
 #pragma unroll
@@ -104,9 +106,10 @@ __global__ void __launch_bounds__(128)
                          T* __restrict__ dK, T* __restrict__ dV, int N, float scale, int causal) {
     constexpr int E = D / 32;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int j = blockIdx.x * kRowsPerCta + warp;
+    const int nrb = (N + kRowsPerCta - 1) / kRowsPerCta;
+    const long long bh = blockIdx.x / nrb;
+    const int j = static_cast<int>(blockIdx.x - bh * nrb) * kRowsPerCta + warp;
     if (j >= N) return;
-    const long long bh = blockIdx.y;
     const long long rowK = (bh * N + j) * D;
     float k[E], v[E], ak[E], av[E];
 #pragma unroll
@@ -149,24 +152,24 @@ FlashAttentionError bwd_simt_typed(const T* Q, const T* K, const T* V, const T* 
                                    const T* dO, T* dQ, T* dK, T* dV, int BH, int N, float scale,
                                    bool causal, cudaStream_t stream) {
     const long long rows = static_cast<long long>(BH) * N;
-    float* dvec = nullptr;
-    cudaError_t err = cudaMallocAsync(reinterpret_cast<void**>(&dvec), rows * sizeof(float), stream);
-    if (err != cudaSuccess) {
-        cudaGetLastError();
-        return err == cudaErrorMemoryAllocation ? FlashAttentionError::OUT_OF_MEMORY
-                                                : FlashAttentionError::CUDA_ERROR;
-    }
+    const long long nblk = static_cast<long long>((N + kRowsPerCta - 1) / kRowsPerCta) * BH;
+    if (nblk > 0x7fffffffLL) return FlashAttentionError::INVALID_DIMENSION;
+    void* ws = nullptr;
+    const FlashAttentionError werr =
+        workspace_alloc(&ws, static_cast<size_t>(rows) * sizeof(float), stream);
+    if (werr != FlashAttentionError::SUCCESS) return werr;
+    float* dvec = static_cast<float*>(ws);
     bwd_dvec_kernel<T, D><<<static_cast<unsigned>((rows * 32 + 127) / 128), 128, 0, stream>>>(
         O, dO, dvec, rows);
     cudaError_t e1 = cudaGetLastError();
-    dim3 grid((N + kRowsPerCta - 1) / kRowsPerCta, BH);
+    const dim3 grid(static_cast<unsigned>(nblk));
     bwd_dq_simt_kernel<T, D><<<grid, 32 * kRowsPerCta, 0, stream>>>(Q, K, V, L, dO, dvec, dQ, N,
                                                                     scale, causal ? 1 : 0);
     cudaError_t e2 = cudaGetLastError();
     bwd_dkdv_simt_kernel<T, D><<<grid, 32 * kRowsPerCta, 0, stream>>>(
         Q, K, V, L, dO, dvec, dK, dV, N, scale, causal ? 1 : 0);
     cudaError_t e3 = cudaGetLastError();
-    cudaFreeAsync(dvec, stream);
+    workspace_free(ws, stream);
     return (e1 == cudaSuccess && e2 == cudaSuccess && e3 == cudaSuccess)
                ? FlashAttentionError::SUCCESS
                : FlashAttentionError::CUDA_ERROR;
