@@ -160,12 +160,6 @@ FlashAttentionError launch_bwd_sm100(const T* Q, const T* K, const T* V, const T
                                      int H, int N, int D, float scale, bool causal,
                                      cudaStream_t stream);
 
-template <typename T>
-FlashAttentionError launch_bwd_simt(const T* Q, const T* K, const T* V, const T* O,
-                                    const float* L, const T* dO, T* dQ, T* dK, T* dV, int B,
-                                    int H, int N, int D, float scale, bool causal,
-                                    cudaStream_t stream);
-
 FlashAttentionError launch_fwd_f32(const float* Q, const float* K, const float* V, float* O,
                                    float* L, int B, int H, int N, int D, float scale, bool causal,
                                    cudaStream_t stream);
@@ -201,6 +195,7 @@ int fwd_sm100_status();
 int bwd_sm100_status();
 int dec_sm100_status();
 int f32_sm100_status();
+int bwd_f32_sm100_status();
 
 }  // namespace detail
 }  // namespace cuflash

@@ -72,29 +72,8 @@ struct F32Params {
     float scale_log2;
 };
 
-__device__ __forceinline__ float tf32_lo(float x) {
-    return x - __uint_as_float(__float_as_uint(x) & 0xFFFFE000u);
-}
-
-// fp32 K-major operand, k-step kk (8 elements = 32 bytes)
-__device__ __forceinline__ uint64_t f32_kdesc(uint32_t base, int kk, int cb_bytes) {
-    const uint32_t byte = static_cast<uint32_t>(kk) * 32u;
-    return sm100::make_smem_desc(base + (byte >> 7) * cb_bytes + (byte & 127u), 16, 1024,
-                                 sm100::kLayoutSw128);
-}
-
 __device__ __forceinline__ bool f32_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag) {
     return sm100::mbar_wait(bar, parity, abort_flag, &g_f32_status);
-}
-
-__device__ __forceinline__ void mma_tf32_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc,
-                                            uint32_t idesc, uint32_t accumulate) {
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "setp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::1.kind::tf32 [%0], [%1], %2, %3, p;\n\t}\n" ::"r"(d_tmem),
-        "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
-        : "memory");
 }
 
 template <int D>

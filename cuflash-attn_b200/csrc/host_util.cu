@@ -178,8 +178,11 @@ int read_and_clear_device_status() {
     const int b = bwd_sm100_status();
     const int c = f32_sm100_status();
     const int d = dec_sm100_status();
-    if (a < 0 || b < 0 || c < 0 || d < 0) return -1;
-    return a != 0 ? a : (b != 0 ? b : (c != 0 ? c : d));
+    const int e = bwd_f32_sm100_status();
+    if (a < 0 || b < 0 || c < 0 || d < 0 || e < 0) return -1;
+    for (const int v : {a, b, c, d, e})
+        if (v != 0) return v;
+    return 0;
 }
 
 }  // namespace detail

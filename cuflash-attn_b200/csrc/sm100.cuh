@@ -173,6 +173,17 @@ __device__ __forceinline__ void mma_tf32_ss(uint32_t d_tmem, uint64_t a_desc, ui
         : "memory");
 }
 
+// D(tmem) (+)= A(tmem) * B(smem desc), kind::tf32.
+__device__ __forceinline__ void mma_tf32_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc,
+                                            uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::tf32 [%0], [%1], %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+        "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
 // ------------------------------------------------------------ descriptors
 
 // Swizzle modes of the tcgen05 shared-memory matrix descriptor (bits 61-63).
@@ -297,6 +308,22 @@ __device__ __forceinline__ float ex2_approx(float x) {
     float y;
     asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
     return y;
+}
+
+// ------------------------------------------------------------- 3xTF32
+// A kind::tf32 MMA reads the upper 19 bits of each fp32 operand word, so a
+// raw fp32 tile is its own "hi" part and lo = x - hi is exact in fp32; the
+// product a*b is carried as hi(a)hi(b) + hi(a)lo(b) + lo(a)hi(b).
+
+__device__ __forceinline__ float tf32_lo(float x) {
+    return x - __uint_as_float(__float_as_uint(x) & 0xFFFFE000u);
+}
+
+// fp32 K-major operand stored as 128-byte swizzled column blocks of 32
+// elements (cb_bytes apart); descriptor of k-step kk (8 elements = 32 bytes).
+__device__ __forceinline__ uint64_t f32_kdesc(uint32_t base, int kk, int cb_bytes) {
+    const uint32_t byte = static_cast<uint32_t>(kk) * 32u;
+    return make_smem_desc(base + (byte >> 7) * cb_bytes + (byte & 127u), 16, 1024, kLayoutSw128);
 }
 
 }  // namespace sm100
