@@ -20,19 +20,25 @@
 // (A operands), one fp32 accumulator and the per-block S, dP, dS, dS_lo
 // columns, not a second accumulator.
 //
+// Shared memory: the resident tiles F1 (F2), then three rings of streamed
+// tiles, each slot a tile and its lo part:
+//   A1  S1 (S^T's B operand: Q for dV/dK, K for dQ)
+//   A2  S2 (dP's B operand: dO for dK, V for dQ)
+//   T   the accumulation's B operand, transposed in place from its own TMA
+//       copy (dO^T for dV, Q^T for dK, K^T for dQ): every tf32 operand is
+//       K-major (an MN-major tf32 operand would need the 32-byte-atom swizzle)
 // Roles (384 threads):
-//   warp 0      TMA producer: the resident tiles F1 (and F2) once, then per
-//               block the streamed tiles S1, S2 into ring A
+//   warp 0      TMA producer of F1, F2, A1, A2
 //   warp 1      TMEM allocator, MMA issuer
+//   warp 2      TMA producer of T
 //   warps 4-7   element-wise stage (one thread per resident row) and the
 //               epilogue
-//   warps 8-11  splitter: lo parts of F1/F2 into TMEM; per block the lo
-//               parts of S1 (and S2) in place of the ring A layout, and the
-//               transposed operand of the accumulation (dO^T for dV, Q^T for
-//               dK, K^T for dQ) with its lo part into ring T, plus the
-//               per-column scalars -L*log2(e) and D
-// Every tf32 operand is K-major (an MN-major tf32 operand would need the
-// 32-byte-atom swizzle), hence the transposed copies.
+//   warps 8-11  lo parts of F1/F2 into TMEM, then two splitter groups:
+//               warps 8-9 write the lo parts of A1/A2 (element-wise, the
+//               swizzled layout is kept), warps 10-11 transpose T and load
+//               the per-column scalars -L*log2(e) and D
+// The rings are decoupled: a slot of A1 is refilled as soon as its S^T MMAs
+// have read it, whatever the transposes or the accumulation are doing.
 
 #include <cmath>
 
@@ -56,43 +62,50 @@ struct BF32Geom {
     static constexpr int kBS = (D == 128) ? 32 : 64;
     static constexpr int kFBytes = kBM * D * 4;
     static constexpr int kFCb = kBM * 128;
-    static constexpr int kSBytes = kBS * D * 4;     // streamed tile [kBS][D]
-    static constexpr int kSCb = kBS * 128;
-    static constexpr int kTBytes = D * kBS * 4;     // transposed tile [D][kBS]
-    static constexpr int kTCb = D * 128;
+    static constexpr int kSBytes = kBS * D * 4;  // streamed tile [kBS][D], or its transpose
+    static constexpr int kSCb = kBS * 128;       // column block of [kBS][D] (ring T, raw)
+    static constexpr int kACb = 2 * kBS * 128;   // ring A column block: kBS rows, kBS lo rows
+    static constexpr int kTCb = D * 128;         // column block of [D][kBS]
     static constexpr int kNumF = kTwo ? 2 : 1;
-    // ring A: S1, S1_lo, S2 (raw for dV), S2_lo (dK, dQ)
-    static constexpr int kATiles = kTwo ? 4 : 3;
-    static constexpr int kABytes = kATiles * kSBytes;
-    static constexpr int kTStageBytes = 2 * kTBytes;  // T, T_lo
-    static constexpr int kTileBudget = 232448 - 2048;
     static constexpr int kFTotal = kNumF * kFBytes;
-    static constexpr int kStagesA = (kFTotal + 2 * kABytes + kTStageBytes <= kTileBudget) ? 2 : 1;
-    static constexpr int kStagesT =
-        (kFTotal + kStagesA * kABytes + 2 * kTStageBytes <= kTileBudget) ? 2 : 1;
+    static constexpr int kPair = 2 * kSBytes;  // a ring slot: tile + lo part
+    static constexpr int kBudget = 232448 - 2048;
+    static constexpr int kRings = kTwo ? 3 : 2;
+    static constexpr int kPairsFit = (kBudget - kFTotal) / kPair;
+    // one slot per ring, then a second slot for A1, A2, T in that order
+    static constexpr int kExtra =
+        kPairsFit - kRings < kRings ? kPairsFit - kRings : kRings;
+    static constexpr int kStagesA1 = 1 + (kExtra >= 1 ? 1 : 0);
+    static constexpr int kStagesA2 = kTwo ? 1 + (kExtra >= 2 ? 1 : 0) : 0;
+    static constexpr int kStagesT = 1 + (kExtra >= kRings ? 1 : 0);
     static constexpr int kOffF = 0;
-    static constexpr int kOffA = kFTotal;
-    static constexpr int kOffT = kOffA + kStagesA * kABytes;
-    static constexpr int kOffSc = kOffT + kStagesT * kTStageBytes;  // [kStagesT][2][kBS] floats
+    static constexpr int kOffA1 = kFTotal;
+    static constexpr int kOffA2 = kOffA1 + kStagesA1 * kPair;
+    static constexpr int kOffT = kOffA2 + kStagesA2 * kPair;
+    static constexpr int kOffSc = kOffT + kStagesT * kPair;  // [kStagesT][2][kBS] floats
     static constexpr int kOffBar = kOffSc + kStagesT * 2 * kBS * 4;
-    // bar_f, bar_flo, fullA/splitA/emptyA [kStagesA], splitT/emptyT [kStagesT],
-    // bar_x [2], bar_w [2], bar_done
-    static constexpr int kNumBars = 2 + 3 * kStagesA + 2 * kStagesT + 2 + 2 + 1;
+    // bar_f, bar_flo, {full, split, empty} x (A1, A2, T slots), bar_x [2],
+    // bar_w [2], bar_done
+    static constexpr int kNumBars = 2 + 3 * (kStagesA1 + kStagesA2 + kStagesT) + 5;
     static constexpr int kUsed = kOffBar + kNumBars * 8 + 16;
     // at least 116 KB so that one CTA (and its 512 TMEM columns) owns the SM
     static constexpr int kSmemBytes = kUsed > 118784 ? kUsed : 118784;
-    static_assert(kUsed <= 232448, "shared memory budget");
-    // TMEM columns
+    static_assert(kExtra >= 0 && kUsed <= 232448, "shared memory budget");
+    // TMEM columns.  A product of the resident tile with [S; S_lo] occupies
+    // 2 kBS columns: F S^T, then F S_lo^T + F_lo S^T; its value is their
+    // sum.  The element-wise stage overwrites the two halves of X with W
+    // (P for dV, dS for dK / dQ) and W_lo, the A operands of the accumulation.
     static constexpr int kXBufs = kTwo ? 1 : 2;
     static constexpr int kColF1lo = 0;
     static constexpr int kColF2lo = D;  // dK, dQ
     static constexpr int kColAcc = kNumF * D;
-    static constexpr int kColX = kColAcc + D;           // [kXBufs][kBS]; dV: P in place
-    static constexpr int kColY = kColX + kXBufs * kBS;  // dK, dQ: dP
-    static constexpr int kColW = kTwo ? kColY + kBS : kColX;          // dS (dV: P = X)
-    static constexpr int kColWlo = kTwo ? kColW + kBS : kColY;        // [kXBufs][kBS]
-    static constexpr int kColEnd = kColWlo + kXBufs * kBS;
+    static constexpr int kColX = kColAcc + D;               // [kXBufs][2 kBS]
+    static constexpr int kColY = kColX + kXBufs * 2 * kBS;  // dK, dQ: dP [2 kBS]
+    static constexpr int kColEnd = kColY + (kTwo ? 2 * kBS : 0);
     static_assert(kColEnd <= 512, "TMEM budget");
+    // 4x4 blocks of the transposed tile per thread of the 64-thread group
+    static constexpr int kTBlocks = (kBS / 4) * (D / 4) / 64;
+    static_assert(kTBlocks * 64 == (kBS / 4) * (D / 4), "transpose split");
 };
 
 struct BF32Params {
@@ -110,67 +123,52 @@ __device__ __forceinline__ bool bf32_wait(uint64_t* bar, uint32_t parity,
     return sm100::mbar_wait(bar, parity, abort_flag, &g_bf32_status);
 }
 
-// Splitter barrier among warps 8-11.
-__device__ __forceinline__ void splitter_sync() {
-    asm volatile("bar.sync 1, 128;" ::: "memory");
+// Barrier of one 64-thread splitter group (id 1: warps 8-9, id 2: 10-11).
+template <int kId>
+__device__ __forceinline__ void group_sync() {
+    asm volatile("bar.sync %0, 64;" ::"n"(kId) : "memory");
 }
 
-// Same barrier with an AND vote, so that all splitter threads take the same
-// branch after a wait (the named barrier must never miss a participant).
-__device__ __forceinline__ bool splitter_all(bool v) {
+// Same barrier with an AND vote, so that all threads of a group take the
+// same branch after a wait (a named barrier must never miss a participant).
+template <int kId>
+__device__ __forceinline__ bool group_all(bool v) {
     uint32_t r;
     asm volatile(
         "{\n\t.reg .pred p, q;\n\t"
         "setp.ne.u32 q, %1, 0;\n\t"
-        "bar.red.and.pred p, 1, 128, q;\n\t"
+        "bar.red.and.pred p, %2, 64, q;\n\t"
         "selp.u32 %0, 1, 0, p;\n\t}\n"
         : "=r"(r)
-        : "r"(v ? 1u : 0u)
+        : "r"(v ? 1u : 0u), "n"(kId)
         : "memory");
     return r != 0;
 }
 
-// raw [R][D] (128-byte swizzled column blocks of R rows) -> hi, lo [D][R]
-// (128-byte swizzled column blocks of D rows): 4x4 blocks through registers.
-template <int R, int D>
-__device__ __forceinline__ void split_transpose(const uint8_t* raw, uint8_t* thi, uint8_t* tlo,
-                                                int t) {
-    using sm100::tf32_lo;
-    for (int blk = t; blk < (R / 4) * (D / 4); blk += 128) {
-        const int r0 = (blk % (R / 4)) * 4;
-        const int d0 = (blk / (R / 4)) * 4;
-        float4 rr[4];
-#pragma unroll
-        for (int a = 0; a < 4; ++a) {
-            const int r = r0 + a;
-            rr[a] = *reinterpret_cast<const float4*>(raw + (d0 >> 5) * (R * 128) + r * 128 +
-                                                     ((((d0 & 31) >> 2) ^ (r & 7)) << 4));
-        }
-        const float cols[4][4] = {{rr[0].x, rr[1].x, rr[2].x, rr[3].x},
-                                  {rr[0].y, rr[1].y, rr[2].y, rr[3].y},
-                                  {rr[0].z, rr[1].z, rr[2].z, rr[3].z},
-                                  {rr[0].w, rr[1].w, rr[2].w, rr[3].w}};
-#pragma unroll
-        for (int b = 0; b < 4; ++b) {
-            const int d = d0 + b;
-            const int off =
-                (r0 >> 5) * (D * 128) + d * 128 + ((((r0 & 31) >> 2) ^ (d & 7)) << 4);
-            *reinterpret_cast<float4*>(thi + off) =
-                make_float4(cols[b][0], cols[b][1], cols[b][2], cols[b][3]);
-            *reinterpret_cast<float4*>(tlo + off) = make_float4(
-                tf32_lo(cols[b][0]), tf32_lo(cols[b][1]), tf32_lo(cols[b][2]), tf32_lo(cols[b][3]));
-        }
-    }
+// 4x4 block `blk` of an [R][D] tile -> (row block i, column block j).  Eight
+// consecutive threads walk one diagonal of an 8x8 super-block, so the eight
+// 16-byte chunks of a shared-memory phase land in eight different chunk
+// columns of the 128-byte swizzle, for the reads of the [R][D] tile and for
+// the writes of its [D][R] transpose alike (no bank conflicts).
+template <int R>
+__device__ __forceinline__ void diag_block(int blk, int& i, int& j) {
+    const int k = blk & 7;
+    const int g = blk >> 3;
+    const int st = g >> 3, s = g & 7;
+    i = (st % (R / 32)) * 8 + k;
+    j = (st / (R / 32)) * 8 + ((k + s) & 7);
 }
 
-// lo parts over a whole swizzled tile (element-wise, so the layout is kept).
-__device__ __forceinline__ void split_lo(const uint8_t* hi, uint8_t* lo, int bytes, int t) {
+// lo parts of a ring A slot: every 128-byte column block holds R rows of the
+// tile, then the R rows of its lo part (element-wise: same swizzle phase).
+template <int R, int D>
+__device__ __forceinline__ void split_lo_stacked(uint8_t* slot, int t) {
     using sm100::tf32_lo;
-    const float4* h4 = reinterpret_cast<const float4*>(hi);
-    float4* l4 = reinterpret_cast<float4*>(lo);
-    for (int i = t; i < bytes / 16; i += 128) {
-        const float4 a = h4[i];
-        l4[i] = make_float4(tf32_lo(a.x), tf32_lo(a.y), tf32_lo(a.z), tf32_lo(a.w));
+    float4* s4 = reinterpret_cast<float4*>(slot);
+    for (int i = t; i < R * D / 4; i += 64) {
+        const int src = (i / (R * 8)) * (R * 16) + i % (R * 8);
+        const float4 a = s4[src];
+        s4[src + R * 8] = make_float4(tf32_lo(a.x), tf32_lo(a.y), tf32_lo(a.z), tf32_lo(a.w));
     }
 }
 
@@ -215,16 +213,20 @@ __global__ void __launch_bounds__(384, 1)
     uint64_t* bars = reinterpret_cast<uint64_t*>(sptr + G::kOffBar);
     uint64_t* bar_f = bars;
     uint64_t* bar_flo = bars + 1;
-    uint64_t* fullA = bars + 2;
-    uint64_t* splitA = fullA + G::kStagesA;
-    uint64_t* emptyA = splitA + G::kStagesA;
-    uint64_t* splitT = emptyA + G::kStagesA;
+    uint64_t* fullA1 = bars + 2;
+    uint64_t* splitA1 = fullA1 + G::kStagesA1;
+    uint64_t* emptyA1 = splitA1 + G::kStagesA1;
+    uint64_t* fullA2 = emptyA1 + G::kStagesA1;
+    uint64_t* splitA2 = fullA2 + G::kStagesA2;
+    uint64_t* emptyA2 = splitA2 + G::kStagesA2;
+    uint64_t* fullT = emptyA2 + G::kStagesA2;
+    uint64_t* splitT = fullT + G::kStagesT;
     uint64_t* emptyT = splitT + G::kStagesT;
-    uint64_t* bar_x = emptyT + G::kStagesT;  // [2]
     // dV keeps two blocks in flight (S^T of the next block is issued before
     // the current accumulation), so its X and W barriers are double: a
     // waiter can then never fall two phases behind on one barrier
-    uint64_t* bar_w = bar_x + 2;  // [2]
+    uint64_t* bar_x = emptyT + G::kStagesT;  // [2]
+    uint64_t* bar_w = bar_x + 2;             // [2]
     uint64_t* bar_done = bar_w + 2;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar_done + 1);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
@@ -255,13 +257,19 @@ __global__ void __launch_bounds__(384, 1)
     if (threadIdx.x == 0) {
         mbar_init(bar_f, 1);
         mbar_init(bar_flo, 128);
-        for (int s = 0; s < G::kStagesA; ++s) {
-            mbar_init(fullA + s, 1);
-            mbar_init(splitA + s, 128);
-            mbar_init(emptyA + s, 2);  // the MMA commit and the splitter
+        for (int s = 0; s < G::kStagesA1; ++s) {
+            mbar_init(fullA1 + s, 1);
+            mbar_init(splitA1 + s, 64);
+            mbar_init(emptyA1 + s, 1);
+        }
+        for (int s = 0; s < G::kStagesA2; ++s) {
+            mbar_init(fullA2 + s, 1);
+            mbar_init(splitA2 + s, 64);
+            mbar_init(emptyA2 + s, 1);
         }
         for (int s = 0; s < G::kStagesT; ++s) {
-            mbar_init(splitT + s, 128);
+            mbar_init(fullT + s, 1);
+            mbar_init(splitT + s, 64);
             mbar_init(emptyT + s, 1);
         }
         mbar_init(bar_x, 1);
@@ -282,12 +290,12 @@ __global__ void __launch_bounds__(384, 1)
     const uint32_t tmem = *tmem_slot;
 
     if (warp == 0) {
-        // ------------------------------------------------ TMA producer
+        // ------------------------------------------------ TMA producer: F, A1, A2
         if (lane == 0 && n > 0) {
             prefetch_tmap(&tmF1);
             if (kTwo) prefetch_tmap(&tmF2);
             prefetch_tmap(&tmS1);
-            prefetch_tmap(&tmS2);
+            if (kTwo) prefetch_tmap(&tmS2);
             mbar_arrive_expect_tx(bar_f, G::kFTotal);
             for (int cb = 0; cb < D / 32; ++cb) {
                 tma_load_3d(sptr + G::kOffF + cb * G::kFCb, &tmF1, bar_f, cb * 32, f0, bh);
@@ -295,94 +303,126 @@ __global__ void __launch_bounds__(384, 1)
                     tma_load_3d(sptr + G::kOffF + G::kFBytes + cb * G::kFCb, &tmF2, bar_f,
                                 cb * 32, f0, bh);
             }
-            int issued = 0;
+            int issued1 = 0, issued2 = 0;
             for (int t = 0; t < n; ++t) {
-                const int s = t % G::kStagesA;
-                if (t >= G::kStagesA &&
-                    !bf32_wait(emptyA + s, ((t / G::kStagesA) & 1) ^ 1, abort_flag))
-                    break;
-                uint8_t* st = sptr + G::kOffA + s * G::kABytes;
                 const int row = (jb + t) * BS;
-                mbar_arrive_expect_tx(fullA + s, 2 * G::kSBytes);
-                for (int cb = 0; cb < D / 32; ++cb) {
-                    tma_load_3d(st + cb * G::kSCb, &tmS1, fullA + s, cb * 32, row, bh);
-                    tma_load_3d(st + 2 * G::kSBytes + cb * G::kSCb, &tmS2, fullA + s, cb * 32, row,
-                                bh);
+                const int s1 = t % G::kStagesA1;
+                if (t >= G::kStagesA1 &&
+                    !bf32_wait(emptyA1 + s1, ((t / G::kStagesA1) & 1) ^ 1, abort_flag))
+                    break;
+                uint8_t* a1 = sptr + G::kOffA1 + s1 * G::kPair;
+                mbar_arrive_expect_tx(fullA1 + s1, G::kSBytes);
+                for (int cb = 0; cb < D / 32; ++cb)
+                    tma_load_3d(a1 + cb * G::kACb, &tmS1, fullA1 + s1, cb * 32, row, bh);
+                ++issued1;
+                if constexpr (kTwo) {
+                    const int s2 = t % G::kStagesA2;
+                    if (t >= G::kStagesA2 &&
+                        !bf32_wait(emptyA2 + s2, ((t / G::kStagesA2) & 1) ^ 1, abort_flag))
+                        break;
+                    uint8_t* a2 = sptr + G::kOffA2 + s2 * G::kPair;
+                    mbar_arrive_expect_tx(fullA2 + s2, G::kSBytes);
+                    for (int cb = 0; cb < D / 32; ++cb)
+                        tma_load_3d(a2 + cb * G::kACb, &tmS2, fullA2 + s2, cb * 32, row, bh);
+                    ++issued2;
                 }
-                ++issued;
             }
             // no TMA may be in flight when the CTA exits
             volatile int never = 0;
             mbar_wait(bar_f, 0, &never, &g_bf32_status);
-            for (int t = max(0, issued - G::kStagesA); t < issued; ++t)
-                mbar_wait(fullA + t % G::kStagesA, (t / G::kStagesA) & 1, &never, &g_bf32_status);
+            for (int t = max(0, issued1 - G::kStagesA1); t < issued1; ++t)
+                mbar_wait(fullA1 + t % G::kStagesA1, (t / G::kStagesA1) & 1, &never,
+                          &g_bf32_status);
+            if constexpr (kTwo)
+                for (int t = max(0, issued2 - G::kStagesA2); t < issued2; ++t)
+                    mbar_wait(fullA2 + t % G::kStagesA2, (t / G::kStagesA2) & 1, &never,
+                              &g_bf32_status);
+        }
+    } else if (warp == 2) {
+        // ------------------------------------------------ TMA producer: T
+        if (lane == 0 && n > 0) {
+            const CUtensorMap* src = kTwo ? &tmS1 : &tmS2;
+            prefetch_tmap(src);
+            int issued = 0;
+            for (int t = 0; t < n; ++t) {
+                const int s = t % G::kStagesT;
+                if (t >= G::kStagesT &&
+                    !bf32_wait(emptyT + s, ((t / G::kStagesT) & 1) ^ 1, abort_flag))
+                    break;
+                uint8_t* tt = sptr + G::kOffT + s * G::kPair;
+                mbar_arrive_expect_tx(fullT + s, G::kSBytes);
+                for (int cb = 0; cb < D / 32; ++cb)
+                    tma_load_3d(tt + cb * G::kSCb, src, fullT + s, cb * 32, (jb + t) * BS, bh);
+                ++issued;
+            }
+            volatile int never = 0;
+            for (int t = max(0, issued - G::kStagesT); t < issued; ++t)
+                mbar_wait(fullT + t % G::kStagesT, (t / G::kStagesT) & 1, &never, &g_bf32_status);
         }
     } else if (warp == 1) {
         // ------------------------------------------------ MMA issuer
         if (lane == 0) {
-            constexpr uint32_t idesc_x = make_idesc(kFmtTF32, 128, BS, false, false);
+            constexpr uint32_t idesc_x1 = make_idesc(kFmtTF32, 128, BS, false, false);
+            constexpr uint32_t idesc_x2 = make_idesc(kFmtTF32, 128, 2 * BS, false, false);
             constexpr uint32_t idesc_acc = make_idesc(kFmtTF32, 128, D, false, false);
             const uint32_t sF1 = sbase + G::kOffF;
             const uint32_t sF2 = sF1 + G::kFBytes;
-            // one 3xTF32 product of a resident tile (A) with a streamed tile (B)
-            auto product = [&](uint32_t d_t, uint32_t sF, uint32_t f_lo, uint32_t sS,
-                               uint32_t sSlo) {
+            // one 3xTF32 product of a resident tile (A) with a ring A slot:
+            // F [S; S_lo]^T in one N = 2 kBS MMA per k-step (a tf32 MMA costs
+            // about the same below N = 64 as at N = 64), then F_lo S^T into
+            // the second half
+            auto product = [&](uint32_t d_t, uint32_t sF, uint32_t f_lo, uint32_t slot) {
 #pragma unroll
                 for (int kk = 0; kk < D / 8; ++kk)
-                    mma_tf32_ss(d_t, f32_kdesc(sF, kk, G::kFCb), f32_kdesc(sS, kk, G::kSCb), idesc_x,
-                                kk > 0 ? 1u : 0u);
+                    mma_tf32_ss(d_t, f32_kdesc(sF, kk, G::kFCb), f32_kdesc(slot, kk, G::kACb),
+                                idesc_x2, kk > 0 ? 1u : 0u);
 #pragma unroll
                 for (int kk = 0; kk < D / 8; ++kk)
-                    mma_tf32_ss(d_t, f32_kdesc(sF, kk, G::kFCb), f32_kdesc(sSlo, kk, G::kSCb),
-                                idesc_x, 1u);
-#pragma unroll
-                for (int kk = 0; kk < D / 8; ++kk)
-                    mma_tf32_ts(d_t, f_lo + kk * 8, f32_kdesc(sS, kk, G::kSCb), idesc_x, 1u);
+                    mma_tf32_ts(d_t + BS, f_lo + kk * 8, f32_kdesc(slot, kk, G::kACb), idesc_x1,
+                                1u);
             };
-            auto a_ready = [&](int t) {
-                const int s = t % G::kStagesA;
-                const uint32_t ph = (t / G::kStagesA) & 1;
-                return bf32_wait(fullA + s, ph, abort_flag) && bf32_wait(splitA + s, ph, abort_flag);
+            auto ready = [&](uint64_t* full, uint64_t* split, int stages, int t) {
+                const int s = t % stages;
+                const uint32_t ph = (t / stages) & 1;
+                return bf32_wait(full + s, ph, abort_flag) && bf32_wait(split + s, ph, abort_flag);
             };
-            auto issue_x = [&](int t) {
-                const int s = t % G::kStagesA;
-                const uint32_t sS1 = sbase + G::kOffA + s * G::kABytes;
-                product(tmem + G::kColX + (kTwo ? 0 : (t & 1) * BS), sF1, tmem + G::kColF1lo, sS1,
-                        sS1 + G::kSBytes);
-                if constexpr (kTwo)
-                    product(tmem + G::kColY, sF2, tmem + G::kColF2lo, sS1 + 2 * G::kSBytes,
-                            sS1 + 3 * G::kSBytes);
+            // S^T (S) of block t, then (dK, dQ) dP^T (dP); X and Y complete on bar_x
+            auto issue_x = [&](int t) -> bool {
+                if (!ready(fullA1, splitA1, G::kStagesA1, t)) return false;
+                tc_fence_after();
+                const int s1 = t % G::kStagesA1;
+                product(tmem + G::kColX + (kTwo ? 0 : (t & 1) * 2 * BS), sF1, tmem + G::kColF1lo,
+                        sbase + G::kOffA1 + s1 * G::kPair);
+                tc_commit(emptyA1 + s1);
+                if constexpr (kTwo) {
+                    if (!ready(fullA2, splitA2, G::kStagesA2, t)) return false;
+                    tc_fence_after();
+                    const int s2 = t % G::kStagesA2;
+                    product(tmem + G::kColY, sF2, tmem + G::kColF2lo,
+                            sbase + G::kOffA2 + s2 * G::kPair);
+                    tc_commit(emptyA2 + s2);
+                }
                 tc_commit(bar_x + (kTwo ? 0 : (t & 1)));
-                tc_commit(emptyA + s);
+                return true;
             };
             bool ok = n > 0 && bf32_wait(bar_f, 0, abort_flag) && bf32_wait(bar_flo, 0, abort_flag);
-            if (ok && !kTwo) {  // dV: S^T of the next block runs behind the current softmax
-                ok = a_ready(0);
-                if (ok) {
-                    tc_fence_after();
-                    issue_x(0);
-                }
-            }
+            if (ok && !kTwo) ok = issue_x(0);  // dV: S^T(t+1) runs behind the softmax of t
             for (int t = 0; ok && t < n; ++t) {
                 if constexpr (kTwo) {
-                    if (!a_ready(t)) break;
-                    tc_fence_after();
-                    issue_x(t);
+                    if (!issue_x(t)) break;
                 } else if (t + 1 < n) {
-                    if (!a_ready(t + 1)) break;
-                    tc_fence_after();
-                    issue_x(t + 1);
+                    if (!issue_x(t + 1)) break;
                 }
                 const int sT = t % G::kStagesT;
                 const uint32_t wpar = kTwo ? (t & 1) : ((t >> 1) & 1);
                 if (!bf32_wait(bar_w + (kTwo ? 0 : (t & 1)), wpar, abort_flag) ||
-                    !bf32_wait(splitT + sT, (t / G::kStagesT) & 1, abort_flag))
+                    !ready(fullT, splitT, G::kStagesT, t))
                     break;
                 tc_fence_after();
-                const uint32_t sTh = sbase + G::kOffT + sT * G::kTStageBytes;
-                const uint32_t sTl = sTh + G::kTBytes;
-                const uint32_t a_w = tmem + G::kColW + (kTwo ? 0 : (t & 1) * BS);
-                const uint32_t a_wlo = tmem + G::kColWlo + (kTwo ? 0 : (t & 1) * BS);
+                const uint32_t sTh = sbase + G::kOffT + sT * G::kPair;
+                const uint32_t sTl = sTh + G::kSBytes;
+                const uint32_t a_w = tmem + G::kColX + (kTwo ? 0 : (t & 1) * 2 * BS);
+                const uint32_t a_wlo = a_w + BS;
                 const uint32_t d_acc = tmem + G::kColAcc;
 #pragma unroll
                 for (int kk = 0; kk < BS / 8; ++kk)
@@ -429,29 +469,33 @@ __global__ void __launch_bounds__(384, 1)
             tc_fence_after();
             const float* sc = sc_all + sT * 2 * BS;  // [-L log2e][D] per column
             const int col0 = (jb + t) * BS;
+            const uint32_t t_x = tmem + lane_addr + G::kColX + xb * 2 * BS;
+            const uint32_t t_y = tmem + lane_addr + G::kColY;
 #pragma unroll
-            for (int ch = 0; ch < BS / 32; ++ch) {
-                uint32_t xv[32];
-                uint32_t yv[32];
-                tmem_ld_x32(tmem + lane_addr + G::kColX + xb * BS + ch * 32, xv);
-                if constexpr (kTwo) tmem_ld_x32(tmem + lane_addr + G::kColY + ch * 32, yv);
+            for (int ch = 0; ch < BS / 16; ++ch) {
+                uint32_t xh[16], xl[16], yh[16], yl[16];
+                tmem_ld2_x16_nw(t_x + ch * 16, xh, t_x + BS + ch * 16, xl);
+                if constexpr (kTwo) tmem_ld2_x16_nw(t_y + ch * 16, yh, t_y + BS + ch * 16, yl);
+                tmem_wait_ld2_x16(xh, xl);
+                if constexpr (kTwo) tmem_wait_ld2_x16(yh, yl);
 #pragma unroll
-                for (int i = 0; i < 32; ++i) {
-                    const int col = col0 + ch * 32 + i;
+                for (int i = 0; i < 16; ++i) {
+                    const int col = col0 + ch * 16 + i;
                     bool vis = col < N;
                     if (p.causal) vis = vis && (kMode == kModeDQ ? col <= row : col >= row);
-                    const float nl2 = (kMode == kModeDQ) ? nl2_row : sc[ch * 32 + i];
-                    const float pr = vis ? ex2_approx(fmaf(__uint_as_float(xv[i]), c, nl2)) : 0.f;
+                    const float nl2 = (kMode == kModeDQ) ? nl2_row : sc[ch * 16 + i];
+                    const float x = __uint_as_float(xh[i]) + __uint_as_float(xl[i]);
+                    const float pr = vis ? ex2_approx(fmaf(x, c, nl2)) : 0.f;
                     float w = pr;
                     if constexpr (kTwo) {
-                        const float dv = (kMode == kModeDQ) ? dv_row : sc[BS + ch * 32 + i];
-                        w = pr * (__uint_as_float(yv[i]) - dv);
+                        const float dv = (kMode == kModeDQ) ? dv_row : sc[BS + ch * 16 + i];
+                        w = pr * (__uint_as_float(yh[i]) + __uint_as_float(yl[i]) - dv);
                     }
-                    xv[i] = __float_as_uint(w);
-                    yv[i] = __float_as_uint(tf32_lo(w));
+                    xh[i] = __float_as_uint(w);
+                    xl[i] = __float_as_uint(tf32_lo(w));
                 }
-                tmem_st_x32_nw(tmem + lane_addr + G::kColW + xb * BS + ch * 32, xv);
-                tmem_st_x32_nw(tmem + lane_addr + G::kColWlo + xb * BS + ch * 32, yv);
+                tmem_st_x16_nw(t_x + ch * 16, xh);
+                tmem_st_x16_nw(t_x + BS + ch * 16, xl);
             }
             tmem_wait_st();
             tc_fence_before();
@@ -483,12 +527,15 @@ __global__ void __launch_bounds__(384, 1)
             }
         }
     } else if (warp >= 8) {
-        // ------------------------------------------------ splitter
-        const int t0 = threadIdx.x - 256;  // 0..127
+        // ------------------------------------------------ lo parts / transposes
         const int wq = warp & 3;
         const int r = wq * 32 + lane;
-        bool ok = splitter_all(n > 0 && bf32_wait(bar_f, 0, abort_flag));
+        const bool group_t = warp >= 10;
+        const int tg = (threadIdx.x - 256) & 63;  // thread index within the group
+        bool ok = n > 0 && bf32_wait(bar_f, 0, abort_flag);
+        ok = group_t ? group_all<2>(ok) : group_all<1>(ok);
         if (ok) {
+            // lo parts of the resident tiles, rows of this warp's TMEM lanes
             const uint32_t t_lane = tmem + (static_cast<uint32_t>(wq * 32) << 16);
             split_rows_to_tmem<D>(sptr + G::kOffF, t_lane + G::kColF1lo, r);
             if constexpr (kTwo)
@@ -496,33 +543,83 @@ __global__ void __launch_bounds__(384, 1)
             tc_fence_before();
             mbar_arrive(bar_flo);
         }
-        const size_t rowbase = static_cast<size_t>(bh) * N;
-        for (int t = 0; ok && t < n; ++t) {
-            const int s = t % G::kStagesA;
-            if (!splitter_all(bf32_wait(fullA + s, (t / G::kStagesA) & 1, abort_flag))) break;
-            uint8_t* st = sptr + G::kOffA + s * G::kABytes;
-            split_lo(st, st + G::kSBytes, G::kSBytes, t0);
-            if constexpr (kTwo) split_lo(st + 2 * G::kSBytes, st + 3 * G::kSBytes, G::kSBytes, t0);
-            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-            mbar_arrive(splitA + s);
-            const int sT = t % G::kStagesT;
-            if (!splitter_all(t < G::kStagesT ||
-                              bf32_wait(emptyT + sT, ((t / G::kStagesT) & 1) ^ 1, abort_flag)))
-                break;
-            uint8_t* tt = sptr + G::kOffT + sT * G::kTStageBytes;
-            // dV: dO^T (the raw S2); dK, dQ: the S1 operand transposed
-            split_transpose<BS, D>(kTwo ? st : st + 2 * G::kSBytes, tt, tt + G::kTBytes, t0);
-            if (kMode != kModeDQ && t0 < BS) {
-                const int col = (jb + t) * BS + t0;
-                float* sc = sc_all + sT * 2 * BS;
-                sc[t0] = col < N ? -p.L[rowbase + col] * kLog2eB : 0.f;
-                sc[BS + t0] = (kTwo && col < N) ? p.Dv[rowbase + col] : 0.f;
+        if (!group_t) {
+            // lo parts of ring A1 (and A2), element-wise in place of the layout
+            for (int t = 0; ok && t < n; ++t) {
+                const int s1 = t % G::kStagesA1;
+                if (!group_all<1>(bf32_wait(fullA1 + s1, (t / G::kStagesA1) & 1, abort_flag)))
+                    break;
+                split_lo_stacked<BS, D>(sptr + G::kOffA1 + s1 * G::kPair, tg);
+                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                mbar_arrive(splitA1 + s1);
+                if constexpr (kTwo) {
+                    const int s2 = t % G::kStagesA2;
+                    if (!group_all<1>(
+                            bf32_wait(fullA2 + s2, (t / G::kStagesA2) & 1, abort_flag)))
+                        break;
+                    split_lo_stacked<BS, D>(sptr + G::kOffA2 + s2 * G::kPair, tg);
+                    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                    mbar_arrive(splitA2 + s2);
+                }
             }
-            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-            mbar_arrive(splitT + sT);
-            // ring A slot is free once every splitter thread is done reading it
-            splitter_sync();
-            if (t0 == 0) mbar_arrive(emptyA + s);
+        } else {
+            // ring T: [kBS][D] as loaded -> [D][kBS] in place, and its lo part
+            const size_t rowbase = static_cast<size_t>(bh) * N;
+            for (int t = 0; ok && t < n; ++t) {
+                // the block's per-column scalars, loaded ahead of the wait
+                float nl2 = 0.f, dv = 0.f;
+                const int col = (jb + t) * BS + tg;
+                if (kMode != kModeDQ && tg < BS && col < N) {
+                    nl2 = -p.L[rowbase + col] * kLog2eB;
+                    if (kTwo) dv = p.Dv[rowbase + col];
+                }
+                const int s = t % G::kStagesT;
+                if (!group_all<2>(bf32_wait(fullT + s, (t / G::kStagesT) & 1, abort_flag))) break;
+                uint8_t* tt = sptr + G::kOffT + s * G::kPair;
+                float4 rr[G::kTBlocks][4];
+#pragma unroll
+                for (int b = 0; b < G::kTBlocks; ++b) {
+                    int i, j;
+                    diag_block<BS>(tg + 64 * b, i, j);
+                    const int d0 = 4 * j;
+#pragma unroll
+                    for (int a = 0; a < 4; ++a) {
+                        const int row = 4 * i + a;
+                        rr[b][a] = *reinterpret_cast<const float4*>(
+                            tt + (d0 >> 5) * G::kSCb + row * 128 +
+                            ((((d0 & 31) >> 2) ^ (row & 7)) << 4));
+                    }
+                }
+                group_sync<2>();  // every read of the tile before any write
+#pragma unroll
+                for (int b = 0; b < G::kTBlocks; ++b) {
+                    int i, j;
+                    diag_block<BS>(tg + 64 * b, i, j);
+                    const int r0 = 4 * i, d0 = 4 * j;
+                    const float cols[4][4] = {{rr[b][0].x, rr[b][1].x, rr[b][2].x, rr[b][3].x},
+                                              {rr[b][0].y, rr[b][1].y, rr[b][2].y, rr[b][3].y},
+                                              {rr[b][0].z, rr[b][1].z, rr[b][2].z, rr[b][3].z},
+                                              {rr[b][0].w, rr[b][1].w, rr[b][2].w, rr[b][3].w}};
+#pragma unroll
+                    for (int c = 0; c < 4; ++c) {
+                        const int d = d0 + c;
+                        const int off =
+                            (r0 >> 5) * G::kTCb + d * 128 + ((((r0 & 31) >> 2) ^ (d & 7)) << 4);
+                        *reinterpret_cast<float4*>(tt + off) =
+                            make_float4(cols[c][0], cols[c][1], cols[c][2], cols[c][3]);
+                        *reinterpret_cast<float4*>(tt + G::kSBytes + off) =
+                            make_float4(tf32_lo(cols[c][0]), tf32_lo(cols[c][1]),
+                                        tf32_lo(cols[c][2]), tf32_lo(cols[c][3]));
+                    }
+                }
+                if (tg < BS) {
+                    float* sc = sc_all + s * 2 * BS;
+                    sc[tg] = nl2;
+                    sc[BS + tg] = dv;
+                }
+                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                mbar_arrive(splitT + s);
+            }
         }
     }
 
