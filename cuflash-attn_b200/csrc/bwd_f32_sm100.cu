@@ -703,12 +703,51 @@ FlashAttentionError bwd_f32_typed(const float* Q, const float* K, const float* V
         O, dO, dvec, rows);
     e = cudaGetLastError() == cudaSuccess ? FlashAttentionError::SUCCESS
                                           : FlashAttentionError::CUDA_ERROR;
+    // The three gradients are independent: dV and dK run on side streams
+    // next to dQ on the caller's stream (a small problem fills the GPU three
+    // times over instead of once), joined back before the workspace is freed.
+    // Under stream capture everything stays on the caller's stream.
+    cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+    cudaStream_t s_dv = stream, s_dk = stream;
+    cudaEvent_t ev[3] = {nullptr, nullptr, nullptr};
+    bool fork = e == FlashAttentionError::SUCCESS &&
+                cudaStreamIsCapturing(stream, &cap) == cudaSuccess &&
+                cap == cudaStreamCaptureStatusNone;
+    if (fork) {
+        s_dv = side_stream(0);
+        s_dk = side_stream(1);
+        fork = s_dv != nullptr && s_dk != nullptr;
+        for (int i = 0; fork && i < 3; ++i)
+            fork = cudaEventCreateWithFlags(&ev[i], cudaEventDisableTiming) == cudaSuccess;
+        fork = fork && cudaEventRecord(ev[0], stream) == cudaSuccess &&
+               cudaStreamWaitEvent(s_dv, ev[0], 0) == cudaSuccess &&
+               cudaStreamWaitEvent(s_dk, ev[0], 0) == cudaSuccess;
+        if (!fork) {
+            s_dv = stream;
+            s_dk = stream;
+        }
+    }
     if (e == FlashAttentionError::SUCCESS)
-        e = launch_mode<D, kModeDV>(k128, k128, qs, dos, L, dvec, dV, BH, N, scale, causal, stream);
+        e = launch_mode<D, kModeDV>(k128, k128, qs, dos, L, dvec, dV, BH, N, scale, causal, s_dv);
     if (e == FlashAttentionError::SUCCESS)
-        e = launch_mode<D, kModeDK>(k128, v128, qs, dos, L, dvec, dK, BH, N, scale, causal, stream);
+        e = launch_mode<D, kModeDK>(k128, v128, qs, dos, L, dvec, dK, BH, N, scale, causal, s_dk);
     if (e == FlashAttentionError::SUCCESS)
         e = launch_mode<D, kModeDQ>(q128, do128, ks, vs, L, dvec, dQ, BH, N, scale, causal, stream);
+    if (fork) {
+        // joined whatever happened above, so nothing of this call outlives it
+        // on a side stream
+        const bool joined = cudaEventRecord(ev[1], s_dv) == cudaSuccess &&
+                            cudaEventRecord(ev[2], s_dk) == cudaSuccess &&
+                            cudaStreamWaitEvent(stream, ev[1], 0) == cudaSuccess &&
+                            cudaStreamWaitEvent(stream, ev[2], 0) == cudaSuccess;
+        if (!joined) {
+            cudaStreamSynchronize(s_dv);
+            cudaStreamSynchronize(s_dk);
+            if (e == FlashAttentionError::SUCCESS) e = FlashAttentionError::CUDA_ERROR;
+        }
+    }
+    for (cudaEvent_t x : ev)
+        if (x != nullptr) cudaEventDestroy(x);
     workspace_free(ws, stream);
     return e;
 }

@@ -85,6 +85,13 @@ int env_int(const char* name, int dflt);
 FlashAttentionError workspace_alloc(void** ptr, size_t bytes, cudaStream_t stream);
 void workspace_free(void* ptr, cudaStream_t stream);
 
+// Non-blocking side stream i (< kNumSideStreams) of the current device,
+// created on first use and kept for the life of the process; a launcher runs
+// independent kernels there, forked from and joined back into the caller's
+// stream with events.  nullptr if it cannot be created.
+constexpr int kNumSideStreams = 2;
+cudaStream_t side_stream(int i);
+
 // Launchers (defined in the kernel .cu files).  All pointers are device
 // pointers; validation has already happened.
 template <typename T>

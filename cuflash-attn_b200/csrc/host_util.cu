@@ -168,6 +168,23 @@ FlashAttentionError workspace_alloc(void** ptr, size_t bytes, cudaStream_t strea
     return FlashAttentionError::SUCCESS;
 }
 
+cudaStream_t side_stream(int i) {
+    constexpr int kMaxDev = 64;
+    static std::mutex mu;
+    static cudaStream_t streams[kMaxDev][kNumSideStreams] = {};
+    int dev = 0;
+    if (i < 0 || i >= kNumSideStreams || cudaGetDevice(&dev) != cudaSuccess || dev < 0 ||
+        dev >= kMaxDev)
+        return nullptr;
+    std::lock_guard<std::mutex> lock(mu);
+    if (streams[dev][i] == nullptr) {
+        cudaStream_t st = nullptr;
+        if (cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking) != cudaSuccess) return nullptr;
+        streams[dev][i] = st;
+    }
+    return streams[dev][i];
+}
+
 void workspace_free(void* ptr, cudaStream_t stream) {
     if (ptr != nullptr) cudaFreeAsync(ptr, stream);
 }
