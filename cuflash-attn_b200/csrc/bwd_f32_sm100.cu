@@ -145,20 +145,6 @@ __device__ __forceinline__ bool group_all(bool v) {
     return r != 0;
 }
 
-// 4x4 block `blk` of an [R][D] tile -> (row block i, column block j).  Eight
-// consecutive threads walk one diagonal of an 8x8 super-block, so the eight
-// 16-byte chunks of a shared-memory phase land in eight different chunk
-// columns of the 128-byte swizzle, for the reads of the [R][D] tile and for
-// the writes of its [D][R] transpose alike (no bank conflicts).
-template <int R>
-__device__ __forceinline__ void diag_block(int blk, int& i, int& j) {
-    const int k = blk & 7;
-    const int g = blk >> 3;
-    const int st = g >> 3, s = g & 7;
-    i = (st % (R / 32)) * 8 + k;
-    j = (st / (R / 32)) * 8 + ((k + s) & 7);
-}
-
 // lo parts of a ring A slot: every 128-byte column block holds R rows of the
 // tile, then the R rows of its lo part (element-wise: same swizzle phase).
 template <int R, int D>

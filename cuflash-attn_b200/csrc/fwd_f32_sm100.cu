@@ -23,6 +23,12 @@
 //               would need the 32-byte-atom swizzle)
 // S(j+1) is issued before PV(j), so the tensor pipe works on the next block
 // while the softmax of the current one runs (S/P double-buffered in TMEM).
+// A kind::tf32 MMA costs about the same at N = 32 or 64 as at N = 64, so a
+// tile and its lo part are stacked along N: every 128-byte column block of a
+// stage holds K's rows then K_lo's rows (and V^T's rows then V^T_lo's), one
+// MMA per k-step computes Q [K; K_lo]^T into 2 kBN TMEM columns (Q_lo K^T
+// accumulates into the second half, the softmax adds the halves), and at
+// head_dim <= 64 likewise P [V^T; V^T_lo]^T into two O halves.
 
 #include <cmath>
 
@@ -46,21 +52,26 @@ struct F32Geom {
     static constexpr int kNumCb = D / 32;           // 128-byte column blocks (32 fp32)
     static constexpr int kQCbBytes = kBM * 128;
     static constexpr int kQBytes = kBM * D * 4;
-    static constexpr int kKvCbBytes = kBN * 128;
+    static constexpr int kKvCbBytes = kBN * 128;      // V as loaded: kBN rows per block
     static constexpr int kKvBytes = kBN * D * 4;
+    static constexpr int kKkCbBytes = 2 * kBN * 128;  // [K; K_lo] column block
     static constexpr int kStages = 2;
     static constexpr int kOffQ = 0;
     static constexpr int kOffStage = kQBytes;
-    static constexpr int kStageBytes = 5 * kKvBytes;  // K, K_lo, V (as loaded), V^T, V^T_lo
-    static constexpr int kVtCbBytes = D * 128;         // V^T: D rows x 32 kv per 128-byte block
+    // [K; K_lo] (2 kKvBytes), V as loaded, [V^T; V^T_lo] (2 kKvBytes)
+    static constexpr int kStageBytes = 5 * kKvBytes;
+    static constexpr int kOffV = 2 * kKvBytes;
+    static constexpr int kOffVt = 3 * kKvBytes;
+    static constexpr int kVtCbBytes = 2 * D * 128;  // 32 kv of D V^T rows, then D V^T_lo rows
     static constexpr int kOffBar = kOffStage + kStages * kStageBytes;
     static constexpr int kNumBars = 2 + 3 * kStages + 2 + 2 + 1;
     static constexpr int kSmemBytes = kOffBar + kNumBars * 8 + 16;
+    static constexpr bool kStackPV = D <= 64;       // P [V^T; V^T_lo]^T in one MMA
+    static constexpr int kOCols = kStackPV ? 2 * D : D;
     // TMEM columns
-    static constexpr int kColS = 0;                 // [2][kBN]  S, overwritten by P
-    static constexpr int kColPlo = 2 * kBN;         // [2][kBN]
-    static constexpr int kColO = 4 * kBN;           // D
-    static constexpr int kColQlo = 4 * kBN + D;     // D
+    static constexpr int kColS = 0;                 // [2][2 kBN]: S halves, then P | P_lo
+    static constexpr int kColO = 4 * kBN;           // kOCols (O, or its two halves)
+    static constexpr int kColQlo = kColO + kOCols;  // D
     static_assert(kColQlo + D <= 512, "TMEM budget");
 };
 
@@ -158,8 +169,8 @@ __global__ void __launch_bounds__(384, 1)
                 uint8_t* st = sptr + G::kOffStage + s * G::kStageBytes;
                 mbar_arrive_expect_tx(full + s, 2 * G::kKvBytes);
                 for (int cb = 0; cb < G::kNumCb; ++cb) {
-                    tma_load_3d(st + cb * G::kKvCbBytes, &tmK, full + s, cb * 32, j * BN, bh);
-                    tma_load_3d(st + 2 * G::kKvBytes + cb * G::kKvCbBytes, &tmV, full + s, cb * 32,
+                    tma_load_3d(st + cb * G::kKkCbBytes, &tmK, full + s, cb * 32, j * BN, bh);
+                    tma_load_3d(st + G::kOffV + cb * G::kKvCbBytes, &tmV, full + s, cb * 32,
                                 j * BN, bh);
                 }
                 ++issued;
@@ -172,25 +183,22 @@ __global__ void __launch_bounds__(384, 1)
     } else if (warp == 1) {
         if (lane == 0) {
             constexpr uint32_t idesc_s = make_idesc(kFmtTF32, 128, BN, false, false);
+            constexpr uint32_t idesc_s2 = make_idesc(kFmtTF32, 128, 2 * BN, false, false);
             constexpr uint32_t idesc_pv = make_idesc(kFmtTF32, 128, D, false, false);
+            constexpr uint32_t idesc_pv2 = make_idesc(kFmtTF32, 128, G::kOCols, false, false);
             const uint32_t sQ = sbase + G::kOffQ;
             auto issue_s = [&](int j) {
                 const int s = j % G::kStages;
                 const uint32_t sK = sbase + G::kOffStage + s * G::kStageBytes;
-                const uint32_t sKlo = sK + G::kKvBytes;
-                const uint32_t d_t = tmem + G::kColS + (j & 1) * BN;
+                const uint32_t d_t = tmem + G::kColS + (j & 1) * 2 * BN;
 #pragma unroll
                 for (int kk = 0; kk < D / 8; ++kk)
-                    mma_tf32_ss(d_t, f32_kdesc(sQ, kk, G::kQCbBytes), f32_kdesc(sK, kk, G::kKvCbBytes),
-                                idesc_s, kk > 0 ? 1u : 0u);
+                    mma_tf32_ss(d_t, f32_kdesc(sQ, kk, G::kQCbBytes), f32_kdesc(sK, kk, G::kKkCbBytes),
+                                idesc_s2, kk > 0 ? 1u : 0u);
 #pragma unroll
                 for (int kk = 0; kk < D / 8; ++kk)
-                    mma_tf32_ss(d_t, f32_kdesc(sQ, kk, G::kQCbBytes),
-                                f32_kdesc(sKlo, kk, G::kKvCbBytes), idesc_s, 1u);
-#pragma unroll
-                for (int kk = 0; kk < D / 8; ++kk)
-                    mma_tf32_ts(d_t, tmem + G::kColQlo + kk * 8, f32_kdesc(sK, kk, G::kKvCbBytes),
-                                idesc_s, 1u);
+                    mma_tf32_ts(d_t + BN, tmem + G::kColQlo + kk * 8,
+                                f32_kdesc(sK, kk, G::kKkCbBytes), idesc_s, 1u);
                 tc_commit(bar_s + (j & 1));
             };
             auto stage_ready = [&](int j) {
@@ -214,22 +222,35 @@ __global__ void __launch_bounds__(384, 1)
                 if (!mbar_wait(bar_p, j & 1, abort_flag, &g_f32_status)) break;
                 tc_fence_after();
                 const int s = j % G::kStages;
-                const uint32_t sVt = sbase + G::kOffStage + s * G::kStageBytes + 3 * G::kKvBytes;
-                const uint32_t sVtlo = sVt + G::kKvBytes;
-                const uint32_t a_p = tmem + G::kColS + (j & 1) * BN;
-                const uint32_t a_plo = tmem + G::kColPlo + (j & 1) * BN;
+                const uint32_t sVt = sbase + G::kOffStage + s * G::kStageBytes + G::kOffVt;
+                const uint32_t a_p = tmem + G::kColS + (j & 1) * 2 * BN;
+                const uint32_t a_plo = a_p + BN;
+                if constexpr (G::kStackPV) {
+                    // O | O_lo += P [V^T; V^T_lo]^T, then O_lo += P_lo V^T
 #pragma unroll
-                for (int kk = 0; kk < BN / 8; ++kk)
-                    mma_tf32_ts(tmem + G::kColO, a_p + kk * 8, f32_kdesc(sVt, kk, G::kVtCbBytes),
-                                idesc_pv, (j > 0 || kk > 0) ? 1u : 0u);
+                    for (int kk = 0; kk < BN / 8; ++kk)
+                        mma_tf32_ts(tmem + G::kColO, a_p + kk * 8,
+                                    f32_kdesc(sVt, kk, G::kVtCbBytes), idesc_pv2,
+                                    (j > 0 || kk > 0) ? 1u : 0u);
 #pragma unroll
-                for (int kk = 0; kk < BN / 8; ++kk)
-                    mma_tf32_ts(tmem + G::kColO, a_p + kk * 8, f32_kdesc(sVtlo, kk, G::kVtCbBytes),
-                                idesc_pv, 1u);
+                    for (int kk = 0; kk < BN / 8; ++kk)
+                        mma_tf32_ts(tmem + G::kColO + D, a_plo + kk * 8,
+                                    f32_kdesc(sVt, kk, G::kVtCbBytes), idesc_pv, 1u);
+                } else {
 #pragma unroll
-                for (int kk = 0; kk < BN / 8; ++kk)
-                    mma_tf32_ts(tmem + G::kColO, a_plo + kk * 8, f32_kdesc(sVt, kk, G::kVtCbBytes),
-                                idesc_pv, 1u);
+                    for (int kk = 0; kk < BN / 8; ++kk)
+                        mma_tf32_ts(tmem + G::kColO, a_p + kk * 8,
+                                    f32_kdesc(sVt, kk, G::kVtCbBytes), idesc_pv,
+                                    (j > 0 || kk > 0) ? 1u : 0u);
+#pragma unroll
+                    for (int kk = 0; kk < BN / 8; ++kk)
+                        mma_tf32_ts(tmem + G::kColO, a_p + kk * 8,
+                                    f32_kdesc(sVt + D * 128, kk, G::kVtCbBytes), idesc_pv, 1u);
+#pragma unroll
+                    for (int kk = 0; kk < BN / 8; ++kk)
+                        mma_tf32_ts(tmem + G::kColO, a_plo + kk * 8,
+                                    f32_kdesc(sVt, kk, G::kVtCbBytes), idesc_pv, 1u);
+                }
                 tc_commit(bar_o);
                 tc_commit(empty + s);
             }
@@ -253,13 +274,22 @@ __global__ void __launch_bounds__(384, 1)
                 break;
             }
             tc_fence_after();
-            const uint32_t t_s = tmem + lane_addr + G::kColS + (j & 1) * BN;
-            const uint32_t t_plo = tmem + lane_addr + G::kColPlo + (j & 1) * BN;
+            const uint32_t t_s = tmem + lane_addr + G::kColS + (j & 1) * 2 * BN;
+            const uint32_t t_plo = t_s + BN;
             uint32_t sr[BN];
-            if constexpr (BN == 64) {
-                tmem_ld_x64(t_s, sr);
-            } else {
-                tmem_ld_x32(t_s, *reinterpret_cast<uint32_t(*)[32]>(sr));
+            {
+                // S = Q K^T + (Q K_lo^T + Q_lo K^T): the two halves of the block
+                uint32_t sl[BN];
+                if constexpr (BN == 64) {
+                    tmem_ld_x64(t_s, sr);
+                    tmem_ld_x64(t_plo, sl);
+                } else {
+                    tmem_ld2_x32(t_s, *reinterpret_cast<uint32_t(*)[32]>(sr), t_plo,
+                                 *reinterpret_cast<uint32_t(*)[32]>(sl));
+                }
+#pragma unroll
+                for (int i = 0; i < BN; ++i)
+                    sr[i] = __float_as_uint(__uint_as_float(sr[i]) + __uint_as_float(sl[i]));
             }
             const int col0 = j * BN;
             const int vis_end = (p.causal ? min(row, p.N - 1) : p.N - 1) - col0;
@@ -291,7 +321,7 @@ __global__ void __launch_bounds__(384, 1)
                 if (__any_sync(0xffffffffu, need)) {
                     const uint32_t t_o = tmem + lane_addr + G::kColO;
 #pragma unroll
-                    for (int cb = 0; cb < D / 32; ++cb) {
+                    for (int cb = 0; cb < G::kOCols / 32; ++cb) {
                         uint32_t o[32];
                         tmem_ld_x32(t_o + cb * 32, o);
 #pragma unroll
@@ -341,6 +371,13 @@ __global__ void __launch_bounds__(384, 1)
             uint32_t o[32];
             if (ok && n > 0) {
                 tmem_ld_x32(tmem + lane_addr + G::kColO + cb * 32, o);
+                if constexpr (G::kStackPV) {
+                    uint32_t o2[32];
+                    tmem_ld_x32(tmem + lane_addr + G::kColO + D + cb * 32, o2);
+#pragma unroll
+                    for (int i = 0; i < 32; ++i)
+                        o[i] = __float_as_uint(__uint_as_float(o[i]) + __uint_as_float(o2[i]));
+                }
             } else {
 #pragma unroll
                 for (int i = 0; i < 32; ++i) o[i] = 0u;
@@ -389,22 +426,26 @@ __global__ void __launch_bounds__(384, 1)
             const int s = j % G::kStages;
             if (!f32_wait(full + s, (j / G::kStages) & 1, abort_flag)) break;
             uint8_t* st = sptr + G::kOffStage + s * G::kStageBytes;
-            // K_lo: element-wise over the swizzled buffer (layout preserved)
-            const float4* k4 = reinterpret_cast<const float4*>(st);
-            float4* klo4 = reinterpret_cast<float4*>(st + G::kKvBytes);
+            // K_lo: element-wise, into the rows below K's in each column block
+            // (same swizzle phase, so the layout is preserved)
+            float4* k4 = reinterpret_cast<float4*>(st);
             for (int i = t; i < G::kKvBytes / 16; i += 128) {
-                const float4 a = k4[i];
-                klo4[i] = make_float4(tf32_lo(a.x), tf32_lo(a.y), tf32_lo(a.z), tf32_lo(a.w));
+                const int src = (i / (BN * 8)) * (BN * 16) + i % (BN * 8);
+                const float4 a = k4[src];
+                k4[src + BN * 8] =
+                    make_float4(tf32_lo(a.x), tf32_lo(a.y), tf32_lo(a.z), tf32_lo(a.w));
             }
             // V^T and V^T_lo: 4x4 blocks transposed in registers.  V as loaded
             // is [kv][d] (32-float, 128-byte swizzled column blocks of kBN
             // rows); V^T is [d][kv] with 32-kv column blocks of D rows.
-            const uint8_t* vraw = st + 2 * G::kKvBytes;
-            uint8_t* vt = st + 3 * G::kKvBytes;
-            uint8_t* vtlo = st + 4 * G::kKvBytes;
+            const uint8_t* vraw = st + G::kOffV;
+            uint8_t* vt = st + G::kOffVt;
+            uint8_t* vtlo = vt + D * 128;  // V^T_lo rows follow V^T's in each column block
             for (int blk = t; blk < (BN / 4) * (D / 4); blk += 128) {
-                const int kv0 = (blk % (BN / 4)) * 4;
-                const int d0 = (blk / (BN / 4)) * 4;
+                int bi, bj;
+                diag_block<BN>(blk, bi, bj);
+                const int kv0 = bi * 4;
+                const int d0 = bj * 4;
                 float4 rr[4];
 #pragma unroll
                 for (int a = 0; a < 4; ++a) {

@@ -319,6 +319,21 @@ __device__ __forceinline__ float tf32_lo(float x) {
     return x - __uint_as_float(__float_as_uint(x) & 0xFFFFE000u);
 }
 
+// 4x4 block `blk` of an [R][C] fp32 tile (R, C multiples of 32) -> (row
+// block i, column block j), for transposes between 128-byte swizzled tiles.
+// Eight consecutive threads walk one diagonal of an 8x8 super-block, so the
+// eight 16-byte chunks of a shared-memory phase fall in eight different
+// chunk columns of the swizzle, for the reads of the [R][C] tile and for the
+// writes of its [C][R] transpose alike (no bank conflicts).
+template <int R>
+__device__ __forceinline__ void diag_block(int blk, int& i, int& j) {
+    const int k = blk & 7;
+    const int g = blk >> 3;
+    const int st = g >> 3, s = g & 7;
+    i = (st % (R / 32)) * 8 + k;
+    j = (st / (R / 32)) * 8 + ((k + s) & 7);
+}
+
 // fp32 K-major operand stored as 128-byte swizzled column blocks of 32
 // elements (cb_bytes apart); descriptor of k-step kk (8 elements = 32 bytes).
 __device__ __forceinline__ uint64_t f32_kdesc(uint32_t base, int kk, int cb_bytes) {
