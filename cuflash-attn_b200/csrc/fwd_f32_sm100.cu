@@ -12,7 +12,7 @@
 //   S  = Q K^T  = (Q, K) + (Q, K_lo) + (Q_lo, K)
 //   O += P V    = (P, V) + (P, V_lo) + (P_lo, V)
 // CTA = 128 query rows of one (b,h); 384 threads:
-//   warp 0      TMA producer (Q once; K, V blocks of kBN rows, 2 stages)
+//   warp 0      TMA producer (Q once; K, V blocks of kBN rows, 2-4 stages)
 //   warp 1      TMEM allocator, MMA issuer
 //   warps 4-7   softmax, one thread per query row (TMEM lane); writes P and
 //               P_lo into TMEM (A operands of the PV products)
@@ -55,13 +55,17 @@ struct F32Geom {
     static constexpr int kKvCbBytes = kBN * 128;      // V as loaded: kBN rows per block
     static constexpr int kKvBytes = kBN * D * 4;
     static constexpr int kKkCbBytes = 2 * kBN * 128;  // [K; K_lo] column block
-    static constexpr int kStages = 2;
     static constexpr int kOffQ = 0;
     static constexpr int kOffStage = kQBytes;
-    // [K; K_lo] (2 kKvBytes), V as loaded, [V^T; V^T_lo] (2 kKvBytes)
-    static constexpr int kStageBytes = 5 * kKvBytes;
-    static constexpr int kOffV = 2 * kKvBytes;
-    static constexpr int kOffVt = 3 * kKvBytes;
+    // [K; K_lo] (2 kKvBytes), then [V^T; V^T_lo] (2 kKvBytes), whose first
+    // half receives V as loaded and is transposed in place
+    static constexpr int kStageBytes = 4 * kKvBytes;
+    static constexpr int kOffVt = 2 * kKvBytes;
+    static constexpr int kStagesFit = (232448 - 2048 - kQBytes) / kStageBytes;
+    static constexpr int kStages = kStagesFit > 4 ? 4 : kStagesFit;
+    static_assert(kStages >= 2, "K/V ring depth");
+    static constexpr int kVBlocks = (kBN / 4) * (D / 4) / 128;  // 4x4 blocks per splitter thread
+    static_assert(kVBlocks * 128 == (kBN / 4) * (D / 4), "transpose split");
     static constexpr int kVtCbBytes = 2 * D * 128;  // 32 kv of D V^T rows, then D V^T_lo rows
     static constexpr int kOffBar = kOffStage + kStages * kStageBytes;
     static constexpr int kNumBars = 2 + 3 * kStages + 2 + 2 + 1;
@@ -82,6 +86,22 @@ struct F32Params {
     int causal;
     float scale_log2;
 };
+
+// AND vote over the 128 splitter threads (warps 8-11) on named barrier 1, so
+// that they all take the same branch after a wait: the barrier inside the
+// splitter loop must never miss a participant.
+__device__ __forceinline__ bool splitter_all(bool v) {
+    uint32_t r;
+    asm volatile(
+        "{\n\t.reg .pred p, q;\n\t"
+        "setp.ne.u32 q, %1, 0;\n\t"
+        "bar.red.and.pred p, 1, 128, q;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}\n"
+        : "=r"(r)
+        : "r"(v ? 1u : 0u)
+        : "memory");
+    return r != 0;
+}
 
 __device__ __forceinline__ bool f32_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag) {
     return sm100::mbar_wait(bar, parity, abort_flag, &g_f32_status);
@@ -170,7 +190,7 @@ __global__ void __launch_bounds__(384, 1)
                 mbar_arrive_expect_tx(full + s, 2 * G::kKvBytes);
                 for (int cb = 0; cb < G::kNumCb; ++cb) {
                     tma_load_3d(st + cb * G::kKkCbBytes, &tmK, full + s, cb * 32, j * BN, bh);
-                    tma_load_3d(st + G::kOffV + cb * G::kKvCbBytes, &tmV, full + s, cb * 32,
+                    tma_load_3d(st + G::kOffVt + cb * G::kKvCbBytes, &tmV, full + s, cb * 32,
                                 j * BN, bh);
                 }
                 ++issued;
@@ -400,7 +420,7 @@ __global__ void __launch_bounds__(384, 1)
         const int t = threadIdx.x - 256;  // 0..127
         const int wq = warp & 3;
         const int r = wq * 32 + lane;
-        bool ok = n > 0 && f32_wait(bar_q, 0, abort_flag);
+        bool ok = splitter_all(n > 0 && f32_wait(bar_q, 0, abort_flag));
         if (ok) {
             // Q_lo of row r into TMEM (A operand of the (Q_lo, K) product)
             const uint8_t* sQ = sptr + G::kOffQ;
@@ -424,7 +444,7 @@ __global__ void __launch_bounds__(384, 1)
         }
         for (int j = 0; ok && j < n; ++j) {
             const int s = j % G::kStages;
-            if (!f32_wait(full + s, (j / G::kStages) & 1, abort_flag)) break;
+            if (!splitter_all(f32_wait(full + s, (j / G::kStages) & 1, abort_flag))) break;
             uint8_t* st = sptr + G::kOffStage + s * G::kStageBytes;
             // K_lo: element-wise, into the rows below K's in each column block
             // (same swizzle phase, so the layout is preserved)
@@ -435,39 +455,45 @@ __global__ void __launch_bounds__(384, 1)
                 k4[src + BN * 8] =
                     make_float4(tf32_lo(a.x), tf32_lo(a.y), tf32_lo(a.z), tf32_lo(a.w));
             }
-            // V^T and V^T_lo: 4x4 blocks transposed in registers.  V as loaded
-            // is [kv][d] (32-float, 128-byte swizzled column blocks of kBN
-            // rows); V^T is [d][kv] with 32-kv column blocks of D rows.
-            const uint8_t* vraw = st + G::kOffV;
+            // V^T and V^T_lo, in place: V as loaded is [kv][d] (32-float,
+            // 128-byte swizzled column blocks of kBN rows) in the first half of
+            // the region; V^T is [d][kv], 32-kv column blocks of D V^T rows and
+            // D V^T_lo rows.  Every thread reads its 4x4 blocks, then all write.
             uint8_t* vt = st + G::kOffVt;
-            uint8_t* vtlo = vt + D * 128;  // V^T_lo rows follow V^T's in each column block
-            for (int blk = t; blk < (BN / 4) * (D / 4); blk += 128) {
+            float4 rr[G::kVBlocks][4];
+#pragma unroll
+            for (int b = 0; b < G::kVBlocks; ++b) {
                 int bi, bj;
-                diag_block<BN>(blk, bi, bj);
-                const int kv0 = bi * 4;
+                diag_block<BN>(t + 128 * b, bi, bj);
                 const int d0 = bj * 4;
-                float4 rr[4];
 #pragma unroll
                 for (int a = 0; a < 4; ++a) {
-                    const int kv = kv0 + a;
-                    rr[a] = *reinterpret_cast<const float4*>(
-                        vraw + (d0 >> 5) * G::kKvCbBytes + kv * 128 +
-                        (((((d0 & 31) >> 2) ^ (kv & 7))) << 4));
+                    const int kv = bi * 4 + a;
+                    rr[b][a] = *reinterpret_cast<const float4*>(
+                        vt + (d0 >> 5) * G::kKvCbBytes + kv * 128 +
+                        ((((d0 & 31) >> 2) ^ (kv & 7)) << 4));
                 }
-                const float cols[4][4] = {{rr[0].x, rr[1].x, rr[2].x, rr[3].x},
-                                          {rr[0].y, rr[1].y, rr[2].y, rr[3].y},
-                                          {rr[0].z, rr[1].z, rr[2].z, rr[3].z},
-                                          {rr[0].w, rr[1].w, rr[2].w, rr[3].w}};
+            }
+            asm volatile("bar.sync 1, 128;" ::: "memory");
 #pragma unroll
-                for (int b = 0; b < 4; ++b) {
-                    const int d = d0 + b;
+            for (int b = 0; b < G::kVBlocks; ++b) {
+                int bi, bj;
+                diag_block<BN>(t + 128 * b, bi, bj);
+                const int kv0 = bi * 4, d0 = bj * 4;
+                const float cols[4][4] = {{rr[b][0].x, rr[b][1].x, rr[b][2].x, rr[b][3].x},
+                                          {rr[b][0].y, rr[b][1].y, rr[b][2].y, rr[b][3].y},
+                                          {rr[b][0].z, rr[b][1].z, rr[b][2].z, rr[b][3].z},
+                                          {rr[b][0].w, rr[b][1].w, rr[b][2].w, rr[b][3].w}};
+#pragma unroll
+                for (int c = 0; c < 4; ++c) {
+                    const int d = d0 + c;
                     const int off = (kv0 >> 5) * G::kVtCbBytes + d * 128 +
                                     ((((kv0 & 31) >> 2) ^ (d & 7)) << 4);
                     *reinterpret_cast<float4*>(vt + off) =
-                        make_float4(cols[b][0], cols[b][1], cols[b][2], cols[b][3]);
-                    *reinterpret_cast<float4*>(vtlo + off) =
-                        make_float4(tf32_lo(cols[b][0]), tf32_lo(cols[b][1]), tf32_lo(cols[b][2]),
-                                    tf32_lo(cols[b][3]));
+                        make_float4(cols[c][0], cols[c][1], cols[c][2], cols[c][3]);
+                    *reinterpret_cast<float4*>(vt + D * 128 + off) =
+                        make_float4(tf32_lo(cols[c][0]), tf32_lo(cols[c][1]),
+                                    tf32_lo(cols[c][2]), tf32_lo(cols[c][3]));
                 }
             }
             asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
