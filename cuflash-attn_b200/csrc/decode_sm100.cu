@@ -517,7 +517,7 @@ FlashAttentionError decode_group_typed(const T* Q, const DecodeKv<T>& kvp, T* O,
 }
 
 // ---------------------------------------------------------------------------
-// Grouped-query decode on the tensor cores (head_dim 128).  The SIMT kernel
+// Grouped-query decode on the tensor cores (head_dim 64 and 128).  The SIMT kernel
 // above reduces every (cache row, query head) dot product across 16 lanes
 // with shuffles, and that chain, not the cache bytes, sets its speed.  Here a
 // CTA serves up to 16 query heads of one K/V head over a range of cache rows,
@@ -530,34 +530,46 @@ FlashAttentionError decode_group_typed(const T* Q, const DecodeKv<T>& kvp, T* O,
 //                  P^T (16-bit) written to shared memory;
 //   O^T += V^T P^T M = head_dim, N = 16 heads, K = 128 cache rows (A = the V
 //                  block read MN-major, B = P^T K-major).
-// K/V blocks arrive by TMA through a 3-stage ring (contiguous cache: one box
+// K/V blocks arrive by TMA through a ring of 3 stages (head_dim 128; head_dim
+// 64: 2 stages, two CTAs per SM) (contiguous cache: one box
 // per 64 columns; paged cache: one box per page and 64 columns, pages of 8 or
 // more rows).  MMA order S0, S1, O0, S2, O1, ...: S_j is issued right behind
 // O_{j-2}, so the completion of S_j (which the softmax waits for) also means
 // O_{j-2} has read the P^T buffer the softmax is about to overwrite.  TMEM:
-// S^T double-buffered in columns [0,32), O^T in [32,48).
+// S^T double-buffered in columns [0,32), O^T in [32,48).  At head_dim 64 the
+// V block keeps its 128-element width with the upper half zero, so O^T stays
+// an M = 128 product (at N = 16 it costs what an M = 64 one does) and its
+// rows 64-127, never read, stay zero.
 // ---------------------------------------------------------------------------
 __device__ int g_dec_status;
 
 constexpr int kTcHeads = 16;
 constexpr int kTcRows = 128;
-constexpr int kTcStages = 3;
 constexpr int kTcThreads = 192;  // warp 0 TMA, warp 1 MMA, warps 2-5 softmax / epilogue
 
-struct TcGeom {  // head_dim 128
+template <int D>
+struct TcGeom {
+    // head_dim 64: two CTAs per SM (a 128-row block is half the bytes for the
+    // same MMA / softmax chain), so two stages each; head_dim 128: one CTA,
+    // three stages
+    static constexpr int kCtasPerSm = D == 64 ? 2 : 1;
+    static constexpr int kStages = D == 64 ? 2 : 3;
+    static constexpr int kKcb = D / 64;                   // 64-element column blocks of K, Q
     static constexpr int kKvCbBytes = kTcRows * 128;      // 128 rows x 64 elements
-    static constexpr int kKvTileBytes = 2 * kKvCbBytes;   // one K or V block
-    static constexpr int kStageBytes = 2 * kKvTileBytes;  // K + V
+    static constexpr int kKTileBytes = kKcb * kKvCbBytes;  // one K block
+    static constexpr int kVTileBytes = 2 * kKvCbBytes;     // one V block, 128 wide (see above)
+    static constexpr int kStageBytes = kKTileBytes + kVTileBytes;
+    static constexpr int kLoadBytes = 2 * kKTileBytes;     // TMA bytes per stage (K, V)
     static constexpr int kQCbBytes = kTcHeads * 128;
-    static constexpr int kQBytes = 2 * kQCbBytes;
+    static constexpr int kQBytes = kKcb * kQCbBytes;
     static constexpr int kPCbBytes = kTcHeads * 128;      // 16 heads x 64 cache rows (16-bit)
     static constexpr int kPBytes = 2 * kPCbBytes;
-    static constexpr int kOffQ = kTcStages * kStageBytes;
+    static constexpr int kOffQ = kStages * kStageBytes;
     static constexpr int kOffP = kOffQ + kQBytes;
     static constexpr int kOffRed = kOffP + 2 * kPBytes;
     static constexpr int kRedFloats = 4 * kTcHeads;
     static constexpr int kOffBar = kOffRed + 3 * kRedFloats * 4;
-    static constexpr int kNumBars = 1 + 2 * kTcStages + 2 + 2 + 2 + 1 + 1;
+    static constexpr int kNumBars = 1 + 2 * kStages + 2 + 2 + 2 + 1 + 1;
     static constexpr int kSmemBytes = kOffBar + kNumBars * 8 + 16 + 1024;
     static_assert(kOffQ % 1024 == 0 && kOffP % 1024 == 0, "swizzled tiles need 1024-byte alignment");
 };
@@ -606,12 +618,12 @@ __device__ __forceinline__ void softmax_group_sync() {
     asm volatile("bar.sync 1, 128;" ::: "memory");
 }
 
-template <typename T, bool kPaged, bool kDirect>
-__global__ void __launch_bounds__(kTcThreads, 1)
+template <typename T, int D, bool kPaged, bool kDirect>
+__global__ void __launch_bounds__(kTcThreads, TcGeom<D>::kCtasPerSm)
     decode_gqa_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
                          const __grid_constant__ CUtensorMap tmK,
                          const __grid_constant__ CUtensorMap tmV, const TcParams p) {
-    using G = TcGeom;
+    using G = TcGeom<D>;
     using namespace sm100;
     extern __shared__ uint8_t smem_raw[];
     if (*reinterpret_cast<volatile int*>(&g_dec_status) != 0) return;
@@ -621,8 +633,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     uint64_t* bars = reinterpret_cast<uint64_t*>(sptr + G::kOffBar);
     uint64_t* bar_q = bars;
     uint64_t* full = bar_q + 1;
-    uint64_t* empty = full + kTcStages;
-    uint64_t* bar_s = empty + kTcStages;  // [2] S^T_j in TMEM
+    uint64_t* empty = full + G::kStages;
+    uint64_t* bar_s = empty + G::kStages;  // [2] S^T_j in TMEM
     uint64_t* bar_sfree = bar_s + 2;      // [2] S^T_j read by the softmax (128 arrivals)
     uint64_t* bar_p = bar_sfree + 2;      // [2] P^T_j in shared memory (128 arrivals)
     uint64_t* bar_ofin = bar_p + 2;       // one completion per O^T product
@@ -649,7 +661,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 
     if (threadIdx.x == 0) {
         mbar_init(bar_q, 1);
-        for (int s = 0; s < kTcStages; ++s) {
+        for (int s = 0; s < G::kStages; ++s) {
             mbar_init(full + s, 1);
             mbar_init(empty + s, 1);
         }
@@ -681,7 +693,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             // query rows bhq0 .. bhq0+15; rows of the next group or past the
             // tensor end fill heads this CTA does not report
             mbar_arrive_expect_tx(bar_q, G::kQBytes);
-            for (int cb = 0; cb < 2; ++cb)
+            for (int cb = 0; cb < G::kKcb; ++cb)
                 tma_load_3d(sptr + G::kOffQ + cb * G::kQCbBytes, &tmQ, bar_q, cb * 64,
                             static_cast<int>(bhq0), 0);
             int issued = 0;
@@ -689,7 +701,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             const int per = ps < kTcRows ? ps : kTcRows;  // rows per TMA box (paged)
             const int npb = kTcRows / per;                // boxes per block (paged, <= 16)
             for (int j = 0; j < nb; ++j) {
-                const int s = j % kTcStages;
+                const int s = j % G::kStages;
                 const int r0 = r_begin + j * kTcRows;
                 // paged: the block's page indices, loaded before the ring wait
                 // so their latency overlaps it
@@ -703,16 +715,16 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                         }
                     }
                 }
-                if (j >= kTcStages &&
-                    !mbar_wait(empty + s, ((j / kTcStages) - 1) & 1, abort_flag, &g_dec_status))
+                if (j >= G::kStages &&
+                    !mbar_wait(empty + s, ((j / G::kStages) - 1) & 1, abort_flag, &g_dec_status))
                     break;
                 ++issued;
                 uint8_t* st = sptr + s * G::kStageBytes;
-                mbar_arrive_expect_tx(full + s, G::kStageBytes);
+                mbar_arrive_expect_tx(full + s, G::kLoadBytes);
                 if constexpr (!kPaged) {
-                    for (int cb = 0; cb < 2; ++cb) {
+                    for (int cb = 0; cb < G::kKcb; ++cb) {
                         tma_load_3d(st + cb * G::kKvCbBytes, &tmK, full + s, cb * 64, r0, bhk);
-                        tma_load_3d(st + G::kKvTileBytes + cb * G::kKvCbBytes, &tmV, full + s,
+                        tma_load_3d(st + G::kKTileBytes + cb * G::kKvCbBytes, &tmV, full + s,
                                     cb * 64, r0, bhk);
                     }
                 } else {
@@ -722,10 +734,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                         const int rr = q * per;
                         const int pg = min(max(page[q], 0), p.num_pages - 1);
                         const int slot = (pg << p.page_shift) + ((r0 + rr) & (ps - 1));
-                        for (int cb = 0; cb < 2; ++cb) {
+                        for (int cb = 0; cb < G::kKcb; ++cb) {
                             tma_load_3d(st + cb * G::kKvCbBytes + rr * 128, &tmK, full + s, cb * 64,
                                         hk, slot);
-                            tma_load_3d(st + G::kKvTileBytes + cb * G::kKvCbBytes + rr * 128, &tmV,
+                            tma_load_3d(st + G::kKTileBytes + cb * G::kKvCbBytes + rr * 128, &tmV,
                                         full + s, cb * 64, hk, slot);
                         }
                     }
@@ -734,8 +746,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             // every issued copy lands before the CTA can exit, also after an abort
             volatile int never = 0;
             mbar_wait(bar_q, 0, &never, &g_dec_status);
-            for (int j = issued > kTcStages ? issued - kTcStages : 0; j < issued; ++j)
-                mbar_wait(full + j % kTcStages, (j / kTcStages) & 1, &never, &g_dec_status);
+            for (int j = issued > G::kStages ? issued - G::kStages : 0; j < issued; ++j)
+                mbar_wait(full + j % G::kStages, (j / G::kStages) & 1, &never, &g_dec_status);
         }
     } else if (warp == 1) {
         // ------------------------------------------------ MMA issuer
@@ -746,15 +758,15 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             const uint32_t sQ = sbase + G::kOffQ;
             bool ok = mbar_wait(bar_q, 0, abort_flag, &g_dec_status);
             auto issue_s = [&](int j) {
-                const int s = j % kTcStages;
-                if (!mbar_wait(full + s, (j / kTcStages) & 1, abort_flag, &g_dec_status)) return false;
+                const int s = j % G::kStages;
+                if (!mbar_wait(full + s, (j / G::kStages) & 1, abort_flag, &g_dec_status)) return false;
                 if (j >= 2 &&
                     !mbar_wait(bar_sfree + (j & 1), ((j >> 1) - 1) & 1, abort_flag, &g_dec_status))
                     return false;
                 tc_fence_after();
                 const uint32_t sK = sbase + s * G::kStageBytes;
 #pragma unroll
-                for (int kk = 0; kk < 8; ++kk)
+                for (int kk = 0; kk < D / 16; ++kk)
                     mma_f16_ss(tmem + (j & 1) * kTcHeads, tc_kmajor(sK, G::kKvCbBytes, kk),
                                tc_kmajor(sQ, G::kQCbBytes, kk), idesc_s, kk > 0 ? 1u : 0u);
                 tc_commit(bar_s + (j & 1));
@@ -763,14 +775,14 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             auto issue_o = [&](int j) {
                 if (!mbar_wait(bar_p + (j & 1), (j >> 1) & 1, abort_flag, &g_dec_status)) return false;
                 tc_fence_after();
-                const uint32_t sV = sbase + (j % kTcStages) * G::kStageBytes + G::kKvTileBytes;
+                const uint32_t sV = sbase + (j % G::kStages) * G::kStageBytes + G::kKTileBytes;
                 const uint32_t sP = sbase + G::kOffP + (j & 1) * G::kPBytes;
 #pragma unroll
                 for (int kk = 0; kk < 8; ++kk)
                     mma_f16_ss(tmem + 2 * kTcHeads, tc_mnmajor(sV, G::kKvCbBytes, kk),
                                tc_kmajor(sP, G::kPCbBytes, kk), idesc_o,
                                (j > 0 || kk > 0) ? 1u : 0u);
-                tc_commit(empty + (j % kTcStages));
+                tc_commit(empty + (j % G::kStages));
                 tc_commit(bar_ofin);
                 return true;
             };
@@ -795,6 +807,19 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         for (int g = 0; g < kTcHeads; ++g) {
             m_run[g] = -INFINITY;
             l_part[g] = 0.f;
+        }
+        if constexpr (D < 128) {
+            // the V blocks' upper 64 columns: zero once, never loaded (made
+            // visible to the tensor core by the proxy fence before the first
+            // P^T hand-off)
+            const int t = threadIdx.x - 64;
+            for (int s = 0; s < G::kStages; ++s) {
+                const uint32_t hi = sbase + s * G::kStageBytes + G::kKTileBytes + G::kKvCbBytes;
+                for (int i = t; i < G::kKvCbBytes / 16; i += 128)
+                    asm volatile("st.shared.v4.b32 [%0], {%1, %1, %1, %1};" ::"r"(hi + i * 16),
+                                 "r"(0u)
+                                 : "memory");
+            }
         }
         // Every softmax thread runs all nb iterations and both group barriers
         // per iteration whatever happens; after a failed (timed-out or
@@ -872,7 +897,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 // rows past the sequence end hold whatever the cache page has;
                 // zero their V so that P = 0 cannot meet a non-finite value
                 if (!live) {
-                    const uint32_t vrow = sbase + (j % kTcStages) * G::kStageBytes + G::kKvTileBytes +
+                    const uint32_t vrow = sbase + (j % G::kStages) * G::kStageBytes + G::kKTileBytes +
                                           r * 128;
 #pragma unroll
                     for (int cb = 0; cb < 2; ++cb)
@@ -914,16 +939,16 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         const int d = r;
 #pragma unroll
         for (int g = 0; g < kTcHeads; ++g) {
-            if (g >= nh) continue;
+            if (g >= nh || d >= D) continue;
             const float lt = rs[g] + rs[kTcHeads + g] + rs[2 * kTcHeads + g] + rs[3 * kTcHeads + g];
             const float outv = lt > 0.f ? __uint_as_float(ov[g]) / lt : 0.f;
             const float lse = lt > 0.f ? (m_run[g] + log2f(lt)) * kLn2f : -INFINITY;
             const long long bhq = bhq0 + g;
             if constexpr (kDirect) {
-                static_cast<T*>(p.O)[bhq * 128 + d] = DType<T>::from_float(outv);
+                static_cast<T*>(p.O)[bhq * D + d] = DType<T>::from_float(outv);
                 if (d == 0) p.L[bhq] = lse;
             } else {
-                p.O_part[(bhq * gridDim.y + split) * 128 + d] = outv;
+                p.O_part[(bhq * gridDim.y + split) * D + d] = outv;
                 if (d == 0) p.L_part[bhq * gridDim.y + split] = lse;
             }
         }
@@ -937,12 +962,12 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     }
 }
 
-// Tensor-core grouped-query decode for head_dim 128 (see the kernel above).
-template <typename T, bool kPaged>
+// Tensor-core grouped-query decode for head_dim 64 and 128 (see the kernel above).
+template <typename T, int D, bool kPaged>
 FlashAttentionError decode_gqa_tc(const T* Q, const DecodeKv<T>& kvp, T* O, float* L, int B,
                                   int hq, int max_len, float scale, int num_splits,
                                   cudaStream_t stream) {
-    using G = TcGeom;
+    using G = TcGeom<D>;
     const int group = hq / kvp.hkv;
     const int tiles = (group + kTcHeads - 1) / kTcHeads;
     const long long units = static_cast<long long>(B) * kvp.hkv * tiles;
@@ -954,7 +979,8 @@ FlashAttentionError decode_gqa_tc(const T* Q, const DecodeKv<T>& kvp, T* O, floa
         // B200 over B 8-64, Nkv 4k-32k, groups 2-16, the best split count is
         // about SMs / units (units 16 / 32 / 64 / >= 128 -> 8 / 4 / 2 / 1);
         // at least two blocks per split.
-        S = static_cast<int>(std::max<long long>(1, current_sm_count() / units));
+        S = static_cast<int>(
+            std::max<long long>(1, static_cast<long long>(G::kCtasPerSm) * current_sm_count() / units));
         S = std::min(S, std::max(1, blocks_total / 2));
     }
     S = std::max(1, std::min(S, std::min(64, std::max(1, blocks_total))));
@@ -964,20 +990,21 @@ FlashAttentionError decode_gqa_tc(const T* Q, const DecodeKv<T>& kvp, T* O, floa
 
     const CUtensorMapDataType dt = DType<T>::kTmaType;
     CUtensorMap mq, mk, mv;
-    if (!encode_tmap_3d(&mq, Q, dt, 2, 128, static_cast<uint64_t>(B) * hq, 1, 64, kTcHeads,
+    if (!encode_tmap_3d(&mq, Q, dt, 2, D, static_cast<uint64_t>(B) * hq, 1, 64, kTcHeads,
                         CU_TENSOR_MAP_SWIZZLE_128B))
         return FlashAttentionError::CUDA_ERROR;
     if (!kPaged) {
-        if (!encode_tmap_3d(&mk, kvp.K, dt, 2, 128, kvp.kv_len, static_cast<uint64_t>(B) * kvp.hkv,
+        if (!encode_tmap_3d(&mk, kvp.K, dt, 2, D, kvp.kv_len, static_cast<uint64_t>(B) * kvp.hkv,
                             64, kTcRows, CU_TENSOR_MAP_SWIZZLE_128B) ||
-            !encode_tmap_3d(&mv, kvp.V, dt, 2, 128, kvp.kv_len, static_cast<uint64_t>(B) * kvp.hkv,
+            !encode_tmap_3d(&mv, kvp.V, dt, 2, D, kvp.kv_len, static_cast<uint64_t>(B) * kvp.hkv,
                             64, kTcRows, CU_TENSOR_MAP_SWIZZLE_128B))
             return FlashAttentionError::CUDA_ERROR;
     } else {
         const int ps = 1 << kvp.page_shift;
-        const uint64_t dims[3] = {128, static_cast<uint64_t>(kvp.hkv),
+        const uint64_t dims[3] = {static_cast<uint64_t>(D), static_cast<uint64_t>(kvp.hkv),
                                   static_cast<uint64_t>(kvp.num_pages) << kvp.page_shift};
-        const uint64_t strides[2] = {128 * 2, static_cast<uint64_t>(kvp.hkv) * 128 * 2};
+        const uint64_t strides[2] = {static_cast<uint64_t>(D) * 2,
+                                     static_cast<uint64_t>(kvp.hkv) * D * 2};
         const uint32_t box[3] = {64, 1, static_cast<uint32_t>(ps < kTcRows ? ps : kTcRows)};
         if (!encode_tmap_3d_strided(&mk, kvp.K, dt, dims, strides, box,
                                     CU_TENSOR_MAP_SWIZZLE_128B) ||
@@ -1000,7 +1027,7 @@ FlashAttentionError decode_gqa_tc(const T* Q, const DecodeKv<T>& kvp, T* O, floa
     prm.scale_log2 = scale * kLog2ef;
     const dim3 grid(static_cast<unsigned>(units), S);
     if (S == 1) {
-        auto k = decode_gqa_tc_kernel<T, kPaged, true>;
+        auto k = decode_gqa_tc_kernel<T, D, kPaged, true>;
         if (!ensure_smem_attr(reinterpret_cast<const void*>(k), G::kSmemBytes))
             return FlashAttentionError::CUDA_ERROR;
         prm.O = O;
@@ -1010,21 +1037,21 @@ FlashAttentionError decode_gqa_tc(const T* Q, const DecodeKv<T>& kvp, T* O, floa
                                                  : FlashAttentionError::CUDA_ERROR;
     }
     const int BHq = B * hq;
-    const size_t part_elems = static_cast<size_t>(BHq) * S * 128;
+    const size_t part_elems = static_cast<size_t>(BHq) * S * D;
     const size_t bytes = (part_elems + static_cast<size_t>(BHq) * S) * sizeof(float);
     void* wsv = nullptr;
     FlashAttentionError werr = workspace_alloc(&wsv, bytes, stream);
     if (werr != FlashAttentionError::SUCCESS) return werr;
     prm.O_part = static_cast<float*>(wsv);
     prm.L_part = prm.O_part + part_elems;
-    auto k = decode_gqa_tc_kernel<T, kPaged, false>;
+    auto k = decode_gqa_tc_kernel<T, D, kPaged, false>;
     if (!ensure_smem_attr(reinterpret_cast<const void*>(k), G::kSmemBytes)) {
         workspace_free(wsv, stream);
         return FlashAttentionError::CUDA_ERROR;
     }
     k<<<grid, kTcThreads, G::kSmemBytes, stream>>>(mq, mk, mv, prm);
     cudaError_t e1 = cudaGetLastError();
-    decode_combine_kernel<T, 128><<<BHq, 128, 0, stream>>>(prm.O_part, prm.L_part, O, L, S);
+    decode_combine_kernel<T, D><<<BHq, 128, 0, stream>>>(prm.O_part, prm.L_part, O, L, S);
     cudaError_t e2 = cudaGetLastError();
     workspace_free(wsv, stream);
     return (e1 == cudaSuccess && e2 == cudaSuccess) ? FlashAttentionError::SUCCESS
@@ -1042,11 +1069,11 @@ FlashAttentionError decode_group_tile(const T* Q, const DecodeKv<T>& kvp, T* O, 
     // 8): contiguous 1.31 / 1.26 ms with 4 heads per CTA against 1.31 / 1.96
     // with 8; paged 1.67 / 1.62 ms with 2 against 2.91 / 2.76 with 4.
     const int group = hq / kvp.hkv;
-    if constexpr (D == 128) {
+    if constexpr (D == 128 || D == 64) {
         // tensor-core kernel from two heads per K/V head up (pages of 8+ rows)
         if (group >= 2 && (!kPaged || kvp.page_shift >= 3) && env_int("CUFLASH_DECODE_GQA_TC", 1) != 0)
-            return decode_gqa_tc<T, kPaged>(Q, kvp, O, L, B, hq, max_len, scale, num_splits,
-                                            stream);
+            return decode_gqa_tc<T, D, kPaged>(Q, kvp, O, L, B, hq, max_len, scale, num_splits,
+                                               stream);
     }
     if (group % 4 == 0 && !kPaged)
         return decode_group_typed<T, D, 4, kPaged>(Q, kvp, O, L, B, hq, max_len, scale,

@@ -26,13 +26,16 @@ def _ref_decode(q, K, V, scale):
     return oracle.decode_f64(q, np.repeat(K, g, axis=1), np.repeat(V, g, axis=1), scale)
 
 
+@pytest.mark.parametrize("D", [64, 128])
 @pytest.mark.parametrize("dt", ["bf16", "f16"])
 @pytest.mark.parametrize("Hq,Hkv", [(8, 8), (8, 4), (16, 4), (32, 4), (12, 2), (14, 2), (7, 1)])
 @pytest.mark.parametrize("splits", [0, 1, 3])
-def test_decode_gqa_vs_fp64(lib, cuda, dt, Hq, Hkv, splits):
+def test_decode_gqa_vs_fp64(lib, cuda, dt, Hq, Hkv, splits, D):
+    """Head_dim 64 and 128 take the tensor-core kernel from two heads per
+    K/V head up, the SIMT kernel for one."""
     import torch
 
-    B, N, D = 2, 777, 128
+    B, N = 2, 777
     scale = 1.0 / np.sqrt(D)
     q = round_to(oracle.normal((B, Hq, 1, D), 1), dt)
     K = round_to(oracle.normal((B, Hkv, N, D), 2), dt)
@@ -73,13 +76,14 @@ def test_decode_gqa_group_one_matches_mha_decode(lib, cuda):
     assert max_err(host(L1), host(L2)) < 1e-5
 
 
+@pytest.mark.parametrize("D", [64, 128])
 @pytest.mark.parametrize("dt", ["bf16", "f16"])
 @pytest.mark.parametrize("page_size,Hq,Hkv", [(16, 8, 2), (64, 4, 4), (128, 32, 8), (1, 4, 1)])
 @pytest.mark.parametrize("splits", [0, 2])
-def test_decode_paged_vs_fp64(lib, cuda, dt, page_size, Hq, Hkv, splits):
+def test_decode_paged_vs_fp64(lib, cuda, dt, page_size, Hq, Hkv, splits, D):
     import torch
 
-    B, D = 5, 128
+    B = 5
     max_pages = max(1, 700 // page_size + 2)
     num_pages = B * max_pages + 3
     rng = np.random.default_rng(page_size + Hq)
@@ -110,18 +114,19 @@ def test_decode_paged_vs_fp64(lib, cuda, dt, page_size, Hq, Hkv, splits):
         assert max_err(Lg[b:b + 1], L64) < TOL_L, b
 
 
+@pytest.mark.parametrize("D", [64, 128])
 @pytest.mark.parametrize("tc", ["1", "0"])
 @pytest.mark.parametrize("Hq,Hkv", [(48, 2), (64, 2), (4, 2)])
-def test_decode_gqa_large_groups_and_rescale(lib, cuda, monkeypatch, tc, Hq, Hkv):
+def test_decode_gqa_large_groups_and_rescale(lib, cuda, monkeypatch, tc, Hq, Hkv, D):
     """Groups above 16 heads (several head tiles per K/V head on the tensor-
     core path) and scores that grow along the cache (later rows dominate,
     so running maxima rise across blocks and O is rescaled), on both the
-    tensor-core kernel (CUFLASH_DECODE_GQA_TC=1, head_dim 128) and the SIMT
-    kernel (=0)."""
+    tensor-core kernel (CUFLASH_DECODE_GQA_TC=1, head_dim 64 and 128) and the
+    SIMT kernel (=0)."""
     import torch
 
     monkeypatch.setenv("CUFLASH_DECODE_GQA_TC", tc)
-    B, N, D, dt = 2, 1500, 128, "bf16"
+    B, N, dt = 2, 1500, "bf16"
     scale = 1.0 / np.sqrt(D)
     q = round_to(oracle.normal((B, Hq, 1, D), 21), dt)
     ramp = (1.0 + 4.0 * np.arange(N, dtype=np.float32) / N)[None, None, :, None]
