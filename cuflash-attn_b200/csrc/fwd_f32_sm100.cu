@@ -62,12 +62,18 @@ struct F32Geom {
     static constexpr int kStageBytes = 4 * kKvBytes;
     static constexpr int kOffVt = 2 * kKvBytes;
     static constexpr int kStagesFit = (232448 - 2048 - kQBytes) / kStageBytes;
-    static constexpr int kStages = kStagesFit > 4 ? 4 : kStagesFit;
-    static_assert(kStages >= 2, "K/V ring depth");
+    static constexpr int kStagesMain = kStagesFit > 4 ? 4 : kStagesFit;
+    static_assert(kStagesMain >= 2, "K/V ring depth");
+    // head_dim 128: Q's hi part goes to TMEM next to Q_lo (the S product takes
+    // both A operands from TMEM), and Q's shared-memory region, one stage in
+    // size, serves as a further stage once the splitter has copied Q out
+    static constexpr bool kQInTmem = D == 128;
+    static constexpr int kStages = kStagesMain + (kQInTmem ? 1 : 0);
+    static_assert(!kQInTmem || kStageBytes == kQBytes, "Q region as a stage");
     static constexpr int kVBlocks = (kBN / 4) * (D / 4) / 128;  // 4x4 blocks per splitter thread
     static_assert(kVBlocks * 128 == (kBN / 4) * (D / 4), "transpose split");
     static constexpr int kVtCbBytes = 2 * D * 128;  // 32 kv of D V^T rows, then D V^T_lo rows
-    static constexpr int kOffBar = kOffStage + kStages * kStageBytes;
+    static constexpr int kOffBar = kOffStage + kStagesMain * kStageBytes;
     static constexpr int kNumBars = 2 + 3 * kStages + 2 + 2 + 1;
     static constexpr int kSmemBytes = kOffBar + kNumBars * 8 + 16;
     static constexpr bool kStackPV = D <= 64;       // P [V^T; V^T_lo]^T in one MMA
@@ -76,7 +82,11 @@ struct F32Geom {
     static constexpr int kColS = 0;                 // [2][2 kBN]: S halves, then P | P_lo
     static constexpr int kColO = 4 * kBN;           // kOCols (O, or its two halves)
     static constexpr int kColQlo = kColO + kOCols;  // D
-    static_assert(kColQlo + D <= 512, "TMEM budget");
+    static constexpr int kColQhi = kColQlo + D;     // D (head_dim 128)
+    static_assert((kQInTmem ? kColQhi : kColQlo) + D <= 512, "TMEM budget");
+    __host__ __device__ static constexpr int stage_off(int s) {
+        return s < kStagesMain ? kOffStage + s * kStageBytes : kOffQ;
+    }
 };
 
 struct F32Params {
@@ -186,7 +196,11 @@ __global__ void __launch_bounds__(384, 1)
                 if (j >= G::kStages &&
                     !mbar_wait(empty + s, ((j / G::kStages) & 1) ^ 1, abort_flag, &g_f32_status))
                     break;
-                uint8_t* st = sptr + G::kOffStage + s * G::kStageBytes;
+                // the stage in Q's region: only once Q is in TMEM
+                if (G::kQInTmem && j == G::kStagesMain &&
+                    !mbar_wait(bar_qlo, 0, abort_flag, &g_f32_status))
+                    break;
+                uint8_t* st = sptr + G::stage_off(s);
                 mbar_arrive_expect_tx(full + s, 2 * G::kKvBytes);
                 for (int cb = 0; cb < G::kNumCb; ++cb) {
                     tma_load_3d(st + cb * G::kKkCbBytes, &tmK, full + s, cb * 32, j * BN, bh);
@@ -209,12 +223,17 @@ __global__ void __launch_bounds__(384, 1)
             const uint32_t sQ = sbase + G::kOffQ;
             auto issue_s = [&](int j) {
                 const int s = j % G::kStages;
-                const uint32_t sK = sbase + G::kOffStage + s * G::kStageBytes;
+                const uint32_t sK = sbase + G::stage_off(s);
                 const uint32_t d_t = tmem + G::kColS + (j & 1) * 2 * BN;
 #pragma unroll
-                for (int kk = 0; kk < D / 8; ++kk)
-                    mma_tf32_ss(d_t, f32_kdesc(sQ, kk, G::kQCbBytes), f32_kdesc(sK, kk, G::kKkCbBytes),
-                                idesc_s2, kk > 0 ? 1u : 0u);
+                for (int kk = 0; kk < D / 8; ++kk) {
+                    if constexpr (G::kQInTmem)
+                        mma_tf32_ts(d_t, tmem + G::kColQhi + kk * 8,
+                                    f32_kdesc(sK, kk, G::kKkCbBytes), idesc_s2, kk > 0 ? 1u : 0u);
+                    else
+                        mma_tf32_ss(d_t, f32_kdesc(sQ, kk, G::kQCbBytes),
+                                    f32_kdesc(sK, kk, G::kKkCbBytes), idesc_s2, kk > 0 ? 1u : 0u);
+                }
 #pragma unroll
                 for (int kk = 0; kk < D / 8; ++kk)
                     mma_tf32_ts(d_t + BN, tmem + G::kColQlo + kk * 8,
@@ -242,7 +261,7 @@ __global__ void __launch_bounds__(384, 1)
                 if (!mbar_wait(bar_p, j & 1, abort_flag, &g_f32_status)) break;
                 tc_fence_after();
                 const int s = j % G::kStages;
-                const uint32_t sVt = sbase + G::kOffStage + s * G::kStageBytes + G::kOffVt;
+                const uint32_t sVt = sbase + G::stage_off(s) + G::kOffVt;
                 const uint32_t a_p = tmem + G::kColS + (j & 1) * 2 * BN;
                 const uint32_t a_plo = a_p + BN;
                 if constexpr (G::kStackPV) {
@@ -422,12 +441,13 @@ __global__ void __launch_bounds__(384, 1)
         const int r = wq * 32 + lane;
         bool ok = splitter_all(n > 0 && f32_wait(bar_q, 0, abort_flag));
         if (ok) {
-            // Q_lo of row r into TMEM (A operand of the (Q_lo, K) product)
+            // Q_lo of row r into TMEM (A operand of the (Q_lo, K) product),
+            // and at head_dim 128 Q itself (A operand of Q [K; K_lo]^T)
             const uint8_t* sQ = sptr + G::kOffQ;
             const uint32_t t_q = tmem + (static_cast<uint32_t>(wq * 32) << 16) + G::kColQlo;
 #pragma unroll
             for (int cb = 0; cb < D / 32; ++cb) {
-                uint32_t v[32];
+                uint32_t v[32], h[32];
 #pragma unroll
                 for (int ch = 0; ch < 8; ++ch) {
                     const float4 x = *reinterpret_cast<const float4*>(
@@ -436,16 +456,24 @@ __global__ void __launch_bounds__(384, 1)
                     v[4 * ch + 1] = __float_as_uint(tf32_lo(x.y));
                     v[4 * ch + 2] = __float_as_uint(tf32_lo(x.z));
                     v[4 * ch + 3] = __float_as_uint(tf32_lo(x.w));
+                    h[4 * ch] = __float_as_uint(x.x);
+                    h[4 * ch + 1] = __float_as_uint(x.y);
+                    h[4 * ch + 2] = __float_as_uint(x.z);
+                    h[4 * ch + 3] = __float_as_uint(x.w);
                 }
                 tmem_st_x32(t_q + cb * 32, v);
+                if constexpr (G::kQInTmem) tmem_st_x32(t_q + D + cb * 32, h);
             }
             tc_fence_before();
+            // head_dim 128: the producer refills Q's region by TMA after this
+            // arrival, so the reads above are ordered before those writes
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
             mbar_arrive(bar_qlo);
         }
         for (int j = 0; ok && j < n; ++j) {
             const int s = j % G::kStages;
             if (!splitter_all(f32_wait(full + s, (j / G::kStages) & 1, abort_flag))) break;
-            uint8_t* st = sptr + G::kOffStage + s * G::kStageBytes;
+            uint8_t* st = sptr + G::stage_off(s);
             // K_lo: element-wise, into the rows below K's in each column block
             // (same swizzle phase, so the layout is preserved)
             float4* k4 = reinterpret_cast<float4*>(st);
