@@ -29,7 +29,7 @@ def _full_forward(lib, Q, K, V, scale):
     return O, L
 
 
-@pytest.mark.parametrize("world", [1, 2, 4])
+@pytest.mark.parametrize("world", [1, 2, 4, 8])  # 8: the BASELINE CP setting
 def test_ring_emulated_on_one_gpu(lib, cuda, world):
     import torch
 
@@ -112,7 +112,7 @@ def test_cp_step_matches_partial_plus_merge(lib, cuda, D, dt):
     assert torch.allclose(La[fin], Lb[fin], rtol=1e-6, atol=1e-5)
 
 
-@pytest.mark.parametrize("world", [1, 2, 4])
+@pytest.mark.parametrize("world", [1, 2, 4, 8])  # 8: the BASELINE CP setting
 def test_ring_cp_step_emulated_on_one_gpu(lib, cuda, world):
     """The ring schedule through the single-launch step entry, P ranks
     emulated on one GPU, equals the single-GPU causal forward."""

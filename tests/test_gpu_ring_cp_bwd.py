@@ -74,6 +74,7 @@ def _emulated_ring_backward(lib, Q, K, V, O, L, dO, world, C, scale):
     (4, 128, 64, "bf16"),
     (2, 200, 128, "f16"),   # chunk not a multiple of the 128-row block
     (3, 96, 32, "bf16"),
+    (8, 128, 64, "bf16"),   # the BASELINE CP world size
 ])
 def test_cp_backward_emulated_ring_vs_fp64(lib, cuda, world, C, D, dt):
     import torch
