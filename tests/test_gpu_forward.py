@@ -93,6 +93,21 @@ def test_forward_f32_within_1e4(lib, cuda, causal, shape):
     assert max_err(L, L64) < F32_TOL
 
 
+@pytest.mark.parametrize("causal", [False, True])
+@pytest.mark.parametrize("shape", SHAPES, ids=lambda s: "x".join(map(str, s)))
+def test_forward_f32_shapes(lib, cuda, causal, shape):
+    """3xTF32 forward at every head_dim and ragged length, N(0,1) inputs:
+    long enough at head_dim 128 (up to 32 K/V blocks) that every ring stage,
+    the one in Q's shared-memory region included, is refilled many times."""
+    D = shape[3]
+    Q, K, V = (oracle.normal(shape, 700 + shape[2] + D + i) for i in range(3))
+    scale = 1.0 / np.sqrt(D)
+    O, L = run_fwd(lib, (Q, K, V), "f32", causal, scale)
+    O64, L64 = oracle.forward_f64(Q, K, V, scale, causal)
+    assert max_err(O, O64) < F32_TOL, max_err(O, O64)
+    assert max_err(L, L64) < F32_TOL, max_err(L, L64)
+
+
 def test_config2_forward_sampled_units(lib, cuda):
     """BASELINE config 2 (fp16, B4 H16 N2048 D128, non-causal): the whole
     problem runs on the GPU, a sample of (b,h) units is checked in fp64."""
