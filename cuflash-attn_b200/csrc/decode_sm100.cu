@@ -686,16 +686,22 @@ __global__ void __launch_bounds__(kTcThreads, TcGeom<D>::kCtasPerSm)
 
     if (warp == 0) {
         // ------------------------------------------------ TMA producer
-        if (lane == 0 && nb > 0) {
-            prefetch_tmap(&tmQ);
-            prefetch_tmap(&tmK);
-            prefetch_tmap(&tmV);
-            // query rows bhq0 .. bhq0+15; rows of the next group or past the
-            // tensor end fill heads this CTA does not report
-            mbar_arrive_expect_tx(bar_q, G::kQBytes);
-            for (int cb = 0; cb < G::kKcb; ++cb)
-                tma_load_3d(sptr + G::kOffQ + cb * G::kQCbBytes, &tmQ, bar_q, cb * 64,
-                            static_cast<int>(bhq0), 0);
+        // Lane 0 owns the ring (waits, expected bytes); on a paged cache each
+        // lane q < boxes-per-block also loads its page's index and issues that
+        // page's boxes, so small pages do not serialise dozens of copies on
+        // one thread (16-row pages: 32 boxes per 128-row block).
+        if (nb > 0) {
+            if (lane == 0) {
+                prefetch_tmap(&tmQ);
+                prefetch_tmap(&tmK);
+                prefetch_tmap(&tmV);
+                // query rows bhq0 .. bhq0+15; rows of the next group or past the
+                // tensor end fill heads this CTA does not report
+                mbar_arrive_expect_tx(bar_q, G::kQBytes);
+                for (int cb = 0; cb < G::kKcb; ++cb)
+                    tma_load_3d(sptr + G::kOffQ + cb * G::kQCbBytes, &tmQ, bar_q, cb * 64,
+                                static_cast<int>(bhq0), 0);
+            }
             int issued = 0;
             const int ps = 1 << p.page_shift;
             const int per = ps < kTcRows ? ps : kTcRows;  // rows per TMA box (paged)
@@ -703,51 +709,52 @@ __global__ void __launch_bounds__(kTcThreads, TcGeom<D>::kCtasPerSm)
             for (int j = 0; j < nb; ++j) {
                 const int s = j % G::kStages;
                 const int r0 = r_begin + j * kTcRows;
-                // paged: the block's page indices, loaded before the ring wait
-                // so their latency overlaps it
-                int page[kTcRows / 8];
-                if constexpr (kPaged) {
-#pragma unroll
-                    for (int q = 0; q < kTcRows / 8; ++q) {
-                        if (q < npb) {
-                            const int pi = min((r0 + q * per) >> p.page_shift, p.max_pages - 1);
-                            page[q] = p.block_table[static_cast<long long>(b) * p.max_pages + pi];
-                        }
-                    }
+                // paged: this lane's page index, loaded before the ring wait so
+                // that its latency overlaps it
+                int page = 0;
+                if (kPaged && lane < npb) {
+                    const int pi = min((r0 + lane * per) >> p.page_shift, p.max_pages - 1);
+                    page = p.block_table[static_cast<long long>(b) * p.max_pages + pi];
                 }
-                if (j >= G::kStages &&
-                    !mbar_wait(empty + s, ((j / G::kStages) - 1) & 1, abort_flag, &g_dec_status))
-                    break;
+                bool go = true;
+                if (lane == 0) {
+                    go = j < G::kStages ||
+                         mbar_wait(empty + s, ((j / G::kStages) - 1) & 1, abort_flag, &g_dec_status);
+                    if (go) mbar_arrive_expect_tx(full + s, G::kLoadBytes);
+                }
+                // every lane sees lane 0's decision; its expect_tx precedes
+                // every lane's copies
+                if (!__shfl_sync(0xffffffffu, go, 0)) break;
+                __syncwarp();
                 ++issued;
                 uint8_t* st = sptr + s * G::kStageBytes;
-                mbar_arrive_expect_tx(full + s, G::kLoadBytes);
                 if constexpr (!kPaged) {
-                    for (int cb = 0; cb < G::kKcb; ++cb) {
-                        tma_load_3d(st + cb * G::kKvCbBytes, &tmK, full + s, cb * 64, r0, bhk);
-                        tma_load_3d(st + G::kKTileBytes + cb * G::kKvCbBytes, &tmV, full + s,
-                                    cb * 64, r0, bhk);
-                    }
-                } else {
-#pragma unroll
-                    for (int q = 0; q < kTcRows / 8; ++q) {
-                        if (q >= npb) break;
-                        const int rr = q * per;
-                        const int pg = min(max(page[q], 0), p.num_pages - 1);
-                        const int slot = (pg << p.page_shift) + ((r0 + rr) & (ps - 1));
+                    if (lane == 0) {
                         for (int cb = 0; cb < G::kKcb; ++cb) {
-                            tma_load_3d(st + cb * G::kKvCbBytes + rr * 128, &tmK, full + s, cb * 64,
-                                        hk, slot);
-                            tma_load_3d(st + G::kKTileBytes + cb * G::kKvCbBytes + rr * 128, &tmV,
-                                        full + s, cb * 64, hk, slot);
+                            tma_load_3d(st + cb * G::kKvCbBytes, &tmK, full + s, cb * 64, r0, bhk);
+                            tma_load_3d(st + G::kKTileBytes + cb * G::kKvCbBytes, &tmV, full + s,
+                                        cb * 64, r0, bhk);
                         }
+                    }
+                } else if (lane < npb) {
+                    const int rr = lane * per;
+                    const int pg = min(max(page, 0), p.num_pages - 1);
+                    const int slot = (pg << p.page_shift) + ((r0 + rr) & (ps - 1));
+                    for (int cb = 0; cb < G::kKcb; ++cb) {
+                        tma_load_3d(st + cb * G::kKvCbBytes + rr * 128, &tmK, full + s, cb * 64,
+                                    hk, slot);
+                        tma_load_3d(st + G::kKTileBytes + cb * G::kKvCbBytes + rr * 128, &tmV,
+                                    full + s, cb * 64, hk, slot);
                     }
                 }
             }
             // every issued copy lands before the CTA can exit, also after an abort
-            volatile int never = 0;
-            mbar_wait(bar_q, 0, &never, &g_dec_status);
-            for (int j = issued > G::kStages ? issued - G::kStages : 0; j < issued; ++j)
-                mbar_wait(full + j % G::kStages, (j / G::kStages) & 1, &never, &g_dec_status);
+            if (lane == 0) {
+                volatile int never = 0;
+                mbar_wait(bar_q, 0, &never, &g_dec_status);
+                for (int j = issued > G::kStages ? issued - G::kStages : 0; j < issued; ++j)
+                    mbar_wait(full + j % G::kStages, (j / G::kStages) & 1, &never, &g_dec_status);
+            }
         }
     } else if (warp == 1) {
         // ------------------------------------------------ MMA issuer
