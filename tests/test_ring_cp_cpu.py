@@ -1,5 +1,5 @@
 """Ring context parallelism on CPU: the schedule and the multi-process ring
-(world_size 2 and 3, gloo) with the fp64 oracle standing in for the GPU
+(world_size 2 to 4, gloo) with the fp64 oracle standing in for the GPU
 partial-attention kernels, forward and backward.  The assembled result must
 equal full causal attention (and its gradients) over the whole sequence."""
 
@@ -102,7 +102,7 @@ def _worker(rank, world, port, Q, K, V, scale, out_path):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("world", [2, 3])
+@pytest.mark.parametrize("world", [2, 3, 4])
 def test_ring_over_gloo_equals_full_causal_attention(world, tmp_path):
     B, H, D = 1, 2, 32
     N = 2 * world * 12
@@ -214,7 +214,7 @@ def _bwd_worker(rank, world, port, Q, K, V, dO, scale, out_path):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("world", [1, 2, 3])
+@pytest.mark.parametrize("world", [1, 2, 3, 4])
 def test_ring_backward_over_gloo_equals_full_backward(world, tmp_path):
     B, H, D = 1, 2, 16
     N = 2 * world * 8
