@@ -426,8 +426,9 @@ def run_decode(args, lib, dev, world, rank, pk, pk_kind):
     import torch.distributed as dist
 
     c = DECODE
-    B, H, N, D = (args.batch if args.batch_set else c["B"]), c["H"], c["N"], c["D"]
+    B, H, N, D = (args.batch if args.batch_set else c["B"]), c["H"], c["N"], args.head_dim
     Hkv = args.kv_heads or H  # fewer K/V heads than query heads: grouped-query decode
+    is_config4 = B == c["B"] and Hkv == H and D == c["D"]
     g = torch.Generator(device=dev).manual_seed(31 + 1000 * rank)
     q = torch.randn((B, H, 1, D), device=dev, generator=g).to(torch.bfloat16)
     K = torch.randn((B, Hkv, N, D), device=dev, generator=g).to(torch.bfloat16)
@@ -458,14 +459,14 @@ def run_decode(args, lib, dev, world, rank, pk, pk_kind):
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": results[best]["ms"], "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-            "config": {"workload": ("BASELINE config 4: " if B == 64 and Hkv == H else "custom: ") +
+            "config": {"workload": ("BASELINE config 4: " if is_config4 else "custom: ") +
                                    (f"split-KV decode B{B} H{H} Nkv{N} D{D}" if Hkv == H else
                                     f"grouped-query split-KV decode B{B} Hq{H} Hkv{Hkv} Nkv{N} D{D}"),
                        "best_num_splits": best},
             "splits": results,
             "roofline": {"bound": "hbm", "achieved": results[best]["GBps"], "peak": peak,
                          "unit": "GB/s", "frac": results[best]["GBps"] / peak,
-                         "traffic": traffic_from_profiles("decode")},
+                         "traffic": traffic_from_profiles("decode") if is_config4 else None},
         }), flush=True)
     return 0
 
