@@ -249,3 +249,19 @@ def test_ring_backward_over_nccl_two_gpus(tmp_path):
     for r in range(world):
         err, ok = (tmp_path / f"rank{r}.txt").read_text().split()
         assert ok == "True", (r, err)
+
+
+def test_ring_backward_over_nccl_every_gpu(tmp_path):
+    """The ring backward over every GPU of the box when it has more than two
+    (eight on the BASELINE's CP setting), one rank per GPU."""
+    import torch
+    import torch.multiprocessing as mp
+
+    world = torch.cuda.device_count()
+    if world <= 2:
+        pytest.skip("needs more than two GPUs")
+    mp.start_processes(_nccl_worker, args=(world, _free_port(), str(tmp_path)), nprocs=world,
+                       join=True, start_method="spawn")
+    for r in range(world):
+        err, ok = (tmp_path / f"rank{r}.txt").read_text().split()
+        assert ok == "True", (r, err)
