@@ -1,0 +1,620 @@
+// Context-parallel attention over NCCL: the ring driver behind
+// cuflash_attention_{forward,backward}_cp_{bf16,f16} (libcuflash_attn_cp.so).
+//
+// The reference library is single-device; this file has no counterpart
+// there.  It keeps the reference's C-ABI conventions (validation before any
+// CUDA or NCCL call, src/api/flash_attention_api.cu:45-79; stream-ordered
+// workspace, src/backward/flash_attention_backward_typed.cu:373-394) and runs
+// every step's attention through libcuflash_attn.so's one-launch ring-step
+// entry points; the only kernel here fills the running log-sum-exp with -inf.
+//
+// Streams.  The caller's stream runs the step kernels; a library-owned stream
+// per device (comm) runs the NCCL groups and, in the backward, the fp32 adds
+// of the travelling dK/dV accumulators.  K/V of step s (X_s) is the caller's
+// K/V for s = 0 and ring buffer (s - 1) % 2 afterwards; the group of step s
+// sends X_s to rank + 1 and receives X_{s+1} from rank - 1 into the buffer
+// that X_{s-1} used, after step s - 1's kernels have read it.  Step s + 1's
+// kernels wait for that receive.  Every rank issues the same NCCL groups in
+// the same order (forward: one K/V group per step but the last; backward: a
+// K/V group per step but the last and an accumulator group after every
+// step), so the pairing of sends and receives is the same on all ranks.
+
+#include <cuda_runtime.h>
+#include <nccl.h>
+
+#include <cmath>
+#include <cstdint>
+#include <cstring>
+#include <mutex>
+
+#include "cuflash/flash_attention.h"
+#include "cuflash/flash_attention_cp.h"
+
+namespace {
+
+using cuflash::FlashAttentionError;
+
+constexpr int kMaxDevices = 64;
+constexpr int kDefaultReserveSms = 16;
+constexpr int kMaxWorld = 256;  // ranks of one ring (bounds the events of a call)
+
+// ------------------------------------------------------------------ schedule
+
+struct StepPlan {
+    int owner = 0;
+    int n = 0;
+    int q_slot[4] = {};
+    int kv_slot[4] = {};
+    int q_chunk[4] = {};
+    int kv_chunk[4] = {};
+    int launch[4] = {};
+    int num_launches = 0;
+};
+
+void zigzag(int rank, int world, int out[2]) {
+    out[0] = rank;
+    out[1] = 2 * world - 1 - rank;
+}
+
+// Pairs (query slot qi, K/V slot ki) in the order qi-major; a pair is visible
+// unless causal masking hides the whole K/V chunk (it lies after the query
+// chunk).  Forward launches: each pair joins the first launch that does not
+// yet merge its query slot.
+StepPlan plan_step(int rank, int world, int step, bool causal) {
+    StepPlan p;
+    p.owner = ((rank - step) % world + world) % world;
+    int qc[2], kc[2];
+    zigzag(rank, world, qc);
+    zigzag(p.owner, world, kc);
+    bool used[4][2] = {};
+    for (int qi = 0; qi < 2; ++qi)
+        for (int ki = 0; ki < 2; ++ki) {
+            if (causal && kc[ki] > qc[qi]) continue;
+            const int i = p.n++;
+            p.q_slot[i] = qi;
+            p.kv_slot[i] = ki;
+            p.q_chunk[i] = qc[qi];
+            p.kv_chunk[i] = kc[ki];
+            int l = 0;
+            while (used[l][qi]) ++l;
+            used[l][qi] = true;
+            p.launch[i] = l;
+            if (l + 1 > p.num_launches) p.num_launches = l + 1;
+        }
+    return p;
+}
+
+// ------------------------------------------------------------ device state
+
+// Stream-ordered workspace from a library-private pool per device (freed
+// blocks stay cached, so repeated calls do not remap memory).
+FlashAttentionError ws_alloc(void** ptr, size_t bytes, cudaStream_t stream) {
+    static std::mutex mu;
+    static cudaMemPool_t pools[kMaxDevices] = {};
+    *ptr = nullptr;
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices)
+        return FlashAttentionError::CUDA_ERROR;
+    cudaMemPool_t pool;
+    {
+        std::lock_guard<std::mutex> lock(mu);
+        if (pools[dev] == nullptr) {
+            cudaMemPoolProps props = {};
+            props.allocType = cudaMemAllocationTypePinned;
+            props.location.type = cudaMemLocationTypeDevice;
+            props.location.id = dev;
+            cudaMemPool_t p = nullptr;
+            if (cudaMemPoolCreate(&p, &props) != cudaSuccess) return FlashAttentionError::CUDA_ERROR;
+            uint64_t keep = ~0ull;
+            cudaMemPoolSetAttribute(p, cudaMemPoolAttrReleaseThreshold, &keep);
+            pools[dev] = p;
+        }
+        pool = pools[dev];
+    }
+    const cudaError_t err = cudaMallocFromPoolAsync(ptr, bytes, pool, stream);
+    if (err != cudaSuccess) {
+        cudaGetLastError();
+        *ptr = nullptr;
+        return err == cudaErrorMemoryAllocation ? FlashAttentionError::OUT_OF_MEMORY
+                                                : FlashAttentionError::CUDA_ERROR;
+    }
+    return FlashAttentionError::SUCCESS;
+}
+
+// The comm stream of the current device (non-blocking, kept for the life of
+// the process).
+cudaStream_t comm_stream() {
+    static std::mutex mu;
+    static cudaStream_t streams[kMaxDevices] = {};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return nullptr;
+    std::lock_guard<std::mutex> lock(mu);
+    if (streams[dev] == nullptr) {
+        cudaStream_t st = nullptr;
+        if (cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking) != cudaSuccess) return nullptr;
+        streams[dev] = st;
+    }
+    return streams[dev];
+}
+
+__global__ void fill_f32_kernel(float* __restrict__ dst, float value, long long n) {
+    const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;
+    for (long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+         i += stride)
+        dst[i] = value;
+}
+
+FlashAttentionError fill_f32(float* dst, float value, long long n, cudaStream_t stream) {
+    long long blocks = (n + 255) / 256;
+    if (blocks > 1184) blocks = 1184;
+    if (blocks < 1) blocks = 1;
+    fill_f32_kernel<<<static_cast<unsigned>(blocks), 256, 0, stream>>>(dst, value, n);
+    return cudaGetLastError() == cudaSuccess ? FlashAttentionError::SUCCESS
+                                             : FlashAttentionError::CUDA_ERROR;
+}
+
+// Events of one call, destroyed when the call returns (an event destroyed
+// while its record is pending is released once it completes).
+struct Events {
+    static constexpr int kMax = 3 * kMaxWorld + 4;
+    cudaEvent_t ev[kMax] = {};
+    int n = 0;
+    cudaEvent_t make() {
+        if (n >= kMax) return nullptr;
+        cudaEvent_t e = nullptr;
+        if (cudaEventCreateWithFlags(&e, cudaEventDisableTiming) != cudaSuccess) return nullptr;
+        ev[n++] = e;
+        return e;
+    }
+    ~Events() {
+        for (int i = 0; i < n; ++i) cudaEventDestroy(ev[i]);
+    }
+};
+
+// `waiter` waits for the work enqueued on `producer` so far.
+bool join(Events& evs, cudaStream_t waiter, cudaStream_t producer) {
+    cudaEvent_t e = evs.make();
+    return e != nullptr && cudaEventRecord(e, producer) == cudaSuccess &&
+           cudaStreamWaitEvent(waiter, e, 0) == cudaSuccess;
+}
+
+// --------------------------------------------------------------- dtype glue
+
+template <typename T>
+struct CpOps;
+
+template <>
+struct CpOps<__nv_bfloat16> {
+    using T = __nv_bfloat16;
+    static int step(const T* Q, const T* K, const T* V, float* O, float* L, int B, int H, int C,
+                    int D, float s, bool causal, int n, const int* qs, const int* ks,
+                    const long long* qo, const long long* ko, int reserve, cudaStream_t st) {
+        return cuflash_attention_forward_cp_step_bf16(Q, K, V, O, L, 2, 2, B, H, C, D, s, causal,
+                                                      n, qs, ks, qo, ko, reserve, st);
+    }
+    static int convert(const float* src, T* dst, long long n, cudaStream_t st) {
+        return cuflash_convert_f32_to_bf16(src, dst, n, st);
+    }
+    static int bwd_prepare(const T* O, const T* dO, const float* L, void* ws, int B, int H, int C,
+                           int D, cudaStream_t st) {
+        return cuflash_attention_backward_cp_prepare_bf16(O, dO, L, ws, 2, B, H, C, D, st);
+    }
+    static int bwd_step(const T* Q, const T* dO, const T* K, const T* V, void* ws, float* dk,
+                        float* dv, int B, int H, int C, int D, float s, bool causal, int n,
+                        const int* qs, const int* ks, const long long* qo, const long long* ko,
+                        int reserve, cudaStream_t st) {
+        return cuflash_attention_backward_cp_step_bf16(Q, dO, K, V, ws, dk, dv, 2, 2, B, H, C, D,
+                                                       s, causal, n, qs, ks, qo, ko, reserve, st);
+    }
+    static int bwd_finish(const void* ws, T* dQ, int B, int H, int C, int D, float s,
+                          cudaStream_t st) {
+        return cuflash_attention_backward_cp_finish_bf16(ws, dQ, 2, B, H, C, D, s, st);
+    }
+};
+
+template <>
+struct CpOps<half> {
+    using T = half;
+    static int step(const T* Q, const T* K, const T* V, float* O, float* L, int B, int H, int C,
+                    int D, float s, bool causal, int n, const int* qs, const int* ks,
+                    const long long* qo, const long long* ko, int reserve, cudaStream_t st) {
+        return cuflash_attention_forward_cp_step_f16(Q, K, V, O, L, 2, 2, B, H, C, D, s, causal,
+                                                     n, qs, ks, qo, ko, reserve, st);
+    }
+    static int convert(const float* src, T* dst, long long n, cudaStream_t st) {
+        return cuflash_convert_f32_to_f16(src, dst, n, st);
+    }
+    static int bwd_prepare(const T* O, const T* dO, const float* L, void* ws, int B, int H, int C,
+                           int D, cudaStream_t st) {
+        return cuflash_attention_backward_cp_prepare_f16(O, dO, L, ws, 2, B, H, C, D, st);
+    }
+    static int bwd_step(const T* Q, const T* dO, const T* K, const T* V, void* ws, float* dk,
+                        float* dv, int B, int H, int C, int D, float s, bool causal, int n,
+                        const int* qs, const int* ks, const long long* qo, const long long* ko,
+                        int reserve, cudaStream_t st) {
+        return cuflash_attention_backward_cp_step_f16(Q, dO, K, V, ws, dk, dv, 2, 2, B, H, C, D, s,
+                                                      causal, n, qs, ks, qo, ko, reserve, st);
+    }
+    static int bwd_finish(const void* ws, T* dQ, int B, int H, int C, int D, float s,
+                          cudaStream_t st) {
+        return cuflash_attention_backward_cp_finish_f16(ws, dQ, 2, B, H, C, D, s, st);
+    }
+};
+
+FlashAttentionError code(int c) { return static_cast<FlashAttentionError>(c); }
+
+// -------------------------------------------------------------- validation
+
+FlashAttentionError validate(const void* const* ptrs, int nptrs, int B, int H, int N, int D,
+                             float scale, ncclComm_t comm, int rank, int world, int reserve_sms) {
+    for (int i = 0; i < nptrs; ++i)
+        if (ptrs[i] == nullptr) return FlashAttentionError::NULL_POINTER;
+    if (B <= 0 || H <= 0 || N <= 0 || D <= 0 || world <= 0 || world > kMaxWorld || rank < 0 ||
+        rank >= world || reserve_sms < -1)
+        return FlashAttentionError::INVALID_DIMENSION;
+    if (N % (2 * world) != 0) return FlashAttentionError::INVALID_DIMENSION;
+    if (static_cast<long long>(B) * H * 2 > 0x7fffffffLL)
+        return FlashAttentionError::INVALID_DIMENSION;
+    if (!(D == 32 || D == 64 || D == 128)) return FlashAttentionError::UNSUPPORTED_HEAD_DIM;
+    if (!std::isfinite(scale) || scale < 0.0f) return FlashAttentionError::INVALID_DIMENSION;
+    if (world > 1 && comm == nullptr) return FlashAttentionError::NULL_POINTER;
+    return FlashAttentionError::SUCCESS;
+}
+
+// After validation: the communicator must match the ranks the caller names.
+FlashAttentionError check_comm(ncclComm_t comm, int rank, int world) {
+    if (world == 1 && comm == nullptr) return FlashAttentionError::SUCCESS;
+    int n = 0, r = 0;
+    if (ncclCommCount(comm, &n) != ncclSuccess || ncclCommUserRank(comm, &r) != ncclSuccess)
+        return FlashAttentionError::CUDA_ERROR;
+    if (n != world || r != rank) return FlashAttentionError::DIMENSION_MISMATCH;
+    return FlashAttentionError::SUCCESS;
+}
+
+// One ring hop of a K/V pair (and nothing else) in one NCCL group.
+bool exchange(const void* send_k, const void* send_v, void* recv_k, void* recv_v, size_t bytes,
+              int rank, int world, ncclComm_t comm, cudaStream_t st) {
+    const int next = (rank + 1) % world, prev = (rank - 1 + world) % world;
+    bool ok = ncclGroupStart() == ncclSuccess;
+    ok = ok && ncclSend(send_k, bytes, ncclUint8, next, comm, st) == ncclSuccess;
+    ok = ok && ncclSend(send_v, bytes, ncclUint8, next, comm, st) == ncclSuccess;
+    ok = ok && ncclRecv(recv_k, bytes, ncclUint8, prev, comm, st) == ncclSuccess;
+    ok = ok && ncclRecv(recv_v, bytes, ncclUint8, prev, comm, st) == ncclSuccess;
+    return (ncclGroupEnd() == ncclSuccess) && ok;
+}
+
+bool exchange_one(const void* send, void* recv, size_t bytes, int rank, int world,
+                  ncclComm_t comm, cudaStream_t st) {
+    const int next = (rank + 1) % world, prev = (rank - 1 + world) % world;
+    bool ok = ncclGroupStart() == ncclSuccess;
+    ok = ok && ncclSend(send, bytes, ncclUint8, next, comm, st) == ncclSuccess;
+    ok = ok && ncclRecv(recv, bytes, ncclUint8, prev, comm, st) == ncclSuccess;
+    return (ncclGroupEnd() == ncclSuccess) && ok;
+}
+
+int effective_reserve(int reserve_sms, int world) {
+    if (world == 1) return 0;  // no transfer runs beside the kernels
+    return reserve_sms < 0 ? kDefaultReserveSms : reserve_sms;
+}
+
+// ------------------------------------------------------------------ forward
+
+template <typename T>
+FlashAttentionError forward_cp(const T* Q, const T* K, const T* V, T* O, float* L, int B, int H,
+                               int N, int D, float scale, bool causal, ncclComm_t comm, int rank,
+                               int world, int reserve_sms, cudaStream_t stream) {
+    const void* ptrs[] = {Q, K, V, O, L};
+    FlashAttentionError e = validate(ptrs, 5, B, H, N, D, scale, comm, rank, world, reserve_sms);
+    if (e != FlashAttentionError::SUCCESS) return e;
+    e = check_comm(comm, rank, world);
+    if (e != FlashAttentionError::SUCCESS) return e;
+
+    const int C = N / (2 * world);
+    const long long elems = 2LL * B * H * C * D;  // both slots of one tensor
+    const size_t kv_bytes = static_cast<size_t>(elems) * sizeof(T);
+    const size_t oacc_bytes = static_cast<size_t>(elems) * sizeof(float);
+    const size_t ws_bytes = oacc_bytes + (world > 1 ? 4 * kv_bytes : 0);
+    const int reserve = effective_reserve(reserve_sms, world);
+    cudaStream_t cs = world > 1 ? comm_stream() : nullptr;
+    if (world > 1 && cs == nullptr) return FlashAttentionError::CUDA_ERROR;
+
+    void* ws = nullptr;
+    e = ws_alloc(&ws, ws_bytes, stream);
+    if (e != FlashAttentionError::SUCCESS) return e;
+    float* O_acc = static_cast<float*>(ws);
+    T* buf_k[2] = {nullptr, nullptr};
+    T* buf_v[2] = {nullptr, nullptr};
+    if (world > 1) {
+        char* b = static_cast<char*>(ws) + oacc_bytes;
+        for (int i = 0; i < 2; ++i) {
+            buf_k[i] = reinterpret_cast<T*>(b + (2 * i) * kv_bytes);
+            buf_v[i] = reinterpret_cast<T*>(b + (2 * i + 1) * kv_bytes);
+        }
+    }
+    Events evs;
+    bool ok = cudaMemsetAsync(O_acc, 0, oacc_bytes, stream) == cudaSuccess;
+    if (ok) e = fill_f32(L, -INFINITY, elems / D, stream);
+    ok = ok && e == FlashAttentionError::SUCCESS;
+    if (ok && world > 1) ok = join(evs, cs, stream);  // K, V and the workspace are ready
+
+    const T* cur_k = K;
+    const T* cur_v = V;
+    cudaEvent_t comp_prev = nullptr;  // step s-1's kernels have been enqueued up to here
+    for (int s = 0; ok && s < world; ++s) {
+        const StepPlan p = plan_step(rank, world, s, causal);
+        cudaEvent_t recv_done = nullptr;
+        if (s + 1 < world) {
+            T* nk = buf_k[s % 2];
+            T* nv = buf_v[s % 2];
+            // the buffer receiving X_{s+1} held X_{s-1}: step s-1 must have read it
+            if (s >= 2) ok = cudaStreamWaitEvent(cs, comp_prev, 0) == cudaSuccess;
+            ok = ok && exchange(cur_k, cur_v, nk, nv, kv_bytes, rank, world, comm, cs);
+            recv_done = evs.make();
+            ok = ok && recv_done != nullptr && cudaEventRecord(recv_done, cs) == cudaSuccess;
+        }
+        for (int l = 0; ok && l < p.num_launches; ++l) {
+            int qs[4], ks[4], n = 0;
+            long long qo[4], ko[4];
+            for (int i = 0; i < p.n; ++i) {
+                if (p.launch[i] != l) continue;
+                qs[n] = p.q_slot[i];
+                ks[n] = p.kv_slot[i];
+                qo[n] = static_cast<long long>(p.q_chunk[i]) * C;
+                ko[n] = static_cast<long long>(p.kv_chunk[i]) * C;
+                ++n;
+            }
+            e = code(CpOps<T>::step(Q, cur_k, cur_v, O_acc, L, B, H, C, D, scale, causal, n, qs,
+                                    ks, qo, ko, reserve, stream));
+            ok = e == FlashAttentionError::SUCCESS;
+        }
+        if (ok && s + 1 < world) {
+            comp_prev = evs.make();
+            ok = comp_prev != nullptr && cudaEventRecord(comp_prev, stream) == cudaSuccess;
+            ok = ok && cudaStreamWaitEvent(stream, recv_done, 0) == cudaSuccess;
+            cur_k = buf_k[s % 2];
+            cur_v = buf_v[s % 2];
+        }
+    }
+    if (ok) {
+        e = code(CpOps<T>::convert(O_acc, O, elems, stream));
+        ok = e == FlashAttentionError::SUCCESS;
+    }
+    // the comm stream has no work left past the last receive the caller's
+    // stream waited for, so the workspace can go back to the pool
+    if (world > 1 && !ok) join(evs, stream, cs);
+    cudaFreeAsync(ws, stream);
+    if (!ok) return e != FlashAttentionError::SUCCESS ? e : FlashAttentionError::CUDA_ERROR;
+    return FlashAttentionError::SUCCESS;
+}
+
+// ----------------------------------------------------------------- backward
+
+template <typename T>
+FlashAttentionError backward_cp(const T* Q, const T* K, const T* V, const T* O, const float* L,
+                                const T* dO, T* dQ, T* dK, T* dV, int B, int H, int N, int D,
+                                float scale, bool causal, ncclComm_t comm, int rank, int world,
+                                int reserve_sms, cudaStream_t stream) {
+    if (!dO || !dQ || !dK || !dV) return FlashAttentionError::NULL_POINTER;
+    const void* ptrs[] = {Q, K, V, O, L};
+    FlashAttentionError e = validate(ptrs, 5, B, H, N, D, scale, comm, rank, world, reserve_sms);
+    if (e != FlashAttentionError::SUCCESS) return e;
+    e = check_comm(comm, rank, world);
+    if (e != FlashAttentionError::SUCCESS) return e;
+
+    const int C = N / (2 * world);
+    const long long elems = 2LL * B * H * C * D;
+    const size_t kv_bytes = static_cast<size_t>(elems) * sizeof(T);
+    const long long bwd_ws = cuflash_attention_backward_cp_workspace_size(2, B, H, C, D);
+    if (bwd_ws <= 0) return FlashAttentionError::INVALID_DIMENSION;
+    const size_t bwd_bytes = (static_cast<size_t>(bwd_ws) + 255) & ~static_cast<size_t>(255);
+    // one accumulator = dK and dV of both K/V slots, fp32
+    const size_t acc_bytes = 2 * static_cast<size_t>(elems) * sizeof(float);
+    const int n_acc = world > 1 ? 2 : 1;
+    const int n_part = world > 1 ? 2 : 0;
+    const size_t ws_bytes =
+        bwd_bytes + (n_acc + n_part) * acc_bytes + (world > 1 ? 4 * kv_bytes : 0);
+    const int reserve = effective_reserve(reserve_sms, world);
+    cudaStream_t cs = world > 1 ? comm_stream() : nullptr;
+    if (world > 1 && cs == nullptr) return FlashAttentionError::CUDA_ERROR;
+
+    void* ws = nullptr;
+    e = ws_alloc(&ws, ws_bytes, stream);
+    if (e != FlashAttentionError::SUCCESS) return e;
+    char* base = static_cast<char*>(ws);
+    void* ws_bwd = base;
+    float* acc[2] = {nullptr, nullptr};
+    float* part[2] = {nullptr, nullptr};
+    char* b = base + bwd_bytes;
+    for (int i = 0; i < n_acc; ++i, b += acc_bytes) acc[i] = reinterpret_cast<float*>(b);
+    for (int i = 0; i < n_part; ++i, b += acc_bytes) part[i] = reinterpret_cast<float*>(b);
+    T* buf_k[2] = {nullptr, nullptr};
+    T* buf_v[2] = {nullptr, nullptr};
+    if (world > 1)
+        for (int i = 0; i < 2; ++i) {
+            buf_k[i] = reinterpret_cast<T*>(b + (2 * i) * kv_bytes);
+            buf_v[i] = reinterpret_cast<T*>(b + (2 * i + 1) * kv_bytes);
+        }
+    // dK of both slots, then dV of both slots
+    auto dk_of = [&](float* a) { return a; };
+    auto dv_of = [&](float* a) { return a + elems; };
+
+    Events evs;
+    e = code(CpOps<T>::bwd_prepare(O, dO, L, ws_bwd, B, H, C, D, stream));
+    bool ok = e == FlashAttentionError::SUCCESS;
+    ok = ok && cudaMemsetAsync(acc[0], 0, acc_bytes, stream) == cudaSuccess;
+    for (int i = 0; ok && i < n_part; ++i)
+        ok = cudaMemsetAsync(part[i], 0, acc_bytes, stream) == cudaSuccess;
+    if (ok && world > 1) ok = join(evs, cs, stream);
+
+    const T* cur_k = K;
+    const T* cur_v = V;
+    cudaEvent_t comp_prev = nullptr;
+    cudaEvent_t part_free[2] = {nullptr, nullptr};  // part buffer cleared by its add
+    int acc_cur = 0;
+    for (int s = 0; ok && s < world; ++s) {
+        const StepPlan p = plan_step(rank, world, s, causal);
+        cudaEvent_t recv_done = nullptr;
+        if (s + 1 < world) {
+            if (s >= 2) ok = cudaStreamWaitEvent(cs, comp_prev, 0) == cudaSuccess;
+            ok = ok && exchange(cur_k, cur_v, buf_k[s % 2], buf_v[s % 2], kv_bytes, rank, world,
+                                comm, cs);
+            recv_done = evs.make();
+            ok = ok && recv_done != nullptr && cudaEventRecord(recv_done, cs) == cudaSuccess;
+        }
+        float* target = s == 0 ? acc[0] : part[s % 2];
+        if (ok && s >= 2 && part_free[s % 2] != nullptr)
+            ok = cudaStreamWaitEvent(stream, part_free[s % 2], 0) == cudaSuccess;
+        if (ok && p.n > 0) {
+            int qs[4], ks[4];
+            long long qo[4], ko[4];
+            for (int i = 0; i < p.n; ++i) {
+                qs[i] = p.q_slot[i];
+                ks[i] = p.kv_slot[i];
+                qo[i] = static_cast<long long>(p.q_chunk[i]) * C;
+                ko[i] = static_cast<long long>(p.kv_chunk[i]) * C;
+            }
+            e = code(CpOps<T>::bwd_step(Q, dO, cur_k, cur_v, ws_bwd, dk_of(target), dv_of(target),
+                                        B, H, C, D, scale, causal, p.n, qs, ks, qo, ko, reserve,
+                                        stream));
+            ok = e == FlashAttentionError::SUCCESS;
+        }
+        if (ok && world > 1) {
+            comp_prev = evs.make();
+            ok = comp_prev != nullptr && cudaEventRecord(comp_prev, stream) == cudaSuccess;
+            ok = ok && cudaStreamWaitEvent(cs, comp_prev, 0) == cudaSuccess;
+            if (ok && s > 0) {
+                // the accumulator of this step's K/V owner arrived in the
+                // previous group; add this step's part into it and clear the part
+                e = code(cuflash_accumulate_f32(acc[acc_cur], target, 2 * elems, true, cs));
+                ok = e == FlashAttentionError::SUCCESS;
+                part_free[s % 2] = evs.make();
+                ok = ok && part_free[s % 2] != nullptr &&
+                     cudaEventRecord(part_free[s % 2], cs) == cudaSuccess;
+            }
+            ok = ok && exchange_one(acc[acc_cur], acc[1 - acc_cur], acc_bytes, rank, world, comm,
+                                    cs);
+            acc_cur = 1 - acc_cur;
+        }
+        if (ok && s + 1 < world) {
+            ok = cudaStreamWaitEvent(stream, recv_done, 0) == cudaSuccess;
+            cur_k = buf_k[s % 2];
+            cur_v = buf_v[s % 2];
+        }
+    }
+    // this rank's own accumulator came in with the last group
+    if (ok && world > 1) ok = join(evs, stream, cs);
+    float* final_acc = acc[world > 1 ? acc_cur : 0];
+    if (ok) {
+        e = code(CpOps<T>::bwd_finish(ws_bwd, dQ, B, H, C, D, scale, stream));
+        ok = e == FlashAttentionError::SUCCESS;
+    }
+    if (ok) {
+        e = code(CpOps<T>::convert(dk_of(final_acc), dK, elems, stream));
+        ok = e == FlashAttentionError::SUCCESS;
+    }
+    if (ok) {
+        e = code(CpOps<T>::convert(dv_of(final_acc), dV, elems, stream));
+        ok = e == FlashAttentionError::SUCCESS;
+    }
+    if (world > 1 && !ok) join(evs, stream, cs);
+    cudaFreeAsync(ws, stream);
+    if (!ok) return e != FlashAttentionError::SUCCESS ? e : FlashAttentionError::CUDA_ERROR;
+    return FlashAttentionError::SUCCESS;
+}
+
+}  // namespace
+
+extern "C" {
+
+int cuflash_attention_forward_cp_bf16(const __nv_bfloat16* Q, const __nv_bfloat16* K,
+                                      const __nv_bfloat16* V, __nv_bfloat16* O, float* L,
+                                      int batch_size, int num_heads, int seq_len, int head_dim,
+                                      float scale, bool causal, ncclComm_t comm, int rank,
+                                      int world, int reserve_sms, cudaStream_t stream) {
+    return static_cast<int>(forward_cp<__nv_bfloat16>(Q, K, V, O, L, batch_size, num_heads,
+                                                      seq_len, head_dim, scale, causal, comm,
+                                                      rank, world, reserve_sms, stream));
+}
+
+int cuflash_attention_forward_cp_f16(const half* Q, const half* K, const half* V, half* O,
+                                     float* L, int batch_size, int num_heads, int seq_len,
+                                     int head_dim, float scale, bool causal, ncclComm_t comm,
+                                     int rank, int world, int reserve_sms, cudaStream_t stream) {
+    return static_cast<int>(forward_cp<half>(Q, K, V, O, L, batch_size, num_heads, seq_len,
+                                             head_dim, scale, causal, comm, rank, world,
+                                             reserve_sms, stream));
+}
+
+int cuflash_attention_backward_cp_bf16(const __nv_bfloat16* Q, const __nv_bfloat16* K,
+                                       const __nv_bfloat16* V, const __nv_bfloat16* O,
+                                       const float* L, const __nv_bfloat16* dO,
+                                       __nv_bfloat16* dQ, __nv_bfloat16* dK, __nv_bfloat16* dV,
+                                       int batch_size, int num_heads, int seq_len, int head_dim,
+                                       float scale, bool causal, ncclComm_t comm, int rank,
+                                       int world, int reserve_sms, cudaStream_t stream) {
+    return static_cast<int>(backward_cp<__nv_bfloat16>(
+        Q, K, V, O, L, dO, dQ, dK, dV, batch_size, num_heads, seq_len, head_dim, scale, causal,
+        comm, rank, world, reserve_sms, stream));
+}
+
+int cuflash_attention_backward_cp_f16(const half* Q, const half* K, const half* V, const half* O,
+                                      const float* L, const half* dO, half* dQ, half* dK,
+                                      half* dV, int batch_size, int num_heads, int seq_len,
+                                      int head_dim, float scale, bool causal, ncclComm_t comm,
+                                      int rank, int world, int reserve_sms, cudaStream_t stream) {
+    return static_cast<int>(backward_cp<half>(Q, K, V, O, L, dO, dQ, dK, dV, batch_size,
+                                              num_heads, seq_len, head_dim, scale, causal, comm,
+                                              rank, world, reserve_sms, stream));
+}
+
+int cuflash_cp_ring_schedule(int rank, int world, int step, bool causal, int* kv_owner,
+                             int* num_pairs, int* q_slot, int* kv_slot, int* q_chunk,
+                             int* kv_chunk, int* fwd_launch) {
+    if (!kv_owner || !num_pairs || !q_slot || !kv_slot || !q_chunk || !kv_chunk || !fwd_launch)
+        return static_cast<int>(FlashAttentionError::NULL_POINTER);
+    if (world <= 0 || rank < 0 || rank >= world || step < 0 || step >= world)
+        return static_cast<int>(FlashAttentionError::INVALID_DIMENSION);
+    const StepPlan p = plan_step(rank, world, step, causal);
+    *kv_owner = p.owner;
+    *num_pairs = p.n;
+    for (int i = 0; i < p.n; ++i) {
+        q_slot[i] = p.q_slot[i];
+        kv_slot[i] = p.kv_slot[i];
+        q_chunk[i] = p.q_chunk[i];
+        kv_chunk[i] = p.kv_chunk[i];
+        fwd_launch[i] = p.launch[i];
+    }
+    return static_cast<int>(FlashAttentionError::SUCCESS);
+}
+
+int cuflash_cp_nccl_unique_id(void* unique_id, int nbytes) {
+    if (unique_id == nullptr) return static_cast<int>(FlashAttentionError::NULL_POINTER);
+    if (nbytes < static_cast<int>(sizeof(ncclUniqueId)))
+        return static_cast<int>(FlashAttentionError::INVALID_DIMENSION);
+    ncclUniqueId id;
+    if (ncclGetUniqueId(&id) != ncclSuccess)
+        return static_cast<int>(FlashAttentionError::CUDA_ERROR);
+    std::memcpy(unique_id, &id, sizeof(id));
+    return static_cast<int>(FlashAttentionError::SUCCESS);
+}
+
+int cuflash_cp_nccl_comm_init(ncclComm_t* comm, int world, const void* unique_id, int rank) {
+    if (comm == nullptr || unique_id == nullptr)
+        return static_cast<int>(FlashAttentionError::NULL_POINTER);
+    if (world <= 0 || rank < 0 || rank >= world)
+        return static_cast<int>(FlashAttentionError::INVALID_DIMENSION);
+    ncclUniqueId id;
+    std::memcpy(&id, unique_id, sizeof(id));
+    return static_cast<int>(ncclCommInitRank(comm, world, id, rank) == ncclSuccess
+                                ? FlashAttentionError::SUCCESS
+                                : FlashAttentionError::CUDA_ERROR);
+}
+
+int cuflash_cp_nccl_comm_destroy(ncclComm_t comm) {
+    if (comm == nullptr) return static_cast<int>(FlashAttentionError::NULL_POINTER);
+    return static_cast<int>(ncclCommDestroy(comm) == ncclSuccess
+                                ? FlashAttentionError::SUCCESS
+                                : FlashAttentionError::CUDA_ERROR);
+}
+
+}  // extern "C"

@@ -258,7 +258,7 @@ template <typename T>
 FlashAttentionError cp_step_impl(const T* Q, const T* K, const T* V, float* O_acc, float* L_acc,
                                  int nq, int nk, int B, int H, int C, int D, float scale,
                                  bool causal, int num_pairs, const int* q_slot, const int* kv_slot,
-                                 const long long* q_off, const long long* kv_off,
+                                 const long long* q_off, const long long* kv_off, int reserve_sms,
                                  cudaStream_t stream) {
     if (!Q || !K || !V || !O_acc || !L_acc || !q_slot || !kv_slot || !q_off || !kv_off)
         return FlashAttentionError::NULL_POINTER;
@@ -266,7 +266,8 @@ FlashAttentionError cp_step_impl(const T* Q, const T* K, const T* V, float* O_ac
         return FlashAttentionError::INVALID_DIMENSION;
     if (!(D == 32 || D == 64 || D == 128)) return FlashAttentionError::UNSUPPORTED_HEAD_DIM;
     if (!std::isfinite(scale) || scale < 0.0f) return FlashAttentionError::INVALID_DIMENSION;
-    if (num_pairs < 1 || num_pairs > 4) return FlashAttentionError::INVALID_DIMENSION;
+    if (num_pairs < 1 || num_pairs > 4 || reserve_sms < 0)
+        return FlashAttentionError::INVALID_DIMENSION;
     if (static_cast<long long>(B) * H * (nq > nk ? nq : nk) > 0x7fffffffLL)
         return FlashAttentionError::INVALID_DIMENSION;
     for (int i = 0; i < num_pairs; ++i) {
@@ -278,7 +279,7 @@ FlashAttentionError cp_step_impl(const T* Q, const T* K, const T* V, float* O_ac
     }
     return cuflash::detail::launch_fwd_cp_step_sm100<T>(Q, K, V, O_acc, L_acc, nq, nk, B, H, C, D,
                                                         scale, causal, num_pairs, q_slot, kv_slot,
-                                                        q_off, kv_off, stream);
+                                                        q_off, kv_off, reserve_sms, stream);
 }
 
 FlashAttentionError cp_dims_check(int nq, int B, int H, int C, int D) {
@@ -304,7 +305,7 @@ FlashAttentionError cp_bwd_step_impl(const T* Q, const T* dO, const T* K, const 
                                      int C, int D, float scale, bool causal, int num_pairs,
                                      const int* q_slot, const int* kv_slot,
                                      const long long* q_off, const long long* kv_off,
-                                     cudaStream_t stream) {
+                                     int reserve_sms, cudaStream_t stream) {
     if (!Q || !dO || !K || !V || !ws || !dK_acc || !dV_acc || !q_slot || !kv_slot || !q_off ||
         !kv_off)
         return FlashAttentionError::NULL_POINTER;
@@ -312,14 +313,21 @@ FlashAttentionError cp_bwd_step_impl(const T* Q, const T* dO, const T* K, const 
     if (e == FlashAttentionError::SUCCESS) e = cp_dims_check(nk, B, H, C, D);
     if (e != FlashAttentionError::SUCCESS) return e;
     if (!std::isfinite(scale) || scale < 0.0f) return FlashAttentionError::INVALID_DIMENSION;
-    if (num_pairs < 1 || num_pairs > 4) return FlashAttentionError::INVALID_DIMENSION;
-    for (int i = 0; i < num_pairs; ++i)
+    if (num_pairs < 1 || num_pairs > 4 || reserve_sms < 0)
+        return FlashAttentionError::INVALID_DIMENSION;
+    for (int i = 0; i < num_pairs; ++i) {
         if (q_slot[i] < 0 || q_slot[i] >= nq || kv_slot[i] < 0 || kv_slot[i] >= nk ||
             q_off[i] < 0 || kv_off[i] < 0)
             return FlashAttentionError::INVALID_DIMENSION;
+        // a repeated (query slot, K/V slot) pair would add its gradients twice
+        for (int k = 0; k < i; ++k)
+            if (q_slot[k] == q_slot[i] && kv_slot[k] == kv_slot[i])
+                return FlashAttentionError::INVALID_DIMENSION;
+    }
     return cuflash::detail::launch_bwd_cp_step_sm100<T>(Q, dO, K, V, ws, dK_acc, dV_acc, nq, nk,
                                                         B * H, C, D, scale, causal, num_pairs,
-                                                        q_slot, kv_slot, q_off, kv_off, stream);
+                                                        q_slot, kv_slot, q_off, kv_off,
+                                                        reserve_sms, stream);
 }
 
 template <typename T>
@@ -515,10 +523,12 @@ int cuflash_attention_forward_cp_step_bf16(const __nv_bfloat16* Q, const __nv_bf
                                            int num_heads, int chunk_len, int head_dim, float scale,
                                            bool causal, int num_pairs, const int* q_slot,
                                            const int* kv_slot, const long long* q_offset,
-                                           const long long* kv_offset, cudaStream_t stream) {
+                                           const long long* kv_offset, int reserve_sms,
+                                           cudaStream_t stream) {
     return static_cast<int>(cp_step_impl<__nv_bfloat16>(
         Q, K, V, O_acc, L_acc, num_q_slots, num_kv_slots, batch_size, num_heads, chunk_len,
-        head_dim, scale, causal, num_pairs, q_slot, kv_slot, q_offset, kv_offset, stream));
+        head_dim, scale, causal, num_pairs, q_slot, kv_slot, q_offset, kv_offset, reserve_sms,
+        stream));
 }
 
 int cuflash_attention_forward_cp_step_f16(const half* Q, const half* K, const half* V,
@@ -527,11 +537,11 @@ int cuflash_attention_forward_cp_step_f16(const half* Q, const half* K, const ha
                                           int chunk_len, int head_dim, float scale, bool causal,
                                           int num_pairs, const int* q_slot, const int* kv_slot,
                                           const long long* q_offset, const long long* kv_offset,
-                                          cudaStream_t stream) {
+                                          int reserve_sms, cudaStream_t stream) {
     return static_cast<int>(cp_step_impl<half>(Q, K, V, O_acc, L_acc, num_q_slots, num_kv_slots,
                                                batch_size, num_heads, chunk_len, head_dim, scale,
                                                causal, num_pairs, q_slot, kv_slot, q_offset,
-                                               kv_offset, stream));
+                                               kv_offset, reserve_sms, stream));
 }
 
 long long cuflash_attention_backward_cp_workspace_size(int num_q_slots, int batch_size,
@@ -557,11 +567,11 @@ long long cuflash_attention_backward_cp_workspace_size(int num_q_slots, int batc
         float* dV_acc, int num_q_slots, int num_kv_slots, int batch_size, int num_heads,         \
         int chunk_len, int head_dim, float scale, bool causal, int num_pairs, const int* q_slot, \
         const int* kv_slot, const long long* q_offset, const long long* kv_offset,               \
-        cudaStream_t stream) {                                                                   \
+        int reserve_sms, cudaStream_t stream) {                                                  \
         return static_cast<int>(cp_bwd_step_impl<T>(                                             \
             Q, dO, K, V, workspace, dK_acc, dV_acc, num_q_slots, num_kv_slots, batch_size,       \
             num_heads, chunk_len, head_dim, scale, causal, num_pairs, q_slot, kv_slot, q_offset, \
-            kv_offset, stream));                                                                 \
+            kv_offset, reserve_sms, stream));                                                    \
     }                                                                                            \
     int cuflash_attention_backward_cp_finish_##SUFFIX(const void* workspace, T* dQ,              \
                                                       int num_q_slots, int batch_size,           \
@@ -628,5 +638,12 @@ int cuflash_attention_decode_bf16_noalloc(const __nv_bfloat16* Q, const __nv_bfl
 }
 
 int cuflash_device_status(void) { return cuflash::detail::read_and_clear_device_status(); }
+
+int cuflash_set_option(const char* name, int value) {
+    if (name == nullptr) return static_cast<int>(FlashAttentionError::NULL_POINTER);
+    return static_cast<int>(cuflash::detail::set_option(name, value)
+                                ? FlashAttentionError::SUCCESS
+                                : FlashAttentionError::INVALID_DIMENSION);
+}
 
 }  // extern "C"

@@ -1236,7 +1236,8 @@ FlashAttentionError bwd_cp_step_typed(const T* Q, const T* dO, const T* K, const
                                       float* dk_acc, float* dv_acc, int nq, int nk, int BH, int C,
                                       float scale, bool causal, int num_pairs, const int* q_slot,
                                       const int* kv_slot, const long long* q_off,
-                                      const long long* kv_off, cudaStream_t stream) {
+                                      const long long* kv_off, int reserve_sms,
+                                      cudaStream_t stream) {
     using G = BwdGeom<D>;
     const long long qheads = static_cast<long long>(nq) * BH;
     const long long kheads = static_cast<long long>(nk) * BH;
@@ -1303,9 +1304,10 @@ FlashAttentionError bwd_cp_step_typed(const T* Q, const T* dO, const T* K, const
     if (units > 0x7fffffffLL) return FlashAttentionError::CUDA_ERROR;
     prm.seg_units = static_cast<int>(seg_units);
     prm.num_units = static_cast<int>(units);
-    // Leave SMs to the ring's concurrent transfers, as the forward step does.
+    // reserve_sms SMs stay free for the ring's concurrent transfer kernels,
+    // as in the forward step.
     int grid = persistent_grid(units, env_int("CUFLASH_BWD_WAVES", 1));
-    grid = std::max(1, std::min(grid, sms - env_int("CUFLASH_CP_RESERVE_SMS", 16)));
+    grid = std::max(1, std::min(grid, sms - reserve_sms));
     kern<<<grid, kBwdThreads, G::kSmemBytes, stream>>>(mq, mk, mv, mdo, mdq, prm);
     return cudaGetLastError() == cudaSuccess ? FlashAttentionError::SUCCESS
                                              : FlashAttentionError::CUDA_ERROR;
@@ -1369,10 +1371,12 @@ FlashAttentionError launch_bwd_cp_step_sm100(const T* Q, const T* dO, const T* K
                                              int nk, int BH, int C, int D, float scale,
                                              bool causal, int num_pairs, const int* q_slot,
                                              const int* kv_slot, const long long* q_off,
-                                             const long long* kv_off, cudaStream_t stream) {
+                                             const long long* kv_off, int reserve_sms,
+                                             cudaStream_t stream) {
 #define CUFLASH_CP_STEP(DD)                                                                    \
     return bwd_cp_step_typed<T, DD>(Q, dO, K, V, ws, dk_acc, dv_acc, nq, nk, BH, C, scale,    \
-                                    causal, num_pairs, q_slot, kv_slot, q_off, kv_off, stream)
+                                    causal, num_pairs, q_slot, kv_slot, q_off, kv_off,        \
+                                    reserve_sms, stream)
     switch (D) {
         case 32: CUFLASH_CP_STEP(32);
         case 64: CUFLASH_CP_STEP(64);
@@ -1406,7 +1410,7 @@ FlashAttentionError launch_accumulate_f32(float* dst, float* src, long long coun
         const T*, const T*, const float*, void*, int, int, int, int, cudaStream_t);             \
     template FlashAttentionError launch_bwd_cp_step_sm100<T>(                                   \
         const T*, const T*, const T*, const T*, void*, float*, float*, int, int, int, int, int, \
-        float, bool, int, const int*, const int*, const long long*, const long long*,           \
+        float, bool, int, const int*, const int*, const long long*, const long long*, int,      \
         cudaStream_t);                                                                          \
     template FlashAttentionError launch_bwd_cp_finish_sm100<T>(const void*, T*, int, int, int, \
                                                                int, float, cudaStream_t);

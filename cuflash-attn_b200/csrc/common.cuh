@@ -74,14 +74,18 @@ bool ensure_smem_attr(const void* kernel, int bytes);
 
 int current_sm_count();
 int persistent_grid(long long units, int waves);
+// Value of a process-wide option (initialised once from the environment
+// variable of the same name, changed by cuflash_set_option), or dflt when
+// it is not set.
 int env_int(const char* name, int dflt);
+bool set_option(const char* name, int value);
 
 // Stream-ordered workspace from a library-private memory pool on the current
 // device (created on first use; freed blocks stay cached in the pool so
 // repeated calls do not remap memory).  Returns OUT_OF_MEMORY when the pool
-// cannot grow.  Setting the environment variable
-// CUFLASH_FAULT_WORKSPACE_OOM=1 makes every request fail with OUT_OF_MEMORY
-// before any CUDA call (host-side fault injection for tests).
+// cannot grow.  The option CUFLASH_FAULT_WORKSPACE_OOM=1 makes every request
+// fail with OUT_OF_MEMORY before any CUDA call (host-side fault injection for
+// tests).
 FlashAttentionError workspace_alloc(void** ptr, size_t bytes, cudaStream_t stream);
 void workspace_free(void* ptr, cudaStream_t stream);
 
@@ -127,14 +131,15 @@ FlashAttentionError launch_fwd_gqa_sm100(const T* Q, const T* K, const T* V, T* 
 
 // One context-parallel ring step: num_pairs (<= 4) partial forwards of query
 // slot q_slot[i] against K/V slot k_slot[i] (global offsets q_off/k_off), each
-// merged in place into O_acc / L_acc of its query slot; one launch.
+// merged in place into O_acc / L_acc of its query slot; one launch that keeps
+// reserve_sms SMs free.
 template <typename T>
 FlashAttentionError launch_fwd_cp_step_sm100(const T* Q, const T* K, const T* V, float* O_acc,
                                              float* L_acc, int nq, int nk, int B, int H, int C,
                                              int D, float scale, bool causal, int num_pairs,
                                              const int* q_slot, const int* k_slot,
                                              const long long* q_off, const long long* k_off,
-                                             cudaStream_t stream);
+                                             int reserve_sms, cudaStream_t stream);
 
 // Context-parallel backward.  The workspace (bwd_cp_workspace_bytes) holds
 // the fp32 dQ accumulator and the per-query -L*log2(e) / -rowsum(dO*O) of nq
@@ -152,7 +157,8 @@ FlashAttentionError launch_bwd_cp_step_sm100(const T* Q, const T* dO, const T* K
                                              int nk, int BH, int C, int D, float scale,
                                              bool causal, int num_pairs, const int* q_slot,
                                              const int* kv_slot, const long long* q_off,
-                                             const long long* kv_off, cudaStream_t stream);
+                                             const long long* kv_off, int reserve_sms,
+                                             cudaStream_t stream);
 template <typename T>
 FlashAttentionError launch_bwd_cp_finish_sm100(const void* ws, T* dQ, int nq, int BH, int C, int D,
                                                float scale, cudaStream_t stream);

@@ -700,6 +700,7 @@ struct FwdSegs {
     long long q_off[kMaxSegs] = {0, 0, 0, 0};
     long long k_off[kMaxSegs] = {0, 0, 0, 0};
     bool merge = false;
+    int reserve_sms = 0;  // SMs a ring-step launch leaves free (merge only)
     int hq = 1;     // query heads per batch entry (BH = batch * hq)
     int group = 1;  // query heads per K/V head
 };
@@ -759,8 +760,7 @@ FlashAttentionError launch_typed(const T* Q, const T* K, const T* V, void* O, fl
     // the transfer kernels run concurrently instead of after this launch.
     // Measured on 8 B200s (config 5): 16 free SMs 17.0 ms per step, 8: 21.3,
     // none: 20.4 (the transfer then waits for the launch to end).
-    if (sg.merge)
-        grid = std::max(1, std::min(grid, sms - env_int("CUFLASH_CP_RESERVE_SMS", 16)));
+    if (sg.merge) grid = std::max(1, std::min(grid, sms - sg.reserve_sms));
     if (grid <= 0) return FlashAttentionError::SUCCESS;
     kern<<<grid, 384, G::kSmemBytes, stream>>>(mq, mk, mv, prm);
     return cudaGetLastError() == cudaSuccess ? FlashAttentionError::SUCCESS
@@ -828,13 +828,14 @@ FlashAttentionError launch_fwd_cp_step_sm100(const T* Q, const T* K, const T* V,
                                              int D, float scale, bool causal, int num_pairs,
                                              const int* q_slot, const int* k_slot,
                                              const long long* q_off, const long long* k_off,
-                                             cudaStream_t stream) {
+                                             int reserve_sms, cudaStream_t stream) {
     if (num_pairs < 1 || num_pairs > kMaxSegs) return FlashAttentionError::INVALID_DIMENSION;
     FwdSegs sg;
     sg.nq_slots = nq;
     sg.nk_slots = nk;
     sg.num_segs = num_pairs;
     sg.merge = true;
+    sg.reserve_sms = reserve_sms;
     for (int i = 0; i < num_pairs; ++i) {
         sg.q_slot[i] = q_slot[i];
         sg.k_slot[i] = k_slot[i];
@@ -847,10 +848,10 @@ FlashAttentionError launch_fwd_cp_step_sm100(const T* Q, const T* K, const T* V,
 template FlashAttentionError launch_fwd_cp_step_sm100<__nv_bfloat16>(
     const __nv_bfloat16*, const __nv_bfloat16*, const __nv_bfloat16*, float*, float*, int, int,
     int, int, int, int, float, bool, int, const int*, const int*, const long long*,
-    const long long*, cudaStream_t);
+    const long long*, int, cudaStream_t);
 template FlashAttentionError launch_fwd_cp_step_sm100<half>(
     const half*, const half*, const half*, float*, float*, int, int, int, int, int, int, float,
-    bool, int, const int*, const int*, const long long*, const long long*, cudaStream_t);
+    bool, int, const int*, const int*, const long long*, const long long*, int, cudaStream_t);
 
 template FlashAttentionError launch_fwd_sm100<__nv_bfloat16>(const __nv_bfloat16*,
                                                              const __nv_bfloat16*,

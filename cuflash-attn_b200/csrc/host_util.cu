@@ -4,7 +4,9 @@
 
 #include <cudaTypedefs.h>
 
+#include <atomic>
 #include <cstdlib>
+#include <cstring>
 #include <mutex>
 #include <utility>
 
@@ -109,11 +111,54 @@ int persistent_grid(long long units, int waves) {
     return static_cast<int>(units < cap ? units : cap);
 }
 
+namespace {
+
+// Process-wide options.  Each starts from its environment variable, read
+// once on first use (so no launch calls getenv, which is not safe against a
+// concurrent setenv in another thread), and can be changed at any time
+// through cuflash_set_option.  -1 = not set (the call site's default).
+struct Option {
+    const char* name;
+    std::atomic<int> value;
+};
+Option g_options[] = {
+    {"CUFLASH_RESERVE_SMS", {-1}},       // SMs left out of every persistent launch
+    {"CUFLASH_FWD_WAVES", {-1}},         // persistent forward grid, in waves of SMs
+    {"CUFLASH_BWD_WAVES", {-1}},         // persistent backward grid
+    {"CUFLASH_CP_WAVES", {-1}},          // context-parallel forward step grid
+    {"CUFLASH_DECODE_GQA_TC", {-1}},     // 0 selects the SIMT grouped-query decode
+    {"CUFLASH_FAULT_WORKSPACE_OOM", {-1}},  // 1 fails every workspace request (tests)
+};
+constexpr int kNumOptions = sizeof(g_options) / sizeof(g_options[0]);
+
+Option* find_option(const char* name) {
+    static std::once_flag once;
+    std::call_once(once, [] {
+        for (Option& o : g_options) {
+            const char* v = getenv(o.name);
+            if (v == nullptr || *v == '\0') continue;
+            const int n = atoi(v);
+            if (n >= 0 && n <= 64) o.value.store(n);
+        }
+    });
+    for (int i = 0; i < kNumOptions; ++i)
+        if (std::strcmp(g_options[i].name, name) == 0) return &g_options[i];
+    return nullptr;
+}
+
+}  // namespace
+
 int env_int(const char* name, int dflt) {
-    const char* v = getenv(name);
-    if (!v || !*v) return dflt;
-    const int n = atoi(v);
-    return n >= 0 && n <= 64 ? n : dflt;
+    Option* o = find_option(name);
+    const int v = o != nullptr ? o->value.load(std::memory_order_relaxed) : -1;
+    return v >= 0 ? v : dflt;
+}
+
+bool set_option(const char* name, int value) {
+    Option* o = find_option(name);
+    if (o == nullptr) return false;
+    o->value.store(value < 0 ? -1 : value);
+    return true;
 }
 
 int current_sm_count() {
@@ -134,9 +179,7 @@ int current_sm_count() {
 
 FlashAttentionError workspace_alloc(void** ptr, size_t bytes, cudaStream_t stream) {
     *ptr = nullptr;
-    const char* fault = std::getenv("CUFLASH_FAULT_WORKSPACE_OOM");
-    if (fault != nullptr && fault[0] != '\0' && fault[0] != '0')
-        return FlashAttentionError::OUT_OF_MEMORY;
+    if (env_int("CUFLASH_FAULT_WORKSPACE_OOM", 0) != 0) return FlashAttentionError::OUT_OF_MEMORY;
     static std::mutex mu;
     static cudaMemPool_t pools[64] = {};
     int dev = 0;

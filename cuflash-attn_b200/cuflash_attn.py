@@ -63,13 +63,17 @@ SIGNATURES = {
     "cuflash_attention_forward_gqa_f16": [_P] * 5 + [_I] * 6 + [_F, _B, _P],
     "cuflash_attention_backward_gqa_bf16": [_P] * 9 + [_I] * 6 + [_F, _B, _P],
     "cuflash_attention_backward_gqa_f16": [_P] * 9 + [_I] * 6 + [_F, _B, _P],
-    "cuflash_attention_forward_cp_step_bf16": [_P] * 5 + [_I] * 6 + [_F, _B, _I] + [_P] * 5,
-    "cuflash_attention_forward_cp_step_f16": [_P] * 5 + [_I] * 6 + [_F, _B, _I] + [_P] * 5,
+    "cuflash_attention_forward_cp_step_bf16": [_P] * 5 + [_I] * 6 + [_F, _B, _I] + [_P] * 4
+    + [_I, _P],
+    "cuflash_attention_forward_cp_step_f16": [_P] * 5 + [_I] * 6 + [_F, _B, _I] + [_P] * 4
+    + [_I, _P],
     "cuflash_attention_backward_cp_workspace_size": [_I] * 5,
     "cuflash_attention_backward_cp_prepare_bf16": [_P] * 4 + [_I] * 5 + [_P],
     "cuflash_attention_backward_cp_prepare_f16": [_P] * 4 + [_I] * 5 + [_P],
-    "cuflash_attention_backward_cp_step_bf16": [_P] * 7 + [_I] * 6 + [_F, _B, _I] + [_P] * 5,
-    "cuflash_attention_backward_cp_step_f16": [_P] * 7 + [_I] * 6 + [_F, _B, _I] + [_P] * 5,
+    "cuflash_attention_backward_cp_step_bf16": [_P] * 7 + [_I] * 6 + [_F, _B, _I] + [_P] * 4
+    + [_I, _P],
+    "cuflash_attention_backward_cp_step_f16": [_P] * 7 + [_I] * 6 + [_F, _B, _I] + [_P] * 4
+    + [_I, _P],
     "cuflash_attention_backward_cp_finish_bf16": [_P] * 2 + [_I] * 5 + [_F, _P],
     "cuflash_attention_backward_cp_finish_f16": [_P] * 2 + [_I] * 5 + [_F, _P],
     "cuflash_accumulate_f32": [_P, _P, _LL, _B, _P],
@@ -77,6 +81,7 @@ SIGNATURES = {
     "cuflash_convert_f32_to_bf16": [_P, _P, _LL, _P],
     "cuflash_convert_f32_to_f16": [_P, _P, _LL, _P],
     "cuflash_device_status": [],
+    "cuflash_set_option": [ctypes.c_char_p, _I],
 }
 _RESTYPES = {"cuflash_error_string": ctypes.c_char_p,
              "cuflash_attention_backward_cp_workspace_size": ctypes.c_longlong}
@@ -306,11 +311,13 @@ class CuFlashAttn:
         return dQ, dK, dV
 
     def forward_cp_step(self, Q, K, V, O_acc, L_acc, pairs, causal: bool = True,
-                        scale: Optional[float] = None, stream=None) -> None:
+                        scale: Optional[float] = None, reserve_sms: int = 0,
+                        stream=None) -> None:
         """One context-parallel ring step in one launch.  Q [nq,B,H,C,D] and
         K, V [nk,B,H,C,D] hold stacked chunks; O_acc fp32 [nq,B,H,C,D] and
         L_acc fp32 [nq,B,H,C] are updated in place.  `pairs` lists up to four
-        (q_slot, kv_slot, q_offset, kv_offset) with distinct q_slot."""
+        (q_slot, kv_slot, q_offset, kv_offset) with distinct q_slot;
+        `reserve_sms` SMs stay free for concurrent transfers."""
         nq, B, H, C, D = Q.shape
         nk = K.shape[0]
         if scale is None:
@@ -324,7 +331,7 @@ class CuFlashAttn:
         self.check_error(fn(_ptr(Q), _ptr(K), _ptr(V), _ptr(O_acc), _ptr(L_acc), nq, nk, B, H, C,
                             D, float(scale), bool(causal), n, ctypes.cast(qs, _P),
                             ctypes.cast(ks, _P), ctypes.cast(qo, _P), ctypes.cast(ko, _P),
-                            _stream_handle(stream)))
+                            int(reserve_sms), _stream_handle(stream)))
 
     @staticmethod
     def _pair_arrays(pairs):
@@ -355,7 +362,7 @@ class CuFlashAttn:
 
     def backward_cp_step(self, Q, dO, K, V, workspace, dK_acc, dV_acc, pairs,
                          causal: bool = True, scale: Optional[float] = None,
-                         stream=None) -> None:
+                         reserve_sms: int = 0, stream=None) -> None:
         """One ring step of the context-parallel backward in one launch: Q, dO
         [nq,B,H,C,D], K, V [nk,B,H,C,D]; scale*dK and dV of the step are added
         into dK_acc / dV_acc fp32 [nk,B,H,C,D], dQ into the workspace.
@@ -369,7 +376,7 @@ class CuFlashAttn:
         self.check_error(fn(_ptr(Q), _ptr(dO), _ptr(K), _ptr(V), _ptr(workspace), _ptr(dK_acc),
                             _ptr(dV_acc), nq, nk, B, H, C, D, float(scale), bool(causal), n,
                             ctypes.cast(qs, _P), ctypes.cast(ks, _P), ctypes.cast(qo, _P),
-                            ctypes.cast(ko, _P), _stream_handle(stream)))
+                            ctypes.cast(ko, _P), int(reserve_sms), _stream_handle(stream)))
 
     def backward_cp_finish(self, workspace, dQ, scale: Optional[float] = None,
                            stream=None) -> None:
@@ -399,3 +406,8 @@ class CuFlashAttn:
 
     def device_status(self) -> int:
         return int(self.lib.cuflash_device_status())
+
+    def set_option(self, name: str, value: int) -> None:
+        """Sets a process-wide option (see ``cuflash_set_option``); a
+        negative value restores the built-in default."""
+        self.check_error(self.lib.cuflash_set_option(name.encode(), int(value)))

@@ -276,18 +276,21 @@ CUFLASH_EXPORT int cuflash_attention_backward_gqa_f16(
 // positions when causal is set, and folds the result into O_acc / L_acc of
 // that slot with the log-sum-exp merge of cuflash_lse_merge_f32.  The pairs
 // of one call must name distinct query slots.  O_acc / L_acc start as 0 /
-// -inf; the slot-index and offset arrays are host memory.
+// -inf; the slot-index and offset arrays are host memory.  reserve_sms (>= 0)
+// SMs are left out of the launch's persistent grid, for kernels that run at
+// the same time (a ring's NCCL transfer); 0 uses every SM.
 CUFLASH_EXPORT int cuflash_attention_forward_cp_step_bf16(
     const __nv_bfloat16* Q, const __nv_bfloat16* K, const __nv_bfloat16* V, float* O_acc,
     float* L_acc, int num_q_slots, int num_kv_slots, int batch_size, int num_heads,
     int chunk_len, int head_dim, float scale, bool causal, int num_pairs, const int* q_slot,
-    const int* kv_slot, const long long* q_offset, const long long* kv_offset,
+    const int* kv_slot, const long long* q_offset, const long long* kv_offset, int reserve_sms,
     cudaStream_t stream);
 CUFLASH_EXPORT int cuflash_attention_forward_cp_step_f16(
     const half* Q, const half* K, const half* V, float* O_acc, float* L_acc, int num_q_slots,
     int num_kv_slots, int batch_size, int num_heads, int chunk_len, int head_dim, float scale,
     bool causal, int num_pairs, const int* q_slot, const int* kv_slot,
-    const long long* q_offset, const long long* kv_offset, cudaStream_t stream);
+    const long long* q_offset, const long long* kv_offset, int reserve_sms,
+    cudaStream_t stream);
 
 // Context-parallel backward, the ring counterpart of the step above (no
 // reference counterpart).  Per query slot q the caller holds the forward's
@@ -301,7 +304,9 @@ CUFLASH_EXPORT int cuflash_attention_forward_cp_step_f16(
 //                   as in the forward step): dQ of the query slot is added into
 //                   the workspace, scale*dK and dV of the K/V slot are ADDED
 //                   into dK_acc / dV_acc, fp32 [kv slot][B][H][C][D].  Pairs
-//                   may share query or K/V slots;
+//                   may share query or K/V slots, but a (query slot, K/V
+//                   slot) pair may not repeat (INVALID_DIMENSION);
+//                   reserve_sms as in the forward step;
 //   finish          writes dQ = scale * (accumulated dQ) for all query slots.
 // The slot-index and offset arrays are host memory.  dK_acc / dV_acc travel
 // the ring with the K/V they belong to; the final dK / dV are their values
@@ -323,12 +328,13 @@ CUFLASH_EXPORT int cuflash_attention_backward_cp_step_bf16(
     const __nv_bfloat16* V, void* workspace, float* dK_acc, float* dV_acc, int num_q_slots,
     int num_kv_slots, int batch_size, int num_heads, int chunk_len, int head_dim, float scale,
     bool causal, int num_pairs, const int* q_slot, const int* kv_slot,
-    const long long* q_offset, const long long* kv_offset, cudaStream_t stream);
+    const long long* q_offset, const long long* kv_offset, int reserve_sms,
+    cudaStream_t stream);
 CUFLASH_EXPORT int cuflash_attention_backward_cp_step_f16(
     const half* Q, const half* dO, const half* K, const half* V, void* workspace, float* dK_acc,
     float* dV_acc, int num_q_slots, int num_kv_slots, int batch_size, int num_heads,
     int chunk_len, int head_dim, float scale, bool causal, int num_pairs, const int* q_slot,
-    const int* kv_slot, const long long* q_offset, const long long* kv_offset,
+    const int* kv_slot, const long long* q_offset, const long long* kv_offset, int reserve_sms,
     cudaStream_t stream);
 CUFLASH_EXPORT int cuflash_attention_backward_cp_finish_bf16(const void* workspace,
                                                              __nv_bfloat16* dQ, int num_q_slots,
@@ -366,6 +372,22 @@ CUFLASH_EXPORT int cuflash_convert_f32_to_f16(const float* src, half* dst, long 
 // out; the host reads and clears it with this call (synchronises the
 // current device).  Returns 0 when no kernel reported a timeout.
 CUFLASH_EXPORT int cuflash_device_status(void);
+
+// Process-wide tuning and test options (no reference counterpart).  Each
+// option starts from the environment variable of the same name, read once
+// when the library first needs an option; this call changes it afterwards
+// (thread-safe; launches already enqueued keep the value they saw).  A
+// negative value returns the option to its built-in default.  Options:
+//   CUFLASH_RESERVE_SMS          SMs left out of every persistent launch
+//                                (for collectives that run concurrently);
+//   CUFLASH_FWD_WAVES, CUFLASH_BWD_WAVES, CUFLASH_CP_WAVES
+//                                persistent grid size in waves of SMs;
+//   CUFLASH_DECODE_GQA_TC        0 routes grouped-query decode to the SIMT
+//                                kernel instead of the tensor-core one;
+//   CUFLASH_FAULT_WORKSPACE_OOM  1 makes every workspace request fail with
+//                                OUT_OF_MEMORY (host-side fault injection).
+// Returns SUCCESS, NULL_POINTER, or INVALID_DIMENSION for an unknown name.
+CUFLASH_EXPORT int cuflash_set_option(const char* name, int value);
 
 #ifdef __cplusplus
 }

@@ -456,6 +456,23 @@ long long oracle_train_step_rows_f32(const float* Q, const float* K, const float
     return tot;
 }
 
+// fp64 forward of selected query rows only (for problems too large for the
+// full O(N^2) oracle): Q, K, V [U, N, D]; rows[r] is both the row index and
+// the query's global position (keys at 0..N-1), so each sampled row is
+// fwd_unit_f64 with one query; O [U, nrows, D], L [U, nrows] for the units
+// u0 <= u < u1 (indexed from u0).  Work items are (unit, row) pairs.
+void oracle_forward_rows_f64(const float* Q, const float* K, const float* V, double* O, double* L,
+                             long long u0, long long u1, const long long* rows, int nrows, int N,
+                             int D, double scale, int causal, int nthreads) {
+    const size_t T = (size_t)N * D;
+    parallel_units(0, (u1 - u0) * nrows, nthreads, [&](long long w) {
+        const long long u = u0 + w / nrows;
+        const int r = static_cast<int>(w % nrows);
+        fwd_unit_f64(Q + u * T + (size_t)rows[r] * D, K + u * T, V + u * T, O + (size_t)w * D,
+                     L + w, 1, N, D, scale, causal != 0, rows[r], 0);
+    });
+}
+
 int oracle_abi_version(void) { return 1; }
 
 }  // extern "C"

@@ -59,9 +59,11 @@ def lib():
         L.oracle_train_step_rows_f32.argtypes = [_f32p] * 9 + [_LL, _LL, _I, _I, ctypes.c_float,
                                                    _I, _I, _I, _I]
         L.oracle_train_step_rows_f32.restype = ctypes.c_longlong
+        L.oracle_forward_rows_f64.argtypes = [_f32p] * 3 + [ctypes.c_void_p] * 2 + [
+            _LL, _LL, ctypes.c_void_p, _I, _I, _I, ctypes.c_double, _I, _I]
         for f in ("oracle_fill_interleaved_uniform", "oracle_fill_uniform", "oracle_fill_normal",
                   "oracle_forward_f32", "oracle_backward_f32", "oracle_forward_f64",
-                  "oracle_backward_f64", "oracle_backward_gen_f64"):
+                  "oracle_backward_f64", "oracle_backward_gen_f64", "oracle_forward_rows_f64"):
             getattr(L, f).restype = None
         _lib = L
     return _lib
@@ -146,6 +148,19 @@ def forward_f64(Q, K, V, scale, causal, q_offset=0, k_offset=0, units=None, nthr
     L = np.zeros((B, H, Nq), np.float64)
     lib().oracle_forward_f64(Q, K, V, _vp(O), _vp(L), u0, u1, Nq, Nk, D, float(scale),
                              int(causal), int(q_offset), int(k_offset), int(nthreads))
+    return O, L
+
+
+def forward_rows_f64(Q, K, V, scale, causal, rows, nthreads=16):
+    """fp64 forward of the query rows `rows` only; Q, K, V [B,H,N,D], row
+    index = global position.  Returns O [B,H,len(rows),D], L [B,H,len(rows)]."""
+    Q, K, V = (np.ascontiguousarray(x, np.float32) for x in (Q, K, V))
+    B, H, N, D = Q.shape
+    r = np.ascontiguousarray(rows, np.int64)
+    O = np.zeros((B, H, len(r), D), np.float64)
+    L = np.zeros((B, H, len(r)), np.float64)
+    lib().oracle_forward_rows_f64(Q, K, V, _vp(O), _vp(L), 0, B * H, _vp(r), len(r), N, D,
+                                  float(scale), int(causal), int(nthreads))
     return O, L
 
 

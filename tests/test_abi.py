@@ -45,6 +45,26 @@ def test_library_exports_every_declared_symbol():
         assert hasattr(lib, name), name
 
 
+CP_HEADER = ROOT / "include" / "cuflash" / "flash_attention_cp.h"
+
+
+def test_cp_library_exports_every_declared_symbol():
+    """libcuflash_attn_cp.so (the NCCL ring) exports exactly what
+    flash_attention_cp.h declares, and the ctypes binding covers it."""
+    import subprocess
+
+    import ring_cp
+
+    text = CP_HEADER.read_text()
+    c_part = text[text.index('extern "C"'):]
+    declared = set(re.findall(r"CUFLASH_EXPORT\s+[\w\s\*]+?\b(cuflash_\w+)\s*\(", c_part))
+    assert declared == set(ring_cp.CP_SIGNATURES)
+    out = subprocess.run(["nm", "-D", "--defined-only", str(ring_cp.DEFAULT_CP_LIB)],
+                         capture_output=True, text=True, check=True).stdout
+    exported = {ln.split()[-1] for ln in out.splitlines() if " T " in ln}
+    assert exported == declared, exported ^ declared
+
+
 def test_library_hides_internal_symbols():
     import subprocess
 
@@ -222,10 +242,11 @@ def test_cp_step_validation(lib, sfx):
     def arr(ct, vals):
         return ctypes.cast((ct * len(vals))(*vals), ctypes.c_void_p)
 
-    def call(q=(0, 1), k=(0, 1), qo=(0, 64), ko=(0, 64), n=2, D=64, nq=2, nk=2, ptr=None):
+    def call(q=(0, 1), k=(0, 1), qo=(0, 64), ko=(0, 64), n=2, D=64, nq=2, nk=2, ptr=None,
+             reserve=0):
         args = [FAKE] * 5 + [nq, nk, 1, 2, 64, D, 0.1, True, n, arr(ctypes.c_int, q),
                              arr(ctypes.c_int, k), arr(ctypes.c_longlong, qo),
-                             arr(ctypes.c_longlong, ko), STREAM]
+                             arr(ctypes.c_longlong, ko), reserve, STREAM]
         if ptr is not None:
             args[ptr] = NUL
         return fn(*args)
@@ -240,6 +261,7 @@ def test_cp_step_validation(lib, sfx):
     assert call(k=(0, -1)) == 1
     assert call(qo=(0, -64)) == 1                 # negative global offset
     assert call(nq=0) == 1
+    assert call(reserve=-1) == 1                  # SM reserve must be >= 0
 
 
 @pytest.mark.parametrize("sfx", ["f16", "bf16"])
@@ -269,10 +291,10 @@ def test_cp_backward_validation(lib, sfx):
         return ctypes.cast((ct * len(vals))(*vals), ctypes.c_void_p)
 
     def call(q=(0, 1), k=(0, 0), qo=(0, 64), ko=(0, 0), n=2, D=64, nq=2, nk=2, ptr=None,
-             scale=0.1):
+             scale=0.1, reserve=0):
         args = [FAKE] * 7 + [nq, nk, 1, 2, 64, D, scale, True, n, arr(ctypes.c_int, q),
                              arr(ctypes.c_int, k), arr(ctypes.c_longlong, qo),
-                             arr(ctypes.c_longlong, ko), STREAM]
+                             arr(ctypes.c_longlong, ko), reserve, STREAM]
         if ptr is not None:
             args[ptr] = NUL
         return fn(*args)
@@ -288,6 +310,9 @@ def test_cp_backward_validation(lib, sfx):
     assert call(ko=(0, -1)) == 1                  # negative global offset
     assert call(nk=0) == 1
     assert call(scale=-1.0) == 1
+    assert call(reserve=-2) == 1
+    # a repeated (query slot, K/V slot) pair would add its gradients twice
+    assert call(q=(1, 1), k=(0, 0), qo=(64, 64), ko=(0, 0)) == 1
 
     acc = L.cuflash_accumulate_f32
     assert acc(NUL, FAKE, 16, False, STREAM) == 3
@@ -305,13 +330,23 @@ def test_oracle_is_test_infrastructure_only():
     assert oracle.LIB_PATH.name == "liboracle.so"
 
 
-def test_workspace_oom_fault_injection(lib, monkeypatch):
+def test_workspace_oom_fault_injection(lib):
     """Host-side fault injection: a failing workspace allocation surfaces as
     OUT_OF_MEMORY (the reference maps cudaMallocAsync failure the same way,
     src/backward/flash_attention_backward_typed.cu:378-387).  The request
     fails before any CUDA call, so no GPU is involved."""
-    monkeypatch.setenv("CUFLASH_FAULT_WORKSPACE_OOM", "1")
-    for sfx in ("f16", "bf16"):
-        assert _bwd(lib, sfx, N=256, D=64) == cf.OUT_OF_MEMORY
-        fn = getattr(lib.lib, f"cuflash_attention_decode_{sfx}")
-        assert fn(FAKE, FAKE, FAKE, FAKE, FAKE, 2, 2, 4096, 128, 0.1, 8, STREAM) == cf.OUT_OF_MEMORY
+    lib.set_option("CUFLASH_FAULT_WORKSPACE_OOM", 1)
+    try:
+        for sfx in ("f16", "bf16"):
+            assert _bwd(lib, sfx, N=256, D=64) == cf.OUT_OF_MEMORY
+            fn = getattr(lib.lib, f"cuflash_attention_decode_{sfx}")
+            assert fn(FAKE, FAKE, FAKE, FAKE, FAKE, 2, 2, 4096, 128, 0.1, 8,
+                      STREAM) == cf.OUT_OF_MEMORY
+    finally:
+        lib.set_option("CUFLASH_FAULT_WORKSPACE_OOM", -1)
+
+
+def test_set_option_validation(lib):
+    assert lib.lib.cuflash_set_option(None, 1) == cf.NULL_POINTER
+    assert lib.lib.cuflash_set_option(b"CUFLASH_NO_SUCH_OPTION", 1) == cf.INVALID_DIMENSION
+    assert lib.lib.cuflash_set_option(b"CUFLASH_RESERVE_SMS", -1) == cf.SUCCESS

@@ -117,15 +117,22 @@ def test_decode_paged_vs_fp64(lib, cuda, dt, page_size, Hq, Hkv, splits, D):
 @pytest.mark.parametrize("D", [64, 128])
 @pytest.mark.parametrize("tc", ["1", "0"])
 @pytest.mark.parametrize("Hq,Hkv", [(48, 2), (64, 2), (4, 2)])
-def test_decode_gqa_large_groups_and_rescale(lib, cuda, monkeypatch, tc, Hq, Hkv, D):
+def test_decode_gqa_large_groups_and_rescale(lib, cuda, tc, Hq, Hkv, D):
     """Groups above 16 heads (several head tiles per K/V head on the tensor-
     core path) and scores that grow along the cache (later rows dominate,
     so running maxima rise across blocks and O is rescaled), on both the
     tensor-core kernel (CUFLASH_DECODE_GQA_TC=1, head_dim 64 and 128) and the
     SIMT kernel (=0)."""
+    lib.set_option("CUFLASH_DECODE_GQA_TC", int(tc))
+    try:
+        _check_large_groups(lib, Hq, Hkv, D)
+    finally:
+        lib.set_option("CUFLASH_DECODE_GQA_TC", -1)
+
+
+def _check_large_groups(lib, Hq, Hkv, D):
     import torch
 
-    monkeypatch.setenv("CUFLASH_DECODE_GQA_TC", tc)
     B, N, dt = 2, 1500, "bf16"
     scale = 1.0 / np.sqrt(D)
     q = round_to(oracle.normal((B, Hq, 1, D), 21), dt)

@@ -1,15 +1,14 @@
-"""Ring context parallelism on the GPU.
+"""Ring context parallelism on the GPU, step by step.
 
 * P ranks emulated in one process on one GPU (no communication: each
-  "rank" receives the next owner's K/V payload directly), through the real
-  partial-forward / LSE-merge / convert kernels; every rank's output chunks
-  must match the single-GPU causal forward over the whole sequence.
-* With two or more GPUs: a real two-process ring over NCCL
-  (RingAttention, batch_isend_irecv), checked the same way.
+  "rank" receives the next owner's K/V payload directly), walking the
+  library's ring schedule through the real partial-forward / LSE-merge /
+  convert kernels or the one-launch ring-step entry; every rank's output
+  chunks must match the single-GPU causal forward over the whole sequence
+  and the fp64 oracle on sampled rows.
+* The ring entry point itself (cuflash_attention_forward_cp_*, NCCL) is
+  tested in test_gpu_ring_cp_nccl.py.
 """
-
-import os
-import socket
 
 import numpy as np
 import pytest
@@ -17,6 +16,7 @@ import pytest
 import oracle
 import ring_cp
 from helpers import host, max_err, round_to, to_dev
+from ring_drivers import run_ring
 
 pytestmark = pytest.mark.gpu
 
@@ -65,7 +65,7 @@ def test_ring_emulated_on_one_gpu(lib, cuda, world):
             owner = ring_cp.kv_owner(r, step["s"], world)
             return lambda: payload[owner]
 
-        ring_cp.run_ring(r, world, C, payload[r], compute_pair, exchange)
+        run_ring(r, world, payload[r], compute_pair, exchange)
         for qi, c in enumerate(chunks):
             o = torch.empty((B, H, C, D), device="cuda", dtype=torch.bfloat16)
             lib.convert(O_acc[qi], o)
@@ -115,7 +115,8 @@ def test_cp_step_matches_partial_plus_merge(lib, cuda, D, dt):
 @pytest.mark.parametrize("world", [1, 2, 4, 8])  # 8: the BASELINE CP setting
 def test_ring_cp_step_emulated_on_one_gpu(lib, cuda, world):
     """The ring schedule through the single-launch step entry, P ranks
-    emulated on one GPU, equals the single-GPU causal forward."""
+    emulated on one GPU, equals the single-GPU causal forward and, on every
+    7th query row, the fp64 oracle."""
     import torch
 
     B, H, D = 1, 4, 128
@@ -134,8 +135,8 @@ def test_ring_cp_step_emulated_on_one_gpu(lib, cuda, world):
         L_acc = torch.full((2, B, H, C), float("-inf"), device="cuda")
         for st in ring_cp.ring_steps(r, world):
             Ks, Vs = stack(K, st.k_chunks), stack(V, st.k_chunks)
-            pairs = [(qi, ki, chunks[qi] * C, st.k_chunks[ki] * C) for qi, ki in st.pairs]
-            for grp in ring_cp.distinct_q_groups(pairs):
+            for launch in st.launches:
+                grp = [(qi, ki, chunks[qi] * C, st.k_chunks[ki] * C) for qi, ki in launch]
                 lib.forward_cp_step(Qs, Ks, Vs, O_acc, L_acc, grp, causal=True, scale=scale)
         for qi, c in enumerate(chunks):
             o = torch.empty((B, H, C, D), device="cuda", dtype=torch.bfloat16)
@@ -143,80 +144,7 @@ def test_ring_cp_step_emulated_on_one_gpu(lib, cuda, world):
             torch.cuda.synchronize()
             assert max_err(host(o), host(O_full[:, :, c * C:(c + 1) * C])) < 1e-2
             assert max_err(host(L_acc[qi]), host(L_full[:, :, c * C:(c + 1) * C])) < 1e-4
-
-
-def _free_port():
-    with socket.socket() as s:
-        s.bind(("127.0.0.1", 0))
-        return s.getsockname()[1]
-
-
-def _nccl_worker(rank, world, port, seed_base, result_dir):
-    import torch
-    import torch.distributed as dist
-
-    import cuflash_attn
-
-    os.environ["MASTER_ADDR"] = "127.0.0.1"
-    os.environ["MASTER_PORT"] = str(port)
-    os.environ["NCCL_NVLS_ENABLE"] = "0"
-    torch.cuda.set_device(rank)
-    from datetime import timedelta
-
-    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=120),
-                            device_id=torch.device("cuda", rank))
-    ok = False
-    try:
-        lib = cuflash_attn.CuFlashAttn()
-        B, H, D, C = 1, 8, 128, 512
-        N = 2 * world * C
-        g = torch.Generator(device="cuda").manual_seed(seed_base)  # same inputs on every rank
-        Q, K, V = (torch.randn((B, H, N, D), device="cuda", generator=g).to(torch.bfloat16)
-                   for _ in range(3))
-        scale = 1.0 / np.sqrt(D)
-        O_full, L_full = lib.forward(Q, K, V, causal=True, scale=scale)
-        chunks = ring_cp.zigzag_chunks(rank, world)
-        sl = lambda x, c: x[:, :, c * C:(c + 1) * C].contiguous()
-        ring = ring_cp.RingAttention(lib)
-        outs, lses = ring.forward([sl(Q, c) for c in chunks], [sl(K, c) for c in chunks],
-                                  [sl(V, c) for c in chunks], scale)
-        torch.cuda.synchronize()
-        err_o = max(float((outs[i].float() - sl(O_full, c).float()).abs().max())
-                    for i, c in enumerate(chunks))
-        err_l = max(float((lses[i] - sl(L_full, c)).abs().max()) for i, c in enumerate(chunks))
-        ok = err_o < 1e-2 and err_l < 1e-4
-        with open(os.path.join(result_dir, f"rank{rank}.txt"), "w") as f:
-            f.write(f"{err_o} {err_l} {ok}\n")
-    finally:
-        dist.barrier()
-        dist.destroy_process_group()
-
-
-def test_ring_over_nccl_two_gpus(tmp_path):
-    import torch
-    import torch.multiprocessing as mp
-
-    if torch.cuda.device_count() < 2:
-        pytest.skip("needs two GPUs")
-    world = 2
-    mp.start_processes(_nccl_worker, args=(world, _free_port(), 7, str(tmp_path)), nprocs=world,
-                       join=True, start_method="spawn")
-    for r in range(world):
-        err_o, err_l, ok = (tmp_path / f"rank{r}.txt").read_text().split()
-        assert ok == "True", (r, err_o, err_l)
-
-
-def test_ring_over_nccl_every_gpu(tmp_path):
-    """The same ring over every GPU of the box when it has more than two
-    (eight on the BASELINE's CP setting), one rank per GPU."""
-    import torch
-    import torch.multiprocessing as mp
-
-    world = torch.cuda.device_count()
-    if world <= 2:
-        pytest.skip("needs more than two GPUs")
-    mp.start_processes(_nccl_worker, args=(world, _free_port(), 11, str(tmp_path)), nprocs=world,
-                       join=True, start_method="spawn")
-    for r in range(world):
-        err_o, err_l, ok = (tmp_path / f"rank{r}.txt").read_text().split()
-        assert ok == "True", (r, err_o, err_l)
+            rows = np.arange(c * C, (c + 1) * C, 7)
+            O64, L64 = oracle.forward_rows_f64(Qh, Kh, Vh, scale, True, rows)
+            assert max_err(host(o)[:, :, rows - c * C], O64) < 2e-2
+            assert max_err(host(L_acc[qi])[:, :, rows - c * C], L64) < 1e-3

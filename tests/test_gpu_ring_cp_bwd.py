@@ -9,11 +9,9 @@
 * One launch over several pairs equals one launch per pair.
 * Pairs whose K/V blocks are partly invisible (K/V chunk starting inside or
   after the query chunk) match the oracle's per-pair backward.
-* RingAttention.backward on one rank and, with two GPUs, over NCCL.
+* The ring entry point itself (cuflash_attention_backward_cp_*, NCCL) is
+  tested in test_gpu_ring_cp_nccl.py.
 """
-
-import os
-import socket
 
 import numpy as np
 import pytest
@@ -163,105 +161,3 @@ def test_cp_step_partial_visibility_vs_pair_oracle(lib, cuda, rel):
     if rel < 0:  # K/V rows after the last query stay untouched
         last_key = C + rel  # keys 0..C+rel-1 are visible to some query
         assert float(dk[0, :, :, last_key:].abs().max()) == 0.0
-
-
-def test_ring_attention_backward_single_rank(lib, cuda):
-    import torch
-
-    B, H, C, D = 1, 4, 256, 128
-    N = 2 * C
-    scale = 1.0 / np.sqrt(D)
-    Qh, Kh, Vh, dOh = (round_to(oracle.normal((B, H, N, D), s), "bf16") for s in (71, 72, 73, 74))
-    Q, K, V, dO = (to_dev(x, "bf16") for x in (Qh, Kh, Vh, dOh))
-    sl = lambda x, c: x[:, :, c * C:(c + 1) * C].contiguous()
-    ring = ring_cp.RingAttention(lib)
-    outs, lses = ring.forward([sl(Q, 0), sl(Q, 1)], [sl(K, 0), sl(K, 1)], [sl(V, 0), sl(V, 1)],
-                              scale)
-    dq, dk, dv = ring.backward([sl(Q, 0), sl(Q, 1)], [sl(K, 0), sl(K, 1)], [sl(V, 0), sl(V, 1)],
-                               outs, lses, [sl(dO, 0), sl(dO, 1)], scale)
-    torch.cuda.synchronize()
-    assert lib.device_status() == 0
-    gQ, gK, gV = oracle.backward_f64(Qh, Kh, Vh, dOh, scale, True)
-    for c in range(2):
-        s = slice(c * C, (c + 1) * C)
-        assert max_err(host(dq[c]), gQ[:, :, s]) < TOL
-        assert max_err(host(dk[c]), gK[:, :, s]) < TOL
-        assert max_err(host(dv[c]), gV[:, :, s]) < TOL
-
-
-def _free_port():
-    with socket.socket() as s:
-        s.bind(("127.0.0.1", 0))
-        return s.getsockname()[1]
-
-
-def _nccl_worker(rank, world, port, result_dir):
-    import torch
-    import torch.distributed as dist
-
-    import cuflash_attn
-
-    os.environ["MASTER_ADDR"] = "127.0.0.1"
-    os.environ["MASTER_PORT"] = str(port)
-    os.environ["NCCL_NVLS_ENABLE"] = "0"
-    torch.cuda.set_device(rank)
-    from datetime import timedelta
-
-    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=120),
-                            device_id=torch.device("cuda", rank))
-    try:
-        lib = cuflash_attn.CuFlashAttn()
-        B, H, D, C = 1, 8, 128, 512
-        N = 2 * world * C
-        g = torch.Generator(device="cuda").manual_seed(17)  # same inputs on every rank
-        Q, K, V, dO = (torch.randn((B, H, N, D), device="cuda", generator=g).to(torch.bfloat16)
-                       for _ in range(4))
-        scale = 1.0 / np.sqrt(D)
-        O, L = lib.forward(Q, K, V, causal=True, scale=scale)
-        rQ, rK, rV = lib.backward(Q, K, V, O, L, dO, causal=True, scale=scale)
-        chunks = ring_cp.zigzag_chunks(rank, world)
-        sl = lambda x, c: x[:, :, c * C:(c + 1) * C].contiguous()
-        ring = ring_cp.RingAttention(lib)
-        cs = lambda x: [sl(x, c) for c in chunks]
-        outs, lses = ring.forward(cs(Q), cs(K), cs(V), scale)
-        dq, dk, dv = ring.backward(cs(Q), cs(K), cs(V), outs, lses, cs(dO), scale)
-        torch.cuda.synchronize()
-        err = 0.0
-        for i, c in enumerate(chunks):
-            for got, ref in ((dq[i], rQ), (dk[i], rK), (dv[i], rV)):
-                err = max(err, float((got.float() - sl(ref, c).float()).abs().max()))
-        with open(os.path.join(result_dir, f"rank{rank}.txt"), "w") as f:
-            f.write(f"{err} {err < TOL}\n")
-    finally:
-        dist.barrier()
-        dist.destroy_process_group()
-
-
-def test_ring_backward_over_nccl_two_gpus(tmp_path):
-    import torch
-    import torch.multiprocessing as mp
-
-    if torch.cuda.device_count() < 2:
-        pytest.skip("needs two GPUs")
-    world = 2
-    mp.start_processes(_nccl_worker, args=(world, _free_port(), str(tmp_path)), nprocs=world,
-                       join=True, start_method="spawn")
-    for r in range(world):
-        err, ok = (tmp_path / f"rank{r}.txt").read_text().split()
-        assert ok == "True", (r, err)
-
-
-def test_ring_backward_over_nccl_every_gpu(tmp_path):
-    """The ring backward over every GPU of the box when it has more than two
-    (eight on the BASELINE's CP setting), one rank per GPU."""
-    import torch
-    import torch.multiprocessing as mp
-
-    world = torch.cuda.device_count()
-    if world <= 2:
-        pytest.skip("needs more than two GPUs")
-    mp.start_processes(_nccl_worker, args=(world, _free_port(), str(tmp_path)), nprocs=world,
-                       join=True, start_method="spawn")
-    for r in range(world):
-        err, ok = (tmp_path / f"rank{r}.txt").read_text().split()
-        assert ok == "True", (r, err)

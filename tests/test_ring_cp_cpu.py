@@ -1,7 +1,12 @@
-"""Ring context parallelism on CPU: the schedule and the multi-process ring
-(world_size 2 to 4, gloo) with the fp64 oracle standing in for the GPU
-partial-attention kernels, forward and backward.  The assembled result must
-equal full causal attention (and its gradients) over the whole sequence."""
+"""Ring context parallelism on CPU: the library's ring schedule
+(cuflash_cp_ring_schedule, the host function libcuflash_attn_cp.so's NCCL
+ring follows) and the multi-process ring (world_size 2 to 4, gloo) walking
+that schedule with the fp64 oracle standing in for the GPU kernels, forward
+and backward.  The assembled result must equal full attention (and its
+gradients) over the whole sequence."""
+
+import ctypes
+
 
 import os
 import socket
@@ -12,8 +17,10 @@ import torch
 import torch.distributed as dist
 import torch.multiprocessing as mp
 
+import cuflash_attn as cf
 import oracle
 import ring_cp
+from ring_drivers import run_ring, run_ring_backward
 
 
 @pytest.mark.parametrize("world", [1, 2, 3, 4, 8])
@@ -37,18 +44,43 @@ def test_schedule_covers_every_visible_pair_once(world):
     assert max(work) == min(work)
 
 
-def test_distinct_q_groups():
-    pairs = [(0, 0, "a"), (0, 1, "b"), (1, 0, "c"), (1, 1, "d")]
-    groups = ring_cp.distinct_q_groups(pairs)
-    assert groups == [[(0, 0, "a"), (1, 0, "c")], [(0, 1, "b"), (1, 1, "d")]]
-    for g in groups:
-        assert len({x[0] for x in g}) == len(g)
-    # every step of every schedule splits into at most two launches
+@pytest.mark.parametrize("causal", [True, False])
+def test_forward_launch_groups(causal):
+    """A forward launch merges every query slot at most once; every step
+    needs at most two launches and covers each of its pairs once."""
     for world in (1, 2, 3, 8):
         for r in range(world):
-            for st in ring_cp.ring_steps(r, world):
-                gs = ring_cp.distinct_q_groups([(qi, ki) for qi, ki in st.pairs])
-                assert sum(len(g) for g in gs) == len(st.pairs) and len(gs) <= 2
+            for st in ring_cp.ring_steps(r, world, causal):
+                for g in st.launches:
+                    assert len({qi for qi, _ in g}) == len(g)
+                assert sorted(p for g in st.launches for p in g) == sorted(st.pairs)
+                assert len(st.launches) <= 2
+                if not causal:
+                    assert len(st.pairs) == 4
+
+
+def test_non_causal_schedule_covers_every_pair():
+    world = 3
+    seen = set()
+    for r in range(world):
+        qc = ring_cp.zigzag_chunks(r, world)
+        for st in ring_cp.ring_steps(r, world, causal=False):
+            seen |= {(qc[qi], st.k_chunks[ki]) for qi, ki in st.pairs}
+    assert seen == {(q, k) for q in range(2 * world) for k in range(2 * world)}
+
+
+def test_schedule_validation():
+    lib = ring_cp.load_cp_library()
+    out = [ctypes.c_int() for _ in range(2)]
+    arrs = [(ctypes.c_int * 4)() for _ in range(5)]
+    call = lambda r, w, s, nul=False: lib.cuflash_cp_ring_schedule(
+        r, w, s, True, None if nul else ctypes.byref(out[0]), ctypes.byref(out[1]),
+        *[ctypes.cast(a, ctypes.c_void_p) for a in arrs])
+    assert call(0, 2, 0) == cf.SUCCESS
+    assert call(0, 2, 0, nul=True) == cf.NULL_POINTER
+    assert call(2, 2, 0) == cf.INVALID_DIMENSION      # rank outside [0, world)
+    assert call(0, 2, 2) == cf.INVALID_DIMENSION      # step outside [0, world)
+    assert call(0, 0, 0) == cf.INVALID_DIMENSION
 
 
 def _free_port():
@@ -57,7 +89,7 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _worker(rank, world, port, Q, K, V, scale, out_path):
+def _worker(rank, world, port, Q, K, V, scale, out_path, causal=True):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     dist.init_process_group("gloo", rank=rank, world_size=world)
@@ -74,7 +106,7 @@ def _worker(rank, world, port, Q, K, V, scale, out_path):
 
         def compute_pair(qi, qc, kvbuf, ki, kc):
             kb = kvbuf.numpy()
-            Op, Lp = oracle.forward_f64(q_local[qi], kb[0, ki], kb[1, ki], scale, True,
+            Op, Lp = oracle.forward_f64(q_local[qi], kb[0, ki], kb[1, ki], scale, causal,
                                         q_offset=qc * C, k_offset=kc * C)
             M = np.maximum(L_acc[qi], Lp)
             fin = np.isfinite(M)
@@ -96,22 +128,22 @@ def _worker(rank, world, port, Q, K, V, scale, out_path):
 
             return wait
 
-        ring_cp.run_ring(rank, world, C, kv, compute_pair, exchange)
+        run_ring(rank, world, kv, compute_pair, exchange, causal)
         np.savez(out_path + f".{rank}.npz", O0=O_acc[0], O1=O_acc[1], L0=L_acc[0], L1=L_acc[1])
     finally:
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("world", [2, 3, 4])
-def test_ring_over_gloo_equals_full_causal_attention(world, tmp_path):
+@pytest.mark.parametrize("world,causal", [(2, True), (3, True), (4, True), (2, False)])
+def test_ring_over_gloo_equals_full_attention(world, causal, tmp_path):
     B, H, D = 1, 2, 32
     N = 2 * world * 12
     Q, K, V = (oracle.uniform((B, H, N, D), s) for s in (5, 6, 7))
     scale = 1.0 / np.sqrt(D)
     out = str(tmp_path / "ring")
-    mp.start_processes(_worker, args=(world, _free_port(), Q, K, V, scale, out), nprocs=world,
-                       join=True, start_method="spawn")
-    O_full, L_full = oracle.forward_f64(Q, K, V, scale, True)
+    mp.start_processes(_worker, args=(world, _free_port(), Q, K, V, scale, out, causal),
+                       nprocs=world, join=True, start_method="spawn")
+    O_full, L_full = oracle.forward_f64(Q, K, V, scale, causal)
     C = N // (2 * world)
     for r in range(world):
         res = np.load(out + f".{r}.npz")
@@ -203,7 +235,7 @@ def _bwd_worker(rank, world, port, Q, K, V, dO, scale, out_path):
 
             return wait
 
-        acc = ring_cp.run_ring_backward(
+        acc = run_ring_backward(
             rank, world, kv, compute_step, exchange,
             lambda: torch.zeros((2, 2, B, H, C, D), dtype=torch.float64),
             lambda a, b: a + b)
@@ -232,3 +264,44 @@ def test_ring_backward_over_gloo_equals_full_backward(world, tmp_path):
             np.testing.assert_allclose(res[f"dQ{slot}"], rQ[:, :, sl], atol=1e-10)
             np.testing.assert_allclose(res[f"dK{slot}"], rK[:, :, sl], atol=1e-10)
             np.testing.assert_allclose(res[f"dV{slot}"], rV[:, :, sl], atol=1e-10)
+
+
+@pytest.mark.parametrize("sfx", ["bf16", "f16"])
+def test_ring_entry_validation(sfx):
+    """cuflash_attention_{forward,backward}_cp_*: argument checks happen
+    before any CUDA or NCCL call, in the reference's order (null pointers,
+    sizes, head_dim, scale), so they run on a machine without a GPU."""
+    lib = ring_cp.load_cp_library()
+    fake, nul = ctypes.c_void_p(0x10000), ctypes.c_void_p(0)
+    comm = ctypes.c_void_p(0x20000)  # never dereferenced: every call below fails validation
+    fwd = getattr(lib, f"cuflash_attention_forward_cp_{sfx}")
+    bwd = getattr(lib, f"cuflash_attention_backward_cp_{sfx}")
+
+    def f(nul_at=None, B=1, H=2, N=512, D=64, scale=0.1, comm_=comm, rank=0, world=2,
+          reserve=-1):
+        a = [fake] * 5 + [B, H, N, D, scale, True, comm_, rank, world, reserve, nul]
+        if nul_at is not None:
+            a[nul_at] = nul
+        return fwd(*a)
+
+    def b(nul_at=None, **kw):
+        a = [fake] * 9 + [1, 2, 512, kw.get("D", 64), 0.1, True, comm, 0, kw.get("world", 2),
+                          -1, nul]
+        if nul_at is not None:
+            a[nul_at] = nul
+        return bwd(*a)
+
+    assert f(nul_at=0) == cf.NULL_POINTER and f(nul_at=4) == cf.NULL_POINTER
+    assert f(B=0) == cf.INVALID_DIMENSION and f(N=-4) == cf.INVALID_DIMENSION
+    assert f(N=510) == cf.INVALID_DIMENSION           # not a multiple of 2 * world
+    assert f(world=0) == cf.INVALID_DIMENSION and f(rank=2) == cf.INVALID_DIMENSION
+    assert f(world=257, N=257 * 2 * 4) == cf.INVALID_DIMENSION
+    assert f(reserve=-2) == cf.INVALID_DIMENSION
+    assert f(D=80) == cf.UNSUPPORTED_HEAD_DIM
+    assert f(scale=-1.0) == cf.INVALID_DIMENSION and f(scale=float("inf")) == cf.INVALID_DIMENSION
+    assert f(comm_=nul) == cf.NULL_POINTER             # several ranks need a communicator
+    # the reference's backward order: gradient pointers first
+    assert b(nul_at=5) == cf.NULL_POINTER and b(nul_at=8) == cf.NULL_POINTER
+    assert b(nul_at=0) == cf.NULL_POINTER
+    assert b(D=48) == cf.UNSUPPORTED_HEAD_DIM
+    assert b(world=0) == cf.INVALID_DIMENSION

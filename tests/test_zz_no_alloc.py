@@ -14,9 +14,11 @@ This file is named so that pytest collects it last.
 
 import ctypes
 
+import numpy as np
 import pytest
 
 import cuflash_attn as cf
+import oracle
 
 pytestmark = pytest.mark.gpu
 
@@ -77,3 +79,30 @@ def test_noalloc_decode_rejects_splits_beyond_its_buffer(lib, cuda):
     O_ref, L_ref = lib.decode(q, K, V, scale=128 ** -0.5, num_splits=4)
     torch.cuda.synchronize()
     assert (O.float() - O_ref.float()).abs().max().item() < TOL_O
+
+
+def test_noalloc_decode_against_fp64(lib, cuda):
+    """Directly against the fp64 oracle (not only through the regular decode),
+    twice in a row, with an explicit split count and with the automatic one at
+    a large batch (B64 H32: 2048 heads share the buffer; with 148 SMs the
+    automatic split count, about 4 CTAs per SM, stays far below the 8 MiB
+    limit, so the cap on it never binds)."""
+    import torch
+
+    for B, H, N, D, splits, seed in [(2, 4, 2500, 128, 8, 11), (64, 32, 1024, 128, 0, 12)]:
+        q, K, V = _inputs(B, H, N, D, seed)
+        O = torch.full_like(q, float("nan"))
+        L = torch.full((B, H), float("nan"), device="cuda", dtype=torch.float32)
+        for _ in range(2):
+            assert _noalloc(lib, q, K, V, O, L, splits) == cf.SUCCESS
+            torch.cuda.synchronize()
+            heads = [(0, 0), (B - 1, H - 1), (B // 2, H // 3)]
+            for b, h in heads:
+                qh = q[b:b + 1, h:h + 1].float().cpu().numpy()
+                Kh = K[b:b + 1, h:h + 1].float().cpu().numpy()
+                Vh = V[b:b + 1, h:h + 1].float().cpu().numpy()
+                O64, L64 = oracle.decode_f64(qh, Kh, Vh, D ** -0.5)
+                got_o = O[b, h].float().cpu().numpy().reshape(O64.shape)
+                got_l = L[b, h].cpu().numpy().reshape(L64.shape)
+                assert np.max(np.abs(got_o - O64)) < TOL_O
+                assert np.max(np.abs(got_l - L64)) < TOL_L
