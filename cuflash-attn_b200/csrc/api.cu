@@ -58,6 +58,7 @@ FlashAttentionError forward_lowp(const T* Q, const T* K, const T* V, T* O, float
     FlashAttentionError e = validate_common(Q, K, V, O, L, B, H, N, D, scale);
     if (e != FlashAttentionError::SUCCESS) return e;
     if (!fits_grid(B, H)) return FlashAttentionError::INVALID_DIMENSION;
+    if (cuflash::detail::sticky_failure()) return FlashAttentionError::CUDA_ERROR;
     return launch_fwd_sm100<T>(Q, K, V, O, L, B, H, N, N, D, scale, causal, 0, 0, false, stream);
 }
 
@@ -68,6 +69,7 @@ FlashAttentionError backward_lowp(const T* Q, const T* K, const T* V, const T* O
     FlashAttentionError e = validate_backward(Q, K, V, O, L, dO, dQ, dK, dV, B, H, N, D, scale);
     if (e != FlashAttentionError::SUCCESS) return e;
     if (!fits_grid(B, H)) return FlashAttentionError::INVALID_DIMENSION;
+    if (cuflash::detail::sticky_failure()) return FlashAttentionError::CUDA_ERROR;
     return launch_bwd_sm100<T>(Q, K, V, O, L, dO, dQ, dK, dV, B, H, N, D, scale, causal, stream);
 }
 
@@ -104,6 +106,7 @@ FlashAttentionError flash_attention_forward(const float* Q, const float* K, cons
         validate_common(Q, K, V, O, L, batch_size, num_heads, seq_len, head_dim, scale);
     if (e != FlashAttentionError::SUCCESS) return e;
     if (!fits_grid(batch_size, num_heads)) return FlashAttentionError::INVALID_DIMENSION;
+    if (cuflash::detail::sticky_failure()) return FlashAttentionError::CUDA_ERROR;
     return launch_fwd_f32(Q, K, V, O, L, batch_size, num_heads, seq_len, head_dim, scale, causal,
                           stream);
 }
@@ -134,6 +137,7 @@ FlashAttentionError flash_attention_backward(const float* Q, const float* K, con
                                               num_heads, seq_len, head_dim, scale);
     if (e != FlashAttentionError::SUCCESS) return e;
     if (!fits_grid(batch_size, num_heads)) return FlashAttentionError::INVALID_DIMENSION;
+    if (cuflash::detail::sticky_failure()) return FlashAttentionError::CUDA_ERROR;
     return launch_bwd_f32(Q, K, V, O, L, dO, dQ, dK, dV, batch_size, num_heads, seq_len,
                           head_dim, scale, causal, stream);
 }
@@ -174,6 +178,7 @@ FlashAttentionError decode_impl(const T* Q, const T* K, const T* V, T* O, float*
     if (!std::isfinite(scale) || scale < 0.0f) return FlashAttentionError::INVALID_DIMENSION;
     if (num_splits < 0 || num_splits > 64) return FlashAttentionError::INVALID_DIMENSION;
     if (static_cast<long long>(B) * H > 0x7fffffffLL) return FlashAttentionError::INVALID_DIMENSION;
+    if (cuflash::detail::sticky_failure()) return FlashAttentionError::CUDA_ERROR;
     return cuflash::detail::launch_decode<T>(Q, K, V, O, L, B, H, kv_len, D, scale, num_splits,
                                              stream);
 }
@@ -197,6 +202,7 @@ FlashAttentionError decode_gqa_impl(const T* Q, const T* K, const T* V, T* O, fl
     if (!std::isfinite(scale) || scale < 0.0f) return FlashAttentionError::INVALID_DIMENSION;
     if (num_splits < 0 || num_splits > 64) return FlashAttentionError::INVALID_DIMENSION;
     if (static_cast<long long>(B) * Hq > 0x7fffffffLL) return FlashAttentionError::INVALID_DIMENSION;
+    if (cuflash::detail::sticky_failure()) return FlashAttentionError::CUDA_ERROR;
     return cuflash::detail::launch_decode_gqa<T>(Q, K, V, O, L, B, Hq, Hkv, kv_len, D, scale,
                                                  num_splits, block_table, seq_lens, page_size,
                                                  max_pages, num_pages, stream);
@@ -214,6 +220,7 @@ FlashAttentionError partial_impl(const T* Q, const T* K, const T* V, float* O, f
     if (!std::isfinite(scale) || scale < 0.0f) return FlashAttentionError::INVALID_DIMENSION;
     if (q_offset < 0 || k_offset < 0) return FlashAttentionError::INVALID_DIMENSION;
     if (static_cast<long long>(B) * H > 0x7fffffffLL) return FlashAttentionError::INVALID_DIMENSION;
+    if (cuflash::detail::sticky_failure()) return FlashAttentionError::CUDA_ERROR;
     return cuflash::detail::launch_fwd_sm100<T>(Q, K, V, O, L, B, H, seq_q, seq_k, D, scale,
                                                 causal, q_offset, k_offset, true, stream);
 }
@@ -239,6 +246,7 @@ FlashAttentionError fwd_gqa_impl(const T* Q, const T* K, const T* V, T* O, float
                                  cudaStream_t stream) {
     const FlashAttentionError e = validate_gqa({Q, K, V, O, L}, B, Hq, Hkv, Nq, Nk, D, scale);
     if (e != FlashAttentionError::SUCCESS) return e;
+    if (cuflash::detail::sticky_failure()) return FlashAttentionError::CUDA_ERROR;
     return cuflash::detail::launch_fwd_gqa_sm100<T>(Q, K, V, O, L, B, Hq, Hkv, Nq, Nk, D, scale,
                                                     causal, stream);
 }
@@ -250,6 +258,7 @@ FlashAttentionError bwd_gqa_impl(const T* Q, const T* K, const T* V, const T* O,
     const FlashAttentionError e =
         validate_gqa({dO, dQ, dK, dV, Q, K, V, O, L}, B, Hq, Hkv, Nq, Nk, D, scale);
     if (e != FlashAttentionError::SUCCESS) return e;
+    if (cuflash::detail::sticky_failure()) return FlashAttentionError::CUDA_ERROR;
     return cuflash::detail::launch_bwd_gqa_sm100<T>(Q, K, V, O, L, dO, dQ, dK, dV, B, Hq, Hkv, Nq,
                                                     Nk, D, scale, causal, stream);
 }
@@ -277,6 +286,7 @@ FlashAttentionError cp_step_impl(const T* Q, const T* K, const T* V, float* O_ac
         for (int k = 0; k < i; ++k)  // the merge writes each query slot once per launch
             if (q_slot[k] == q_slot[i]) return FlashAttentionError::INVALID_DIMENSION;
     }
+    if (cuflash::detail::sticky_failure()) return FlashAttentionError::CUDA_ERROR;
     return cuflash::detail::launch_fwd_cp_step_sm100<T>(Q, K, V, O_acc, L_acc, nq, nk, B, H, C, D,
                                                         scale, causal, num_pairs, q_slot, kv_slot,
                                                         q_off, kv_off, reserve_sms, stream);
@@ -296,6 +306,7 @@ FlashAttentionError cp_bwd_prepare_impl(const T* O, const T* dO, const float* L,
     if (!O || !dO || !L || !ws) return FlashAttentionError::NULL_POINTER;
     const FlashAttentionError e = cp_dims_check(nq, B, H, C, D);
     if (e != FlashAttentionError::SUCCESS) return e;
+    if (cuflash::detail::sticky_failure()) return FlashAttentionError::CUDA_ERROR;
     return cuflash::detail::launch_bwd_cp_prepare_sm100<T>(O, dO, L, ws, nq, B * H, C, D, stream);
 }
 
@@ -324,6 +335,7 @@ FlashAttentionError cp_bwd_step_impl(const T* Q, const T* dO, const T* K, const 
             if (q_slot[k] == q_slot[i] && kv_slot[k] == kv_slot[i])
                 return FlashAttentionError::INVALID_DIMENSION;
     }
+    if (cuflash::detail::sticky_failure()) return FlashAttentionError::CUDA_ERROR;
     return cuflash::detail::launch_bwd_cp_step_sm100<T>(Q, dO, K, V, ws, dK_acc, dV_acc, nq, nk,
                                                         B * H, C, D, scale, causal, num_pairs,
                                                         q_slot, kv_slot, q_off, kv_off,
@@ -337,6 +349,7 @@ FlashAttentionError cp_bwd_finish_impl(const void* ws, T* dQ, int nq, int B, int
     const FlashAttentionError e = cp_dims_check(nq, B, H, C, D);
     if (e != FlashAttentionError::SUCCESS) return e;
     if (!std::isfinite(scale) || scale < 0.0f) return FlashAttentionError::INVALID_DIMENSION;
+    if (cuflash::detail::sticky_failure()) return FlashAttentionError::CUDA_ERROR;
     return cuflash::detail::launch_bwd_cp_finish_sm100<T>(ws, dQ, nq, B * H, C, D, scale, stream);
 }
 
@@ -592,6 +605,8 @@ int cuflash_accumulate_f32(float* dst, float* src, long long count, bool zero_sr
     if (count <= 0 || count % 4 != 0 || (reinterpret_cast<uintptr_t>(dst) & 15u) != 0 ||
         (reinterpret_cast<uintptr_t>(src) & 15u) != 0)
         return static_cast<int>(FlashAttentionError::INVALID_DIMENSION);
+    if (cuflash::detail::sticky_failure())
+        return static_cast<int>(FlashAttentionError::CUDA_ERROR);
     return static_cast<int>(
         cuflash::detail::launch_accumulate_f32(dst, src, count, zero_src, stream));
 }
@@ -601,6 +616,8 @@ int cuflash_lse_merge_f32(float* O_acc, float* L_acc, const float* O_part, const
     if (!O_acc || !L_acc || !O_part || !L_part)
         return static_cast<int>(FlashAttentionError::NULL_POINTER);
     if (rows <= 0 || head_dim <= 0) return static_cast<int>(FlashAttentionError::INVALID_DIMENSION);
+    if (cuflash::detail::sticky_failure())
+        return static_cast<int>(FlashAttentionError::CUDA_ERROR);
     return static_cast<int>(
         cuflash::detail::launch_lse_merge(O_acc, L_acc, O_part, L_part, rows, head_dim, stream));
 }
@@ -609,6 +626,8 @@ int cuflash_convert_f32_to_bf16(const float* src, __nv_bfloat16* dst, long long 
                                 cudaStream_t stream) {
     if (!src || !dst) return static_cast<int>(FlashAttentionError::NULL_POINTER);
     if (count <= 0) return static_cast<int>(FlashAttentionError::INVALID_DIMENSION);
+    if (cuflash::detail::sticky_failure())
+        return static_cast<int>(FlashAttentionError::CUDA_ERROR);
     return static_cast<int>(
         cuflash::detail::launch_convert_f32<__nv_bfloat16>(src, dst, count, stream));
 }
@@ -617,6 +636,8 @@ int cuflash_convert_f32_to_f16(const float* src, half* dst, long long count,
                                cudaStream_t stream) {
     if (!src || !dst) return static_cast<int>(FlashAttentionError::NULL_POINTER);
     if (count <= 0) return static_cast<int>(FlashAttentionError::INVALID_DIMENSION);
+    if (cuflash::detail::sticky_failure())
+        return static_cast<int>(FlashAttentionError::CUDA_ERROR);
     return static_cast<int>(cuflash::detail::launch_convert_f32<half>(src, dst, count, stream));
 }
 
@@ -633,6 +654,8 @@ int cuflash_attention_decode_bf16_noalloc(const __nv_bfloat16* Q, const __nv_bfl
         return static_cast<int>(FlashAttentionError::INVALID_DIMENSION);
     if (static_cast<long long>(batch_size) * num_heads > 0x7fffffffLL)
         return static_cast<int>(FlashAttentionError::INVALID_DIMENSION);
+    if (cuflash::detail::sticky_failure())
+        return static_cast<int>(FlashAttentionError::CUDA_ERROR);
     return static_cast<int>(cuflash::detail::launch_decode_bf16_noalloc(
         Q, K, V, O, L, batch_size, num_heads, kv_len, head_dim, scale, num_splits, stream));
 }

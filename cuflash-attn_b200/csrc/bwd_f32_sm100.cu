@@ -49,7 +49,7 @@ namespace detail {
 
 namespace {
 
-__device__ int g_bf32_status;
+__device__ sm100::StatusWord g_bf32_status;
 
 constexpr float kLog2eB = 1.4426950408889634f;
 
@@ -189,10 +189,10 @@ __global__ void __launch_bounds__(384, 1)
     constexpr int BS = G::kBS;
     constexpr bool kTwo = G::kTwo;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
-    if (*reinterpret_cast<volatile int*>(&g_bf32_status) != 0) return;
+    if (sm100::cta_skip(&g_bf32_status)) return;
     const uint32_t sbase = smem_u32(smem_raw);
     if ((sbase & 1023u) != 0) {
-        if (threadIdx.x == 0) atomicExch(&g_bf32_status, 2);
+        if (threadIdx.x == 0) sm100::record_status(&g_bf32_status, sm100::kStatusMisaligned);
         return;
     }
     uint8_t* sptr = smem_raw;
@@ -651,6 +651,7 @@ FlashAttentionError launch_mode(const CUtensorMap& f1, const CUtensorMap& f2,
     prm.scale_log2 = scale * kLog2eB;
     prm.out_scale = kMode == kModeDV ? 1.f : scale;
     const long long nf = (N + G::kBM - 1) / G::kBM;
+    bind_status_word(reinterpret_cast<const void*>(&g_bf32_status), stream);
     kern<<<dim3(static_cast<unsigned>(nf * BH)), 384, G::kSmemBytes, stream>>>(f1, f2, s1, s2,
                                                                              prm);
     return cudaGetLastError() == cudaSuccess ? FlashAttentionError::SUCCESS

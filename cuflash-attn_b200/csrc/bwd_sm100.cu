@@ -53,7 +53,7 @@ namespace detail {
 
 namespace {
 
-__device__ int g_bwd_status;
+__device__ sm100::StatusWord g_bwd_status;
 
 constexpr float kLog2eB = 1.4426950408889634f;
 // With kBwdExp2EmuEvery = k > 0, one pair of exponentials in k is computed on
@@ -532,10 +532,10 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
                                        : (CUFLASH_BWD_DQ_MODE_SMALL == 0 ? 1 : CUFLASH_BWD_DQ_MODE_SMALL);
     constexpr bool kTransposedDq = (kDqMode == 0);
 
-    if (*reinterpret_cast<volatile int*>(&g_bwd_status) != 0) return;
+    if (sm100::cta_skip(&g_bwd_status)) return;
     const uint32_t sbase = smem_u32(smem_raw);
     if ((sbase & 1023u) != 0) {  // swizzled operands need 1024-byte alignment
-        if (threadIdx.x == 0) atomicExch(&g_bwd_status, 2);
+        if (threadIdx.x == 0) sm100::record_status(&g_bwd_status, sm100::kStatusMisaligned);
         return;
     }
     uint8_t* sptr = smem_raw;
@@ -1161,6 +1161,7 @@ FlashAttentionError bwd_typed(const T* Q, const T* K, const T* V, const T* O, co
     prm.scale = scale;
     // persistent: one CTA per SM (the shared-memory footprint allows one)
     const int grid = persistent_grid(units, env_int("CUFLASH_BWD_WAVES", 1));
+    bind_status_word(reinterpret_cast<const void*>(&g_bwd_status), stream);
     kern<<<grid, kBwdThreads, G::kSmemBytes, stream>>>(mq, mk, mv, mdo, mdq, prm);
     if (cudaGetLastError() != cudaSuccess) return fail(FlashAttentionError::CUDA_ERROR);
 
@@ -1308,6 +1309,7 @@ FlashAttentionError bwd_cp_step_typed(const T* Q, const T* dO, const T* K, const
     // as in the forward step.
     int grid = persistent_grid(units, env_int("CUFLASH_BWD_WAVES", 1));
     grid = std::max(1, std::min(grid, sms - reserve_sms));
+    bind_status_word(reinterpret_cast<const void*>(&g_bwd_status), stream);
     kern<<<grid, kBwdThreads, G::kSmemBytes, stream>>>(mq, mk, mv, mdo, mdq, prm);
     return cudaGetLastError() == cudaSuccess ? FlashAttentionError::SUCCESS
                                              : FlashAttentionError::CUDA_ERROR;

@@ -541,7 +541,7 @@ FlashAttentionError decode_group_typed(const T* Q, const DecodeKv<T>& kvp, T* O,
 // an M = 128 product (at N = 16 it costs what an M = 64 one does) and its
 // rows 64-127, never read, stay zero.
 // ---------------------------------------------------------------------------
-__device__ int g_dec_status;
+__device__ sm100::StatusWord g_dec_status;
 
 constexpr int kTcHeads = 16;
 constexpr int kTcRows = 128;
@@ -626,7 +626,7 @@ __global__ void __launch_bounds__(kTcThreads, TcGeom<D>::kCtasPerSm)
     using G = TcGeom<D>;
     using namespace sm100;
     extern __shared__ uint8_t smem_raw[];
-    if (*reinterpret_cast<volatile int*>(&g_dec_status) != 0) return;
+    if (sm100::cta_skip(&g_dec_status)) return;
     const uint32_t raw = smem_u32(smem_raw);
     const uint32_t sbase = (raw + 1023u) & ~1023u;
     uint8_t* sptr = smem_raw + (sbase - raw);
@@ -1039,6 +1039,7 @@ FlashAttentionError decode_gqa_tc(const T* Q, const DecodeKv<T>& kvp, T* O, floa
             return FlashAttentionError::CUDA_ERROR;
         prm.O = O;
         prm.L = L;
+        bind_status_word(reinterpret_cast<const void*>(&g_dec_status), stream);
         k<<<grid, kTcThreads, G::kSmemBytes, stream>>>(mq, mk, mv, prm);
         return cudaGetLastError() == cudaSuccess ? FlashAttentionError::SUCCESS
                                                  : FlashAttentionError::CUDA_ERROR;
@@ -1056,6 +1057,7 @@ FlashAttentionError decode_gqa_tc(const T* Q, const DecodeKv<T>& kvp, T* O, floa
         workspace_free(wsv, stream);
         return FlashAttentionError::CUDA_ERROR;
     }
+    bind_status_word(reinterpret_cast<const void*>(&g_dec_status), stream);
     k<<<grid, kTcThreads, G::kSmemBytes, stream>>>(mq, mk, mv, prm);
     cudaError_t e1 = cudaGetLastError();
     decode_combine_kernel<T, D><<<BHq, 128, 0, stream>>>(prm.O_part, prm.L_part, O, L, S);

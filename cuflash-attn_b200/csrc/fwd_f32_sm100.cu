@@ -39,7 +39,7 @@ namespace detail {
 
 namespace {
 
-__device__ int g_f32_status;
+__device__ sm100::StatusWord g_f32_status;
 
 constexpr float kLn2F = 0.6931471805599453f;
 constexpr float kLog2eF = 1.4426950408889634f;
@@ -125,10 +125,10 @@ __global__ void __launch_bounds__(384, 1)
     using namespace sm100;
     constexpr int BN = G::kBN;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
-    if (*reinterpret_cast<volatile int*>(&g_f32_status) != 0) return;
+    if (sm100::cta_skip(&g_f32_status)) return;
     const uint32_t sbase = smem_u32(smem_raw);
     if ((sbase & 1023u) != 0) {
-        if (threadIdx.x == 0) atomicExch(&g_f32_status, 2);
+        if (threadIdx.x == 0) sm100::record_status(&g_f32_status, sm100::kStatusMisaligned);
         return;
     }
     uint8_t* sptr = smem_raw;
@@ -562,6 +562,7 @@ FlashAttentionError fwd_f32_typed(const float* Q, const float* K, const float* V
     prm.N = N;
     prm.causal = causal ? 1 : 0;
     prm.scale_log2 = fmaxf(scale * kLog2eF, 1e-30f);
+    bind_status_word(reinterpret_cast<const void*>(&g_f32_status), stream);
     kern<<<dim3(static_cast<unsigned>(static_cast<long long>(nq) * BH)), 384, G::kSmemBytes,
            stream>>>(mq, mk, mv, prm);
     return cudaGetLastError() == cudaSuccess ? FlashAttentionError::SUCCESS

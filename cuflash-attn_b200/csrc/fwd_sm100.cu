@@ -41,7 +41,7 @@ namespace detail {
 
 namespace {
 
-__device__ int g_fwd_status;
+__device__ sm100::StatusWord g_fwd_status;
 
 constexpr float kRescaleThreshold = 8.0f;  // log2 units
 // With kExp2EmuEvery = k > 0, one pair of exponentials in k is computed on the
@@ -104,6 +104,12 @@ struct FwdParams {
     int k_base[4];   // outer index of the segment's first (b,h) in K / V
     long long q_off[4];
     long long k_off[4];
+    // Bounded waits give up after wait_ns.  Test hook: with skip_k_load set,
+    // CTA 0's producer leaves out its first K load (it still counts it), so
+    // the MMA thread's wait for it runs out and the kernel reports
+    // kStatusWaitTimeout and tears down.
+    unsigned long long wait_ns;
+    int skip_k_load;
 };
 constexpr int kMaxSegs = 4;
 
@@ -192,17 +198,19 @@ __device__ __forceinline__ int tile_blocks(const FwdParams& p, const FwdItem& it
 }
 
 // Warp-uniform bounded wait.
-__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag) {
+__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
+                                          unsigned long long limit_ns) {
     // Every lane polls the barrier itself: all lanes observe the same phase,
     // timer and abort flag, so the warp stays converged without a shuffle.
-    return sm100::mbar_wait(bar, parity, abort_flag, &g_fwd_status);
+    return sm100::mbar_wait(bar, parity, abort_flag, &g_fwd_status, limit_ns);
 }
 
 // Wait used by the producer at exit to make sure its TMA writes have landed;
 // ignores the abort flag but is still bounded in time.
-__device__ __forceinline__ void drain_wait(uint64_t* bar, uint32_t parity) {
+__device__ __forceinline__ void drain_wait(uint64_t* bar, uint32_t parity,
+                                           unsigned long long limit_ns) {
     volatile int never = 0;
-    sm100::mbar_wait(bar, parity, &never, &g_fwd_status);
+    sm100::mbar_wait(bar, parity, &never, &g_fwd_status, limit_ns);
 }
 
 template <typename T, int D, bool kF32Out>
@@ -213,7 +221,7 @@ __global__ void __launch_bounds__(384, 1)
     using namespace sm100;
     extern __shared__ uint8_t smem_raw[];
 
-    if (*reinterpret_cast<volatile int*>(&g_fwd_status) != 0) return;
+    if (sm100::cta_skip(&g_fwd_status)) return;
 
     const uint32_t raw_addr = smem_u32(smem_raw);
     const uint32_t sbase = (raw_addr + 1023u) & ~1023u;
@@ -290,7 +298,7 @@ __global__ void __launch_bounds__(384, 1)
                         if (nt[t] == 0 || !ok) continue;
                         // the slot is free once the previous item's last QK on it retired
                         if (q_cnt[t] > 0 && !mbar_wait(bar_qfree + t, (q_cnt[t] - 1) & 1,
-                                                       abort_flag, &g_fwd_status)) {
+                                                       abort_flag, &g_fwd_status, p.wait_ns)) {
                             ok = false;
                             break;
                         }
@@ -306,17 +314,19 @@ __global__ void __launch_bounds__(384, 1)
                         const int s = g % G::kStages;
                         const uint32_t ph = (g / G::kStages) & 1;
                         if (g >= G::kStages &&
-                            !mbar_wait(empty_k + s, ph ^ 1, abort_flag, &g_fwd_status)) {
+                            !mbar_wait(empty_k + s, ph ^ 1, abort_flag, &g_fwd_status, p.wait_ns)) {
                             ok = false;
                             break;
                         }
-                        mbar_arrive_expect_tx(full_k + s, G::kTileBytes);
-                        for (int cb = 0; cb < G::kNumCb; ++cb)
-                            tma_load_3d(sptr + G::kOffK + s * G::kTileBytes + cb * G::kCbBytes,
-                                        &tmK, full_k + s, cb * G::kCbElems, j * 128, it.bhk);
+                        if (!(p.skip_k_load && blockIdx.x == 0 && issued_k == 0)) {
+                            mbar_arrive_expect_tx(full_k + s, G::kTileBytes);
+                            for (int cb = 0; cb < G::kNumCb; ++cb)
+                                tma_load_3d(sptr + G::kOffK + s * G::kTileBytes + cb * G::kCbBytes,
+                                            &tmK, full_k + s, cb * G::kCbElems, j * 128, it.bhk);
+                        }
                         ++issued_k;
                         if (g >= G::kStages &&
-                            !mbar_wait(empty_v + s, ph ^ 1, abort_flag, &g_fwd_status)) {
+                            !mbar_wait(empty_v + s, ph ^ 1, abort_flag, &g_fwd_status, p.wait_ns)) {
                             ok = false;
                             break;
                         }
@@ -331,11 +341,11 @@ __global__ void __launch_bounds__(384, 1)
             // every issued load must land before the CTA can exit
 #pragma unroll
             for (int t = 0; t < 2; ++t)
-                if (q_cnt[t] > 0) drain_wait(bar_q + t, (q_cnt[t] - 1) & 1);
+                if (q_cnt[t] > 0) drain_wait(bar_q + t, (q_cnt[t] - 1) & 1, p.wait_ns);
             for (uint32_t g = issued_k > G::kStages ? issued_k - G::kStages : 0; g < issued_k; ++g)
-                drain_wait(full_k + g % G::kStages, (g / G::kStages) & 1);
+                drain_wait(full_k + g % G::kStages, (g / G::kStages) & 1, p.wait_ns);
             for (uint32_t g = issued_v > G::kStages ? issued_v - G::kStages : 0; g < issued_v; ++g)
-                drain_wait(full_v + g % G::kStages, (g / G::kStages) & 1);
+                drain_wait(full_v + g % G::kStages, (g / G::kStages) & 1, p.wait_ns);
         }
     } else if (warp == 1) {
         // ------------------------------------------------ MMA issuer
@@ -389,8 +399,8 @@ __global__ void __launch_bounds__(384, 1)
 #pragma unroll
                         for (int t = 0; t < 2; ++t)
                             if (nt[t] > 0 && ok)
-                                ok = mbar_wait(bar_q + t, q_cnt[t] & 1, abort_flag, &g_fwd_status);
-                        ok = ok && mbar_wait(full_k + s0, ph0, abort_flag, &g_fwd_status);
+                                ok = mbar_wait(bar_q + t, q_cnt[t] & 1, abort_flag, &g_fwd_status, p.wait_ns);
+                        ok = ok && mbar_wait(full_k + s0, ph0, abort_flag, &g_fwd_status, p.wait_ns);
                         if (!ok) break;
                         tc_fence_after();
 #pragma unroll
@@ -407,7 +417,7 @@ __global__ void __launch_bounds__(384, 1)
                         const uint32_t g = kv_g + j;
                         const int s = g % G::kStages;
                         const uint32_t ph = (g / G::kStages) & 1;
-                        if (!mbar_wait(full_v + s, ph, abort_flag, &g_fwd_status)) {
+                        if (!mbar_wait(full_v + s, ph, abort_flag, &g_fwd_status, p.wait_ns)) {
                             ok = false;
                             break;
                         }
@@ -419,7 +429,7 @@ __global__ void __launch_bounds__(384, 1)
 #pragma unroll
                         for (int t = 0; t < 2; ++t) {
                             if (j >= nt[t] || !ok) continue;
-                            if (!mbar_wait(bar_p + t, p_cnt[t] & 1, abort_flag, &g_fwd_status)) {
+                            if (!mbar_wait(bar_p + t, p_cnt[t] & 1, abort_flag, &g_fwd_status, p.wait_ns)) {
                                 ok = false;
                                 break;
                             }
@@ -427,7 +437,7 @@ __global__ void __launch_bounds__(384, 1)
                             if (kSplitP) {
                                 issue_pv(t, s, j > 0, 0, 4);
                                 if (!mbar_wait(bar_p2 + t, p_cnt[t] & 1, abort_flag,
-                                               &g_fwd_status)) {
+                                               &g_fwd_status, p.wait_ns)) {
                                     ok = false;
                                     break;
                                 }
@@ -440,7 +450,7 @@ __global__ void __launch_bounds__(384, 1)
                             if (j == nt[t] - 1) tc_commit(bar_o + t);
                             if (j + 1 < nt[t]) {
                                 if (!k_next_ready) {
-                                    if (!mbar_wait(full_k + sn, phn, abort_flag, &g_fwd_status)) {
+                                    if (!mbar_wait(full_k + sn, phn, abort_flag, &g_fwd_status, p.wait_ns)) {
                                         ok = false;
                                         break;
                                     }
@@ -462,7 +472,7 @@ __global__ void __launch_bounds__(384, 1)
             // all MMAs (and their commits) retire before teardown
             tc_commit(bar_done);
             volatile int never = 0;
-            mbar_wait(bar_done, 0, &never, &g_fwd_status);
+            mbar_wait(bar_done, 0, &never, &g_fwd_status, p.wait_ns);
         }
         __syncwarp();
     }
@@ -490,7 +500,7 @@ __global__ void __launch_bounds__(384, 1)
                 float m_run = -INFINITY;
                 float l_run = 0.f;
                 for (int j = 0; j < n; ++j) {
-                    if (!warp_wait(bar_s + t, s_cnt & 1, abort_flag)) {
+                    if (!warp_wait(bar_s + t, s_cnt & 1, abort_flag, p.wait_ns)) {
                         ok = false;
                         break;
                     }
@@ -606,7 +616,7 @@ __global__ void __launch_bounds__(384, 1)
 
                 // epilogue
                 if (n > 0 && ok) {
-                    ok = warp_wait(bar_o + t, o_cnt & 1, abort_flag);
+                    ok = warp_wait(bar_o + t, o_cnt & 1, abort_flag, p.wait_ns);
                     ++o_cnt;
                     tc_fence_after();
                 }
@@ -743,6 +753,10 @@ FlashAttentionError launch_typed(const T* Q, const T* K, const T* V, void* O, fl
         prm.k_off[i] = sg.k_off[i];
     }
     prm.npairs = (prm.num_ctiles + 1) / 2;
+    const int limit_ms = env_int("CUFLASH_TEST_WAIT_LIMIT_MS", 0);
+    prm.wait_ns = limit_ms > 0 ? static_cast<unsigned long long>(limit_ms) * 1000000ull
+                               : sm100::kWaitTimeoutNs;
+    prm.skip_k_load = env_int("CUFLASH_TEST_SKIP_K_LOAD", 0) != 0 ? 1 : 0;
     const int sms = current_sm_count();
     long long seg_units = static_cast<long long>(BH) * prm.npairs;
     prm.paired = seg_units * sg.num_segs >= sms ? 1 : 0;
@@ -762,6 +776,7 @@ FlashAttentionError launch_typed(const T* Q, const T* K, const T* V, void* O, fl
     // none: 20.4 (the transfer then waits for the launch to end).
     if (sg.merge) grid = std::max(1, std::min(grid, sms - sg.reserve_sms));
     if (grid <= 0) return FlashAttentionError::SUCCESS;
+    bind_status_word(reinterpret_cast<const void*>(&g_fwd_status), stream);
     kern<<<grid, 384, G::kSmemBytes, stream>>>(mq, mk, mv, prm);
     return cudaGetLastError() == cudaSuccess ? FlashAttentionError::SUCCESS
                                              : FlashAttentionError::CUDA_ERROR;

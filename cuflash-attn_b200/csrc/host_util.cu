@@ -5,6 +5,7 @@
 #include <cudaTypedefs.h>
 
 #include <atomic>
+#include <cstddef>
 #include <cstdlib>
 #include <cstring>
 #include <mutex>
@@ -128,6 +129,10 @@ Option g_options[] = {
     {"CUFLASH_CP_WAVES", {-1}},          // context-parallel forward step grid
     {"CUFLASH_DECODE_GQA_TC", {-1}},     // 0 selects the SIMT grouped-query decode
     {"CUFLASH_FAULT_WORKSPACE_OOM", {-1}},  // 1 fails every workspace request (tests)
+    // tests of the bounded waits (fp16/bf16 forward only): wait limit in ms
+    // (unset: 4 s), and 1 = CTA 0 leaves out its first K load
+    {"CUFLASH_TEST_WAIT_LIMIT_MS", {-1}},
+    {"CUFLASH_TEST_SKIP_K_LOAD", {-1}},
 };
 constexpr int kNumOptions = sizeof(g_options) / sizeof(g_options[0]);
 
@@ -138,7 +143,7 @@ Option* find_option(const char* name) {
             const char* v = getenv(o.name);
             if (v == nullptr || *v == '\0') continue;
             const int n = atoi(v);
-            if (n >= 0 && n <= 64) o.value.store(n);
+            if (n >= 0 && n <= 100000) o.value.store(n);
         }
     });
     for (int i = 0; i < kNumOptions; ++i)
@@ -232,6 +237,88 @@ void workspace_free(void* ptr, cudaStream_t stream) {
     if (ptr != nullptr) cudaFreeAsync(ptr, stream);
 }
 
+namespace {
+
+// The host-mapped status word (pinned, mapped into every device's address
+// space) and, next to it, its device address as the source of the copies
+// that bind each kernel family's StatusWord::host to it.
+struct HostStatus {
+    int word;
+    int pad;
+    int* dev_word;
+};
+std::atomic<HostStatus*> g_host_status{nullptr};
+
+HostStatus* host_status_block() {
+    static std::mutex mu;
+    HostStatus* b = g_host_status.load(std::memory_order_acquire);
+    if (b != nullptr) return b;
+    std::lock_guard<std::mutex> lock(mu);
+    b = g_host_status.load(std::memory_order_relaxed);
+    if (b != nullptr) return b;
+    void* p = nullptr;
+    if (cudaHostAlloc(&p, sizeof(HostStatus), cudaHostAllocMapped | cudaHostAllocPortable) !=
+        cudaSuccess) {
+        cudaGetLastError();
+        return nullptr;
+    }
+    b = static_cast<HostStatus*>(p);
+    b->word = 0;
+    void* d = nullptr;
+    if (cudaHostGetDevicePointer(&d, &b->word, 0) != cudaSuccess) {
+        cudaGetLastError();
+        cudaFreeHost(p);
+        return nullptr;
+    }
+    b->dev_word = static_cast<int*>(d);
+    g_host_status.store(b, std::memory_order_release);
+    return b;
+}
+
+}  // namespace
+
+int host_status() {
+    HostStatus* b = g_host_status.load(std::memory_order_acquire);
+    return b != nullptr ? *reinterpret_cast<volatile int*>(&b->word) : 0;
+}
+
+bool bind_status_word(const void* symbol, cudaStream_t stream) {
+    struct Entry {
+        const void* symbol;
+        int dev;
+    };
+    constexpr int kCap = 8 * 64;
+    static std::mutex mu;
+    static Entry bound[kCap];
+    static std::atomic<int> n_bound{0};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return false;
+    const int n = n_bound.load(std::memory_order_acquire);
+    for (int i = 0; i < n; ++i)
+        if (bound[i].symbol == symbol && bound[i].dev == dev) return true;
+    std::lock_guard<std::mutex> lock(mu);
+    const int m = n_bound.load(std::memory_order_relaxed);
+    for (int i = n; i < m; ++i)
+        if (bound[i].symbol == symbol && bound[i].dev == dev) return true;
+    if (m >= kCap) return false;
+    // not while the stream is being captured: the binding is a one-time copy,
+    // not part of the caller's work (the next uncaptured launch binds)
+    cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+    if (cudaStreamIsCapturing(stream, &cap) != cudaSuccess || cap != cudaStreamCaptureStatusNone)
+        return false;
+    HostStatus* b = host_status_block();
+    if (b == nullptr) return false;
+    if (cudaMemcpyToSymbolAsync(symbol, &b->dev_word, sizeof(int*),
+                                offsetof(sm100::StatusWord, host), cudaMemcpyHostToDevice,
+                                stream) != cudaSuccess) {
+        cudaGetLastError();
+        return false;
+    }
+    bound[m] = Entry{symbol, dev};
+    n_bound.store(m + 1, std::memory_order_release);
+    return true;
+}
+
 int read_and_clear_device_status() {
     if (cudaDeviceSynchronize() != cudaSuccess) return -1;
     const int a = fwd_sm100_status();
@@ -240,7 +327,10 @@ int read_and_clear_device_status() {
     const int d = dec_sm100_status();
     const int e = bwd_f32_sm100_status();
     if (a < 0 || b < 0 || c < 0 || d < 0 || e < 0) return -1;
-    for (const int v : {a, b, c, d, e})
+    const int h = host_status();
+    if (HostStatus* blk = g_host_status.load(std::memory_order_acquire))
+        *reinterpret_cast<volatile int*>(&blk->word) = 0;
+    for (const int v : {a, b, c, d, e, h})
         if (v != 0) return v;
     return 0;
 }

@@ -25,6 +25,35 @@ constexpr unsigned long long kWaitTimeoutNs = 4000000000ull;  // 4 s
 // Status codes recorded by kernels in their device status word.
 constexpr int kStatusOk = 0;
 constexpr int kStatusWaitTimeout = 1;
+constexpr int kStatusMisaligned = 2;
+
+// Where the kernels of one family record a failure: `code` in device memory
+// (read by every kernel of the family at entry, so work queued behind a
+// failed launch is skipped) and, once the host has bound it, `host`, a
+// host-mapped pinned word shared by all families that the host entry points
+// read without synchronising (so the next call reports the failure).
+struct StatusWord {
+    int code;
+    int pad;
+    int* host;
+};
+
+__device__ __forceinline__ void record_status(StatusWord* st, int code) {
+    atomicExch(&st->code, code);
+    int* h = *reinterpret_cast<int* volatile*>(&st->host);
+    if (h != nullptr) {
+        *reinterpret_cast<volatile int*>(h) = code;
+        __threadfence_system();
+    }
+}
+
+// CTA-uniform entry check: true (for every thread) if an earlier kernel of
+// the family recorded a failure; one barrier, before any other work.
+__device__ __forceinline__ bool cta_skip(const StatusWord* st) {
+    const int mine =
+        threadIdx.x == 0 ? *reinterpret_cast<const volatile int*>(&st->code) : 0;
+    return __syncthreads_or(mine != 0) != 0;
+}
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -70,19 +99,21 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t addr, uint32_t parity) {
 }
 
 // Waits for the phase with the given parity to complete.  Returns false if
-// the CTA-wide abort flag is (or becomes) set or the wait times out; in the
-// latter case the flag is set and `status` receives kStatusWaitTimeout.
+// the CTA-wide abort flag is (or becomes) set or the wait times out after
+// limit_ns; in the latter case the flag is set and `status` records
+// kStatusWaitTimeout.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
-                                          int* status) {
+                                          StatusWord* status,
+                                          unsigned long long limit_ns = kWaitTimeoutNs) {
     const uint32_t addr = smem_u32(bar);
     if (mbar_try_wait(addr, parity)) return true;
     const unsigned long long t0 = globaltimer_ns();
     while (true) {
         if (mbar_try_wait(addr, parity)) return true;
         if (*abort_flag) return false;
-        if (globaltimer_ns() - t0 > kWaitTimeoutNs) {
+        if (globaltimer_ns() - t0 > limit_ns) {
             *abort_flag = 1;
-            atomicExch(status, kStatusWaitTimeout);
+            record_status(status, kStatusWaitTimeout);
             return false;
         }
     }

@@ -367,10 +367,15 @@ CUFLASH_EXPORT int cuflash_convert_f32_to_bf16(const float* src, __nv_bfloat16* 
 CUFLASH_EXPORT int cuflash_convert_f32_to_f16(const float* src, half* dst, long long count,
                                               cudaStream_t stream);
 
-// Device-side status word.  Every kernel with a bounded wait (mbarrier
-// polling) records a non-zero code here instead of hanging when a wait runs
-// out; the host reads and clears it with this call (synchronises the
-// current device).  Returns 0 when no kernel reported a timeout.
+// Failure status.  Every kernel with a bounded wait (mbarrier polling)
+// records a non-zero code instead of hanging when a wait runs out (1), or
+// when it meets a shared-memory layout it cannot use (2); the code goes to a
+// device word (later kernels of the same family skip their work) and to a
+// host-mapped word that every entry point reads, without synchronising,
+// after validating its arguments: while it is set, calls return CUDA_ERROR
+// and launch nothing (a sticky error, as CUDA's own).  This call
+// synchronises the current device, returns the code (0: no failure) and
+// clears it, after which the library works again.
 CUFLASH_EXPORT int cuflash_device_status(void);
 
 // Process-wide tuning and test options (no reference counterpart).  Each
@@ -385,7 +390,12 @@ CUFLASH_EXPORT int cuflash_device_status(void);
 //   CUFLASH_DECODE_GQA_TC        0 routes grouped-query decode to the SIMT
 //                                kernel instead of the tensor-core one;
 //   CUFLASH_FAULT_WORKSPACE_OOM  1 makes every workspace request fail with
-//                                OUT_OF_MEMORY (host-side fault injection).
+//                                OUT_OF_MEMORY (host-side fault injection);
+//   CUFLASH_TEST_WAIT_LIMIT_MS   bounded-wait limit of the fp16/bf16 forward
+//                                in ms (default 4000);
+//   CUFLASH_TEST_SKIP_K_LOAD     1 makes the fp16/bf16 forward's first CTA
+//                                leave out one K load, so that one of its
+//                                waits runs out (tests of the timeout path).
 // Returns SUCCESS, NULL_POINTER, or INVALID_DIMENSION for an unknown name.
 CUFLASH_EXPORT int cuflash_set_option(const char* name, int value);
 
