@@ -1,3 +1,5 @@
+import json
+import os
 import sys
 from pathlib import Path
 
@@ -39,3 +41,25 @@ def cuda():
     if not torch.cuda.is_available():
         pytest.fail("GPU test collected on a machine without CUDA")
     return torch.device("cuda:0")
+
+
+@pytest.fixture(scope="session")
+def parity_record():
+    """Records the margins of the low-precision parity checks: each call
+    appends one row (test, tensor, e = error vs fp64, e_ref = the reference
+    library's error on the same inputs, allowance = how far e may exceed
+    e_ref).  With CUFLASH_PARITY_RECORD=<path> the rows are written there as
+    JSON lines when the session ends (summarised in profiles/parity_margin.md)."""
+    rows = []
+
+    def add(test, tensor, e, e_ref, allowance):
+        rows.append({"test": test, "tensor": tensor, "e": float(e), "e_ref": float(e_ref),
+                     "allowance": float(allowance),
+                     "used": (float(e) - float(e_ref)) / float(allowance) if allowance else None})
+
+    yield add
+    path = os.environ.get("CUFLASH_PARITY_RECORD")
+    if path and rows:
+        with open(path, "a") as f:
+            for r in rows:
+                f.write(json.dumps(r) + "\n")

@@ -1,7 +1,7 @@
 """Backward parity on the GPU, through the C ABI (dQ, dK, dV).
 
-Bars: fp32 within 1e-4 of fp64; fp16/bf16 within 2e-2 of fp64 and within one
-output ulp of the reference library's own error on the same inputs; the
+Bars: fp32 within 1e-4 of fp64; fp16/bf16 within 2e-2 of fp64 and within half
+an output ulp of the reference library's own error on the same inputs; the
 reference tests' golden gradients within each test's tolerance.
 """
 
@@ -66,7 +66,8 @@ SHAPES = [(1, 1, 1, 32), (1, 2, 128, 128), (2, 1, 129, 64), (1, 1, 255, 32), (1,
 @pytest.mark.parametrize("dt", ["bf16", "f16"])
 @pytest.mark.parametrize("causal", [False, True])
 @pytest.mark.parametrize("shape", SHAPES, ids=lambda s: "x".join(map(str, s)))
-def test_backward_lowp_vs_f64_and_reference(lib, ref_lib, cuda, dt, causal, shape):
+def test_backward_lowp_vs_f64_and_reference(lib, ref_lib, cuda, parity_record, request, dt,
+                                            causal, shape):
     D = shape[3]
     seed = 2000 + shape[2] * 3 + D + (1 if causal else 0)
     arrs = [round_to(oracle.normal(shape, seed + i, std=0.5 if i < 3 else 1.0), dt)
@@ -77,11 +78,14 @@ def test_backward_lowp_vs_f64_and_reference(lib, ref_lib, cuda, dt, causal, shap
     ref = run_bwd(ref_lib, arrs, dt, causal, scale)
     for name, g, w, r in zip(("dQ", "dK", "dV"), got, want, ref):
         e, er = max_err(g, w), max_err(r, w)
+        allowance = 0.5 * ulp_at(w, dt) + 1e-5
+        parity_record(request.node.name, name, e, er, allowance)
         assert e < LOWP_TOL, (name, e)
         # The reference's backward runs in scalar fp32 (its only rounding is
         # the final store); the tensor-core backward also rounds P and dS to
-        # the input dtype before the MMAs.  Allowed: one output ulp more.
-        assert e <= er + ulp_at(w, dt) + 1e-5, (name, e, er)
+        # the input dtype before the MMAs.  Allowed: half an output ulp more
+        # (measured use: at most a third of one ulp, profiles/parity_margin.md).
+        assert e <= er + allowance, (name, e, er)
 
 
 @pytest.mark.parametrize("causal", [False, True])

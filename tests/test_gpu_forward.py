@@ -22,9 +22,16 @@ pytestmark = pytest.mark.gpu
 GOLDEN = Path(__file__).resolve().parent / "golden" / "reference_outputs.npz"
 LOWP_TOL = 2e-2
 F32_TOL = 1e-4
-# error may exceed the reference's by at most this (one bf16 ulp at 0.25 is
-# 2^-10; differences below that are rounding-order noise)
-REF_SLACK = 1e-3
+# How far the error may exceed the reference library's own on the same
+# inputs.  Both libraries round P to the input dtype before PV and O once at
+# the store; they differ in how P is rounded (ex2.approx and a running
+# maximum raised in steps here, expf and the exact maximum there), which can
+# flip one output rounding.  Measured (profiles/parity_margin.md): causal
+# cases match the reference's error exactly; non-causal bf16 exceeds it by up
+# to 4.8e-4 (half a bf16 ulp at |O| = 0.25 is 9.8e-4), fp16 by up to 2.3e-5,
+# L by up to 3.5e-7.
+REF_SLACK_O = {"bf16": 1e-3, "f16": 1e-4}
+REF_SLACK_L = 1e-5
 
 
 def run_fwd(lib, arrs, dt, causal, scale):
@@ -65,7 +72,8 @@ SHAPES = [
 @pytest.mark.parametrize("dt", ["bf16", "f16"])
 @pytest.mark.parametrize("causal", [False, True])
 @pytest.mark.parametrize("shape", SHAPES, ids=lambda s: "x".join(map(str, s)))
-def test_forward_lowp_vs_f64_and_reference(lib, ref_lib, cuda, dt, causal, shape):
+def test_forward_lowp_vs_f64_and_reference(lib, ref_lib, cuda, parity_record, request, dt,
+                                           causal, shape):
     B, H, N, D = shape
     seed = 1000 + N * 7 + D + (1 if causal else 0)
     Q, K, V = (round_to(oracle.normal(shape, seed + i), dt) for i in range(3))
@@ -76,8 +84,10 @@ def test_forward_lowp_vs_f64_and_reference(lib, ref_lib, cuda, dt, causal, shape
     assert eO < LOWP_TOL and eL < LOWP_TOL, (eO, eL)
     Or, Lr = run_fwd(ref_lib, (Q, K, V), dt, causal, scale)
     rO, rL = max_err(Or, O64), max_err(Lr, L64)
-    assert eO <= rO + REF_SLACK, (eO, rO)
-    assert eL <= rL + REF_SLACK, (eL, rL)
+    parity_record(request.node.name, "O", eO, rO, REF_SLACK_O[dt])
+    parity_record(request.node.name, "L", eL, rL, REF_SLACK_L)
+    assert eO <= rO + REF_SLACK_O[dt], (eO, rO)
+    assert eL <= rL + REF_SLACK_L, (eL, rL)
 
 
 @pytest.mark.parametrize("causal", [False, True])
