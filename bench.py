@@ -641,6 +641,24 @@ def run_decode(args, lib, dev, pk, pk_kind, steps=None):
     stream = torch.cuda.current_stream()
     nbytes = 2 * B * Hkv * N * D * 2 + 2 * B * H * D * 2 + B * H * 4
     call = lib.decode if Hkv == H else lib.decode_gqa
+    ps = args.page_size if args.workload == "decode" else 0
+    if ps:
+        # the same cache as pages [B*N/ps, ps, Hkv, D] in a shuffled order,
+        # addressed through a block table (seeded permutation)
+        npg = B * (N // ps)
+        perm = torch.randperm(npg, device=dev, generator=g).to(torch.int32)
+        table = perm.view(B, N // ps).contiguous()
+        Kp = torch.empty((npg, ps, Hkv, D), device=dev, dtype=torch.bfloat16)
+        Vp = torch.empty_like(Kp)
+        Kp[perm.long()] = K.view(B, Hkv, N // ps, ps, D).permute(0, 2, 3, 1, 4).reshape(npg, ps, Hkv, D)
+        Vp[perm.long()] = V.view(B, Hkv, N // ps, ps, D).permute(0, 2, 3, 1, 4).reshape(npg, ps, Hkv, D)
+        lens = torch.full((B,), N, device=dev, dtype=torch.int32)
+        del K, V
+        K, V = Kp, Vp
+
+        def call(q_, K_, V_, num_splits, O, L, stream):
+            return lib.decode_paged(q_, K_, V_, table, lens, num_splits=num_splits, O=O, L=L,
+                                    stream=stream)
     results = {}
     with Clocks(dev.index) as clk:
         for splits in args.splits:
@@ -655,16 +673,19 @@ def run_decode(args, lib, dev, pk, pk_kind, steps=None):
         "steps": steps, "warmup": 3, "ms_per_step": results[best]["ms"],
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic (torch.randn, seed 31)",
-        "config": {"workload": ("BASELINE config 4: " if is_config4 else "custom: ") +
+        "config": {"workload": ("BASELINE config 4: " if is_config4 and not ps else "custom: ") +
                                (f"split-KV decode B{B} H{H} Nkv{N} D{D}" if Hkv == H else
-                                f"grouped-query split-KV decode B{B} Hq{H} Hkv{Hkv} Nkv{N} D{D}"),
+                                f"grouped-query split-KV decode B{B} Hq{H} Hkv{Hkv} Nkv{N} D{D}") +
+                               (f", paged cache ({ps}-row pages, shuffled block table)" if ps
+                                else ""),
                    "best_num_splits": best, "bytes_per_call": nbytes,
                    "l2": f"K/V {2 * B * Hkv * N * D * 2 / 2**30:.1f} GiB vs 126 MB L2; no flush"},
         "splits": results,
         "roofline": {"bound": "hbm", "achieved": results[best]["GBps"], "peak": peak,
                      "unit": "GB/s", "frac": results[best]["GBps"] / peak,
                      "peak_source": f"hbm_gbs ({pk_kind})",
-                     "traffic": traffic_from_profiles("decode") if is_config4 else None},
+                     "traffic": traffic_from_profiles("decode") if is_config4 and not ps
+                     else None},
         "clocks": clk.summary(),
     }
 
@@ -806,6 +827,9 @@ def main():
     ap.add_argument("--splits", type=int, nargs="*", default=[0, 1, 2, 4, 8, 16, 32, 64])
     ap.add_argument("--kv-heads", type=int, default=0,
                     help="decode workload: K/V heads (fewer than the 32 query heads: grouped-query)")
+    ap.add_argument("--page-size", type=int, default=0,
+                    help="decode workload: read the cache through a paged layout with this many "
+                         "rows per page (power of two; 0 = contiguous)")
     ap.add_argument("--skip-cpu-baseline", action="store_true")
     ap.add_argument("--skip-extras", action="store_true",
                     help="train workload: only config 3 (no weak/cp/decode/fp32/config2 fields)")
