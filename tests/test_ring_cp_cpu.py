@@ -305,3 +305,62 @@ def test_ring_entry_validation(sfx):
     assert b(nul_at=0) == cf.NULL_POINTER
     assert b(D=48) == cf.UNSUPPORTED_HEAD_DIM
     assert b(world=0) == cf.INVALID_DIMENSION
+
+
+def _leaving_worker(rank, world, port, out_path, leave_rank, leave_after):
+    """One ring rank over gloo with a short timeout; rank `leave_rank` leaves
+    (exits without tearing anything down) between ring steps, after
+    `leave_after` steps.  The others record how their next exchange ended."""
+    import time
+    from datetime import timedelta
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=10))
+    B, H, C, D = 1, 1, 8, 16
+    kv = torch.zeros((2, 2, B, H, C, D), dtype=torch.float64)
+    step = {"n": 0}
+
+    def exchange(cur):
+        if rank == leave_rank and step["n"] == leave_after:
+            os._exit(0)  # between steps: nothing of this rank is in flight
+        step["n"] += 1
+        nxt = torch.empty_like(cur)
+        reqs = [dist.isend(cur, (rank + 1) % world), dist.irecv(nxt, (rank - 1) % world)]
+
+        def wait():
+            for r in reqs:
+                r.wait()
+            return nxt
+
+        return wait
+
+    t0 = time.monotonic()
+    try:
+        run_ring(rank, world, kv, lambda *a: None, exchange)
+        outcome = "completed"
+    except Exception as e:  # the transport reports the missing peer
+        outcome = "error:" + type(e).__name__
+    with open(out_path + f".{rank}", "w") as f:
+        f.write(f"{outcome} {time.monotonic() - t0:.2f}\n")
+    os._exit(0)  # the group cannot be torn down cleanly without the peer
+
+
+@pytest.mark.parametrize("world,leave_rank,leave_after", [(3, 1, 1), (4, 2, 2)])
+def test_ring_rank_leaving_between_steps_fails_cleanly(world, leave_rank, leave_after, tmp_path):
+    """A rank that leaves the ring between steps: no survivor hangs, and the
+    two ranks that exchange with it (a ring rank talks only to rank - 1 and
+    rank + 1) see their next exchange end with an error within the process
+    group's timeout.  Ranks further away may finish their own exchanges."""
+    out = str(tmp_path / "leave")
+    mp.start_processes(_leaving_worker,
+                       args=(world, _free_port(), out, leave_rank, leave_after),
+                       nprocs=world, join=True, start_method="spawn")
+    neighbours = {(leave_rank - 1) % world, (leave_rank + 1) % world}
+    for r in range(world):
+        if r == leave_rank:
+            continue
+        outcome, secs = (tmp_path / f"leave.{r}").read_text().split()
+        assert float(secs) < 30.0, (r, secs)
+        if r in neighbours:
+            assert outcome.startswith("error:"), (r, outcome)
