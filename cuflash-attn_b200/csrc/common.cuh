@@ -205,11 +205,12 @@ FlashAttentionError launch_convert_f32(const float* src, T* dst, long long count
 // Failure reporting.  Each kernel family keeps a sm100::StatusWord in device
 // memory; bind_status_word (called by the family's launchers before every
 // launch; cheap after the first call per device) points its `host` field at
-// one host-mapped word shared by all families, which host_status() reads
-// without synchronising.  Non-zero means a kernel abandoned a bounded wait
-// (or met a misaligned buffer) since the last read_and_clear_device_status():
-// the entry points then refuse new work with CUDA_ERROR.  The binding is
-// skipped while `stream` is being captured.
+// the device's host-mapped word, shared by all families, which host_status()
+// reads for the current device without synchronising.  Non-zero means a
+// kernel on that device abandoned a bounded wait (or met a misaligned
+// buffer) since the last read_and_clear_device_status() there: the entry
+// points then refuse new work on that device with CUDA_ERROR.  The binding
+// is skipped while `stream` is being captured.
 bool bind_status_word(const void* symbol, cudaStream_t stream);
 int host_status();
 inline bool sticky_failure() { return host_status() != 0; }

@@ -239,13 +239,14 @@ void workspace_free(void* ptr, cudaStream_t stream) {
 
 namespace {
 
-// The host-mapped status word (pinned, mapped into every device's address
-// space) and, next to it, its device address as the source of the copies
-// that bind each kernel family's StatusWord::host to it.
+constexpr int kMaxStatusDevices = 64;
+
+// The host-mapped status words, one per device (pinned, mapped into every
+// device's address space), and their device addresses, the sources of the
+// copies that bind each kernel family's StatusWord::host on that device.
 struct HostStatus {
-    int word;
-    int pad;
-    int* dev_word;
+    int word[kMaxStatusDevices];
+    int* dev_word[kMaxStatusDevices];
 };
 std::atomic<HostStatus*> g_host_status{nullptr};
 
@@ -263,14 +264,16 @@ HostStatus* host_status_block() {
         return nullptr;
     }
     b = static_cast<HostStatus*>(p);
-    b->word = 0;
-    void* d = nullptr;
-    if (cudaHostGetDevicePointer(&d, &b->word, 0) != cudaSuccess) {
-        cudaGetLastError();
-        cudaFreeHost(p);
-        return nullptr;
+    for (int i = 0; i < kMaxStatusDevices; ++i) {
+        b->word[i] = 0;
+        void* d = nullptr;
+        if (cudaHostGetDevicePointer(&d, &b->word[i], 0) != cudaSuccess) {
+            cudaGetLastError();
+            cudaFreeHost(p);
+            return nullptr;
+        }
+        b->dev_word[i] = static_cast<int*>(d);
     }
-    b->dev_word = static_cast<int*>(d);
     g_host_status.store(b, std::memory_order_release);
     return b;
 }
@@ -279,7 +282,10 @@ HostStatus* host_status_block() {
 
 int host_status() {
     HostStatus* b = g_host_status.load(std::memory_order_acquire);
-    return b != nullptr ? *reinterpret_cast<volatile int*>(&b->word) : 0;
+    if (b == nullptr) return 0;
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxStatusDevices) return 0;
+    return *reinterpret_cast<volatile int*>(&b->word[dev]);
 }
 
 bool bind_status_word(const void* symbol, cudaStream_t stream) {
@@ -292,7 +298,7 @@ bool bind_status_word(const void* symbol, cudaStream_t stream) {
     static Entry bound[kCap];
     static std::atomic<int> n_bound{0};
     int dev = 0;
-    if (cudaGetDevice(&dev) != cudaSuccess) return false;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxStatusDevices) return false;
     const int n = n_bound.load(std::memory_order_acquire);
     for (int i = 0; i < n; ++i)
         if (bound[i].symbol == symbol && bound[i].dev == dev) return true;
@@ -308,7 +314,7 @@ bool bind_status_word(const void* symbol, cudaStream_t stream) {
         return false;
     HostStatus* b = host_status_block();
     if (b == nullptr) return false;
-    if (cudaMemcpyToSymbolAsync(symbol, &b->dev_word, sizeof(int*),
+    if (cudaMemcpyToSymbolAsync(symbol, &b->dev_word[dev], sizeof(int*),
                                 offsetof(sm100::StatusWord, host), cudaMemcpyHostToDevice,
                                 stream) != cudaSuccess) {
         cudaGetLastError();
@@ -328,8 +334,11 @@ int read_and_clear_device_status() {
     const int e = bwd_f32_sm100_status();
     if (a < 0 || b < 0 || c < 0 || d < 0 || e < 0) return -1;
     const int h = host_status();
-    if (HostStatus* blk = g_host_status.load(std::memory_order_acquire))
-        *reinterpret_cast<volatile int*>(&blk->word) = 0;
+    int dev = 0;
+    HostStatus* blk = g_host_status.load(std::memory_order_acquire);
+    if (blk != nullptr && cudaGetDevice(&dev) == cudaSuccess && dev >= 0 &&
+        dev < kMaxStatusDevices)
+        *reinterpret_cast<volatile int*>(&blk->word[dev]) = 0;
     for (const int v : {a, b, c, d, e, h})
         if (v != 0) return v;
     return 0;

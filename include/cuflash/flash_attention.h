@@ -371,11 +371,11 @@ CUFLASH_EXPORT int cuflash_convert_f32_to_f16(const float* src, half* dst, long 
 // records a non-zero code instead of hanging when a wait runs out (1), or
 // when it meets a shared-memory layout it cannot use (2); the code goes to a
 // device word (later kernels of the same family skip their work) and to a
-// host-mapped word that every entry point reads, without synchronising,
-// after validating its arguments: while it is set, calls return CUDA_ERROR
-// and launch nothing (a sticky error, as CUDA's own).  This call
-// synchronises the current device, returns the code (0: no failure) and
-// clears it, after which the library works again.
+// host-mapped word of that device that every entry point reads, without
+// synchronising, after validating its arguments: while it is set, calls on
+// that device return CUDA_ERROR and launch nothing (a sticky error, as
+// CUDA's own).  This call synchronises the current device, returns its code
+// (0: no failure) and clears it, after which the library works again there.
 CUFLASH_EXPORT int cuflash_device_status(void);
 
 // Process-wide tuning and test options (no reference counterpart).  Each
