@@ -65,6 +65,23 @@ __device__ __forceinline__ unsigned long long globaltimer_ns() {
     return t;
 }
 
+// ------------------------------------------------------------ schedules
+
+// Persistent kernels hand out work units round-robin: unit u = r * G + c
+// goes to CTA c (G = gridDim.x) in round r.  When the units are items
+// listed by decreasing cost, this returns the list position unit u takes if
+// the rounds alternate direction ("snake"): the CTA that drew the heaviest
+// item of one round draws the lightest of the next, which balances the CTAs'
+// totals where few rounds leave no room for averaging.  The last, partial
+// round covers exactly the remaining positions.
+__device__ __forceinline__ int snake_position(int u, int num_units) {
+    const int G = static_cast<int>(gridDim.x);
+    const int r = u / G;
+    const int c = u - r * G;
+    const int rem = min(G, num_units - r * G);
+    return r * G + ((r & 1) ? rem - 1 - c : c);
+}
+
 // ---------------------------------------------------------------- mbarrier
 
 __device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
