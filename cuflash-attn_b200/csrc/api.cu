@@ -662,6 +662,20 @@ int cuflash_attention_decode_bf16_noalloc(const __nv_bfloat16* Q, const __nv_bfl
 
 int cuflash_device_status(void) { return cuflash::detail::read_and_clear_device_status(); }
 
+int cuflash_profile_main_kernels(int num_launches) {
+    if (num_launches < 0) return static_cast<int>(FlashAttentionError::INVALID_DIMENSION);
+    return static_cast<int>(cuflash::detail::profile_main_kernels(num_launches) == 0
+                                ? FlashAttentionError::SUCCESS
+                                : FlashAttentionError::CUDA_ERROR);
+}
+
+int cuflash_profile_read_ms(float* ms, int max_launches) {
+    if (ms == nullptr) return -static_cast<int>(FlashAttentionError::NULL_POINTER);
+    if (max_launches < 0) return -static_cast<int>(FlashAttentionError::INVALID_DIMENSION);
+    const int n = cuflash::detail::profile_read_ms(ms, max_launches);
+    return n >= 0 ? n : -static_cast<int>(FlashAttentionError::CUDA_ERROR);
+}
+
 int cuflash_set_option(const char* name, int value) {
     if (name == nullptr) return static_cast<int>(FlashAttentionError::NULL_POINTER);
     return static_cast<int>(cuflash::detail::set_option(name, value)

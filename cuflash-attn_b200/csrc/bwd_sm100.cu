@@ -1179,8 +1179,10 @@ FlashAttentionError bwd_typed(const T* Q, const T* K, const T* V, const T* O, co
     // persistent: one CTA per SM (the shared-memory footprint allows one)
     const int grid = persistent_grid(units, env_int("CUFLASH_BWD_WAVES", 1));
     bind_status_word(reinterpret_cast<const void*>(&g_bwd_status), stream);
+    profile_record(false, stream);
     kern<<<grid, kBwdThreads, G::kSmemBytes, stream>>>(mq, mk, mv, mdo, mdq, prm);
     if (cudaGetLastError() != cudaSuccess) return fail(FlashAttentionError::CUDA_ERROR);
+    profile_record(true, stream);
 
     const long long n4 = static_cast<long long>(acc_elems / 4);
     long long cblocks = (n4 + 255) / 256;

@@ -217,6 +217,14 @@ inline bool sticky_failure() { return host_status() != 0; }
 // Synchronises the device, reads and clears every family's status word and
 // the host word; returns the first non-zero code.
 int read_and_clear_device_status();
+
+// Profiling hook: after profile_main_kernels(n) the next n backward main
+// kernels (fp16/bf16) on the same device get an event pair recorded around
+// them on their stream (profile_record before / after the launch);
+// profile_read_ms returns how many were recorded and their durations.
+int profile_main_kernels(int n);
+void profile_record(bool after, cudaStream_t stream);
+int profile_read_ms(float* ms, int max_n);
 int fwd_sm100_status();
 int bwd_sm100_status();
 int dec_sm100_status();

@@ -325,6 +325,68 @@ bool bind_status_word(const void* symbol, cudaStream_t stream) {
     return true;
 }
 
+namespace {
+
+// Event pairs recorded around the backward main kernel (profiling hook):
+// slot k holds the k-th launch after cuflash_profile_main_kernels(n).
+struct KernelProfile {
+    std::mutex mu;
+    cudaEvent_t* ev = nullptr;  // [2 * cap]
+    int cap = 0;
+    int next = 0;
+    int dev = -1;
+};
+KernelProfile g_profile;
+
+void profile_free_locked() {
+    for (int i = 0; i < 2 * g_profile.cap; ++i)
+        if (g_profile.ev[i] != nullptr) cudaEventDestroy(g_profile.ev[i]);
+    delete[] g_profile.ev;
+    g_profile.ev = nullptr;
+    g_profile.cap = g_profile.next = 0;
+    g_profile.dev = -1;
+}
+
+}  // namespace
+
+int profile_main_kernels(int n) {
+    std::lock_guard<std::mutex> lock(g_profile.mu);
+    profile_free_locked();
+    if (n <= 0) return 0;
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return -1;
+    g_profile.ev = new cudaEvent_t[2 * n]();
+    for (int i = 0; i < 2 * n; ++i)
+        if (cudaEventCreate(&g_profile.ev[i]) != cudaSuccess) {
+            profile_free_locked();
+            return -1;
+        }
+    g_profile.cap = n;
+    g_profile.dev = dev;
+    return 0;
+}
+
+void profile_record(bool after, cudaStream_t stream) {
+    std::lock_guard<std::mutex> lock(g_profile.mu);
+    if (g_profile.cap == 0 || g_profile.next >= g_profile.cap) return;
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev != g_profile.dev) return;
+    cudaEventRecord(g_profile.ev[2 * g_profile.next + (after ? 1 : 0)], stream);
+    if (after) ++g_profile.next;
+}
+
+int profile_read_ms(float* ms, int max_n) {
+    std::lock_guard<std::mutex> lock(g_profile.mu);
+    const int n = g_profile.next < max_n ? g_profile.next : max_n;
+    for (int k = 0; k < n; ++k) {
+        if (cudaEventSynchronize(g_profile.ev[2 * k + 1]) != cudaSuccess ||
+            cudaEventElapsedTime(&ms[k], g_profile.ev[2 * k], g_profile.ev[2 * k + 1]) !=
+                cudaSuccess)
+            return -1;
+    }
+    return n;
+}
+
 int read_and_clear_device_status() {
     if (cudaDeviceSynchronize() != cudaSuccess) return -1;
     const int a = fwd_sm100_status();

@@ -82,6 +82,8 @@ SIGNATURES = {
     "cuflash_convert_f32_to_f16": [_P, _P, _LL, _P],
     "cuflash_device_status": [],
     "cuflash_set_option": [ctypes.c_char_p, _I],
+    "cuflash_profile_main_kernels": [_I],
+    "cuflash_profile_read_ms": [_P, _I],
 }
 _RESTYPES = {"cuflash_error_string": ctypes.c_char_p,
              "cuflash_attention_backward_cp_workspace_size": ctypes.c_longlong}
@@ -406,6 +408,19 @@ class CuFlashAttn:
 
     def device_status(self) -> int:
         return int(self.lib.cuflash_device_status())
+
+    def profile_main_kernels(self, num_launches: int) -> None:
+        """Times the next `num_launches` backward main kernels (see
+        cuflash_profile_main_kernels); 0 stops."""
+        self.check_error(self.lib.cuflash_profile_main_kernels(int(num_launches)))
+
+    def profile_read_ms(self, max_launches: int):
+        """Durations (ms) of the profiled backward main kernels so far."""
+        buf = (ctypes.c_float * max(int(max_launches), 1))()
+        n = int(self.lib.cuflash_profile_read_ms(ctypes.cast(buf, _P), int(max_launches)))
+        if n < 0:
+            self.check_error(-n)
+        return [float(buf[i]) for i in range(n)]
 
     def set_option(self, name: str, value: int) -> None:
         """Sets a process-wide option (see ``cuflash_set_option``); a

@@ -378,6 +378,17 @@ CUFLASH_EXPORT int cuflash_convert_f32_to_f16(const float* src, half* dst, long 
 // (0: no failure) and clears it, after which the library works again there.
 CUFLASH_EXPORT int cuflash_device_status(void);
 
+// Profiling hook (no reference counterpart).  After
+// cuflash_profile_main_kernels(n), the next n launches of the fp16/bf16
+// backward's main kernel on the current device each get a pair of CUDA
+// events recorded right before and right after the launch, on the call's
+// stream, so that the kernel alone can be timed apart from the backward's
+// preprocess and dQ conversion kernels; n = 0 ends profiling.
+// cuflash_profile_read_ms waits for the recorded launches and writes their
+// durations (ms) into ms[0..k); it returns k, or minus an error code.
+CUFLASH_EXPORT int cuflash_profile_main_kernels(int num_launches);
+CUFLASH_EXPORT int cuflash_profile_read_ms(float* ms, int max_launches);
+
 // Process-wide tuning and test options (no reference counterpart).  Each
 // option starts from the environment variable of the same name, read once
 // when the library first needs an option; this call changes it afterwards

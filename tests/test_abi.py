@@ -350,3 +350,17 @@ def test_set_option_validation(lib):
     assert lib.lib.cuflash_set_option(None, 1) == cf.NULL_POINTER
     assert lib.lib.cuflash_set_option(b"CUFLASH_NO_SUCH_OPTION", 1) == cf.INVALID_DIMENSION
     assert lib.lib.cuflash_set_option(b"CUFLASH_RESERVE_SMS", -1) == cf.SUCCESS
+
+
+def test_profile_hook_validation(lib):
+    """The backward main-kernel profiling hook: argument checks and an empty
+    read need no GPU (nothing is recorded until a backward runs)."""
+    import ctypes
+
+    assert lib.lib.cuflash_profile_main_kernels(-1) == cf.INVALID_DIMENSION
+    assert lib.lib.cuflash_profile_main_kernels(0) == cf.SUCCESS
+    assert lib.lib.cuflash_profile_read_ms(None, 4) == -cf.NULL_POINTER
+    buf = (ctypes.c_float * 4)()
+    assert lib.lib.cuflash_profile_read_ms(ctypes.cast(buf, ctypes.c_void_p), -1) == \
+        -cf.INVALID_DIMENSION
+    assert lib.profile_read_ms(4) == []

@@ -126,3 +126,33 @@ def test_config2_backward_sampled_units(lib, cuda):
         want = oracle.backward_f64(*sub, scale, False)
         for g, w in zip(got, want):
             assert max_err(g[b, h], w[0, 0]) < LOWP_TOL
+
+
+def test_profile_hook_times_main_kernel(lib, cuda):
+    """cuflash_profile_main_kernels(2) records the next two backward main
+    kernels only: a third backward adds nothing, and each duration lies
+    between zero and the whole backward call's."""
+    import torch
+
+    B, H, N, D = 2, 4, 1024, 128
+    g = torch.Generator(device="cuda").manual_seed(3)
+    Q, K, V, dO = (torch.randn((B, H, N, D), device="cuda", generator=g).to(torch.bfloat16)
+                   for _ in range(4))
+    O, L = lib.forward(Q, K, V, causal=True)
+    lib.profile_main_kernels(2)
+    try:
+        calls = []
+        for _ in range(3):
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            lib.backward(Q, K, V, O, L, dO, causal=True)
+            b.record()
+            calls.append((a, b))
+        torch.cuda.synchronize()
+        ms = lib.profile_read_ms(8)
+    finally:
+        lib.profile_main_kernels(0)
+    assert lib.device_status() == 0
+    assert len(ms) == 2
+    for t, (a, b) in zip(ms, calls):
+        assert 0.0 < t <= a.elapsed_time(b)
