@@ -796,7 +796,7 @@ def run_cp(args, dev, world, rank, pk, pk_kind, backward, steps, warmup):
         uid = [ring_cp.nccl_unique_id() if rank == 0 else None]
         dist.broadcast_object_list(uid, src=0)
         comm = ring_cp.NcclComm(world, rank, uid[0])
-    ring = ring_cp.RingAttention(comm, rank=rank, world=world)
+    ring = ring_cp.RingAttention(comm, rank=rank, world=world, reserve_sms=args.cp_reserve)
     stream = torch.cuda.current_stream()
 
     def step():
@@ -833,7 +833,8 @@ def run_cp(args, dev, world, rank, pk, pk_kind, backward, steps, warmup):
                                f"context-parallel ring over {world} GPU(s) "
                                f"(cuflash_attention_{'fwd+bwd' if backward else 'forward'}_cp_bf16,"
                                f" NCCL), zigzag chunks of {C}",
-                   "global_batch": B, "seq_len": N, "parallelism": f"cp{world}"},
+                   "global_batch": B, "seq_len": N, "parallelism": f"cp{world}",
+                   "reserve_sms": args.cp_reserve},
         "per_gpu_tflops": value / world,
         "frac_per_gpu": value / world / peak, "peak_source": peak_src,
         "clocks": clocks,
@@ -848,6 +849,9 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=["train", "decode", "cp"], default="train")
     ap.add_argument("--cp-seq", type=int, default=CONFIG5["N"])
+    ap.add_argument("--cp-reserve", type=int, default=-1,
+                    help="cp workload: SMs the step kernels leave to NCCL's transfer kernels "
+                         "(-1 = the library's default)")
     ap.add_argument("--cp-backward", action="store_true",
                     help="cp workload: time the ring forward and backward of a training step")
     ap.add_argument("--splits", type=int, nargs="*", default=[0, 1, 2, 4, 8, 16, 32, 64])

@@ -598,16 +598,27 @@ int cuflash_cp_nccl_unique_id(void* unique_id, int nbytes) {
     return static_cast<int>(FlashAttentionError::SUCCESS);
 }
 
-int cuflash_cp_nccl_comm_init(ncclComm_t* comm, int world, const void* unique_id, int rank) {
+int cuflash_cp_nccl_comm_init_config(ncclComm_t* comm, int world, const void* unique_id,
+                                     int rank, int max_ctas) {
     if (comm == nullptr || unique_id == nullptr)
         return static_cast<int>(FlashAttentionError::NULL_POINTER);
-    if (world <= 0 || rank < 0 || rank >= world)
+    if (world <= 0 || rank < 0 || rank >= world || max_ctas < 0)
         return static_cast<int>(FlashAttentionError::INVALID_DIMENSION);
     ncclUniqueId id;
     std::memcpy(&id, unique_id, sizeof(id));
-    return static_cast<int>(ncclCommInitRank(comm, world, id, rank) == ncclSuccess
+    ncclConfig_t config = NCCL_CONFIG_INITIALIZER;
+    config.blocking = 1;  // the ring entry points require a blocking communicator
+    if (max_ctas > 0) {
+        config.minCTAs = 1;
+        config.maxCTAs = max_ctas;
+    }
+    return static_cast<int>(ncclCommInitRankConfig(comm, world, id, rank, &config) == ncclSuccess
                                 ? FlashAttentionError::SUCCESS
                                 : FlashAttentionError::CUDA_ERROR);
+}
+
+int cuflash_cp_nccl_comm_init(ncclComm_t* comm, int world, const void* unique_id, int rank) {
+    return cuflash_cp_nccl_comm_init_config(comm, world, unique_id, rank, 0);
 }
 
 int cuflash_cp_nccl_comm_destroy(ncclComm_t comm) {

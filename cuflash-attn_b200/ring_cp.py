@@ -45,6 +45,7 @@ CP_SIGNATURES = {
     "cuflash_cp_ring_schedule": [_I, _I, _I, _B] + [_P] * 7,
     "cuflash_cp_nccl_unique_id": [_P, _I],
     "cuflash_cp_nccl_comm_init": [_P, _I, _P, _I],
+    "cuflash_cp_nccl_comm_init_config": [_P, _I, _P, _I, _I],
     "cuflash_cp_nccl_comm_destroy": [_P],
 }
 
@@ -142,14 +143,15 @@ def nccl_unique_id() -> bytes:
 
 class NcclComm:
     """An NCCL communicator over `world` ranks on the current CUDA device
-    (blocking, created with ncclCommInitRank through the library)."""
+    (blocking, created through the library).  ``max_ctas`` > 0 caps the CTAs
+    NCCL's kernels use (ncclConfig_t.maxCTAs); 0 keeps NCCL's default."""
 
-    def __init__(self, world: int, rank: int, unique_id: bytes):
+    def __init__(self, world: int, rank: int, unique_id: bytes, max_ctas: int = 0):
         self.world, self.rank = world, rank
         self.handle = ctypes.c_void_p()
         buf = ctypes.create_string_buffer(unique_id, UNIQUE_ID_BYTES)
-        _check(load_cp_library().cuflash_cp_nccl_comm_init(ctypes.byref(self.handle), world,
-                                                           ctypes.cast(buf, _P), rank))
+        _check(load_cp_library().cuflash_cp_nccl_comm_init_config(
+            ctypes.byref(self.handle), world, ctypes.cast(buf, _P), rank, int(max_ctas)))
 
     def destroy(self) -> None:
         if self.handle:

@@ -100,11 +100,17 @@ CUFLASH_EXPORT int cuflash_cp_ring_schedule(int rank, int world, int step, bool 
 // Communicator helpers for callers without an NCCL binding of their own
 // (ctypes, for instance); they use the same NCCL library as the entry points.
 // unique_id: NCCL_UNIQUE_ID_BYTES bytes, made on one rank and given to all.
-// comm_init runs ncclCommInitRank on the current device.  NCCL failures
-// return CUDA_ERROR.
+// comm_init runs ncclCommInitRank on the current device; comm_init_config
+// creates the same blocking communicator with ncclCommInitRankConfig and, for
+// max_ctas > 0, caps the CTAs (channels) NCCL's kernels use at max_ctas, so
+// that they fit in the SMs the step kernels leave free (reserve_sms); 0 keeps
+// NCCL's default.  NCCL failures return CUDA_ERROR.
 CUFLASH_EXPORT int cuflash_cp_nccl_unique_id(void* unique_id, int nbytes);
 CUFLASH_EXPORT int cuflash_cp_nccl_comm_init(ncclComm_t* comm, int world, const void* unique_id,
                                              int rank);
+CUFLASH_EXPORT int cuflash_cp_nccl_comm_init_config(ncclComm_t* comm, int world,
+                                                    const void* unique_id, int rank,
+                                                    int max_ctas);
 CUFLASH_EXPORT int cuflash_cp_nccl_comm_destroy(ncclComm_t comm);
 
 #ifdef __cplusplus

@@ -65,6 +65,30 @@ def test_cp_library_exports_every_declared_symbol():
     assert exported == declared, exported ^ declared
 
 
+def test_cp_comm_helpers_validate_before_nccl():
+    """The communicator helpers reject bad arguments before any NCCL call
+    (so these run without a GPU)."""
+    import ctypes
+
+    import ring_cp
+
+    lib = ring_cp.load_cp_library()
+    h = ctypes.c_void_p()
+    uid = ctypes.create_string_buffer(ring_cp.UNIQUE_ID_BYTES)
+    P = ctypes.c_void_p
+    assert lib.cuflash_cp_nccl_comm_init_config(None, 2, ctypes.cast(uid, P), 0, 0) == \
+        cf.NULL_POINTER
+    assert lib.cuflash_cp_nccl_comm_init_config(ctypes.byref(h), 2, None, 0, 0) == cf.NULL_POINTER
+    for world, rank, ctas in ((0, 0, 0), (2, 2, 0), (2, -1, 0), (2, 0, -1)):
+        assert lib.cuflash_cp_nccl_comm_init_config(ctypes.byref(h), world, ctypes.cast(uid, P),
+                                                    rank, ctas) == cf.INVALID_DIMENSION
+    assert lib.cuflash_cp_nccl_comm_init(ctypes.byref(h), 2, ctypes.cast(uid, P), 5) == \
+        cf.INVALID_DIMENSION
+    assert lib.cuflash_cp_nccl_unique_id(None, 128) == cf.NULL_POINTER
+    assert lib.cuflash_cp_nccl_unique_id(ctypes.cast(uid, P), 4) == cf.INVALID_DIMENSION
+    assert lib.cuflash_cp_nccl_comm_destroy(None) == cf.NULL_POINTER
+
+
 def test_library_hides_internal_symbols():
     import subprocess
 
