@@ -29,10 +29,12 @@
 
 #include "cuflash/flash_attention.h"
 #include "cuflash/flash_attention_cp.h"
+#include "peer_ring.h"
 
 namespace {
 
 using cuflash::FlashAttentionError;
+using cuflash_cp::PeerCtx;
 
 constexpr int kMaxDevices = 64;
 constexpr int kDefaultReserveSms = 16;
@@ -156,7 +158,7 @@ FlashAttentionError fill_f32(float* dst, float value, long long n, cudaStream_t 
 // Events of one call, destroyed when the call returns (an event destroyed
 // while its record is pending is released once it completes).
 struct Events {
-    static constexpr int kMax = 3 * kMaxWorld + 4;
+    static constexpr int kMax = 4 * kMaxWorld + 8;
     cudaEvent_t ev[kMax] = {};
     int n = 0;
     cudaEvent_t make() {
@@ -292,9 +294,225 @@ bool exchange_one(const void* send, void* recv, size_t bytes, int rank, int worl
     return (ncclGroupEnd() == ncclSuccess) && ok;
 }
 
-int effective_reserve(int reserve_sms, int world) {
+// SMs the step kernels leave free by default: NCCL's send/recv kernels need
+// about 16 to keep up with the steps; the copy-engine transport only runs
+// one-thread flag kernels beside them.
+constexpr int kDefaultReserveSmsPeer = 2;
+
+int effective_reserve(int reserve_sms, int world, bool peer) {
     if (world == 1) return 0;  // no transfer runs beside the kernels
-    return reserve_sms < 0 ? kDefaultReserveSms : reserve_sms;
+    if (reserve_sms >= 0) return reserve_sms;
+    return peer ? kDefaultReserveSmsPeer : kDefaultReserveSms;
+}
+
+// ------------------------------------------------ copy-engine transport drivers
+//
+// Step s of rank r computes with X_s, the K/V of owner (r - s) mod W (X_0 is
+// the caller's).  Each rank first copies its K and V into its export E (on
+// the comm stream, once the readers of the previous call's E are done), then
+// pulls X_s from the owner's E into pull slot s % 2 on the comm stream: X_1
+// and X_2 right away, X_{s+2} once step s's kernels (the slot's previous
+// readers) are done.  Step s's kernels wait for their pull.  The backward
+// pushes step s's dK/dV (s >= 1) into its owner's slot for this rank and,
+// at the end, sums its own and the W - 1 received contributions.
+
+template <typename T>
+struct PullPlan {
+    PeerCtx* ctx;
+    int rank, world;
+    long long k;  // this call's number
+    size_t kv_bytes;
+    // pull slot of step s: [K pair][V pair]
+    char* slot(int s) const { return ctx->pull_slot(s % 2); }
+    int owner(int s) const { return ((rank - s) % world + world) % world; }
+};
+
+// Export this rank's K/V and signal it (comm stream).
+template <typename T>
+bool export_kv(const PullPlan<T>& pp, const T* K, const T* V, cudaStream_t cs) {
+    PeerCtx& c = *pp.ctx;
+    // readers of the previous call's export are done (their flags on this rank)
+    bool ok = cuflash_cp::wait_all_geq(c.flags + 2 + 2 * pp.world, pp.world, pp.rank, c.calls, cs);
+    ok = ok && cudaMemcpyAsync(c.mem, K, pp.kv_bytes, cudaMemcpyDeviceToDevice, cs) == cudaSuccess;
+    ok = ok && cudaMemcpyAsync(c.mem + pp.kv_bytes, V, pp.kv_bytes, cudaMemcpyDeviceToDevice, cs) ==
+                   cudaSuccess;
+    if (cuflash_cp::test_skip_export_signal()) return ok || cuflash_cp::debug_fail("export");
+    return (ok && cuflash_cp::signal(c.flags + 0, pp.k, cs)) || cuflash_cp::debug_fail("export");
+}
+
+// Pull X_s into slot s % 2 (comm stream); `prev_reader` (may be null) is the
+// event of the step that last read the slot.
+template <typename T>
+bool pull_kv(const PullPlan<T>& pp, int s, cudaEvent_t prev_reader, Events& evs, cudaStream_t cs,
+             cudaEvent_t* done) {
+    PeerCtx& c = *pp.ctx;
+    const int o = pp.owner(s);
+    bool ok = prev_reader == nullptr || cudaStreamWaitEvent(cs, prev_reader, 0) == cudaSuccess;
+    ok = ok && cuflash_cp::wait_geq(c.fl(o) + 0, pp.k, cs);
+    ok = ok && cudaMemcpyAsync(pp.slot(s), c.e(o), 2 * pp.kv_bytes, cudaMemcpyDeviceToDevice, cs) ==
+                   cudaSuccess;
+    // this rank is done reading o's export
+    ok = ok && cuflash_cp::signal(c.fl(o) + 2 + 2 * pp.world + pp.rank, pp.k, cs);
+    *done = ok ? evs.make() : nullptr;
+    return (ok && *done != nullptr && cudaEventRecord(*done, cs) == cudaSuccess) ||
+           cuflash_cp::debug_fail("pull");
+}
+
+template <typename T>
+FlashAttentionError forward_cp_peer(PeerCtx& ctx, const T* Q, const T* K, const T* V, T* O,
+                                    float* L, int B, int H, int C, int D, float scale, bool causal,
+                                    int rank, int world, int reserve, cudaStream_t stream,
+                                    cudaStream_t cs) {
+    const long long elems = 2LL * B * H * C * D;
+    const size_t kv_bytes = static_cast<size_t>(elems) * sizeof(T);
+    const size_t oacc_bytes = static_cast<size_t>(elems) * sizeof(float);
+    void* ws = nullptr;
+    FlashAttentionError e = ws_alloc(&ws, oacc_bytes, stream);
+    if (e != FlashAttentionError::SUCCESS) return e;
+    float* O_acc = static_cast<float*>(ws);
+    const PullPlan<T> pp{&ctx, rank, world, ctx.calls + 1, kv_bytes};
+    Events evs;
+    cudaEvent_t recv[kMaxWorld] = {};
+    cudaEvent_t comp[kMaxWorld] = {};
+    bool ok = cudaMemsetAsync(O_acc, 0, oacc_bytes, stream) == cudaSuccess;
+    if (ok) e = fill_f32(L, -INFINITY, elems / D, stream);
+    ok = ok && e == FlashAttentionError::SUCCESS;
+    ok = ok && join(evs, cs, stream);  // K, V, the workspace and the last call's readers
+    ok = ok && export_kv(pp, K, V, cs);
+    for (int s = 1; ok && s < world && s <= 2; ++s) ok = pull_kv(pp, s, nullptr, evs, cs, &recv[s]);
+    for (int s = 0; ok && s < world; ++s) {
+        const StepPlan p = plan_step(rank, world, s, causal);
+        const T* ck = s == 0 ? K : reinterpret_cast<const T*>(pp.slot(s));
+        const T* cv = s == 0 ? V : reinterpret_cast<const T*>(pp.slot(s) + kv_bytes);
+        if (s >= 1) ok = cudaStreamWaitEvent(stream, recv[s], 0) == cudaSuccess;
+        for (int l = 0; ok && l < p.num_launches; ++l) {
+            int qs[4], ks[4], n = 0;
+            long long qo[4], ko[4];
+            for (int i = 0; i < p.n; ++i) {
+                if (p.launch[i] != l) continue;
+                qs[n] = p.q_slot[i];
+                ks[n] = p.kv_slot[i];
+                qo[n] = static_cast<long long>(p.q_chunk[i]) * C;
+                ko[n] = static_cast<long long>(p.kv_chunk[i]) * C;
+                ++n;
+            }
+            e = code(CpOps<T>::step(Q, ck, cv, O_acc, L, B, H, C, D, scale, causal, n, qs, ks, qo,
+                                    ko, reserve, stream));
+            ok = e == FlashAttentionError::SUCCESS || cuflash_cp::debug_fail("forward step");
+        }
+        if (ok && s >= 1 && s + 2 < world) {
+            comp[s] = evs.make();
+            ok = comp[s] != nullptr && cudaEventRecord(comp[s], stream) == cudaSuccess;
+            ok = ok && pull_kv(pp, s + 2, comp[s], evs, cs, &recv[s + 2]);
+        }
+    }
+    if (ok) {
+        e = code(CpOps<T>::convert(O_acc, O, elems, stream));
+        ok = e == FlashAttentionError::SUCCESS;
+    }
+    join(evs, stream, cs);
+    cudaFreeAsync(ws, stream);
+    ++ctx.calls;  // every rank counts every call, failed or not
+    if (!ok) return e != FlashAttentionError::SUCCESS ? e : FlashAttentionError::CUDA_ERROR;
+    return FlashAttentionError::SUCCESS;
+}
+
+template <typename T>
+FlashAttentionError backward_cp_peer(PeerCtx& ctx, const T* Q, const T* K, const T* V, const T* O,
+                                     const float* L, const T* dO, T* dQ, T* dK, T* dV, int B,
+                                     int H, int C, int D, float scale, bool causal, int rank,
+                                     int world, int reserve, cudaStream_t stream,
+                                     cudaStream_t cs) {
+    const long long elems = 2LL * B * H * C * D;
+    const size_t kv_bytes = static_cast<size_t>(elems) * sizeof(T);
+    const size_t acc_bytes = 2 * static_cast<size_t>(elems) * sizeof(float);  // dK, dV
+    const long long bwd_ws = cuflash_attention_backward_cp_workspace_size(2, B, H, C, D);
+    if (bwd_ws <= 0) return FlashAttentionError::INVALID_DIMENSION;
+    const size_t bwd_bytes = (static_cast<size_t>(bwd_ws) + 255) & ~static_cast<size_t>(255);
+    void* ws = nullptr;
+    FlashAttentionError e = ws_alloc(&ws, bwd_bytes + acc_bytes, stream);
+    if (e != FlashAttentionError::SUCCESS) return e;
+    char* base = static_cast<char*>(ws);
+    void* ws_bwd = base;
+    float* own = reinterpret_cast<float*>(base + bwd_bytes);  // this rank's chunks (step 0)
+    float* part[2] = {ctx.part(0), ctx.part(1)};  // pushed from: in the peer allocation
+    const PullPlan<T> pp{&ctx, rank, world, ctx.calls + 1, kv_bytes};
+    const long long k = pp.k;
+    Events evs;
+    cudaEvent_t recv[kMaxWorld] = {};
+    cudaEvent_t comp[kMaxWorld] = {};
+    cudaEvent_t pushed[kMaxWorld] = {};
+    e = code(CpOps<T>::bwd_prepare(O, dO, L, ws_bwd, B, H, C, D, stream));
+    bool ok = e == FlashAttentionError::SUCCESS;
+    ok = ok && cudaMemsetAsync(own, 0, acc_bytes, stream) == cudaSuccess;
+    ok = ok && join(evs, cs, stream);
+    ok = ok && export_kv(pp, K, V, cs);
+    for (int s = 1; ok && s < world && s <= 2; ++s) ok = pull_kv(pp, s, nullptr, evs, cs, &recv[s]);
+    for (int s = 0; ok && s < world; ++s) {
+        const StepPlan p = plan_step(rank, world, s, causal);
+        const T* ck = s == 0 ? K : reinterpret_cast<const T*>(pp.slot(s));
+        const T* cv = s == 0 ? V : reinterpret_cast<const T*>(pp.slot(s) + kv_bytes);
+        float* target = s == 0 ? own : part[s % 2];
+        if (s >= 1) {
+            ok = cudaStreamWaitEvent(stream, recv[s], 0) == cudaSuccess;
+            // the part buffer's previous contents (step s - 2) have been pushed
+            if (ok && s >= 3) ok = cudaStreamWaitEvent(stream, pushed[s - 2], 0) == cudaSuccess;
+            ok = ok && cudaMemsetAsync(target, 0, acc_bytes, stream) == cudaSuccess;
+        }
+        if (ok && p.n > 0) {
+            int qs[4], ks[4];
+            long long qo[4], ko[4];
+            for (int i = 0; i < p.n; ++i) {
+                qs[i] = p.q_slot[i];
+                ks[i] = p.kv_slot[i];
+                qo[i] = static_cast<long long>(p.q_chunk[i]) * C;
+                ko[i] = static_cast<long long>(p.kv_chunk[i]) * C;
+            }
+            e = code(CpOps<T>::bwd_step(Q, dO, ck, cv, ws_bwd, target, target + elems, B, H, C, D,
+                                        scale, causal, p.n, qs, ks, qo, ko, reserve, stream));
+            ok = e == FlashAttentionError::SUCCESS || cuflash_cp::debug_fail("backward step");
+        }
+        if (!ok || s == 0) continue;
+        comp[s] = evs.make();
+        ok = comp[s] != nullptr && cudaEventRecord(comp[s], stream) == cudaSuccess;
+        // push this step's dK/dV to the owner of X_s, once the owner has summed
+        // this rank's contribution of the last backward call (only backward
+        // calls advance that flag)
+        const int o = pp.owner(s);
+        ok = ok && cudaStreamWaitEvent(cs, comp[s], 0) == cudaSuccess;
+        ok = ok && cuflash_cp::wait_geq(ctx.flags + 2 + world + o, ctx.last_bwd, cs);
+        ok = ok && cudaMemcpyAsync(ctx.r_slot(o, rank), target, acc_bytes,
+                                   cudaMemcpyDeviceToDevice, cs) == cudaSuccess;
+        ok = ok && cuflash_cp::signal(ctx.fl(o) + 2 + rank, k, cs);
+        pushed[s] = ok ? evs.make() : nullptr;
+        ok = (ok && pushed[s] != nullptr && cudaEventRecord(pushed[s], cs) == cudaSuccess) ||
+             cuflash_cp::debug_fail("push");
+        if (ok && s + 2 < world) ok = pull_kv(pp, s + 2, comp[s], evs, cs, &recv[s + 2]);
+    }
+    ok = ok && join(evs, stream, cs);
+    // every other rank's contribution to this rank's chunks has landed
+    ok = ok && cuflash_cp::wait_all_geq(ctx.flags + 2, world, rank, k, stream);
+    if (ok) {
+        e = code(CpOps<T>::bwd_finish(ws_bwd, dQ, B, H, C, D, scale, stream));
+        ok = e == FlashAttentionError::SUCCESS;
+    }
+    ok = ok && cuflash_cp::sum_contributions<T>(ctx, own, dK, dV, elems, stream);
+    // the senders may overwrite their slots on this rank in the next call
+    ok = ok && cuflash_cp::signal_peers(ctx, 2 + world + rank, k, stream);
+    if (!ok) join(evs, stream, cs);
+    cudaFreeAsync(ws, stream);
+    ++ctx.calls;
+    ctx.last_bwd = k;
+    if (!ok) return e != FlashAttentionError::SUCCESS ? e : FlashAttentionError::CUDA_ERROR;
+    return FlashAttentionError::SUCCESS;
+}
+
+// The transport of a call with world > 1: sets *ctx for the copy-engine
+// transport, leaves it null for NCCL.
+FlashAttentionError pick_transport(ncclComm_t comm, int rank, int world, size_t e_bytes,
+                                   size_t r_bytes, cudaStream_t cs, PeerCtx** ctx) {
+    *ctx = nullptr;
+    return cuflash_cp::peer_acquire(comm, rank, world, e_bytes, r_bytes, cs, ctx);
 }
 
 // ------------------------------------------------------------------ forward
@@ -314,9 +532,17 @@ FlashAttentionError forward_cp(const T* Q, const T* K, const T* V, T* O, float* 
     const size_t kv_bytes = static_cast<size_t>(elems) * sizeof(T);
     const size_t oacc_bytes = static_cast<size_t>(elems) * sizeof(float);
     const size_t ws_bytes = oacc_bytes + (world > 1 ? 4 * kv_bytes : 0);
-    const int reserve = effective_reserve(reserve_sms, world);
     cudaStream_t cs = world > 1 ? comm_stream() : nullptr;
     if (world > 1 && cs == nullptr) return FlashAttentionError::CUDA_ERROR;
+    if (world > 1) {
+        PeerCtx* ctx = nullptr;
+        e = pick_transport(comm, rank, world, 2 * kv_bytes, 0, cs, &ctx);
+        if (e != FlashAttentionError::SUCCESS) return e;
+        if (ctx != nullptr)
+            return forward_cp_peer<T>(*ctx, Q, K, V, O, L, B, H, C, D, scale, causal, rank, world,
+                                      effective_reserve(reserve_sms, world, true), stream, cs);
+    }
+    const int reserve = effective_reserve(reserve_sms, world, false);
 
     void* ws = nullptr;
     e = ws_alloc(&ws, ws_bytes, stream);
@@ -413,9 +639,18 @@ FlashAttentionError backward_cp(const T* Q, const T* K, const T* V, const T* O, 
     const int n_part = world > 1 ? 2 : 0;
     const size_t ws_bytes =
         bwd_bytes + (n_acc + n_part) * acc_bytes + (world > 1 ? 4 * kv_bytes : 0);
-    const int reserve = effective_reserve(reserve_sms, world);
     cudaStream_t cs = world > 1 ? comm_stream() : nullptr;
     if (world > 1 && cs == nullptr) return FlashAttentionError::CUDA_ERROR;
+    if (world > 1) {
+        PeerCtx* ctx = nullptr;
+        e = pick_transport(comm, rank, world, 2 * kv_bytes, acc_bytes, cs, &ctx);
+        if (e != FlashAttentionError::SUCCESS) return e;
+        if (ctx != nullptr)
+            return backward_cp_peer<T>(*ctx, Q, K, V, O, L, dO, dQ, dK, dV, B, H, C, D, scale,
+                                       causal, rank, world,
+                                       effective_reserve(reserve_sms, world, true), stream, cs);
+    }
+    const int reserve = effective_reserve(reserve_sms, world, false);
 
     void* ws = nullptr;
     e = ws_alloc(&ws, ws_bytes, stream);
@@ -623,9 +858,18 @@ int cuflash_cp_nccl_comm_init(ncclComm_t* comm, int world, const void* unique_id
 
 int cuflash_cp_nccl_comm_destroy(ncclComm_t comm) {
     if (comm == nullptr) return static_cast<int>(FlashAttentionError::NULL_POINTER);
+    cuflash_cp::peer_release(comm);
     return static_cast<int>(ncclCommDestroy(comm) == ncclSuccess
                                 ? FlashAttentionError::SUCCESS
                                 : FlashAttentionError::CUDA_ERROR);
 }
+
+int cuflash_cp_set_transport(int transport) {
+    return cuflash_cp::set_transport(transport) == 0
+               ? static_cast<int>(FlashAttentionError::SUCCESS)
+               : static_cast<int>(FlashAttentionError::INVALID_DIMENSION);
+}
+
+int cuflash_cp_transport_status(void) { return cuflash_cp::status_read_and_clear(); }
 
 }  // extern "C"

@@ -47,6 +47,8 @@ CP_SIGNATURES = {
     "cuflash_cp_nccl_comm_init": [_P, _I, _P, _I],
     "cuflash_cp_nccl_comm_init_config": [_P, _I, _P, _I, _I],
     "cuflash_cp_nccl_comm_destroy": [_P],
+    "cuflash_cp_set_transport": [_I],
+    "cuflash_cp_transport_status": [],
 }
 
 _cp_lib = None
@@ -139,6 +141,22 @@ def nccl_unique_id() -> bytes:
     buf = ctypes.create_string_buffer(UNIQUE_ID_BYTES)
     _check(load_cp_library().cuflash_cp_nccl_unique_id(ctypes.cast(buf, _P), UNIQUE_ID_BYTES))
     return buf.raw
+
+
+TRANSPORT_PEER = 0  # copy engine over CUDA IPC (the library's default)
+TRANSPORT_NCCL = 1  # NCCL send/recv ring
+
+
+def set_transport(transport: int) -> None:
+    """Transport of the ring entry points for this process
+    (cuflash_cp_set_transport); every rank must choose the same."""
+    _check(load_cp_library().cuflash_cp_set_transport(int(transport)))
+
+
+def transport_status() -> int:
+    """Reads and clears the copy-engine transport's status (1: a wait for
+    another rank gave up)."""
+    return int(load_cp_library().cuflash_cp_transport_status())
 
 
 class NcclComm:

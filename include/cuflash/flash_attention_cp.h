@@ -113,6 +113,31 @@ CUFLASH_EXPORT int cuflash_cp_nccl_comm_init_config(ncclComm_t* comm, int world,
                                                     int max_ctas);
 CUFLASH_EXPORT int cuflash_cp_nccl_comm_destroy(ncclComm_t comm);
 
+// Transport of the ring entry points (process-wide; every rank of a
+// communicator must use the same one, else the entry points return
+// DIMENSION_MISMATCH on every rank):
+//   0  copy engine over CUDA IPC (the default): each rank exports its K/V
+//      chunks, the others pull them with copy-engine copies over NVLink and
+//      push their dK/dV contributions straight to the owner; no SMs go to the
+//      transfers (the step kernels leave 2 free for one-thread flag kernels).
+//      The communicator is used for set-up and a small all-reduce per call;
+//      ranks whose processes cannot open each other's memory (CUDA IPC) fall
+//      back to NCCL together.
+//   1  NCCL send/recv ring (the step kernels leave 16 SMs free by default).
+// The environment variable CUFLASH_CP_TRANSPORT=nccl selects 1 at start-up.
+// comm_destroy releases the communicator's copy-engine context: call it on
+// every rank once every rank's ring calls have completed (for instance after
+// a device synchronisation and a barrier), since peers write into the
+// context's memory.
+CUFLASH_EXPORT int cuflash_cp_set_transport(int transport);
+
+// Waits of the copy-engine transport for another rank give up after 60 s
+// (CUFLASH_CP_WAIT_LIMIT_MS), so that a rank that left does not hang the
+// others: the entry points then return CUDA_ERROR, on every rank of the
+// communicator, until this function (which reads and clears the status, 1 =
+// a wait gave up) has been called on the ranks where a wait gave up.
+CUFLASH_EXPORT int cuflash_cp_transport_status(void);
+
 #ifdef __cplusplus
 }
 #endif

@@ -8,7 +8,13 @@
   an NCCL communicator made through the library's helpers (its unique id
   handed out over a gloo group), the same full-sequence inputs on every rank;
   each rank's output chunks and gradients against the single-GPU entry points
-  and the fp64 oracle on sampled rows.  NVLS is off (NCCL_NVLS_ENABLE=0).
+  and the fp64 oracle on sampled rows, over both transports (copy engine
+  over CUDA IPC, NCCL send/recv).  Three shapes in a row: the second reuses
+  the copy-engine context of the first, the third needs larger buffers and
+  rebuilds it.  NVLS is off (NCCL_NVLS_ENABLE=0).
+* A rank whose export never gets signalled (a host-side test switch): the
+  other rank's bounded wait gives up, its transport status reads 1, and the
+  next call returns CUDA_ERROR on both ranks until the status is cleared.
 """
 
 import os
@@ -119,7 +125,7 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _nccl_worker(rank, world, port, result_dir):
+def _nccl_worker(rank, world, port, result_dir, transport):
     import torch
     import torch.distributed as dist
 
@@ -139,11 +145,13 @@ def _nccl_worker(rank, world, port, result_dir):
         dist.broadcast_object_list(obj, src=0)
         comm = ring_cp.NcclComm(world, rank, obj[0])
         lib = cuflash_attn.CuFlashAttn()
+        ring_cp.set_transport(transport)
         ring = ring_cp.RingAttention(comm)
-        B, H, D, C = 1, 4, 128, 256
-        N = 2 * world * C
+        B, H, D = 1, 4, 128
         lines = []
-        for dt, causal, seed in (("bf16", True, 17), ("f16", False, 23)):
+        for dt, causal, seed, C in (("bf16", True, 17, 256), ("f16", False, 23, 256),
+                                    ("bf16", True, 29, 384)):
+            N = 2 * world * C
             arrs = [round_to(oracle.normal((B, H, N, D), seed + i), dt) for i in range(4)]
             err_lib, err_64 = _check_rank(lib, ring, rank, world, *arrs, dt, causal, C)
             lines.append(f"{dt} {causal} {err_lib} {err_64} {err_lib < TOL and err_64 < TOL}")
@@ -156,26 +164,28 @@ def _nccl_worker(rank, world, port, result_dir):
         dist.destroy_process_group()
 
 
-def _run_ring(world, tmp_path):
+def _run_ring(world, tmp_path, transport):
     import torch.multiprocessing as mp
 
-    mp.start_processes(_nccl_worker, args=(world, _free_port(), str(tmp_path)), nprocs=world,
-                       join=True, start_method="spawn")
+    mp.start_processes(_nccl_worker, args=(world, _free_port(), str(tmp_path), transport),
+                       nprocs=world, join=True, start_method="spawn")
     for r in range(world):
         for line in (tmp_path / f"rank{r}.txt").read_text().split("\n"):
             if line:
                 assert line.split()[-1] == "True", (r, line)
 
 
-def test_ring_entry_over_nccl_two_gpus(tmp_path):
+@pytest.mark.parametrize("transport", [ring_cp.TRANSPORT_PEER, ring_cp.TRANSPORT_NCCL])
+def test_ring_entry_over_nccl_two_gpus(tmp_path, transport):
     import torch
 
     if torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")
-    _run_ring(2, tmp_path)
+    _run_ring(2, tmp_path, transport)
 
 
-def test_ring_entry_over_nccl_every_gpu(tmp_path):
+@pytest.mark.parametrize("transport", [ring_cp.TRANSPORT_PEER, ring_cp.TRANSPORT_NCCL])
+def test_ring_entry_over_nccl_every_gpu(tmp_path, transport):
     """The same over every GPU of the box when it has more than two (eight
     on the BASELINE's context-parallel setting), one rank per GPU."""
     import torch
@@ -183,4 +193,65 @@ def test_ring_entry_over_nccl_every_gpu(tmp_path):
     world = torch.cuda.device_count()
     if world <= 2:
         pytest.skip("needs more than two GPUs")
-    _run_ring(world, tmp_path)
+    _run_ring(world, tmp_path, transport)
+
+
+def _timeout_worker(rank, world, port, result_dir):
+    import torch
+    import torch.distributed as dist
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    os.environ["CUFLASH_CP_WAIT_LIMIT_MS"] = "300"
+    if rank == 1:
+        os.environ["CUFLASH_CP_TEST_SKIP_EXPORT_SIGNAL"] = "1"
+    torch.cuda.set_device(rank)
+    from datetime import timedelta
+
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=120))
+    comm = None
+    try:
+        obj = [ring_cp.nccl_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(obj, src=0)
+        comm = ring_cp.NcclComm(world, rank, obj[0])
+        ring_cp.set_transport(ring_cp.TRANSPORT_PEER)
+        fn = ring_cp.load_cp_library().cuflash_attention_forward_cp_bf16
+        B, H, C, D = 1, 2, 128, 64
+        x = torch.randn((2, B, H, C, D), device="cuda").to(torch.bfloat16)
+        O = torch.empty_like(x)
+        L = torch.empty((2, B, H, C), device="cuda")
+        p = ring_cp.cf._ptr
+        st = ring_cp.cf._stream_handle(None)
+        call = lambda: fn(p(x), p(x), p(x), p(O), p(L), B, H, 2 * world * C, D, 0.1, True,
+                          comm.handle, rank, world, -1, st)
+        codes = [call()]  # rank 0's wait for rank 1's export gives up after 300 ms
+        torch.cuda.synchronize()
+        codes.append(call())  # refused on both ranks: rank 0's status is set
+        status = ring_cp.transport_status() if rank == 0 else 0
+        dist.barrier()
+        codes.append(call())  # accepted again once the status has been read
+        torch.cuda.synchronize()
+        ring_cp.transport_status()
+        with open(os.path.join(result_dir, f"rank{rank}.txt"), "w") as f:
+            f.write(f"{codes[0]} {codes[1]} {codes[2]} {status}\n")
+    finally:
+        dist.barrier()
+        if comm is not None:
+            comm.destroy()
+        dist.destroy_process_group()
+
+
+def test_peer_transport_wait_gives_up(tmp_path):
+    import torch
+    import torch.multiprocessing as mp
+
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    mp.start_processes(_timeout_worker, args=(2, _free_port(), str(tmp_path)), nprocs=2,
+                       join=True, start_method="spawn")
+    r0 = (tmp_path / "rank0.txt").read_text().split()
+    r1 = (tmp_path / "rank1.txt").read_text().split()
+    ok, err = str(ring_cp.cf.SUCCESS), str(ring_cp.cf.CUDA_ERROR)
+    assert r0[:3] == [ok, err, ok] and r1[:3] == [ok, err, ok], (r0, r1)
+    assert r0[3] == "1"
