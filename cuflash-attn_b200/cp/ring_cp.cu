@@ -1,5 +1,8 @@
-// Context-parallel attention over NCCL: the ring driver behind
-// cuflash_attention_{forward,backward}_cp_{bf16,f16} (libcuflash_attn_cp.so).
+// Context-parallel attention: the ring drivers behind
+// cuflash_attention_{forward,backward}_cp_{bf16,f16} (libcuflash_attn_cp.so),
+// over either transport: copy-engine copies between CUDA-IPC-shared buffers
+// (the default; drivers forward_cp_peer / backward_cp_peer below, transport
+// in peer_ring.cu) or NCCL send/recv (forward_cp / backward_cp).
 //
 // The reference library is single-device; this file has no counterpart
 // there.  It keeps the reference's C-ABI conventions (validation before any
@@ -8,9 +11,9 @@
 // every step's attention through libcuflash_attn.so's one-launch ring-step
 // entry points; the only kernel here fills the running log-sum-exp with -inf.
 //
-// Streams.  The caller's stream runs the step kernels; a library-owned stream
-// per device (comm) runs the NCCL groups and, in the backward, the fp32 adds
-// of the travelling dK/dV accumulators.  K/V of step s (X_s) is the caller's
+// Streams (NCCL transport).  The caller's stream runs the step kernels; a
+// library-owned stream per device (comm) runs the NCCL groups and, in the
+// backward, the fp32 adds of the travelling dK/dV accumulators.  K/V of step s (X_s) is the caller's
 // K/V for s = 0 and ring buffer (s - 1) % 2 afterwards; the group of step s
 // sends X_s to rank + 1 and receives X_{s+1} from rank - 1 into the buffer
 // that X_{s-1} used, after step s - 1's kernels have read it.  Step s + 1's
@@ -24,8 +27,10 @@
 
 #include <cmath>
 #include <cstdint>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
+#include <vector>
 
 #include "cuflash/flash_attention.h"
 #include "cuflash/flash_attention_cp.h"
@@ -158,18 +163,15 @@ FlashAttentionError fill_f32(float* dst, float value, long long n, cudaStream_t 
 // Events of one call, destroyed when the call returns (an event destroyed
 // while its record is pending is released once it completes).
 struct Events {
-    static constexpr int kMax = 4 * kMaxWorld + 8;
-    cudaEvent_t ev[kMax] = {};
-    int n = 0;
+    std::vector<cudaEvent_t> ev;
     cudaEvent_t make() {
-        if (n >= kMax) return nullptr;
         cudaEvent_t e = nullptr;
         if (cudaEventCreateWithFlags(&e, cudaEventDisableTiming) != cudaSuccess) return nullptr;
-        ev[n++] = e;
+        ev.push_back(e);
         return e;
     }
     ~Events() {
-        for (int i = 0; i < n; ++i) cudaEventDestroy(ev[i]);
+        for (cudaEvent_t e : ev) cudaEventDestroy(e);
     }
 };
 
@@ -316,6 +318,13 @@ int effective_reserve(int reserve_sms, int world, bool peer) {
 // pushes step s's dK/dV (s >= 1) into its owner's slot for this rank and,
 // at the end, sums its own and the W - 1 received contributions.
 
+// A copy between GPUs (or into the export), on the comm stream: one
+// copy-engine copy.  (Splitting it over several streams and engines was
+// measured: no change at 8 GPUs, the copies are not the limiter.)
+bool peer_copy(void* dst, const void* src, size_t bytes, cudaStream_t cs) {
+    return cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToDevice, cs) == cudaSuccess;
+}
+
 template <typename T>
 struct PullPlan {
     PeerCtx* ctx;
@@ -333,9 +342,8 @@ bool export_kv(const PullPlan<T>& pp, const T* K, const T* V, cudaStream_t cs) {
     PeerCtx& c = *pp.ctx;
     // readers of the previous call's export are done (their flags on this rank)
     bool ok = cuflash_cp::wait_all_geq(c.flags + 2 + 2 * pp.world, pp.world, pp.rank, c.calls, cs);
-    ok = ok && cudaMemcpyAsync(c.mem, K, pp.kv_bytes, cudaMemcpyDeviceToDevice, cs) == cudaSuccess;
-    ok = ok && cudaMemcpyAsync(c.mem + pp.kv_bytes, V, pp.kv_bytes, cudaMemcpyDeviceToDevice, cs) ==
-                   cudaSuccess;
+    ok = ok && peer_copy(c.mem, K, pp.kv_bytes, cs);
+    ok = ok && peer_copy(c.mem + pp.kv_bytes, V, pp.kv_bytes, cs);
     if (cuflash_cp::test_skip_export_signal()) return ok || cuflash_cp::debug_fail("export");
     return (ok && cuflash_cp::signal(c.flags + 0, pp.k, cs)) || cuflash_cp::debug_fail("export");
 }
@@ -349,8 +357,7 @@ bool pull_kv(const PullPlan<T>& pp, int s, cudaEvent_t prev_reader, Events& evs,
     const int o = pp.owner(s);
     bool ok = prev_reader == nullptr || cudaStreamWaitEvent(cs, prev_reader, 0) == cudaSuccess;
     ok = ok && cuflash_cp::wait_geq(c.fl(o) + 0, pp.k, cs);
-    ok = ok && cudaMemcpyAsync(pp.slot(s), c.e(o), 2 * pp.kv_bytes, cudaMemcpyDeviceToDevice, cs) ==
-                   cudaSuccess;
+    ok = ok && peer_copy(pp.slot(s), c.e(o), 2 * pp.kv_bytes, cs);
     // this rank is done reading o's export
     ok = ok && cuflash_cp::signal(c.fl(o) + 2 + 2 * pp.world + pp.rank, pp.k, cs);
     *done = ok ? evs.make() : nullptr;
@@ -481,8 +488,7 @@ FlashAttentionError backward_cp_peer(PeerCtx& ctx, const T* Q, const T* K, const
         const int o = pp.owner(s);
         ok = ok && cudaStreamWaitEvent(cs, comp[s], 0) == cudaSuccess;
         ok = ok && cuflash_cp::wait_geq(ctx.flags + 2 + world + o, ctx.last_bwd, cs);
-        ok = ok && cudaMemcpyAsync(ctx.r_slot(o, rank), target, acc_bytes,
-                                   cudaMemcpyDeviceToDevice, cs) == cudaSuccess;
+        ok = ok && peer_copy(ctx.r_slot(o, rank), target, acc_bytes, cs);
         ok = ok && cuflash_cp::signal(ctx.fl(o) + 2 + rank, k, cs);
         pushed[s] = ok ? evs.make() : nullptr;
         ok = (ok && pushed[s] != nullptr && cudaEventRecord(pushed[s], cs) == cudaSuccess) ||
