@@ -6,10 +6,13 @@ The ring runs in the C library (``cuflash_attention_{forward,backward}_cp_*``,
 ``include/cuflash/flash_attention_cp.h``): the sequence of length N is cut
 into 2P chunks of C = N / (2P) tokens, rank r of P holds chunks r and
 2P-1-r ("zigzag", equal causal work per rank), keeps its query chunks and
-passes its K/V chunks around the ring over NCCL send/recv while the step
-kernels run; the backward carries fp32 dK/dV accumulators with the K/V they
-belong to.  This module only stacks torch tensors into the library's shard
-layout, creates NCCL communicators through the library's helpers, and reads
+at step s computes with the K/V chunks of rank r - s while the next ones
+travel: by default pulled from that rank's CUDA-IPC-shared export with a
+copy-engine copy (the backward pushes its fp32 dK/dV straight to the
+owner), or passed around the ring with NCCL send/recv (the backward then
+carries fp32 dK/dV accumulators with the K/V they belong to).  This module
+only stacks torch tensors into the library's shard layout, creates NCCL
+communicators through the library's helpers, selects the transport, and reads
 the ring schedule (``cuflash_cp_ring_schedule``) for callers and tests that
 drive the per-step entry points themselves.
 
@@ -179,9 +182,10 @@ class NcclComm:
 
 class RingAttention:
     """Context-parallel causal attention of one rank's zigzag shard through
-    the library's NCCL ring.  ``comm`` is an :class:`NcclComm` (or None with
-    a single rank).  Each rank passes its shard as two chunks [B, H, C, D]
-    (global chunks rank and 2*world-1-rank)."""
+    the library's ring entry points (transport: :func:`set_transport`).
+    ``comm`` is an :class:`NcclComm` (or None with a single rank).  Each rank
+    passes its shard as two chunks [B, H, C, D] (global chunks rank and
+    2*world-1-rank)."""
 
     def __init__(self, comm: Optional[NcclComm] = None, rank: int = 0, world: int = 1,
                  reserve_sms: int = -1):

@@ -89,6 +89,22 @@ def test_cp_comm_helpers_validate_before_nccl():
     assert lib.cuflash_cp_nccl_comm_destroy(None) == cf.NULL_POINTER
 
 
+def test_cp_transport_switch_and_status_need_no_gpu():
+    """cuflash_cp_set_transport accepts 0 (copy engine) and 1 (NCCL) only;
+    the transport status reads 0 before any wait ran."""
+    import ring_cp
+
+    lib = ring_cp.load_cp_library()
+    assert lib.cuflash_cp_set_transport(2) == cf.INVALID_DIMENSION
+    assert lib.cuflash_cp_set_transport(-1) == cf.INVALID_DIMENSION
+    try:
+        ring_cp.set_transport(ring_cp.TRANSPORT_NCCL)
+        ring_cp.set_transport(ring_cp.TRANSPORT_PEER)
+    finally:
+        ring_cp.set_transport(ring_cp.TRANSPORT_PEER)
+    assert ring_cp.transport_status() == 0
+
+
 def test_library_hides_internal_symbols():
     import subprocess
 
