@@ -60,7 +60,10 @@ constexpr float kLog2eB = 1.4426950408889634f;
 // the FMA pipe (exp2_poly2, relative error below 1e-4, far under the 16-bit
 // rounding that P and dS receive) instead of the MUFU unit, which the
 // pipelined softmax below saturates.  Measured on B200: k = 4 takes config 3
-// from 4.11 to 3.89 ms (k = 2: 3.99, k = 8: 3.97).
+// from 4.11 to 3.89 ms (k = 2: 3.99, k = 8: 3.97).  Re-measured on the
+// current kernel (main kernel, two alternating runs each): k = 4 3.03-3.06
+// ms, off 2.99-3.03, k = 8 3.02-3.04, k = 2 3.08-3.14; MUFU no longer
+// binds, and k = 4 stays.
 #ifndef CUFLASH_BWD_EXP2_EMU_EVERY
 #define CUFLASH_BWD_EXP2_EMU_EVERY 4
 #endif
