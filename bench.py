@@ -475,10 +475,14 @@ def run_ours(args):
     torch.cuda.empty_cache()
 
     # ---- config 5 through the context-parallel ring over all ranks -------------
-    cp = None
+    cp = cp_train = None
     if not args.skip_extras:
         cp = run_cp(args, dev, world, rank, pk, pk_kind, backward=False,
                     steps=min(args.steps, 5 if world == 1 else 10), warmup=2)
+        torch.cuda.empty_cache()
+        # the training step of config 5: ring forward + ring backward
+        cp_train = run_cp(args, dev, world, rank, pk, pk_kind, backward=True,
+                          steps=min(args.steps, 3 if world == 1 else 5), warmup=1)
         torch.cuda.empty_cache()
 
     # ---- single-GPU extras (N = 1) ----------------------------------------------
@@ -552,6 +556,7 @@ def run_ours(args):
                     "ms_per_step": e2e_ms, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
             "weak": weak,
             "cp": cp,
+            "cp_train": cp_train,
             "decode": decode,
             "fp32": fp32,
             "config2": config2,
