@@ -188,6 +188,7 @@ void destroy_ctx(PeerCtx* c) {
     }
     if (c->mem != nullptr) cudaFree(c->mem);
     if (c->flags != nullptr) cudaFree(c->flags);
+    if (c->last_use != nullptr) cudaEventDestroy(c->last_use);
     delete c;
 }
 
@@ -255,6 +256,7 @@ PeerCtx* build_ctx(ncclComm_t comm, int dev, int rank, int world, size_t e_cap, 
     ok = ok && cudaMalloc(reinterpret_cast<void**>(&c->flags), nflags * sizeof(long long)) ==
                    cudaSuccess;
     ok = ok && cudaMemset(c->flags, 0, nflags * sizeof(long long)) == cudaSuccess;
+    ok = ok && cudaEventCreateWithFlags(&c->last_use, cudaEventDisableTiming) == cudaSuccess;
     cudaIpcMemHandle_t hm{}, hf{};
     ok = ok && cudaIpcGetMemHandle(&hm, c->mem) == cudaSuccess &&
          cudaIpcGetMemHandle(&hf, c->flags) == cudaSuccess;

@@ -58,6 +58,10 @@ struct PeerCtx {
     long long* peer_flags[256] = {};
     long long calls = 0;      // calls completed with this context (the same on all ranks)
     long long last_bwd = 0;   // number of the last backward call (0: none yet)
+    // recorded on the caller's stream after a call's last read of the pull
+    // slots and part buffers; the next call's comm stream waits for it
+    // (whatever stream that call is given)
+    cudaEvent_t last_use = nullptr;
 
     static size_t bytes(size_t e_cap, size_t r_cap, int world) {
         return 3 * e_cap + (2 + static_cast<size_t>(world)) * r_cap;

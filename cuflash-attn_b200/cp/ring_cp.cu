@@ -385,6 +385,8 @@ FlashAttentionError forward_cp_peer(PeerCtx& ctx, const T* Q, const T* K, const 
     if (ok) e = fill_f32(L, -INFINITY, elems / D, stream);
     ok = ok && e == FlashAttentionError::SUCCESS;
     ok = ok && join(evs, cs, stream);  // K, V, the workspace and the last call's readers
+    // the previous call's kernels, on whatever stream, are done with the slots
+    ok = ok && cudaStreamWaitEvent(cs, ctx.last_use, 0) == cudaSuccess;
     ok = ok && export_kv(pp, K, V, cs);
     for (int s = 1; ok && s < world && s <= 2; ++s) ok = pull_kv(pp, s, nullptr, evs, cs, &recv[s]);
     for (int s = 0; ok && s < world; ++s) {
@@ -418,6 +420,7 @@ FlashAttentionError forward_cp_peer(PeerCtx& ctx, const T* Q, const T* K, const 
         ok = e == FlashAttentionError::SUCCESS;
     }
     join(evs, stream, cs);
+    cudaEventRecord(ctx.last_use, stream);
     cudaFreeAsync(ws, stream);
     ++ctx.calls;  // every rank counts every call, failed or not
     if (!ok) return e != FlashAttentionError::SUCCESS ? e : FlashAttentionError::CUDA_ERROR;
@@ -453,6 +456,9 @@ FlashAttentionError backward_cp_peer(PeerCtx& ctx, const T* Q, const T* K, const
     bool ok = e == FlashAttentionError::SUCCESS;
     ok = ok && cudaMemsetAsync(own, 0, acc_bytes, stream) == cudaSuccess;
     ok = ok && join(evs, cs, stream);
+    ok = ok && cudaStreamWaitEvent(cs, ctx.last_use, 0) == cudaSuccess;
+    // the part buffers are written on `stream`: after the previous call too
+    ok = ok && cudaStreamWaitEvent(stream, ctx.last_use, 0) == cudaSuccess;
     ok = ok && export_kv(pp, K, V, cs);
     for (int s = 1; ok && s < world && s <= 2; ++s) ok = pull_kv(pp, s, nullptr, evs, cs, &recv[s]);
     for (int s = 0; ok && s < world; ++s) {
@@ -506,6 +512,7 @@ FlashAttentionError backward_cp_peer(PeerCtx& ctx, const T* Q, const T* K, const
     // the senders may overwrite their slots on this rank in the next call
     ok = ok && cuflash_cp::signal_peers(ctx, 2 + world + rank, k, stream);
     if (!ok) join(evs, stream, cs);
+    cudaEventRecord(ctx.last_use, stream);
     cudaFreeAsync(ws, stream);
     ++ctx.calls;
     ctx.last_bwd = k;
