@@ -18,24 +18,33 @@
 // [2][B][H][C][D] (slot 0 = chunk r, slot 1 = chunk 2 * world - 1 - r), and of
 // L [B, H, seq_len] as [2][B][H][C].
 //
-// Each rank keeps its query chunks and passes its K/V chunks around the ring
-// (rank r sends to r + 1 and receives from r - 1) with grouped ncclSend /
-// ncclRecv on a library-owned stream, one hop per step, overlapped with the
-// step's attention kernels on the caller's stream; every received chunk is in
-// local device memory before a kernel reads it.  All ranks of `comm` must make
-// the same call with the same shapes; a rank that does not leaves the others'
-// NCCL transfers waiting, as with any NCCL collective (callers that need to
-// recover use ncclCommAbort from a watchdog).  The communicator must be a
-// blocking one (NCCL's default) of at most 256 ranks.  An NCCL failure
-// returns CUDA_ERROR and leaves the communicator in an unknown state.
+// Each rank keeps its query chunks and, at step s, computes with the K/V
+// chunks of rank (r - s) mod world while the next ones travel, on
+// library-owned streams overlapped with the step's attention kernels on the
+// caller's stream; every chunk is in local device memory before a kernel
+// reads it.  Two transports (cuflash_cp_set_transport, below): copy-engine
+// copies between CUDA-IPC-shared buffers (the default; the backward pushes
+// its fp32 dK/dV straight to the chunks' owner), or a ring of grouped
+// ncclSend / ncclRecv (rank r sends to r + 1, receives from r - 1; the
+// backward carries fp32 dK/dV accumulators with their K/V).  All ranks of
+// `comm` must make the same call with the same shapes; a rank that does not
+// leaves the others waiting in the per-call all-reduce (or the NCCL
+// transfers), as with any NCCL collective (callers that need to recover use
+// ncclCommAbort from a watchdog).  The communicator must be a blocking one
+// (NCCL's default) of at most 256 ranks.  An NCCL failure returns CUDA_ERROR
+// and leaves the communicator in an unknown state.
 //
-// reserve_sms: SMs each step kernel leaves free so that NCCL's transfer
-// kernels run beside it instead of after it; -1 picks the default (16 with
-// world > 1, measured best on 8 B200s at B1 H32 N131072 D128), 0 uses every
-// SM.  With world == 1 no transfer runs and comm may be NULL.
+// reserve_sms: SMs each step kernel leaves free for what runs beside it;
+// -1 picks the default: 2 with the copy-engine transport (its one-thread
+// flag kernels), 16 with NCCL (its transfer kernels; measured best on 8
+// B200s at B1 H32 N131072 D128); 0 uses every SM.  With world == 1 no
+// transfer runs and comm may be NULL.
 //
-// Workspace is allocated stream-ordered inside the call and freed before it
-// returns (as the reference's backward does); OUT_OF_MEMORY if that fails.
+// Workspace (accumulators) is allocated stream-ordered inside the call and
+// freed before it returns (as the reference's backward does); OUT_OF_MEMORY
+// if that fails.  The copy-engine transport also keeps one cudaMalloc
+// allocation per communicator (exports, pull slots, receive slots) until
+// cuflash_cp_nccl_comm_destroy.
 
 #include <nccl.h>
 
